@@ -1,0 +1,394 @@
+/*
+ * klearu_gpu.h -- C ABI of the B200 (sm_100a) SLIDE sparse-layer engine.
+ *
+ * This is the drop-in boundary for klearu-core's SLIDE hot path.  Every entry
+ * point below replaces one method of the Rust reference API and cites it as
+ * `crates/<crate>/src/<file>:<line>`.  A Rust FFI crate binds these symbols 1:1
+ * (`extern "C"` block + `#[repr(C)]` mirrors of the structs below).
+ *
+ * Conventions
+ *  - Every pointer argument is a caller-owned DEVICE buffer unless its name ends
+ *    in `_host`, in which case it is host memory.  Configuration structs and the
+ *    explicit hash/weight parameter arrays passed at creation time are host memory.
+ *  - Every call returns a kl_status.  No C++ exception crosses this boundary.
+ *    On failure, kl_last_error(ctx) returns a message for the failing call.
+ *  - A context is bound to one CUDA device and one CUDA stream.  Calls are
+ *    asynchronous on that stream unless they return host data (`*_host`
+ *    outputs), which synchronise the stream before returning.
+ *  - Handles are not thread-safe: one host thread at a time per handle
+ *    (mirrors `&mut self` in the reference).  Distinct handles are independent.
+ *  - Query outputs are sets sorted by neuron id.  The reference returns them in
+ *    HashMap iteration order (crates/klearu-core/src/lsh/index.rs:219-249); the
+ *    set (and each id's count) is identical, only the order is normalised.
+ *  - Kernels never trap: device-side bound violations are recorded in a
+ *    per-context error word and reported as KL_EBOUNDS by the next
+ *    synchronising call or kl_ctx_check().
+ */
+#ifndef KLEARU_GPU_H
+#define KLEARU_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KLEARU_GPU_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define KL_API __attribute__((visibility("default")))
+#else
+#define KL_API
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Status codes.  The reference panics (assert!) where these are returned;   */
+/* e.g. FifoBucket::new capacity>0 (crates/klearu-core/src/bucket/fifo.rs:18) */
+/* ------------------------------------------------------------------------ */
+typedef enum {
+  KL_OK = 0,
+  KL_EINVAL = 1,       /* bad argument / configuration                       */
+  KL_ENOMEM = 2,       /* device allocation failed                           */
+  KL_ECUDA = 3,        /* CUDA runtime error                                 */
+  KL_ENCCL = 4,        /* NCCL error (sharded networks)                      */
+  KL_ETIMEOUT = 5,     /* bounded device wait gave up                        */
+  KL_EBOUNDS = 6,      /* device kernel saw an out-of-range id/index         */
+  KL_ECAPACITY = 7,    /* an output did not fit its capacity (truncated)     */
+  KL_EUNSUPPORTED = 8  /* valid in the reference but not supported here      */
+} kl_status;
+
+/* Enumerations mirror crates/klearu-core/src/config.rs:3-38 (same order). */
+typedef enum {
+  KL_HASH_SIMHASH = 0,
+  KL_HASH_WTA = 1,
+  KL_HASH_DWTA = 2,
+  KL_HASH_MINHASH = 3,
+  KL_HASH_SRP = 4
+} kl_hash_kind;
+
+typedef enum { KL_BUCKET_FIFO = 0, KL_BUCKET_RESERVOIR = 1 } kl_bucket_type;
+
+typedef enum {
+  KL_SAMPLING_VANILLA = 0,
+  KL_SAMPLING_TOPK = 1,
+  KL_SAMPLING_THRESHOLD = 2
+} kl_sampling;
+
+typedef enum {
+  KL_ACT_RELU = 0,
+  KL_ACT_SIGMOID = 1,
+  KL_ACT_TANH = 2,
+  KL_ACT_SOFTMAX = 3,
+  KL_ACT_IDENTITY = 4
+} kl_activation;
+
+typedef enum { KL_OPT_SGD = 0, KL_OPT_ADAM = 1 } kl_optimizer;
+
+/* Weight storage.  F32 is the reference's storage (Vec<f32> per neuron,
+ * crates/klearu-core/src/network/neuron.rs:6-12).  BF16 is klearu-accel's
+ * Mode 2: bf16 storage, f32 arithmetic, round-to-nearest-even store
+ * (crates/klearu-accel/src/bf16/mod.rs:22-107).  Adam/SGD state is f32. */
+typedef enum { KL_DTYPE_F32 = 0, KL_DTYPE_BF16 = 1 } kl_dtype;
+
+typedef enum { KL_QUERY_COUNTS = 0, KL_QUERY_UNION = 1 } kl_query_mode;
+
+/* EXACT_SEQUENTIAL = Network::train_step semantics: per example forward,
+ * backward and immediate optimizer update (crates/klearu-core/src/network/net.rs:81-119).
+ * BATCHED = every example of the batch is forwarded against the step-start
+ * weights, per-row gradients are summed over the batch (in sample order) and
+ * one optimizer update is applied to every touched row. */
+typedef enum { KL_MODE_EXACT_SEQUENTIAL = 0, KL_MODE_BATCHED = 1 } kl_train_mode;
+
+typedef struct kl_ctx_s* kl_ctx_t;
+typedef struct kl_hash_s* kl_hash_t;
+typedef struct kl_index_s* kl_index_t;
+typedef struct kl_net_s* kl_net_t;
+
+/* ------------------------------------------------------------------------ */
+/* Context                                                                  */
+/* ------------------------------------------------------------------------ */
+
+/* Create a context on `device` issuing work on `stream` (a cudaStream_t; NULL
+ * selects the legacy default stream).  No reference counterpart: the Rust
+ * reference is single-process CPU code with no device state. */
+KL_API kl_status kl_ctx_create(int device, void* stream, kl_ctx_t* out);
+KL_API kl_status kl_ctx_destroy(kl_ctx_t ctx);
+KL_API kl_status kl_ctx_set_stream(kl_ctx_t ctx, void* stream);
+/* Wait for all work issued on the context's stream; reports device errors. */
+KL_API kl_status kl_ctx_sync(kl_ctx_t ctx);
+/* Synchronise and report (then clear) the device-side error word. */
+KL_API kl_status kl_ctx_check(kl_ctx_t ctx);
+KL_API const char* kl_last_error(kl_ctx_t ctx);
+KL_API int kl_abi_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Hash families -- replaces trait HashFamily                               */
+/* (crates/klearu-core/src/hash/mod.rs:24-39)                               */
+/* ------------------------------------------------------------------------ */
+
+/* Explicit hash parameters (host memory).  Only the member(s) of the chosen
+ * kind are read.
+ *  SIMHASH : planes [L][K][d] int8 in {-1,0,1}    (SimHash::hyperplanes, simhash.rs:21-27)
+ *  WTA/DWTA: windows [L][K][window] uint32 dims    (DwtaHash::windows, dwta.rs:19-29; wta.rs:22-32)
+ *  MINHASH : perms [L][d] uint32, perms[t][dim] = permuted index (minhash.rs:18-28)
+ *  SRP     : per (table*K + bit) sorted sparse rows: rowptr [L*K+1], idx, coef in {-1,+1}
+ *            (SparseRandomProjection::projections, srp.rs:22-31) */
+typedef struct {
+  const int8_t* planes;
+  const uint32_t* windows;
+  const uint32_t* perms;
+  const uint32_t* srp_rowptr;
+  const uint32_t* srp_idx;
+  const int8_t* srp_coef;
+} kl_hash_params;
+
+/* Replaces SimHash::new / WtaHash::new / DwtaHash::new / MinHash::new /
+ * SparseRandomProjection::new (simhash.rs:37-58, wta.rs:42-84, dwta.rs:39-84,
+ * minhash.rs:38-60, srp.rs:43-80) with explicit parameters.  `window_size` is
+ * read for WTA/DWTA only. */
+KL_API kl_status kl_hash_create(kl_ctx_t ctx, int kind, int input_dim, int k, int num_tables,
+                         int window_size, const kl_hash_params* params_host, kl_hash_t* out);
+/* Seeded construction following the reference distributions (ternary
+ * 1/6-2/3-1/6 planes, first-w-of-a-shuffle windows, full shuffles for MinHash,
+ * SRP density `srp_sparsity`).  The random stream is this library's SplitMix64,
+ * not rand 0.8.5's ChaCha12, so seeds do not reproduce the Rust parameters. */
+KL_API kl_status kl_hash_create_seeded(kl_ctx_t ctx, int kind, int input_dim, int k, int num_tables,
+                                int window_size, float srp_sparsity, uint64_t seed,
+                                kl_hash_t* out);
+KL_API kl_status kl_hash_destroy(kl_hash_t h);
+/* HashFamily::k / input_dim / num_tables (hash/mod.rs:32-38). */
+KL_API kl_status kl_hash_info(kl_hash_t h, int* kind_host, int* input_dim_host, int* k_host,
+                       int* num_tables_host);
+/* Batched HashFamily::hash_dense (hash/mod.rs:26): codes[i*L + t] =
+ * hash_dense(X[i*ldx ..], t) for all rows i < n and tables t < L.  For
+ * SIMHASH/SRP, `min_abs_proj` (nullable, [n][L]) receives min over the K bits
+ * of |projection|, so callers can log near-zero projections whose sign is
+ * summation-order sensitive. */
+KL_API kl_status kl_hash_dense_batch(kl_hash_t h, const float* X, int n, int ldx, uint64_t* codes,
+                              float* min_abs_proj);
+/* Batched HashFamily::hash_sparse (hash/mod.rs:29) over a CSR batch with
+ * sorted, unique column indices per row. */
+KL_API kl_status kl_hash_sparse_batch(kl_hash_t h, const int32_t* rowptr, const uint32_t* idx,
+                               const float* val, int n, uint64_t* codes, float* min_abs_proj);
+
+/* ------------------------------------------------------------------------ */
+/* LSH index -- replaces trait LshIndexTrait (lsh/index.rs:21-67) and       */
+/* create_lsh_index (lsh/index.rs:339-374)                                  */
+/* ------------------------------------------------------------------------ */
+
+/* LshIndex::new (index.rs:193-205): L tables x 2^K buckets of `capacity` ids.
+ * The index keeps its own reference to `h` (h may be destroyed afterwards). */
+KL_API kl_status kl_index_create(kl_ctx_t ctx, kl_hash_t h, int bucket_type, int capacity,
+                          kl_index_t* out);
+KL_API kl_status kl_index_destroy(kl_index_t ix);
+KL_API kl_status kl_index_info(kl_index_t ix, int* num_tables_host, int* num_buckets_host,
+                        int* capacity_host, int* bucket_type_host);
+/* n sequential LshIndexTrait::insert calls (index.rs:257-262), in array order.
+ * rows: [n][ld] elements of `dtype` (KL_DTYPE_F32 / KL_DTYPE_BF16). */
+KL_API kl_status kl_index_insert_batch(kl_index_t ix, const uint32_t* ids, const void* rows, int n,
+                                int ld, int dtype);
+/* n sequential LshIndexTrait::insert_sparse calls (index.rs:264-269). */
+KL_API kl_status kl_index_insert_sparse_batch(kl_index_t ix, const uint32_t* ids,
+                                       const int32_t* rowptr, const uint32_t* idx,
+                                       const float* val, int n);
+/* n sequential LshIndexTrait::remove calls (index.rs:278-280). */
+KL_API kl_status kl_index_remove(kl_index_t ix, const uint32_t* ids, int n);
+/* n sequential LshIndexTrait::remove_with_weights calls (index.rs:271-276). */
+KL_API kl_status kl_index_remove_with_weights(kl_index_t ix, const uint32_t* ids, const void* rows,
+                                       int n, int ld, int dtype);
+/* LshIndexTrait::rebuild (index.rs:302-307): clear, then insert (ids[i], rows[i])
+ * in order.  ids == NULL means ids 0..n-1 (Layer::rebuild_index, layer.rs:228-233). */
+KL_API kl_status kl_index_rebuild(kl_index_t ix, const uint32_t* ids, const void* rows, int n, int ld,
+                           int dtype);
+/* LshIndexTrait::clear (index.rs:313-315). */
+KL_API kl_status kl_index_clear(kl_index_t ix);
+/* Batched LshIndexTrait::query / query_with_counts / query_union
+ * (index.rs:282-292).  Results for query i are out_ids[out_offsets[i] ..
+ * out_offsets[i+1]) sorted by id; out_counts (COUNTS mode; nullable) holds the
+ * number of tables each id was found in.  out_offsets has n+1 entries.  If the
+ * total exceeds `capacity`, results are truncated, *overflow (device, nullable)
+ * is set to 1 and KL_ECAPACITY is reported by the next synchronising call. */
+KL_API kl_status kl_index_query_batch(kl_index_t ix, const float* X, int n, int ldx, int mode,
+                               uint32_t* out_ids, uint32_t* out_counts, int32_t* out_offsets,
+                               int32_t capacity, int32_t* overflow);
+/* Batched query_sparse_union / query_sparse_with_counts (index.rs:290-300). */
+KL_API kl_status kl_index_query_sparse_batch(kl_index_t ix, const int32_t* rowptr,
+                                      const uint32_t* idx, const float* val, int n, int mode,
+                                      uint32_t* out_ids, uint32_t* out_counts,
+                                      int32_t* out_offsets, int32_t capacity,
+                                      int32_t* overflow);
+/* Copy the bucket arrays out (checkpointing / parity): ids [L][2^K][cap] in
+ * bucket order (Bucket::contents, bucket/mod.rs:11-31), lens [L][2^K],
+ * insertion counts [L][2^K] (ReservoirBucket::total_insertions; nullable). */
+KL_API kl_status kl_index_export(kl_index_t ix, uint32_t* ids, uint32_t* lens, uint64_t* counts);
+/* Inverse of kl_index_export. */
+KL_API kl_status kl_index_import(kl_index_t ix, const uint32_t* ids, const uint32_t* lens,
+                          const uint64_t* counts);
+
+/* ------------------------------------------------------------------------ */
+/* Network -- replaces klearu_core::network::Network (network/net.rs:10-173) */
+/* ------------------------------------------------------------------------ */
+
+/* LshConfig (config.rs:40-65).  range_pow is carried but unused, as in the
+ * reference (the index uses 2^num_hashes buckets, index.rs:194). */
+typedef struct {
+  int32_t hash_function;        /* kl_hash_kind */
+  int32_t bucket_type;          /* kl_bucket_type */
+  int32_t num_tables;           /* L */
+  int32_t range_pow;
+  int32_t num_hashes;           /* K */
+  int32_t bucket_capacity;
+  int32_t rebuild_interval_base;
+  double rebuild_decay;
+} kl_lsh_config;
+
+/* LayerConfig (config.rs:67-106). */
+typedef struct {
+  int32_t input_dim;
+  int32_t num_neurons;
+  int32_t activation;           /* kl_activation */
+  kl_lsh_config lsh;
+  int32_t sampling;             /* kl_sampling */
+  int32_t sampling_threshold;
+  int32_t top_k;
+  int32_t is_output;
+} kl_layer_config;
+
+/* SlideConfig + NetworkConfig (config.rs:108-143) plus device-side knobs. */
+typedef struct {
+  int32_t num_layers;
+  const kl_layer_config* layers; /* host array [num_layers] */
+  int32_t optimizer;             /* kl_optimizer */
+  double learning_rate;          /* carried; train_step takes lr explicitly, as in net.rs:81 */
+  int32_t batch_size;
+  int32_t num_threads;
+  uint64_t seed;
+  int32_t weight_dtype;          /* kl_dtype */
+  int32_t max_batch;             /* capacity of per-step buffers (examples per call) */
+} kl_net_config;
+
+/* Explicit initial parameters of one layer (host memory).  weights/bias are
+ * the reference's per-neuron Vec<f32> rows [num_neurons][input_dim] and biases
+ * (Neuron, neuron.rs:6-12).  NULL weights => seeded N(0, sqrt(2/d)) rows from
+ * this library's generator; NULL bias => 0 (neuron.rs:23-43). */
+typedef struct {
+  const float* weights;
+  const float* bias;
+  kl_hash_params hash;
+} kl_layer_init;
+
+/* A batch of examples (device memory): CSR features with sorted unique
+ * indices per row (Example / SparseVector, data/dataset.rs:5-16,
+ * tensor/sparse.rs:14-20) and CSR label lists. */
+typedef struct {
+  int32_t batch;
+  const int32_t* rowptr;    /* [batch+1] */
+  const uint32_t* idx;      /* [rowptr[batch]] */
+  const float* val;         /* [rowptr[batch]] */
+  const int32_t* label_ptr; /* [batch+1] */
+  const uint32_t* labels;   /* [label_ptr[batch]] */
+  int32_t nnz;              /* host-side copy of rowptr[batch] (sizes scratch) */
+  int32_t nlabels;          /* host-side copy of label_ptr[batch] */
+} kl_batch;
+
+/* Network::new (net.rs:19-57): layers, initial table build (layer.rs:40-44),
+ * optimizer state, RebuildScheduler from layer 0's LSH config.  `init` is
+ * NULL (all seeded) or an array of num_layers entries. */
+KL_API kl_status kl_net_create(kl_ctx_t ctx, const kl_net_config* cfg_host,
+                        const kl_layer_init* init_host, kl_net_t* out);
+KL_API kl_status kl_net_destroy(kl_net_t net);
+/* Network::train_step (net.rs:81-119), returning the mean loss: into
+ * `loss` (device, nullable) and/or `loss_host` (host, nullable; synchronises).
+ * Increments step once and runs the rebuild check, as the reference does. */
+KL_API kl_status kl_net_train_step(kl_net_t net, const kl_batch* batch_host, double lr, int mode,
+                            float* loss, float* loss_host);
+/* Network::forward (net.rs:62-78) for every example of the batch, without any
+ * update.  Per-layer results are read with kl_net_layer_output. */
+KL_API kl_status kl_net_forward(kl_net_t net, const kl_batch* batch_host);
+/* LayerOutput (layer.rs:19-26) of the last forward / train_step, compact:
+ * for example i, active ids (sorted by id) are ids[i*stride ..
+ * i*stride+counts[i]) with their pre-activations and activations at the same
+ * positions; stride is kl_net_layer_info's max_active.  Any output may be NULL. */
+KL_API kl_status kl_net_layer_output(kl_net_t net, int layer, uint32_t* ids, int32_t* counts,
+                              float* pre, float* act);
+KL_API kl_status kl_net_layer_info(kl_net_t net, int layer, int* input_dim_host,
+                            int* num_neurons_host, int* max_active_host);
+/* Network::predict_top_k (net.rs:159-173): per example the k highest final
+ * activations over all N neurons (inactive ones score 0), ties by lower id. */
+KL_API kl_status kl_net_predict_topk(kl_net_t net, const kl_batch* batch_host, int k,
+                              uint32_t* top_ids, float* top_scores);
+/* Read / write one layer's parameters as reference-layout f32 rows (host
+ * memory): weights [N][d], bias [N], optimizer state m/v [N][d] and mb/vb [N]
+ * (Adam m_w, v_w, m_b, v_b; SGD momentum in m/mb).  Any pointer may be NULL. */
+KL_API kl_status kl_net_get_layer(kl_net_t net, int layer, float* weights_host, float* bias_host,
+                           float* m_host, float* v_host, float* mb_host, float* vb_host);
+KL_API kl_status kl_net_set_layer(kl_net_t net, int layer, const float* weights_host,
+                           const float* bias_host, const float* m_host, const float* v_host,
+                           const float* mb_host, const float* vb_host);
+/* Layer::rebuild_index (layer.rs:228-233) on every layer. */
+KL_API kl_status kl_net_rebuild(kl_net_t net);
+/* Borrow a layer's LSH index (Layer::lsh_index, layer.rs:12).  Owned by net. */
+KL_API kl_status kl_net_layer_index(kl_net_t net, int layer, kl_index_t* out);
+/* Network::step and RebuildScheduler state (net.rs:13-14, maintenance.rs:20-26). */
+KL_API kl_status kl_net_get_step(kl_net_t net, uint64_t* step_host, uint64_t* next_rebuild_host,
+                          uint64_t* rebuild_count_host);
+KL_API kl_status kl_net_set_step(kl_net_t net, uint64_t step, uint64_t next_rebuild,
+                          uint64_t rebuild_count);
+
+/* Per-step work counters accumulated on the device since the last reset
+ * (used for the HBM roofline): sum of active set sizes, distinct rows touched
+ * by the optimizer, input nnz, examples, steps, rebuilds; per layer. */
+typedef struct {
+  uint64_t active_sum;      /* sum over examples of |active set| */
+  uint64_t touched_rows;    /* rows (neurons) updated by the optimizer */
+  uint64_t input_nnz;       /* layer 0 only: sum of input nnz */
+  uint64_t examples;
+  uint64_t steps;
+  uint64_t rebuilds;
+} kl_layer_stats;
+KL_API kl_status kl_net_stats(kl_net_t net, int layer, kl_layer_stats* stats_host, int reset);
+
+/* Phase timing for roofline accounting (no reference counterpart; the
+ * reference has no profiler hooks).  When enabled, CUDA events bracket each
+ * phase of each layer on the context stream. */
+typedef enum {
+  KL_PHASE_HASH = 0,     /* hash the layer input against the L tables         */
+  KL_PHASE_PROBE = 1,    /* bucket probe, union/counts, sampling              */
+  KL_PHASE_FORWARD = 2,  /* active-row gather-dot (+ fused loss grad and dX)  */
+  KL_PHASE_BACKWARD = 3, /* local gradients, input gradients                  */
+  KL_PHASE_UPDATE = 4,   /* segmented gradient reduction + optimizer          */
+  KL_PHASE_REBUILD = 5,  /* table rebuild                                     */
+  KL_NPHASES = 6
+} kl_phase;
+KL_API kl_status kl_net_profile(kl_net_t net, int enable);
+/* Accumulated milliseconds and call counts per phase of `layer` since the last
+ * reset (synchronises).  ms_host / calls_host have KL_NPHASES entries. */
+KL_API kl_status kl_net_profile_read(kl_net_t net, int layer, double* ms_host, uint64_t* calls_host,
+                                     int reset);
+/* Kernels launched by this library in this process so far. */
+KL_API kl_status kl_launch_count(uint64_t* count_host);
+
+/* ------------------------------------------------------------------------ */
+/* Neuron sharding of the output layer over NCCL (no reference counterpart: */
+/* the reference's only parallelism is HOGWILD threads, optim/hogwild.rs).  */
+/* ------------------------------------------------------------------------ */
+
+/* Size in bytes of the opaque communicator id (ncclUniqueId). */
+KL_API int kl_dist_unique_id_size(void);
+/* Rank 0 creates the id; it is shared with all ranks out of band. */
+KL_API kl_status kl_dist_get_unique_id(void* id_host);
+/* Like kl_net_create, but the output layer's neurons are split into `nranks`
+ * contiguous slices; this rank owns slice `rank` (its rows, optimizer state
+ * and LSH tables).  Hidden layers are replicated.  `init` holds the FULL
+ * parameters (every rank passes the same).  Collectives per step: broadcast
+ * of the batch's hidden activations' input, all-gather of per-rank candidate
+ * lists, all-reduce of the output layer's input gradient and of the loss. */
+KL_API kl_status kl_net_create_sharded(kl_ctx_t ctx, const kl_net_config* cfg_host,
+                                const kl_layer_init* init_host, const void* unique_id_host,
+                                int rank, int nranks, kl_net_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KLEARU_GPU_H */

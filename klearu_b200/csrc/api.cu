@@ -1,0 +1,1549 @@
+// api.cu -- the C ABI (include/klearu_gpu.h): handles, validation, device
+// memory, and the host-side orchestration of the SLIDE train step.
+//
+// Host orchestration mirrors crates/klearu-core/src/network/net.rs:
+//   Network::new        -> kl_net_create   (net.rs:19-57, layer.rs:30-61)
+//   Network::train_step -> kl_net_train_step (net.rs:81-119)
+//   Network::forward    -> kl_net_forward  (net.rs:62-78)
+//   RebuildScheduler    -> Scheduler below (lsh/maintenance.rs:70-82)
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+
+using namespace kl;
+
+namespace kl {
+static std::atomic<unsigned long long> g_launches{0};
+void count_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+}  // namespace kl
+
+// ---------------------------------------------------------------------------
+// Small host utilities
+// ---------------------------------------------------------------------------
+namespace {
+
+struct KlError {
+  kl_status st;
+  std::string msg;
+};
+[[noreturn]] void raise(kl_status st, const std::string& m) { throw KlError{st, m}; }
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    if (e == cudaErrorMemoryAllocation) raise(KL_ENOMEM, std::string(what) + ": " + cudaGetErrorString(e));
+    raise(KL_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+void ck_launch(const char* what) { ck(cudaGetLastError(), what); }
+void require(bool c, const std::string& m) {
+  if (!c) raise(KL_EINVAL, m);
+}
+void support(bool c, const std::string& m) {
+  if (!c) raise(KL_EUNSUPPORTED, m);
+}
+
+// Device allocation owned by one object.
+struct DBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DBuf() = default;
+  DBuf(const DBuf&) = delete;
+  DBuf& operator=(const DBuf&) = delete;
+  ~DBuf() {
+    if (p) cudaFree(p);
+  }
+  void alloc(size_t n) {
+    if (n <= bytes && p) return;
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+    if (n == 0) n = 16;
+    ck(cudaMalloc(&p, n), "cudaMalloc");
+    bytes = n;
+  }
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+};
+
+// f32::powi lowered to compiler-rt's square-and-multiply (adam.rs:52-53).
+float powi_f32(float a, int b) {
+  const bool recip = b < 0;
+  float r = 1.0f;
+  while (true) {
+    if (b & 1) r *= a;
+    b /= 2;
+    if (b == 0) break;
+    a *= a;
+  }
+  return recip ? 1.0f / r : r;
+}
+
+// SipHash-1-3 (zero keys) over two 8-byte words: DefaultHasher of
+// (usize, usize), used by DwtaHash's sparse fallback (dwta.rs:131-134).
+// Written from the published SipHash specification.
+uint64_t siphash13_two_words(uint64_t a, uint64_t b) {
+  auto rotl = [](uint64_t x, int r) { return (x << r) | (x >> (64 - r)); };
+  uint64_t v0 = 0x736f6d6570736575ULL, v1 = 0x646f72616e646f6dULL, v2 = 0x6c7967656e657261ULL,
+           v3 = 0x7465646279746573ULL;
+  auto round = [&]() {
+    v0 += v1; v1 = rotl(v1, 13); v1 ^= v0; v0 = rotl(v0, 32);
+    v2 += v3; v3 = rotl(v3, 16); v3 ^= v2;
+    v0 += v3; v3 = rotl(v3, 21); v3 ^= v0;
+    v2 += v1; v1 = rotl(v1, 17); v1 ^= v2; v2 = rotl(v2, 32);
+  };
+  for (uint64_t m : {a, b}) {
+    v3 ^= m;
+    round();
+    v0 ^= m;
+  }
+  const uint64_t last = (uint64_t)16 << 56;
+  v3 ^= last;
+  round();
+  v0 ^= last;
+  v2 ^= 0xff;
+  round();
+  round();
+  round();
+  return v0 ^ v1 ^ v2 ^ v3;
+}
+
+// This library's seeded generator (SplitMix64).  Not rand's ChaCha12.
+struct SplitMix {
+  uint64_t s;
+  uint64_t next() {
+    uint64_t z = (s += 0x9e3779b97f4a7c15ULL);
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+    return z ^ (z >> 31);
+  }
+  double unit() { return (double)(next() >> 11) * (1.0 / 9007199254740992.0); }
+  uint64_t below(uint64_t n) { return next() % n; }
+  double normal() {  // Box-Muller
+    double u1 = unit(), u2 = unit();
+    if (u1 < 1e-300) u1 = 1e-300;
+    return std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2);
+  }
+  template <class T>
+  void shuffle(std::vector<T>& v) {
+    for (size_t i = v.size(); i > 1; --i) std::swap(v[i - 1], v[below(i)]);
+  }
+};
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+int bits_for(uint64_t n) {  // bits needed for values < n
+  int b = 0;
+  while (b < 64 && ((n - 1) >> b) != 0 && n > 1) ++b;
+  return b;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Handles
+// ---------------------------------------------------------------------------
+struct kl_ctx_s {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  DBuf err;  // int device error word
+  std::string last_error;
+};
+
+struct HashImpl {
+  kl_ctx_t ctx;
+  DevHash dh;
+  DBuf planes, planesT, windows, fallback, perms;
+};
+struct kl_hash_s {
+  std::shared_ptr<HashImpl> h;
+};
+
+struct IndexImpl {
+  kl_ctx_t ctx;
+  std::shared_ptr<HashImpl> hash;
+  DevTables T;
+  DBuf ids, len, cnt;
+  DBuf bkt, scratch, qids, qcnt, qn, qoff;
+  int nb_bits = 0;
+
+  void hash_dense_to_bkt(const DenseIn& in) {
+    bkt.alloc((size_t)T.L * std::max(in.n, 1) * 2);
+    HashOut o;
+    o.bkt = bkt.as<uint16_t>();
+    o.bkt_ld = in.n;
+    o.nb_mask = (uint32_t)(T.nb - 1);
+    launch_hash_dense(hash->dh, in, o, ctx->stream);
+    ck_launch("hash");
+  }
+  void hash_sparse_to_bkt(const SparseIn& in) {
+    bkt.alloc((size_t)T.L * std::max(in.n, 1) * 2);
+    HashOut o;
+    o.bkt = bkt.as<uint16_t>();
+    o.bkt_ld = in.n;
+    o.nb_mask = (uint32_t)(T.nb - 1);
+    launch_hash_sparse(hash->dh, in, o, ctx->stream);
+    ck_launch("hash");
+  }
+  void insert_from_bkt(const uint32_t* idsin, int n) {
+    if (n <= 0) return;
+    scratch.alloc(insert_scratch_bytes(T, n));
+    InsertScratch s;
+    carve_insert_scratch(T, n, scratch.p, &s);
+    launch_tables_insert(T, idsin, bkt.as<uint16_t>(), n, n, s, ctx->err.as<int>(), ctx->stream);
+    ck_launch("insert");
+  }
+  void clear() {
+    launch_tables_clear(T, ctx->stream);
+    ck_launch("clear");
+  }
+  // Query: padded results into qids/qcnt/qn, then CSR compaction.
+  void query(int n, int mode, uint32_t* out_ids, uint32_t* out_counts, int32_t* out_offsets,
+             int32_t capacity, int32_t* overflow) {
+    const int stride = T.L * T.cap;
+    qids.alloc((size_t)std::max(n, 1) * stride * 4);
+    qcnt.alloc((size_t)std::max(n, 1) * stride * 4);
+    qn.alloc((size_t)std::max(n, 1) * 4);
+    ProbeArgs a;
+    a.T = T;
+    a.bkt = bkt.as<uint16_t>();
+    a.bkt_ld = n;
+    a.nq = n;
+    a.N = 0;
+    a.id_bits = 32;
+    a.out_ids = qids.as<uint32_t>();
+    a.out_counts = qcnt.as<uint32_t>();
+    a.out_stride = stride;
+    a.out_n = qn.as<int32_t>();
+    a.err = ctx->err.as<int>();
+    launch_probe(a, ctx->stream);
+    ck_launch("probe");
+    if (overflow) ck(cudaMemsetAsync(overflow, 0, 4, ctx->stream), "memset");
+    launch_scan(qn.as<int32_t>(), out_offsets, n, nullptr, ctx->stream);
+    ck_launch("scan");
+    launch_compact(qids.as<uint32_t>(), mode == KL_QUERY_COUNTS ? qcnt.as<uint32_t>() : nullptr,
+                   stride, out_offsets, n, out_ids, mode == KL_QUERY_COUNTS ? out_counts : nullptr,
+                   capacity, overflow, ctx->err.as<int>(), ctx->stream);
+    ck_launch("compact");
+  }
+};
+struct kl_index_s {
+  std::shared_ptr<IndexImpl> ix;
+};
+
+namespace {
+
+std::shared_ptr<HashImpl> make_hash(kl_ctx_t ctx, int kind, int d, int k, int L, int w,
+                                    const kl_hash_params* p) {
+  require(d >= 1 && k >= 1 && L >= 1, "hash: input_dim, k and num_tables must be >= 1");
+  auto H = std::make_shared<HashImpl>();
+  H->ctx = ctx;
+  DevHash& h = H->dh;
+  h.kind = kind;
+  h.d = d;
+  h.k = k;
+  h.L = L;
+  cudaStream_t st = ctx->stream;
+  switch (kind) {
+    case KL_HASH_SIMHASH:
+    case KL_HASH_SRP: {
+      support(k <= 32, "SimHash/SRP: num_hashes > 32");
+      support((int64_t)L * k <= 1024, "SimHash/SRP: num_tables*num_hashes > 1024");
+      h.LK = L * k;
+      h.dpad = (int)round_up(d, 16);
+      h.lkpad = (int)round_up(h.LK, 16);
+      std::vector<int8_t> dense((size_t)h.LK * h.dpad, 0), dT((size_t)d * h.lkpad, 0);
+      if (kind == KL_HASH_SIMHASH) {
+        require(p && p->planes, "SimHash: planes required");
+        for (int tb = 0; tb < h.LK; ++tb)
+          for (int i = 0; i < d; ++i) {
+            int8_t v = p->planes[(size_t)tb * d + i];
+            require(v >= -1 && v <= 1, "SimHash: plane entries must be -1, 0 or 1");
+            dense[(size_t)tb * h.dpad + i] = v;
+          }
+      } else {
+        require(p && p->srp_rowptr && (p->srp_rowptr[h.LK] == 0 || (p->srp_idx && p->srp_coef)),
+                "SRP: rowptr/idx/coef required");
+        for (int tb = 0; tb < h.LK; ++tb)
+          for (uint32_t e = p->srp_rowptr[tb]; e < p->srp_rowptr[tb + 1]; ++e) {
+            require(p->srp_idx[e] < (uint32_t)d, "SRP: index >= input_dim");
+            require(p->srp_coef[e] == 1 || p->srp_coef[e] == -1, "SRP: coefficients must be +-1");
+            dense[(size_t)tb * h.dpad + p->srp_idx[e]] = p->srp_coef[e];
+          }
+      }
+      for (int tb = 0; tb < h.LK; ++tb)
+        for (int i = 0; i < d; ++i) dT[(size_t)i * h.lkpad + tb] = dense[(size_t)tb * h.dpad + i];
+      H->planes.alloc(dense.size());
+      H->planesT.alloc(dT.size());
+      ck(cudaMemcpyAsync(H->planes.p, dense.data(), dense.size(), cudaMemcpyHostToDevice, st), "upload");
+      ck(cudaMemcpyAsync(H->planesT.p, dT.data(), dT.size(), cudaMemcpyHostToDevice, st), "upload");
+      ck(cudaStreamSynchronize(st), "sync");
+      h.planes = H->planes.as<int8_t>();
+      h.planesT = H->planesT.as<int8_t>();
+      break;
+    }
+    case KL_HASH_WTA:
+    case KL_HASH_DWTA: {
+      require(w >= 1 && w <= d, "WTA/DWTA: window_size must be in [1, input_dim] (dwta.rs:46-49)");
+      h.w = w;
+      h.bpw = 1;
+      if (w > 1) {
+        h.bpw = 0;
+        while ((1 << h.bpw) < w) ++h.bpw;
+      }
+      require((int64_t)k * h.bpw <= 64, "WTA/DWTA: k * bits_per_window exceeds 64 (dwta.rs:51-54)");
+      require(p && p->windows, "WTA/DWTA: windows required");
+      const size_t nw = (size_t)L * k * w;
+      for (size_t i = 0; i < nw; ++i) require(p->windows[i] < (uint32_t)d, "WTA/DWTA: window dim >= input_dim");
+      std::vector<uint8_t> fb((size_t)L * k);
+      for (int t = 0; t < L; ++t)
+        for (int kk = 0; kk < k; ++kk) fb[(size_t)t * k + kk] = (uint8_t)(siphash13_two_words(t, kk) % (uint64_t)w);
+      H->windows.alloc(nw * 4);
+      H->fallback.alloc(fb.size());
+      ck(cudaMemcpyAsync(H->windows.p, p->windows, nw * 4, cudaMemcpyHostToDevice, st), "upload");
+      ck(cudaMemcpyAsync(H->fallback.p, fb.data(), fb.size(), cudaMemcpyHostToDevice, st), "upload");
+      ck(cudaStreamSynchronize(st), "sync");
+      h.windows = H->windows.as<uint32_t>();
+      h.fallback = H->fallback.as<uint8_t>();
+      break;
+    }
+    case KL_HASH_MINHASH: {
+      support(k <= 64, "MinHash: num_hashes > 64");
+      require(p && p->perms, "MinHash: perms required");
+      h.bin_size = (d + k - 1) / k;
+      const size_t n = (size_t)L * d;
+      H->perms.alloc(n * 4);
+      ck(cudaMemcpyAsync(H->perms.p, p->perms, n * 4, cudaMemcpyHostToDevice, st), "upload");
+      ck(cudaStreamSynchronize(st), "sync");
+      h.perms = H->perms.as<uint32_t>();
+      break;
+    }
+    default:
+      raise(KL_EINVAL, "unknown hash kind");
+  }
+  return H;
+}
+
+// Seeded parameters following the reference distributions.
+struct SeededParams {
+  std::vector<int8_t> planes;
+  std::vector<uint32_t> windows, perms, rowptr, idx;
+  std::vector<int8_t> coef;
+  kl_hash_params p{};
+};
+void seeded_params(int kind, int d, int k, int L, int w, float sparsity, uint64_t seed, SeededParams& sp) {
+  SplitMix rng{seed};
+  switch (kind) {
+    case KL_HASH_SIMHASH:  // simhash.rs:37-71: order table, bit, dim; 1/6, 2/3, 1/6
+      sp.planes.resize((size_t)L * k * d);
+      for (auto& v : sp.planes) {
+        double r = rng.unit();
+        v = r < 1.0 / 6.0 ? -1 : (r < 1.0 / 6.0 + 2.0 / 3.0 ? 0 : 1);
+      }
+      sp.p.planes = sp.planes.data();
+      break;
+    case KL_HASH_WTA:
+    case KL_HASH_DWTA: {  // first w of a full shuffle per (table, fn)
+      std::vector<uint32_t> all(d);
+      for (int t = 0; t < L; ++t)
+        for (int kk = 0; kk < k; ++kk) {
+          for (int i = 0; i < d; ++i) all[i] = (uint32_t)i;
+          rng.shuffle(all);
+          sp.windows.insert(sp.windows.end(), all.begin(), all.begin() + w);
+        }
+      sp.p.windows = sp.windows.data();
+      break;
+    }
+    case KL_HASH_MINHASH: {
+      std::vector<uint32_t> all(d);
+      for (int t = 0; t < L; ++t) {
+        for (int i = 0; i < d; ++i) all[i] = (uint32_t)i;
+        rng.shuffle(all);
+        sp.perms.insert(sp.perms.end(), all.begin(), all.end());
+      }
+      sp.p.perms = sp.perms.data();
+      break;
+    }
+    case KL_HASH_SRP: {  // srp.rs:60-78
+      const double pneg = sparsity / 2.0, pzero_end = pneg + (1.0 - sparsity);
+      sp.rowptr.push_back(0);
+      for (int tb = 0; tb < L * k; ++tb) {
+        for (int i = 0; i < d; ++i) {
+          double r = rng.unit();
+          if (r < pneg) {
+            sp.idx.push_back((uint32_t)i);
+            sp.coef.push_back(-1);
+          } else if (r >= pzero_end) {
+            sp.idx.push_back((uint32_t)i);
+            sp.coef.push_back(1);
+          }
+        }
+        sp.rowptr.push_back((uint32_t)sp.idx.size());
+      }
+      sp.p.srp_rowptr = sp.rowptr.data();
+      sp.p.srp_idx = sp.idx.data();
+      sp.p.srp_coef = sp.coef.data();
+      break;
+    }
+  }
+}
+
+std::shared_ptr<IndexImpl> make_index(kl_ctx_t ctx, std::shared_ptr<HashImpl> h, int bucket_type,
+                                      int cap) {
+  require(cap > 0, "bucket capacity must be positive (fifo.rs:18, reservoir.rs:25)");
+  require(bucket_type == KL_BUCKET_FIFO || bucket_type == KL_BUCKET_RESERVOIR, "unknown bucket type");
+  support(h->dh.k <= 12, "index: num_hashes > 12 (more than 4096 buckets per table)");
+  support(h->dh.L <= 1024, "index: num_tables > 1024");
+  support((int64_t)h->dh.L * cap <= probe_max_items(),
+          "index: num_tables * bucket_capacity exceeds the probe kernel's shared-memory capacity");
+  auto I = std::make_shared<IndexImpl>();
+  I->ctx = ctx;
+  I->hash = std::move(h);
+  DevTables& T = I->T;
+  T.L = I->hash->dh.L;
+  T.nb = 1 << I->hash->dh.k;
+  T.cap = cap;
+  T.type = bucket_type;
+  const size_t LB = (size_t)T.L * T.nb;
+  I->ids.alloc(LB * cap * 4);
+  I->len.alloc(LB * 4);
+  I->cnt.alloc(LB * 8);
+  T.ids = I->ids.as<uint32_t>();
+  T.len = I->len.as<uint32_t>();
+  T.cnt = I->cnt.as<uint64_t>();
+  ck(cudaMemsetAsync(T.ids, 0, LB * cap * 4, ctx->stream), "memset");
+  ck(cudaMemsetAsync(T.len, 0, LB * 4, ctx->stream), "memset");
+  ck(cudaMemsetAsync(T.cnt, 0, LB * 8, ctx->stream), "memset");
+  return I;
+}
+
+DenseIn dense_rows(const void* rows, int dtype, int n, int ld) {
+  require(dtype == KL_DTYPE_F32 || dtype == KL_DTYPE_BF16, "dtype must be KL_DTYPE_F32 or KL_DTYPE_BF16");
+  DenseIn in;
+  in.X = rows;
+  in.dtype = dtype;
+  in.ld_row = ld;
+  in.ld_elem = 1;
+  in.n = n;
+  return in;
+}
+
+kl_status finish(kl_ctx_t ctx, const KlError& e) {
+  if (ctx) ctx->last_error = e.msg;
+  return e.st;
+}
+
+}  // namespace
+
+#define KL_API_BEGIN(ctxexpr)                 \
+  kl_ctx_t ctx__ = (ctxexpr);                 \
+  try {                                       \
+    if (ctx__) ctx__->last_error.clear();     \
+    DeviceGuard guard__(ctx__ ? ctx__->device : 0);
+#define KL_API_END                                                     \
+  }                                                                    \
+  catch (const KlError& e) {                                           \
+    return finish(ctx__, e);                                           \
+  }                                                                    \
+  catch (const std::bad_alloc&) {                                      \
+    return finish(ctx__, KlError{KL_ENOMEM, "host allocation failed"}); \
+  }                                                                    \
+  return KL_OK;
+
+namespace {
+// Read and clear the device error word (synchronises).
+void check_device_errors(kl_ctx_t ctx) {
+  ck(cudaStreamSynchronize(ctx->stream), "stream synchronize");
+  int e = 0;
+  ck(cudaMemcpy(&e, ctx->err.p, 4, cudaMemcpyDeviceToHost), "read error word");
+  if (e) {
+    ck(cudaMemset(ctx->err.p, 0, 4), "clear error word");
+    if (e & DERR_BOUNDS) raise(KL_EBOUNDS, "device kernel saw an out-of-range id or index");
+    if (e & DERR_CAPACITY) raise(KL_ECAPACITY, "an output exceeded its capacity and was truncated");
+    if (e & DERR_TIMEOUT) raise(KL_ETIMEOUT, "a bounded device wait gave up");
+  }
+}
+}  // namespace
+
+// ===========================================================================
+// Context
+// ===========================================================================
+extern "C" int kl_abi_version(void) { return KLEARU_GPU_ABI_VERSION; }
+
+extern "C" kl_status kl_ctx_create(int device, void* stream, kl_ctx_t* out) {
+  if (!out) return KL_EINVAL;
+  *out = nullptr;
+  try {
+    int n = 0;
+    ck(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+    require(device >= 0 && device < n, "device index out of range");
+    DeviceGuard g(device);
+    auto* c = new kl_ctx_s();
+    c->device = device;
+    c->stream = static_cast<cudaStream_t>(stream);
+    try {
+      c->err.alloc(4);
+      ck(cudaMemset(c->err.p, 0, 4), "memset");
+    } catch (...) {
+      delete c;
+      throw;
+    }
+    *out = c;
+  } catch (const KlError& e) {
+    return e.st;
+  }
+  return KL_OK;
+}
+extern "C" kl_status kl_ctx_destroy(kl_ctx_t ctx) {
+  if (!ctx) return KL_EINVAL;
+  {
+    DeviceGuard g(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    ctx->err.~DBuf();
+    new (&ctx->err) DBuf();
+  }
+  delete ctx;
+  return KL_OK;
+}
+extern "C" kl_status kl_ctx_set_stream(kl_ctx_t ctx, void* stream) {
+  if (!ctx) return KL_EINVAL;
+  ctx->stream = static_cast<cudaStream_t>(stream);
+  return KL_OK;
+}
+extern "C" kl_status kl_ctx_sync(kl_ctx_t ctx) {
+  if (!ctx) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  check_device_errors(ctx);
+  KL_API_END
+}
+extern "C" kl_status kl_ctx_check(kl_ctx_t ctx) { return kl_ctx_sync(ctx); }
+extern "C" const char* kl_last_error(kl_ctx_t ctx) {
+  return ctx ? ctx->last_error.c_str() : "null context";
+}
+
+// ===========================================================================
+// Hash
+// ===========================================================================
+extern "C" kl_status kl_hash_create(kl_ctx_t ctx, int kind, int input_dim, int k, int num_tables,
+                                    int window_size, const kl_hash_params* params_host, kl_hash_t* out) {
+  if (!ctx || !out) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  *out = nullptr;
+  auto H = make_hash(ctx, kind, input_dim, k, num_tables, window_size, params_host);
+  *out = new kl_hash_s{H};
+  KL_API_END
+}
+extern "C" kl_status kl_hash_create_seeded(kl_ctx_t ctx, int kind, int input_dim, int k, int num_tables,
+                                           int window_size, float srp_sparsity, uint64_t seed,
+                                           kl_hash_t* out) {
+  if (!ctx || !out) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  *out = nullptr;
+  require(input_dim >= 1 && k >= 1 && num_tables >= 1, "hash: input_dim, k and num_tables must be >= 1");
+  require(srp_sparsity >= 0.0f && srp_sparsity <= 1.0f, "SRP: sparsity must be in [0, 1] (srp.rs:50-53)");
+  if (kind == KL_HASH_WTA || kind == KL_HASH_DWTA)
+    require(window_size >= 1 && window_size <= input_dim, "WTA/DWTA: window_size must be in [1, input_dim]");
+  SeededParams sp;
+  seeded_params(kind, input_dim, k, num_tables, window_size, srp_sparsity, seed, sp);
+  auto H = make_hash(ctx, kind, input_dim, k, num_tables, window_size, &sp.p);
+  *out = new kl_hash_s{H};
+  KL_API_END
+}
+extern "C" kl_status kl_hash_destroy(kl_hash_t h) {
+  if (!h) return KL_EINVAL;
+  delete h;
+  return KL_OK;
+}
+extern "C" kl_status kl_hash_info(kl_hash_t h, int* kind, int* d, int* k, int* L) {
+  if (!h) return KL_EINVAL;
+  if (kind) *kind = h->h->dh.kind;
+  if (d) *d = h->h->dh.d;
+  if (k) *k = h->h->dh.k;
+  if (L) *L = h->h->dh.L;
+  return KL_OK;
+}
+extern "C" kl_status kl_hash_dense_batch(kl_hash_t h, const float* X, int n, int ldx, uint64_t* codes,
+                                         float* min_abs_proj) {
+  if (!h) return KL_EINVAL;
+  KL_API_BEGIN(h->h->ctx)
+  require(n >= 0 && (n == 0 || (X && codes && ldx >= h->h->dh.d)), "hash_dense_batch: bad arguments");
+  HashOut o;
+  o.codes = codes;
+  o.min_abs = min_abs_proj;
+  launch_hash_dense(h->h->dh, dense_rows(X, KL_DTYPE_F32, n, ldx), o, ctx__->stream);
+  ck_launch("hash_dense_batch");
+  KL_API_END
+}
+extern "C" kl_status kl_hash_sparse_batch(kl_hash_t h, const int32_t* rowptr, const uint32_t* idx,
+                                          const float* val, int n, uint64_t* codes, float* min_abs_proj) {
+  if (!h) return KL_EINVAL;
+  KL_API_BEGIN(h->h->ctx)
+  require(n >= 0 && (n == 0 || (rowptr && codes)), "hash_sparse_batch: bad arguments");
+  HashOut o;
+  o.codes = codes;
+  o.min_abs = min_abs_proj;
+  launch_hash_sparse(h->h->dh, SparseIn{rowptr, idx, val, n}, o, ctx__->stream);
+  ck_launch("hash_sparse_batch");
+  KL_API_END
+}
+
+// ===========================================================================
+// Index
+// ===========================================================================
+extern "C" kl_status kl_index_create(kl_ctx_t ctx, kl_hash_t h, int bucket_type, int capacity,
+                                     kl_index_t* out) {
+  if (!ctx || !h || !out) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  *out = nullptr;
+  auto I = make_index(ctx, h->h, bucket_type, capacity);
+  *out = new kl_index_s{I};
+  KL_API_END
+}
+extern "C" kl_status kl_index_destroy(kl_index_t ix) {
+  if (!ix) return KL_EINVAL;
+  delete ix;
+  return KL_OK;
+}
+extern "C" kl_status kl_index_info(kl_index_t ix, int* L, int* nb, int* cap, int* type) {
+  if (!ix) return KL_EINVAL;
+  if (L) *L = ix->ix->T.L;
+  if (nb) *nb = ix->ix->T.nb;
+  if (cap) *cap = ix->ix->T.cap;
+  if (type) *type = ix->ix->T.type;
+  return KL_OK;
+}
+extern "C" kl_status kl_index_insert_batch(kl_index_t ix, const uint32_t* ids, const void* rows, int n,
+                                           int ld, int dtype) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  require(n >= 0 && (n == 0 || (ids && rows && ld >= I.hash->dh.d)), "insert_batch: bad arguments");
+  if (n == 0) return KL_OK;
+  I.hash_dense_to_bkt(dense_rows(rows, dtype, n, ld));
+  I.insert_from_bkt(ids, n);
+  KL_API_END
+}
+extern "C" kl_status kl_index_insert_sparse_batch(kl_index_t ix, const uint32_t* ids, const int32_t* rowptr,
+                                                  const uint32_t* idx, const float* val, int n) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  require(n >= 0 && (n == 0 || (ids && rowptr)), "insert_sparse_batch: bad arguments");
+  if (n == 0) return KL_OK;
+  I.hash_sparse_to_bkt(SparseIn{rowptr, idx, val, n});
+  I.insert_from_bkt(ids, n);
+  KL_API_END
+}
+extern "C" kl_status kl_index_remove(kl_index_t ix, const uint32_t* ids, int n) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  require(n >= 0 && (n == 0 || ids), "remove: bad arguments");
+  launch_tables_remove(I.T, ids, n, ctx__->stream);
+  ck_launch("remove");
+  KL_API_END
+}
+extern "C" kl_status kl_index_remove_with_weights(kl_index_t ix, const uint32_t* ids, const void* rows,
+                                                  int n, int ld, int dtype) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  require(n >= 0 && (n == 0 || (ids && rows && ld >= I.hash->dh.d)), "remove_with_weights: bad arguments");
+  if (n == 0) return KL_OK;
+  I.hash_dense_to_bkt(dense_rows(rows, dtype, n, ld));
+  launch_tables_remove_hashed(I.T, ids, I.bkt.as<uint16_t>(), n, n, ctx__->stream);
+  ck_launch("remove_with_weights");
+  KL_API_END
+}
+extern "C" kl_status kl_index_rebuild(kl_index_t ix, const uint32_t* ids, const void* rows, int n, int ld,
+                                      int dtype) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  require(n >= 0 && (n == 0 || (rows && ld >= I.hash->dh.d)), "rebuild: bad arguments");
+  I.clear();
+  if (n == 0) return KL_OK;
+  I.hash_dense_to_bkt(dense_rows(rows, dtype, n, ld));
+  I.insert_from_bkt(ids, n);
+  KL_API_END
+}
+extern "C" kl_status kl_index_clear(kl_index_t ix) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  I.clear();
+  KL_API_END
+}
+extern "C" kl_status kl_index_query_batch(kl_index_t ix, const float* X, int n, int ldx, int mode,
+                                          uint32_t* out_ids, uint32_t* out_counts, int32_t* out_offsets,
+                                          int32_t capacity, int32_t* overflow) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  require(mode == KL_QUERY_COUNTS || mode == KL_QUERY_UNION, "query: unknown mode");
+  require(n >= 0 && out_offsets && (n == 0 || (X && ldx >= I.hash->dh.d)), "query: bad arguments");
+  require(capacity >= 0 && (capacity == 0 || out_ids), "query: bad capacity");
+  if (n == 0) {
+    ck(cudaMemsetAsync(out_offsets, 0, 4, ctx__->stream), "memset");
+    return KL_OK;
+  }
+  I.hash_dense_to_bkt(dense_rows(X, KL_DTYPE_F32, n, ldx));
+  I.query(n, mode, out_ids, out_counts, out_offsets, capacity, overflow);
+  KL_API_END
+}
+extern "C" kl_status kl_index_query_sparse_batch(kl_index_t ix, const int32_t* rowptr, const uint32_t* idx,
+                                                 const float* val, int n, int mode, uint32_t* out_ids,
+                                                 uint32_t* out_counts, int32_t* out_offsets, int32_t capacity,
+                                                 int32_t* overflow) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  require(mode == KL_QUERY_COUNTS || mode == KL_QUERY_UNION, "query: unknown mode");
+  require(n >= 0 && out_offsets && (n == 0 || rowptr), "query_sparse: bad arguments");
+  require(capacity >= 0 && (capacity == 0 || out_ids), "query: bad capacity");
+  if (n == 0) {
+    ck(cudaMemsetAsync(out_offsets, 0, 4, ctx__->stream), "memset");
+    return KL_OK;
+  }
+  I.hash_sparse_to_bkt(SparseIn{rowptr, idx, val, n});
+  I.query(n, mode, out_ids, out_counts, out_offsets, capacity, overflow);
+  KL_API_END
+}
+extern "C" kl_status kl_index_export(kl_index_t ix, uint32_t* ids, uint32_t* lens, uint64_t* counts) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  const size_t LB = (size_t)I.T.L * I.T.nb;
+  cudaStream_t st = ctx__->stream;
+  if (ids) ck(cudaMemcpyAsync(ids, I.T.ids, LB * I.T.cap * 4, cudaMemcpyDeviceToDevice, st), "export");
+  if (lens) ck(cudaMemcpyAsync(lens, I.T.len, LB * 4, cudaMemcpyDeviceToDevice, st), "export");
+  if (counts) ck(cudaMemcpyAsync(counts, I.T.cnt, LB * 8, cudaMemcpyDeviceToDevice, st), "export");
+  KL_API_END
+}
+extern "C" kl_status kl_index_import(kl_index_t ix, const uint32_t* ids, const uint32_t* lens,
+                                     const uint64_t* counts) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  require(ids && lens, "import: ids and lens required");
+  const size_t LB = (size_t)I.T.L * I.T.nb;
+  cudaStream_t st = ctx__->stream;
+  ck(cudaMemcpyAsync(I.T.ids, ids, LB * I.T.cap * 4, cudaMemcpyDeviceToDevice, st), "import");
+  ck(cudaMemcpyAsync(I.T.len, lens, LB * 4, cudaMemcpyDeviceToDevice, st), "import");
+  if (counts) ck(cudaMemcpyAsync(I.T.cnt, counts, LB * 8, cudaMemcpyDeviceToDevice, st), "import");
+  else ck(cudaMemsetAsync(I.T.cnt, 0, LB * 8, st), "import");
+  KL_API_END
+}
+
+// ===========================================================================
+// Network
+// ===========================================================================
+namespace {
+
+// RebuildScheduler (lsh/maintenance.rs:28-98).
+struct Scheduler {
+  uint64_t base = 100;
+  double decay = 0.1;
+  uint64_t count = 0, next = 100, cur = 0;
+  bool should_rebuild(uint64_t step) {
+    cur = step;
+    if (cur >= next) {
+      count += 1;
+      uint64_t interval = (uint64_t)((double)base * std::exp(decay * (double)count));
+      next = cur + std::max<uint64_t>(interval, 1);
+      return true;
+    }
+    return false;
+  }
+};
+
+struct Layer {
+  kl_layer_config cfg{};
+  int d = 0, N = 0;
+  bool fm = false;   // feature-major weights (layer 0)
+  int ldw = 0;       // weight row pitch (elements)
+  int ldN = 0;       // pitch of dense rows over this layer's neurons
+  int ldd = 0;       // pitch of dense rows over this layer's inputs
+  int stride = 0;    // max active per example
+  int nchunk = 0;
+  int id_bits = 0;
+  DBuf W, b, m, v, mb, vb;
+  std::shared_ptr<IndexImpl> index;
+  // per-step buffers
+  DBuf bkt, ids, cnt, pre, post, lg, h, dx_in, dxpart, lgd, tmask;
+  DBuf hist, cur, touched, ctr, ent_s, ent_v;
+  size_t ent_cap = 0;
+  DBuf stats;  // u64 [3]: active_sum, touched_rows, input_nnz
+  uint64_t examples = 0, steps = 0, rebuilds = 0, input_nnz = 0;
+
+  ActiveSet act() const {
+    return ActiveSet{ids.as<uint32_t>(), cnt.as<int32_t>(), stride, pre.as<float>(), post.as<float>(),
+                     lg.as<float>()};
+  }
+};
+
+}  // namespace
+
+struct kl_net_s {
+  kl_ctx_t ctx;
+  kl_net_config cfg{};
+  std::vector<kl_layer_config> layer_cfgs;
+  std::vector<std::unique_ptr<Layer>> layers;
+  int wdtype = KL_DTYPE_F32;
+  int max_batch = 0;
+  uint64_t step = 0;
+  Scheduler sched;
+  DBuf labprob, loss_acc, rb_bkt, rb_scratch;
+  size_t labprob_cap = 0;
+  std::vector<std::unique_ptr<kl_index_s>> index_handles;
+
+  // Phase profiler: CUDA events on the context stream around each phase of
+  // each layer; read (and synchronised) by kl_net_profile_read.
+  bool prof = false;
+  struct Ev {
+    cudaEvent_t a, b;
+    int layer, phase;
+  };
+  std::vector<Ev> pending;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pool;
+  std::vector<double> prof_ms;
+  std::vector<uint64_t> prof_calls;
+  int prof_begin(int layer, int phase) {
+    if (!prof) return -1;
+    std::pair<cudaEvent_t, cudaEvent_t> e;
+    if (!pool.empty()) {
+      e = pool.back();
+      pool.pop_back();
+    } else {
+      ck(cudaEventCreate(&e.first), "event");
+      ck(cudaEventCreate(&e.second), "event");
+    }
+    ck(cudaEventRecord(e.first, ctx->stream), "event");
+    pending.push_back(Ev{e.first, e.second, layer, phase});
+    return (int)pending.size() - 1;
+  }
+  void prof_end(int i) {
+    if (i >= 0) ck(cudaEventRecord(pending[i].b, ctx->stream), "event");
+  }
+  void prof_collect() {
+    ck(cudaStreamSynchronize(ctx->stream), "sync");
+    prof_ms.resize(layers.size() * KL_NPHASES, 0.0);
+    prof_calls.resize(layers.size() * KL_NPHASES, 0);
+    for (auto& e : pending) {
+      float ms = 0.0f;
+      ck(cudaEventElapsedTime(&ms, e.a, e.b), "elapsed");
+      prof_ms[(size_t)e.layer * KL_NPHASES + e.phase] += ms;
+      prof_calls[(size_t)e.layer * KL_NPHASES + e.phase] += 1;
+      pool.emplace_back(e.a, e.b);
+    }
+    pending.clear();
+  }
+  struct Phase {
+    kl_net_s* n;
+    int i;
+    Phase(kl_net_s* net, int layer, int phase) : n(net), i(net->prof_begin(layer, phase)) {}
+    ~Phase() { n->prof_end(i); }
+  };
+  ~kl_net_s() {
+    for (auto& e : pending) pool.emplace_back(e.a, e.b);
+    for (auto& e : pool) {
+      cudaEventDestroy(e.first);
+      cudaEventDestroy(e.second);
+    }
+  }
+
+  void rebuild_layer(Layer& L) {
+    Phase ph(this, layer_index_of(L), KL_PHASE_REBUILD);
+    cudaStream_t st = ctx->stream;
+    IndexImpl& I = *L.index;
+    DenseIn in;
+    in.X = L.W.p;
+    in.dtype = wdtype;
+    in.n = L.N;
+    if (L.fm) {
+      in.ld_row = 1;
+      in.ld_elem = L.ldw;
+    } else {
+      in.ld_row = L.ldw;
+      in.ld_elem = 1;
+    }
+    rb_bkt.alloc((size_t)I.T.L * L.N * 2);
+    HashOut o;
+    o.bkt = rb_bkt.as<uint16_t>();
+    o.bkt_ld = L.N;
+    o.nb_mask = (uint32_t)(I.T.nb - 1);
+    launch_hash_dense(I.hash->dh, in, o, st);
+    ck_launch("rebuild hash");
+    I.clear();
+    rb_scratch.alloc(insert_scratch_bytes(I.T, L.N));
+    InsertScratch s;
+    carve_insert_scratch(I.T, L.N, rb_scratch.p, &s);
+    launch_tables_insert(I.T, nullptr, rb_bkt.as<uint16_t>(), L.N, L.N, s, ctx->err.as<int>(), st);
+    ck_launch("rebuild insert");
+    L.rebuilds++;
+  }
+  int layer_index_of(const Layer& L) const {
+    for (size_t i = 0; i < layers.size(); ++i)
+      if (layers[i].get() == &L) return (int)i;
+    return 0;
+  }
+  void rebuild_all() {
+    for (auto& L : layers) rebuild_layer(*L);
+  }
+
+  OptStep opt_step(double lr) const {
+    OptStep o;
+    o.opt = cfg.optimizer;
+    o.lr = (float)lr;
+    o.b1 = 0.9f;
+    o.b2 = 0.999f;
+    o.eps = 1e-8f;
+    o.omb1 = 1.0f - o.b1;
+    o.omb2 = 1.0f - o.b2;
+    const uint64_t t = std::max<uint64_t>(step, 1);
+    o.c1 = 1.0f - powi_f32(o.b1, (int)t);
+    o.c2 = 1.0f - powi_f32(o.b2, (int)t);
+    o.mom = 0.9f;
+    return o;
+  }
+
+  // Forward of nq examples starting at example s0 of the batch (views by
+  // pointer offset: CSR offsets stay absolute).  train=true also computes
+  // the loss gradient in the output layer.
+  void forward(const kl_batch& b, int s0, int nq, bool train) {
+    cudaStream_t st = ctx->stream;
+    const int nL = (int)layers.size();
+    SparseIn in{b.rowptr + s0, b.idx, b.val, nq};
+    for (int l = 0; l < nL; ++l) {
+      Layer& L = *layers[l];
+      const bool last = l == nL - 1;
+      IndexImpl& I = *L.index;
+      HashOut ho;
+      ho.bkt = L.bkt.as<uint16_t>();
+      ho.bkt_ld = max_batch;
+      ho.nb_mask = (uint32_t)(I.T.nb - 1);
+      Phase ph_hash(this, l, KL_PHASE_HASH);
+      if (l == 0) {
+        launch_hash_sparse(I.hash->dh, in, ho, st);
+      } else {
+        const Layer& P = *layers[l - 1];
+        DenseIn di;
+        di.X = P.h.p;
+        di.dtype = KL_DTYPE_F32;
+        di.ld_row = P.ldN;
+        di.ld_elem = 1;
+        di.n = nq;
+        launch_hash_dense(I.hash->dh, di, ho, st);
+      }
+      ck_launch("layer hash");
+      ph_hash.~Phase();
+      new (&ph_hash) Phase(this, l, KL_PHASE_PROBE);
+      ProbeArgs pa;
+      pa.T = I.T;
+      pa.bkt = L.bkt.as<uint16_t>();
+      pa.bkt_ld = max_batch;
+      pa.nq = nq;
+      pa.N = L.N;
+      pa.sampling = L.cfg.sampling;
+      pa.top_k = L.cfg.top_k;
+      pa.threshold = L.cfg.sampling_threshold;
+      pa.id_bits = L.id_bits;
+      pa.out_ids = L.ids.as<uint32_t>();
+      pa.out_stride = L.stride;
+      pa.out_n = L.cnt.as<int32_t>();
+      pa.err = ctx->err.as<int>();
+      pa.stat_active = L.stats.as<unsigned long long>();
+      launch_probe(pa, st);
+      ck_launch("probe");
+      ph_hash.~Phase();
+      new (&ph_hash) Phase(this, l, KL_PHASE_FORWARD);
+      float* hout = nullptr;
+      if (!last) {
+        ck(cudaMemsetAsync(L.h.p, 0, (size_t)nq * L.ldN * 4, st), "memset");
+        hout = L.h.as<float>();
+      }
+      const ActiveSet A = L.act();
+      if (L.fm) {
+        launch_fm_forward(L.W.p, wdtype, L.ldw, L.d, L.b.as<float>(), L.cfg.activation, in, A, hout, L.ldN,
+                          ctx->err.as<int>(), st);
+        ck_launch("fm forward");
+        if (L.cfg.activation == KL_ACT_SOFTMAX) {
+          launch_softmax(A, hout, L.ldN, nullptr, nullptr, nullptr, nq, st);
+          ck_launch("softmax");
+        }
+      } else {
+        const Layer& P = *layers[l - 1];
+        RmArgs ra{};
+        ra.W = L.W.p;
+        ra.wdtype = wdtype;
+        ra.ldw = L.ldw;
+        ra.d = L.d;
+        ra.bias = L.b.as<float>();
+        ra.act = L.cfg.activation;
+        ra.X = P.h.as<float>();
+        ra.ldx = P.ldN;
+        ra.A = A;
+        ra.h = hout;
+        ra.ldh = L.ldN;
+        ra.dxpart = L.dxpart.as<float>();
+        ra.nchunk = L.nchunk;
+        ra.lab_ptr = b.label_ptr + s0;
+        ra.labels = b.labels;
+        ra.labprob = labprob.as<float>();
+        ra.err = ctx->err.as<int>();
+        const bool softmax = L.cfg.activation == KL_ACT_SOFTMAX;
+        const bool fused = last && train && !softmax;
+        launch_rm_forward(ra, nq, fused ? RM_FUSED : RM_FWD, st);
+        ck_launch("rm forward");
+        if (softmax) {
+          launch_softmax(A, hout, L.ldN, last && train ? b.label_ptr + s0 : nullptr, b.labels, labprob.as<float>(),
+                         nq, st);
+          ck_launch("softmax");
+          if (last && train) {
+            launch_rm_forward(ra, nq, RM_DX, st);
+            ck_launch("rm dx");
+          }
+        }
+      }
+    }
+  }
+
+  // Backward + updates for the examples of the last forward (net.rs:122-146).
+  void backward(const kl_batch& b, int s0, int nq, double lr) {
+    cudaStream_t st = ctx->stream;
+    const int nL = (int)layers.size();
+    const OptStep o = opt_step(lr);
+    SparseIn in{b.rowptr + s0, b.idx, b.val, nq};
+    // input gradient of the output layer
+    {
+      Phase ph(this, nL - 1, KL_PHASE_BACKWARD);
+      Layer& L = *layers[nL - 1];
+      launch_reduce_dx(L.dxpart.as<float>(), L.nchunk, L.ldd, L.d, L.cnt.as<int32_t>(), L.dx_in.as<float>(), nq,
+                       st);
+      ck_launch("reduce dx");
+    }
+    for (int l = nL - 2; l >= 0; --l) {
+      Phase ph(this, l, KL_PHASE_BACKWARD);
+      Layer& L = *layers[l];
+      const Layer& U = *layers[l + 1];
+      float* lgd = nullptr;
+      uint32_t* tmask = nullptr;
+      if (L.fm) {
+        ck(cudaMemsetAsync(L.lgd.p, 0, (size_t)nq * L.ldN * 4, st), "memset");
+        ck(cudaMemsetAsync(L.tmask.p, 0, (size_t)ceil_div(L.N, 32) * 4, st), "memset");
+        lgd = L.lgd.as<float>();
+        tmask = L.tmask.as<uint32_t>();
+      }
+      launch_local_grads(L.act(), L.cfg.activation, U.dx_in.as<float>(), U.ldd, lgd, L.ldN, tmask, nq, st);
+      ck_launch("local grads");
+      if (!L.fm) {
+        const Layer& P = *layers[l - 1];
+        RmArgs ra{};
+        ra.W = L.W.p;
+        ra.wdtype = wdtype;
+        ra.ldw = L.ldw;
+        ra.d = L.d;
+        ra.bias = L.b.as<float>();
+        ra.act = L.cfg.activation;
+        ra.X = P.h.as<float>();
+        ra.ldx = P.ldN;
+        ra.A = L.act();
+        ra.dxpart = L.dxpart.as<float>();
+        ra.nchunk = L.nchunk;
+        ra.err = ctx->err.as<int>();
+        launch_rm_forward(ra, nq, RM_DX, st);
+        ck_launch("rm dx");
+        launch_reduce_dx(L.dxpart.as<float>(), L.nchunk, L.ldd, L.d, L.cnt.as<int32_t>(), L.dx_in.as<float>(), nq,
+                         st);
+        ck_launch("reduce dx");
+      }
+    }
+    // optimizer updates (every gradient above used the pre-update weights)
+    for (int l = nL - 1; l >= 0; --l) {
+      Phase ph(this, l, KL_PHASE_UPDATE);
+      Layer& L = *layers[l];
+      unsigned long long* stat = L.stats.as<unsigned long long>() + 1;
+      ck(cudaMemsetAsync(L.ctr.p, 0, 8, st), "memset");
+      SegScratch S{L.hist.as<uint32_t>(), L.cur.as<uint32_t>(), L.touched.as<uint32_t>(), L.ctr.as<uint32_t>(),
+                   L.ent_s.as<uint32_t>(), L.ent_v.as<float>()};
+      if (L.fm) {
+        launch_fm_update(L.W.p, wdtype, L.ldw, L.d, L.N, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
+                         L.mb.as<float>(), L.vb.as<float>(), in, L.lgd.as<float>(), L.ldN, L.tmask.as<uint32_t>(),
+                         S, o, stat, st);
+        ck_launch("fm update");
+      } else {
+        const Layer& P = *layers[l - 1];
+        launch_rm_update(L.W.p, wdtype, L.ldw, L.d, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
+                         L.mb.as<float>(), L.vb.as<float>(), P.h.as<float>(), P.ldN, L.act(), nq, L.N, S, o,
+                         stat, st);
+        ck_launch("rm update");
+      }
+    }
+  }
+
+  void ensure_batch_buffers(const kl_batch& b) {
+    if ((size_t)b.nlabels > labprob_cap) {
+      labprob.alloc((size_t)std::max(b.nlabels, 1) * 4);
+      labprob_cap = (size_t)b.nlabels;
+    }
+    Layer& L0 = *layers[0];
+    if ((size_t)b.nnz > L0.ent_cap) {
+      L0.ent_s.alloc((size_t)std::max(b.nnz, 1) * 4);
+      L0.ent_v.alloc((size_t)std::max(b.nnz, 1) * 4);
+      L0.ent_cap = (size_t)b.nnz;
+    }
+  }
+};
+
+namespace {
+
+void validate_batch(const kl_net_s* net, const kl_batch* b) {
+  require(b != nullptr, "batch is NULL");
+  require(b->batch >= 0, "batch size must be >= 0");
+  require(b->batch <= net->max_batch, "batch larger than the network's max_batch");
+  require(b->nnz >= 0 && b->nlabels >= 0, "batch nnz / nlabels must be >= 0");
+  if (b->batch > 0) require(b->rowptr && b->label_ptr, "batch rowptr / label_ptr required");
+  if (b->nnz > 0) require(b->idx && b->val, "batch idx / val required");
+  if (b->nlabels > 0) require(b->labels != nullptr, "batch labels required");
+}
+
+void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_init* init) {
+  kl_ctx_t ctx = net->ctx;
+  cudaStream_t st = ctx->stream;
+  auto Lp = std::make_unique<Layer>();
+  Layer& L = *Lp;
+  L.cfg = c;
+  L.d = c.input_dim;
+  L.N = c.num_neurons;
+  require(L.d >= 1 && L.N >= 1, "layer: input_dim and num_neurons must be >= 1");
+  require(c.activation >= KL_ACT_RELU && c.activation <= KL_ACT_IDENTITY, "layer: unknown activation");
+  require(c.sampling >= KL_SAMPLING_VANILLA && c.sampling <= KL_SAMPLING_THRESHOLD, "layer: unknown sampling");
+  L.fm = (l == 0);
+  if (L.fm) support(L.N <= 1024, "layer 0 (sparse input) supports at most 1024 neurons");
+  else support(L.d <= 8192, "hidden/output layers support input_dim <= 8192");
+  L.ldw = L.fm ? pitch_of(L.N) : pitch_of(L.d);
+  L.ldN = pitch_of(L.N);
+  L.ldd = pitch_of(L.d);
+  L.id_bits = bits_for((uint64_t)L.N);
+  const kl_lsh_config& lc = c.lsh;
+  const int window = std::min(8, L.d);  // index.rs:325-330
+  // hash family: explicit parameters or seeded (seed + 1_000_000, layer.rs:40)
+  std::shared_ptr<HashImpl> H;
+  const uint64_t lseed = net->cfg.seed + (uint64_t)l * 100000ULL;
+  bool explicit_hash = init && (init->hash.planes || init->hash.windows || init->hash.perms || init->hash.srp_rowptr);
+  if (explicit_hash) {
+    H = make_hash(ctx, lc.hash_function, L.d, lc.num_hashes, lc.num_tables, window, &init->hash);
+  } else {
+    SeededParams sp;
+    seeded_params(lc.hash_function, L.d, lc.num_hashes, lc.num_tables, window, 1.0f / 3.0f, lseed + 1000000ULL, sp);
+    H = make_hash(ctx, lc.hash_function, L.d, lc.num_hashes, lc.num_tables, window, &sp.p);
+  }
+  L.index = make_index(ctx, H, lc.bucket_type, lc.bucket_capacity);
+  // active capacity per example
+  int64_t cap = std::min<int64_t>((int64_t)L.N, (int64_t)lc.num_tables * lc.bucket_capacity);
+  if (c.sampling == KL_SAMPLING_TOPK) cap = std::min<int64_t>(cap, std::max(c.top_k, 0));
+  if (L.N <= 8192) cap = std::max<int64_t>(cap, L.N);  // room for the all-neurons fallback
+  L.stride = (int)std::max<int64_t>(cap, 1);
+  if (L.fm) support(L.stride <= 1024, "layer 0 active capacity exceeds 1024");
+  L.nchunk = (int)ceil_div(L.stride, RM_RPB);
+  // parameters
+  const size_t wsz = net->wdtype == KL_DTYPE_BF16 ? 2 : 4;
+  const size_t nrows_store = L.fm ? (size_t)L.d : (size_t)L.N;
+  const size_t welems = nrows_store * L.ldw;
+  L.W.alloc(welems * wsz);
+  L.m.alloc(welems * 4);
+  L.v.alloc(welems * 4);
+  L.b.alloc((size_t)L.N * 4);
+  L.mb.alloc((size_t)L.N * 4);
+  L.vb.alloc((size_t)L.N * 4);
+  ck(cudaMemsetAsync(L.W.p, 0, welems * wsz, st), "memset");
+  ck(cudaMemsetAsync(L.m.p, 0, welems * 4, st), "memset");
+  ck(cudaMemsetAsync(L.v.p, 0, welems * 4, st), "memset");
+  ck(cudaMemsetAsync(L.mb.p, 0, (size_t)L.N * 4, st), "memset");
+  ck(cudaMemsetAsync(L.vb.p, 0, (size_t)L.N * 4, st), "memset");
+  {
+    // initial rows: explicit, or N(0, sqrt(2/d)) from this library's generator (neuron.rs:23-43)
+    std::vector<float> rows;
+    const float* src = init ? init->weights : nullptr;
+    if (!src) {
+      rows.resize((size_t)L.N * L.d);
+      const double sd = std::sqrt(2.0 / (double)L.d);
+      for (int n = 0; n < L.N; ++n) {
+        SplitMix rng{lseed + (uint64_t)n};
+        for (int i = 0; i < L.d; ++i) rows[(size_t)n * L.d + i] = (float)(rng.normal() * sd);
+      }
+      src = rows.data();
+    }
+    DBuf tmp;
+    // upload in row slabs to bound the temporary
+    const int64_t slab = std::max<int64_t>(1, (int64_t)(64u << 20) / (4 * (int64_t)L.d));
+    tmp.alloc((size_t)std::min<int64_t>(slab, L.N) * L.d * 4);
+    for (int64_t r0 = 0; r0 < L.N; r0 += slab) {
+      const int64_t nr = std::min<int64_t>(slab, L.N - r0);
+      ck(cudaMemcpyAsync(tmp.p, src + (size_t)r0 * L.d, (size_t)nr * L.d * 4, cudaMemcpyHostToDevice, st), "upload");
+      void* dst = L.fm ? (void*)((char*)L.W.p + (size_t)r0 * wsz) : (void*)((char*)L.W.p + (size_t)r0 * L.ldw * wsz);
+      launch_f32_to_w(tmp.as<float>(), nr, L.d, L.d, dst, net->wdtype, L.ldw, L.fm, st);
+      ck_launch("weights upload");
+      ck(cudaStreamSynchronize(st), "sync");
+    }
+    std::vector<float> bias((size_t)L.N, 0.0f);
+    if (init && init->bias) std::memcpy(bias.data(), init->bias, (size_t)L.N * 4);
+    ck(cudaMemcpyAsync(L.b.p, bias.data(), (size_t)L.N * 4, cudaMemcpyHostToDevice, st), "upload");
+    ck(cudaStreamSynchronize(st), "sync");
+  }
+  // per-step buffers
+  const int B = net->max_batch;
+  L.bkt.alloc((size_t)lc.num_tables * B * 2);
+  L.ids.alloc((size_t)B * L.stride * 4);
+  L.cnt.alloc((size_t)B * 4);
+  L.pre.alloc((size_t)B * L.stride * 4);
+  L.post.alloc((size_t)B * L.stride * 4);
+  L.lg.alloc((size_t)B * L.stride * 4);
+  L.h.alloc((size_t)B * L.ldN * 4);
+  if (!L.fm) {
+    L.dx_in.alloc((size_t)B * L.ldd * 4);
+    L.dxpart.alloc((size_t)B * L.nchunk * L.ldd * 4);
+  } else {
+    L.lgd.alloc((size_t)B * L.ldN * 4);
+    L.tmask.alloc((size_t)ceil_div(L.N, 32) * 4);
+  }
+  const size_t rows = L.fm ? (size_t)L.d : (size_t)L.N;
+  L.hist.alloc(rows * 4);
+  L.cur.alloc(rows * 4);
+  L.touched.alloc(rows * 4);
+  L.ctr.alloc(8);
+  ck(cudaMemsetAsync(L.hist.p, 0, rows * 4, st), "memset");
+  if (!L.fm) {
+    L.ent_s.alloc((size_t)B * L.stride * 4);
+    L.ent_v.alloc((size_t)B * L.stride * 4);
+    L.ent_cap = (size_t)B * L.stride;
+  }
+  L.stats.alloc(3 * 8);
+  ck(cudaMemsetAsync(L.stats.p, 0, 24, st), "memset");
+  net->layers.push_back(std::move(Lp));
+}
+
+}  // namespace
+
+extern "C" kl_status kl_net_create(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init* init,
+                                   kl_net_t* out) {
+  if (!ctx || !cfg || !out) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  *out = nullptr;
+  require(cfg->num_layers >= 1 && cfg->layers, "net: at least one layer required");
+  support(cfg->num_layers >= 2, "net: single-layer networks are not supported (layer 0 is the sparse-input layer)");
+  require(cfg->optimizer == KL_OPT_SGD || cfg->optimizer == KL_OPT_ADAM, "net: unknown optimizer");
+  require(cfg->weight_dtype == KL_DTYPE_F32 || cfg->weight_dtype == KL_DTYPE_BF16, "net: unknown weight dtype");
+  require(cfg->max_batch >= 1 && cfg->max_batch <= 4096, "net: max_batch must be in [1, 4096]");
+  for (int l = 1; l < cfg->num_layers; ++l)
+    require(cfg->layers[l].input_dim == cfg->layers[l - 1].num_neurons,
+            "net: layer input_dim must equal the previous layer's num_neurons");
+  std::unique_ptr<kl_net_s> net(new kl_net_s());
+  net->ctx = ctx;
+  net->cfg = *cfg;
+  net->layer_cfgs.assign(cfg->layers, cfg->layers + cfg->num_layers);
+  net->cfg.layers = net->layer_cfgs.data();
+  net->wdtype = cfg->weight_dtype;
+  net->max_batch = cfg->max_batch;
+  for (int l = 0; l < cfg->num_layers; ++l) build_layer(net.get(), l, cfg->layers[l], init ? &init[l] : nullptr);
+  // Layer::new inserts every neuron in id order (layer.rs:42-44)
+  for (auto& L : net->layers) {
+    net->rebuild_layer(*L);
+    L->rebuilds = 0;
+  }
+  const kl_lsh_config& l0 = cfg->layers[0].lsh;
+  net->sched.base = (uint64_t)std::max(0, l0.rebuild_interval_base);
+  net->sched.decay = l0.rebuild_decay;
+  net->sched.next = net->sched.base;
+  net->loss_acc.alloc(4);
+  net->labprob.alloc(4);
+  ck(cudaStreamSynchronize(ctx->stream), "sync");
+  *out = net.release();
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_destroy(kl_net_t net) {
+  if (!net) return KL_EINVAL;
+  {
+    DeviceGuard g(net->ctx->device);
+    cudaStreamSynchronize(net->ctx->stream);
+    delete net;
+  }
+  return KL_OK;
+}
+
+namespace {
+__global__ void loss_final_kernel(const float* acc, int B, float* out1, float* out2) {
+  const float v = B > 0 ? __fdiv_rn(*acc, (float)B) : 0.0f;
+  if (out1) *out1 = v;
+  if (out2) *out2 = v;
+}
+}  // namespace
+
+extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double lr, int mode, float* loss,
+                                       float* loss_host) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  validate_batch(net, b);
+  require(mode == KL_MODE_EXACT_SEQUENTIAL || mode == KL_MODE_BATCHED, "train_step: unknown mode");
+  cudaStream_t st = ctx__->stream;
+  if (b->batch == 0) {  // net.rs:82-84
+    if (loss) ck(cudaMemsetAsync(loss, 0, 4, st), "memset");
+    if (loss_host) *loss_host = 0.0f;
+    return KL_OK;
+  }
+  net->ensure_batch_buffers(*b);
+  ck(cudaMemsetAsync(net->loss_acc.p, 0, 4, st), "memset");
+  ck(cudaMemsetAsync(net->labprob.p, 0, (size_t)std::max(b->nlabels, 1) * 4, st), "memset");
+  if (mode == KL_MODE_BATCHED) {
+    net->forward(*b, 0, b->batch, true);
+    launch_loss(b->label_ptr, net->labprob.as<float>(), b->batch, net->loss_acc.as<float>(), st);
+    ck_launch("loss");
+    net->backward(*b, 0, b->batch, lr);
+  } else {
+    for (int s = 0; s < b->batch; ++s) {
+      net->forward(*b, s, 1, true);
+      launch_loss(b->label_ptr + s, net->labprob.as<float>(), 1, net->loss_acc.as<float>(), st);
+      ck_launch("loss");
+      net->backward(*b, s, 1, lr);
+    }
+  }
+  loss_final_kernel<<<1, 1, 0, st>>>(net->loss_acc.as<float>(), b->batch, loss, net->loss_acc.as<float>());
+  ck_launch("loss final");
+  for (auto& L : net->layers) {
+    L->examples += (uint64_t)b->batch;
+    L->steps += 1;
+  }
+  net->layers[0]->input_nnz += (uint64_t)b->nnz;
+  // net.rs:109-116
+  net->step += 1;
+  if (net->sched.should_rebuild(net->step)) net->rebuild_all();
+  if (loss_host) {
+    ck(cudaMemcpyAsync(loss_host, net->loss_acc.p, 4, cudaMemcpyDeviceToHost, st), "loss copy");
+    check_device_errors(ctx__);
+  }
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_forward(kl_net_t net, const kl_batch* b) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  validate_batch(net, b);
+  if (b->batch == 0) return KL_OK;
+  net->ensure_batch_buffers(*b);
+  net->forward(*b, 0, b->batch, false);
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_layer_info(kl_net_t net, int layer, int* d, int* N, int* max_active) {
+  if (!net) return KL_EINVAL;
+  if (layer < 0 || layer >= (int)net->layers.size()) return KL_EINVAL;
+  const Layer& L = *net->layers[layer];
+  if (d) *d = L.d;
+  if (N) *N = L.N;
+  if (max_active) *max_active = L.stride;
+  return KL_OK;
+}
+
+extern "C" kl_status kl_net_layer_output(kl_net_t net, int layer, uint32_t* ids, int32_t* counts, float* pre,
+                                         float* act) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  require(layer >= 0 && layer < (int)net->layers.size(), "layer index out of range");
+  const Layer& L = *net->layers[layer];
+  cudaStream_t st = ctx__->stream;
+  const size_t n = (size_t)net->max_batch * L.stride;
+  if (ids) ck(cudaMemcpyAsync(ids, L.ids.p, n * 4, cudaMemcpyDeviceToDevice, st), "copy");
+  if (counts) ck(cudaMemcpyAsync(counts, L.cnt.p, (size_t)net->max_batch * 4, cudaMemcpyDeviceToDevice, st), "copy");
+  if (pre) ck(cudaMemcpyAsync(pre, L.pre.p, n * 4, cudaMemcpyDeviceToDevice, st), "copy");
+  if (act) ck(cudaMemcpyAsync(act, L.post.p, n * 4, cudaMemcpyDeviceToDevice, st), "copy");
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_predict_topk(kl_net_t net, const kl_batch* b, int k, uint32_t* top_ids,
+                                         float* top_scores) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  validate_batch(net, b);
+  require(k >= 0 && (k == 0 || top_ids), "predict_topk: bad arguments");
+  if (b->batch == 0 || k == 0) return KL_OK;
+  const Layer& L = *net->layers.back();
+  k = std::min(k, L.N);
+  net->ensure_batch_buffers(*b);
+  net->forward(*b, 0, b->batch, false);
+  launch_topk(L.act(), L.N, k, top_ids, top_scores, b->batch, ctx__->stream);
+  ck_launch("topk");
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_get_layer(kl_net_t net, int layer, float* w, float* bias, float* m, float* v,
+                                      float* mb, float* vb) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  require(layer >= 0 && layer < (int)net->layers.size(), "layer index out of range");
+  const Layer& L = *net->layers[layer];
+  cudaStream_t st = ctx__->stream;
+  const size_t nd = (size_t)L.N * L.d;
+  DBuf tmp;
+  tmp.alloc(nd * 4);
+  auto pull = [&](const void* src, int dt, float* dst) {
+    launch_w_to_f32(src, dt, L.ldw, L.fm, tmp.as<float>(), L.N, L.d, st);
+    ck_launch("convert");
+    ck(cudaMemcpyAsync(dst, tmp.p, nd * 4, cudaMemcpyDeviceToHost, st), "copy");
+    ck(cudaStreamSynchronize(st), "sync");
+  };
+  if (w) pull(L.W.p, net->wdtype, w);
+  if (m) pull(L.m.p, KL_DTYPE_F32, m);
+  if (v) pull(L.v.p, KL_DTYPE_F32, v);
+  if (bias) ck(cudaMemcpyAsync(bias, L.b.p, (size_t)L.N * 4, cudaMemcpyDeviceToHost, st), "copy");
+  if (mb) ck(cudaMemcpyAsync(mb, L.mb.p, (size_t)L.N * 4, cudaMemcpyDeviceToHost, st), "copy");
+  if (vb) ck(cudaMemcpyAsync(vb, L.vb.p, (size_t)L.N * 4, cudaMemcpyDeviceToHost, st), "copy");
+  check_device_errors(ctx__);
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_set_layer(kl_net_t net, int layer, const float* w, const float* bias, const float* m,
+                                      const float* v, const float* mb, const float* vb) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  require(layer >= 0 && layer < (int)net->layers.size(), "layer index out of range");
+  Layer& L = *net->layers[layer];
+  cudaStream_t st = ctx__->stream;
+  const size_t nd = (size_t)L.N * L.d;
+  DBuf tmp;
+  tmp.alloc(nd * 4);
+  auto push = [&](const float* src, void* dst, int dt) {
+    ck(cudaMemcpyAsync(tmp.p, src, nd * 4, cudaMemcpyHostToDevice, st), "copy");
+    launch_f32_to_w(tmp.as<float>(), L.N, L.d, L.d, dst, dt, L.ldw, L.fm, st);
+    ck_launch("convert");
+    ck(cudaStreamSynchronize(st), "sync");
+  };
+  if (w) push(w, L.W.p, net->wdtype);
+  if (m) push(m, L.m.p, KL_DTYPE_F32);
+  if (v) push(v, L.v.p, KL_DTYPE_F32);
+  if (bias) ck(cudaMemcpyAsync(L.b.p, bias, (size_t)L.N * 4, cudaMemcpyHostToDevice, st), "copy");
+  if (mb) ck(cudaMemcpyAsync(L.mb.p, mb, (size_t)L.N * 4, cudaMemcpyHostToDevice, st), "copy");
+  if (vb) ck(cudaMemcpyAsync(L.vb.p, vb, (size_t)L.N * 4, cudaMemcpyHostToDevice, st), "copy");
+  ck(cudaStreamSynchronize(st), "sync");
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_rebuild(kl_net_t net) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  net->rebuild_all();
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_layer_index(kl_net_t net, int layer, kl_index_t* out) {
+  if (!net || !out) return KL_EINVAL;
+  if (layer < 0 || layer >= (int)net->layers.size()) return KL_EINVAL;
+  net->index_handles.emplace_back(new kl_index_s{net->layers[layer]->index});
+  *out = net->index_handles.back().get();
+  return KL_OK;
+}
+
+extern "C" kl_status kl_net_get_step(kl_net_t net, uint64_t* step, uint64_t* next_rebuild, uint64_t* count) {
+  if (!net) return KL_EINVAL;
+  if (step) *step = net->step;
+  if (next_rebuild) *next_rebuild = net->sched.next;
+  if (count) *count = net->sched.count;
+  return KL_OK;
+}
+extern "C" kl_status kl_net_set_step(kl_net_t net, uint64_t step, uint64_t next_rebuild, uint64_t count) {
+  if (!net) return KL_EINVAL;
+  net->step = step;
+  net->sched.next = next_rebuild;
+  net->sched.count = count;
+  net->sched.cur = step;
+  return KL_OK;
+}
+
+extern "C" kl_status kl_net_stats(kl_net_t net, int layer, kl_layer_stats* out, int reset) {
+  if (!net || !out) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  require(layer >= 0 && layer < (int)net->layers.size(), "layer index out of range");
+  Layer& L = *net->layers[layer];
+  unsigned long long v[3];
+  ck(cudaStreamSynchronize(ctx__->stream), "sync");
+  ck(cudaMemcpy(v, L.stats.p, 24, cudaMemcpyDeviceToHost), "copy");
+  out->active_sum = v[0];
+  out->touched_rows = v[1];
+  out->input_nnz = L.input_nnz;
+  out->examples = L.examples;
+  out->steps = L.steps;
+  out->rebuilds = L.rebuilds;
+  if (reset) {
+    ck(cudaMemset(L.stats.p, 0, 24), "memset");
+    L.examples = L.steps = L.rebuilds = L.input_nnz = 0;
+  }
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_profile(kl_net_t net, int enable) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  if (!enable && net->prof) net->prof_collect();
+  net->prof = enable != 0;
+  KL_API_END
+}
+extern "C" kl_status kl_net_profile_read(kl_net_t net, int layer, double* ms_host, uint64_t* calls_host,
+                                         int reset) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  require(layer >= 0 && layer < (int)net->layers.size(), "layer index out of range");
+  net->prof_collect();
+  for (int p = 0; p < KL_NPHASES; ++p) {
+    const size_t i = (size_t)layer * KL_NPHASES + p;
+    if (ms_host) ms_host[p] = net->prof_ms[i];
+    if (calls_host) calls_host[p] = net->prof_calls[i];
+    if (reset) {
+      net->prof_ms[i] = 0.0;
+      net->prof_calls[i] = 0;
+    }
+  }
+  KL_API_END
+}
+extern "C" kl_status kl_launch_count(uint64_t* count_host) {
+  if (!count_host) return KL_EINVAL;
+  *count_host = g_launches.load();
+  return KL_OK;
+}
+
+// ===========================================================================
+// Neuron sharding over NCCL: not available in this build configuration.
+// ===========================================================================
+extern "C" int kl_dist_unique_id_size(void) { return 128; }
+extern "C" kl_status kl_dist_get_unique_id(void* id_host) {
+  (void)id_host;
+  return KL_EUNSUPPORTED;
+}
+extern "C" kl_status kl_net_create_sharded(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init* init,
+                                           const void* unique_id, int rank, int nranks, kl_net_t* out) {
+  (void)cfg;
+  (void)init;
+  (void)unique_id;
+  (void)rank;
+  (void)nranks;
+  if (out) *out = nullptr;
+  if (ctx) ctx->last_error = "sharded networks are not built yet";
+  return KL_EUNSUPPORTED;
+}

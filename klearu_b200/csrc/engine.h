@@ -1,0 +1,216 @@
+// engine.h -- internal interfaces between the C-ABI layer (api.cu) and the
+// kernel translation units of the klearu B200 engine.
+#pragma once
+
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace kl {
+
+// Process-wide count of kernels launched by this library (defined in api.cu).
+void count_launch(unsigned n = 1);
+
+// ---------------------------------------------------------------------------
+// Hash families on the device.
+// ---------------------------------------------------------------------------
+struct DevHash {
+  int kind = 0, d = 0, k = 0, L = 0, w = 0, bpw = 0, bin_size = 0;
+  int LK = 0;           // L*K projections (SIMHASH / SRP)
+  int dpad = 0;         // row pitch of `planes` (bytes, multiple of 16)
+  int lkpad = 0;        // row pitch of `planesT` (bytes, multiple of 16)
+  int8_t* planes = nullptr;     // [LK][dpad]  projection rows (SIMHASH, SRP as dense ternary)
+  int8_t* planesT = nullptr;    // [d][lkpad]  transposed, for sparse inputs
+  uint32_t* windows = nullptr;  // [L][K][w]   (WTA, DWTA)
+  uint8_t* fallback = nullptr;  // [L][K]      DWTA sparse fallback position
+  uint32_t* perms = nullptr;    // [L][d]      (MINHASH)
+};
+
+// Dense input: element (i, j) of row i at X[i*ld_row + j*ld_elem], as f32 or bf16.
+struct DenseIn {
+  const void* X;
+  int dtype;
+  int64_t ld_row, ld_elem;
+  int n;
+};
+// CSR input with sorted unique column indices.
+struct SparseIn {
+  const int32_t* rowptr;
+  const uint32_t* idx;
+  const float* val;
+  int n;
+};
+// Hash outputs (each nullable): codes[i*L+t], min_abs[i*L+t] (SIMHASH/SRP),
+// bkt[t*bkt_ld + i] = code & nb_mask (bucket index, 16 bits).
+struct HashOut {
+  uint64_t* codes = nullptr;
+  float* min_abs = nullptr;
+  uint16_t* bkt = nullptr;
+  int64_t bkt_ld = 0;
+  uint32_t nb_mask = 0;
+};
+
+void launch_hash_dense(const DevHash& h, const DenseIn& in, const HashOut& out, cudaStream_t st);
+void launch_hash_sparse(const DevHash& h, const SparseIn& in, const HashOut& out, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Bucket tables: L x nb buckets of `cap` ids each.
+// ---------------------------------------------------------------------------
+struct DevTables {
+  int L = 0, nb = 0, cap = 0, type = 0;
+  uint32_t* ids = nullptr;  // [L][nb][cap]
+  uint32_t* len = nullptr;  // [L][nb]
+  uint64_t* cnt = nullptr;  // [L][nb] total insertions (reservoir)
+};
+
+// Scratch for a batched insert of up to `n` items.
+struct InsertScratch {
+  uint32_t* chunk_cnt = nullptr;  // [L][nchunks][nb]
+  uint32_t* total = nullptr;      // [L][nb]
+  uint32_t* base = nullptr;       // [L][nb] first slot of the new items (FIFO)
+  uint32_t* skip = nullptr;       // [L][nb] new items dropped at the front (FIFO)
+  unsigned long long* temp = nullptr;  // [L][nb][cap] packed (rank, id) (reservoir)
+};
+constexpr int INSERT_CHUNK = 1024;
+size_t insert_scratch_bytes(const DevTables& T, int n);
+void carve_insert_scratch(const DevTables& T, int n, void* base, InsertScratch* s);
+
+// n sequential inserts: item i has id ids[i] (ids == nullptr: id = i) and
+// bucket bkt[t*bkt_ld + i] in table t.
+void launch_tables_insert(const DevTables& T, const uint32_t* ids, const uint16_t* bkt,
+                          int64_t bkt_ld, int n, const InsertScratch& s, int* err,
+                          cudaStream_t st);
+void launch_tables_clear(const DevTables& T, cudaStream_t st);
+void launch_tables_remove(const DevTables& T, const uint32_t* ids, int n, cudaStream_t st);
+void launch_tables_remove_hashed(const DevTables& T, const uint32_t* ids, const uint16_t* bkt,
+                                 int64_t bkt_ld, int n, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Probe: per query the union of its L buckets with per-id counts, sorted by
+// id, then the sampling strategy, the empty-set fallback and retain(id < N).
+// ---------------------------------------------------------------------------
+struct ProbeArgs {
+  DevTables T;
+  const uint16_t* bkt = nullptr;  // bucket of query s in table t: bkt[t*bkt_ld + s]
+  int64_t bkt_ld = 0;
+  int nq = 0;
+  int N = 0;          // neuron count; 0 = plain index query (no selection)
+  int sampling = KL_SAMPLING_VANILLA, top_k = 0, threshold = 0;
+  int id_bits = 32;   // ids are < 2^id_bits
+  uint32_t* out_ids = nullptr;
+  uint32_t* out_counts = nullptr;  // nullable
+  int out_stride = 0;              // capacity per query
+  int32_t* out_n = nullptr;        // [nq] result sizes
+  int* err = nullptr;
+  unsigned long long* stat_active = nullptr;  // nullable: += sum of sizes
+  int maxm = 0;       // set by launch_probe
+};
+int probe_max_items();  // largest L*cap the probe kernel holds in shared memory
+void launch_probe(const ProbeArgs& a, cudaStream_t st);
+
+// Exclusive scan of n int32 counts into offsets[0..n] (offsets[n] = total).
+size_t scan_scratch_bytes(int n);
+void launch_scan(const int32_t* counts, int32_t* offsets, int n, void* scratch, cudaStream_t st);
+// Compact per-query padded results into CSR (capacity-bounded).
+void launch_compact(const uint32_t* ids, const uint32_t* counts, int stride, const int32_t* offs,
+                    int nq, uint32_t* out_ids, uint32_t* out_counts, int32_t capacity,
+                    int32_t* overflow, int* err, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Layer kernels (network/layer.rs, network/net.rs, optim/*.rs).
+// ---------------------------------------------------------------------------
+// Optimizer constants for one step, computed on the host exactly as the
+// reference does in f32 (adam.rs:38-55: t = max(step,1), powi via
+// square-and-multiply).
+struct OptStep {
+  int opt;           // KL_OPT_*
+  float lr, b1, b2, eps, omb1, omb2, c1, c2, mom;
+};
+
+// Active lists of one layer for a batch: ids[s*stride + a], a < cnt[s].
+struct ActiveSet {
+  uint32_t* ids;
+  int32_t* cnt;
+  int stride;
+  float* pre;
+  float* post;
+  float* lg;
+};
+
+// Forward of a feature-major layer (W[d][ldw], neuron j of feature f at
+// W[f*ldw + j]) over CSR input rows.  Writes pre/post and, if h != nullptr,
+// the dense activation rows h[s*ldh + j] (h must be zeroed).
+void launch_fm_forward(const void* W, int wdtype, int ldw, int d, const float* bias, int act,
+                       SparseIn in, ActiveSet A, float* h, int ldh, int* err, cudaStream_t st);
+
+// Row-major layer (W[N][ldw]) over dense inputs X[s*ldx + k], k < d.
+enum RmMode { RM_FWD = 0, RM_FUSED = 1, RM_DX = 2 };
+constexpr int RM_RPB = 256;  // active rows per block
+struct RmArgs {
+  const void* W;
+  int wdtype, ldw, d;
+  const float* bias;
+  int act;
+  const float* X;
+  int ldx;
+  ActiveSet A;
+  float* h;           // FWD: dense output rows (nullable)
+  int ldh;
+  float* dxpart;      // FUSED/DX: [B][nchunk][ldx]
+  int nchunk;
+  const int32_t* lab_ptr;  // FUSED: label CSR (absolute offsets) and per-label activation
+  const uint32_t* labels;
+  float* labprob;
+  int* err;
+};
+void launch_rm_forward(const RmArgs& a, int nq, int mode, cudaStream_t st);
+// dX[s][k] = sum over chunks of dxpart (chunk order).
+void launch_reduce_dx(const float* dxpart, int nchunk, int ld, int d, const int32_t* cnt,
+                      float* dx, int nq, cudaStream_t st);
+// Softmax over each sample's active set (layer.rs:286-308); with labels, also
+// the loss-gradient Jacobian product (layer.rs:141-176) into A.lg.
+void launch_softmax(ActiveSet A, float* h, int ldh, const int32_t* lab_ptr,
+                    const uint32_t* labels, float* labprob, int nq, cudaStream_t st);
+// lg[s][a] = grad[s*ldg + id] * act'(pre, post) (layer.rs:177-193); softmax via
+// the Jacobian.  If lgd != nullptr also the dense rows lgd[s*ldl + id] (zeroed
+// by the caller) and the touched-neuron bitmask.
+void launch_local_grads(ActiveSet A, int act, const float* grad, int ldg, float* lgd, int ldl,
+                        uint32_t* touched_mask, int nq, cudaStream_t st);
+// Per-sample loss (net.rs:180-199) from label activations, summed in sample
+// order into *accum.
+void launch_loss(const int32_t* lab_ptr, const float* labprob, int nq, float* accum,
+                 cudaStream_t st);
+
+// Row-major gradient + optimizer: rows touched by any active (s, a).
+struct SegScratch {
+  uint32_t* hist;     // [rows] zero between uses
+  uint32_t* cur;      // [rows]
+  uint32_t* touched;  // [rows]
+  uint32_t* ctr;      // [2]: touched count, entry total (zeroed per use)
+  uint32_t* ent_s;    // [entries]
+  float* ent_v;       // [entries]
+};
+void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
+                      float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
+                      SegScratch S, const OptStep& o, unsigned long long* stat_touched,
+                      cudaStream_t st);
+// Feature-major gradient + optimizer over ALL features of the touched neurons
+// (Adam decays every element of an active row, adam.rs:57-68).
+void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
+                      float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
+                      const uint32_t* touched_mask, SegScratch S, const OptStep& o,
+                      unsigned long long* stat_touched, cudaStream_t st);
+
+// Predict top-k over the final layer (net.rs:159-173): inactive neurons
+// score 0; order by score descending, ties by lower id.
+void launch_topk(ActiveSet A, int N, int k, uint32_t* top_ids, float* top_scores, int nq,
+                 cudaStream_t st);
+
+// Bit-exact f32/bf16 conversions of whole matrices (reference rows [n][d] <->
+// device storage, optionally transposed for feature-major layers).
+void launch_w_to_f32(const void* src, int wdtype, int64_t ld_src, bool transpose, float* dst,
+                     int64_t n_rows, int d, cudaStream_t st);
+void launch_f32_to_w(const float* src, int64_t n_rows, int d, int64_t ld_src, void* dst,
+                     int wdtype, int64_t ld_dst, bool transpose, cudaStream_t st);
+
+}  // namespace kl

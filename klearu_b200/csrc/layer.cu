@@ -1,0 +1,926 @@
+// layer.cu -- SLIDE layer kernels: active-row forward (gather + sequential f32
+// dot), fused loss gradient and input gradient, softmax, and the sort-free
+// segmented gradient reduction fused with lazy Adam / SGD.
+//
+// Reference (crates/klearu-core/src):
+//  * Layer::forward (network/layer.rs:65-120), Neuron::forward
+//    (network/neuron.rs:47-62): pre = sequential f32 sum of w*x, then + bias.
+//    The kernels keep that order and use non-contracted __fmul_rn/__fadd_rn,
+//    so pre-activations are bit-identical to the reference's.
+//  * compute_loss / compute_loss_gradient (network/net.rs:180-230).
+//  * Layer::backward (network/layer.rs:124-225): local gradients, the input
+//    gradient from the rows BEFORE their update, per-row optimizer update.
+//  * Adam::update (optim/adam.rs:27-76), Sgd::update (optim/sgd.rs:17-58):
+//    evaluated with the same f32 operation sequence (IEEE div/sqrt, no FMA).
+//  * Bf16Weights::update_from_f32 (klearu-accel/src/bf16/mod.rs:85-88):
+//    bf16 rows are updated as bf16_rne(f32(w) + delta).
+#include "engine.h"
+
+namespace kl {
+namespace {
+
+template <class W>
+__device__ __forceinline__ float wload(const void* base, int64_t off) {
+  return to_f(static_cast<const W*>(base)[off]);
+}
+
+__device__ __forceinline__ float block_reduce_max_f(float v, float* tmp) {
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
+  if (l == 0) tmp[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    float x = l < nw ? tmp[l] : __int_as_float(0xff800000);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(FULL, x, o));
+    if (l == 0) tmp[32] = x;
+  }
+  __syncthreads();
+  float r = tmp[32];
+  __syncthreads();
+  return r;
+}
+__device__ __forceinline__ float block_reduce_sum_f(float v, float* tmp) {
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  v = warp_sum_f(v);
+  if (l == 0) tmp[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    float x = l < nw ? tmp[l] : 0.0f;
+    x = warp_sum_f(x);
+    if (l == 0) tmp[32] = x;
+  }
+  __syncthreads();
+  float r = tmp[32];
+  __syncthreads();
+  return r;
+}
+
+// Optimizer step on one element (adam.rs:57-68 / sgd.rs:38-42).
+__device__ __forceinline__ void opt_apply(float& w, float& m, float& v, float g, const OptStep& o) {
+  if (o.opt == KL_OPT_ADAM) {
+    m = __fadd_rn(__fmul_rn(o.b1, m), __fmul_rn(o.omb1, g));
+    v = __fadd_rn(__fmul_rn(o.b2, v), __fmul_rn(__fmul_rn(o.omb2, g), g));
+    const float mh = __fdiv_rn(m, o.c1);
+    const float vh = __fdiv_rn(v, o.c2);
+    const float q = __fdiv_rn(__fmul_rn(o.lr, mh), __fadd_rn(__fsqrt_rn(vh), o.eps));
+    w = __fadd_rn(w, -q);
+  } else {
+    const float vv = __fsub_rn(__fmul_rn(o.mom, m), __fmul_rn(o.lr, g));
+    m = vv;
+    w = __fadd_rn(w, vv);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Feature-major forward over CSR rows: block per sample, thread per active
+// neuron (<= 1024 actives: up to 8 per thread).
+// ---------------------------------------------------------------------------
+template <class W>
+__global__ void __launch_bounds__(128) fm_forward_kernel(const void* Wm, int ldw, int d,
+                                                         const float* bias, int act, SparseIn in,
+                                                         ActiveSet A, float* h, int ldh, int* err) {
+  constexpr int NT = 128, MAXJ = 8, CH = 256;
+  __shared__ uint32_t sidx[CH];
+  __shared__ float sval[CH];
+  const int s = blockIdx.x;
+  const int na = min(A.cnt[s], NT * MAXJ);
+  const uint32_t* ids = A.ids + (int64_t)s * A.stride;
+  float acc[MAXJ];
+  uint32_t myid[MAXJ];
+#pragma unroll
+  for (int j = 0; j < MAXJ; ++j) {
+    const int a = threadIdx.x + j * NT;
+    myid[j] = a < na ? ids[a] : 0u;
+    acc[j] = 0.0f;
+  }
+  const int beg = in.rowptr[s], end = in.rowptr[s + 1];
+  for (int c0 = beg; c0 < end; c0 += CH) {
+    const int m = min(CH, end - c0);
+    for (int e = threadIdx.x; e < m; e += NT) {
+      uint32_t col = in.idx[c0 + e];
+      if (col >= (uint32_t)d) {
+        atomicOr(err, DERR_BOUNDS);
+        col = 0xffffffffu;
+      }
+      sidx[e] = col;
+      sval[e] = in.val[c0 + e];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < MAXJ; ++j) {
+      const int a = threadIdx.x + j * NT;
+      if (a < na) {
+        float x = acc[j];
+        for (int e = 0; e < m; ++e) {
+          const uint32_t col = sidx[e];
+          if (col == 0xffffffffu) continue;
+          x = __fadd_rn(x, __fmul_rn(wload<W>(Wm, (int64_t)col * ldw + myid[j]), sval[e]));
+        }
+        acc[j] = x;
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < MAXJ; ++j) {
+    const int a = threadIdx.x + j * NT;
+    if (a < na) {
+      const float pre = __fadd_rn(acc[j], bias[myid[j]]);
+      const float post = act == KL_ACT_SOFTMAX ? pre : act_apply(pre, act);
+      A.pre[(int64_t)s * A.stride + a] = pre;
+      A.post[(int64_t)s * A.stride + a] = post;
+      if (h && act != KL_ACT_SOFTMAX) h[(int64_t)s * ldh + myid[j]] = post;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row-major active-row kernel.  Block = 8 warps x 32 active rows; grid =
+// (row chunks, samples).  Each warp stages its 32 gathered rows, one
+// TILEB-byte column tile at a time, into shared memory with 16-byte cp.async
+// (coalesced: consecutive lanes fetch consecutive 16-byte pieces of a row).
+// Lane r then computes row r's dot product sequentially from shared memory
+// (bit-exact reference order); in FUSED mode it also forms the loss gradient
+// and the warp accumulates dX = sum_r lg_r * W_r from the same staged tile,
+// so every row is read from HBM once for forward + input gradient.
+// ---------------------------------------------------------------------------
+constexpr int RM_NWB = RM_RPB / 32;
+
+template <class W, int TILEB>
+__device__ __forceinline__ void rm_load_tile(unsigned char* mt, const unsigned char* Wb,
+                                             int64_t rowbytes, int tI, uint32_t myid, int nw) {
+  constexpr int CPR = TILEB / 16;
+  constexpr int PITCH = TILEB + 16;
+  const int l = threadIdx.x & 31;
+#pragma unroll 4
+  for (int c = l; c < 32 * CPR; c += 32) {
+    const int r = c / CPR, q = c % CPR;
+    const uint32_t rid = __shfl_sync(FULL, myid, r);
+    const int64_t boff = (int64_t)tI * TILEB + q * 16;
+    if (r < nw && boff < rowbytes) cp_async16(mt + r * PITCH + q * 16, Wb + (int64_t)rid * rowbytes + boff);
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncwarp();
+}
+
+template <class W, int MODE, int TILEB>
+__global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
+  constexpr int EPT = TILEB / (int)sizeof(W);
+  constexpr int PITCH = TILEB + 16;
+  constexpr int CPL = EPT / 32;
+  extern __shared__ __align__(16) unsigned char dyn[];
+  const int xs_bytes = (int)round_up((int64_t)a.ldx * 4, 16);
+  float* xs = reinterpret_cast<float*>(dyn);
+  unsigned char* tiles = dyn + xs_bytes;
+  float* wpart = reinterpret_cast<float*>(tiles + RM_NWB * 32 * PITCH);
+  const int s = blockIdx.y, chunk = blockIdx.x;
+  const int na_tot = a.A.cnt[s];
+  if (chunk * RM_RPB >= na_tot) return;
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int a0 = chunk * RM_RPB + w * 32;
+  const int nw = max(0, min(32, na_tot - a0));
+  if (MODE != RM_DX)
+    for (int k = threadIdx.x; k < a.ldx; k += RM_RPB) xs[k] = a.X[(int64_t)s * a.ldx + k];
+  const int64_t arow = (int64_t)s * a.A.stride + a0 + l;
+  const bool has = l < nw;
+  const uint32_t myid = has ? a.A.ids[arow] : 0u;
+  unsigned char* mt = tiles + w * 32 * PITCH;
+  const int64_t rowbytes = (int64_t)a.ldw * sizeof(W);
+  const int ntiles = (int)ceil_div(rowbytes, TILEB);
+  const unsigned char* Wb = static_cast<const unsigned char*>(a.W);
+  __syncthreads();
+  float lgv = 0.0f;
+  if (MODE != RM_DX) {
+    float acc = 0.0f;
+    for (int tI = 0; tI < ntiles; ++tI) {
+      rm_load_tile<W, TILEB>(mt, Wb, rowbytes, tI, myid, nw);
+      if (has) {
+        const int k0 = tI * EPT;
+        const int kmax = min(EPT, a.d - k0);
+        const W* rowp = reinterpret_cast<const W*>(mt + l * PITCH);
+        constexpr int VE = 16 / (int)sizeof(W);
+        for (int kb = 0; kb < kmax; kb += VE) {
+          uint4 raw = *reinterpret_cast<const uint4*>(rowp + kb);
+          const W* e = reinterpret_cast<const W*>(&raw);
+#pragma unroll
+          for (int u = 0; u < VE; ++u)
+            if (kb + u < kmax) acc = __fadd_rn(acc, __fmul_rn(to_f(e[u]), xs[k0 + kb + u]));
+        }
+      }
+      __syncwarp();
+    }
+    if (has) {
+      const float pre = __fadd_rn(acc, a.bias[myid]);
+      const float post = a.act == KL_ACT_SOFTMAX ? pre : act_apply(pre, a.act);
+      a.A.pre[arow] = pre;
+      a.A.post[arow] = post;
+      if (MODE == RM_FWD) {
+        if (a.h && a.act != KL_ACT_SOFTMAX) a.h[(int64_t)s * a.ldh + myid] = post;
+      } else {
+        // compute_loss_gradient (net.rs:205-230) times the activation derivative
+        const int lb = a.lab_ptr[s], le = a.lab_ptr[s + 1];
+        float g = post;
+        if (le == lb) {
+          g = 0.0f;
+        } else {
+          const float lw = __fdiv_rn(1.0f, (float)(le - lb));
+          for (int j = lb; j < le; ++j) {
+            if (a.labels[j] == myid) {
+              g = __fsub_rn(g, lw);
+              a.labprob[j] = post;
+            }
+          }
+        }
+        lgv = __fmul_rn(g, act_deriv(pre, post, a.act));
+        a.A.lg[arow] = lgv;
+      }
+    }
+  } else if (has) {
+    lgv = a.A.lg[arow];
+  }
+  if constexpr (MODE == RM_FWD) return;
+  // input gradient of this block's rows (old weights, layer.rs:206-209)
+  for (int tI = 0; tI < ntiles; ++tI) {
+    if (MODE == RM_DX || ntiles > 1) rm_load_tile<W, TILEB>(mt, Wb, rowbytes, tI, myid, nw);
+    float part[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) part[c] = 0.0f;
+    const int kvalid = a.d - tI * EPT;
+    for (int r = 0; r < nw; ++r) {
+      const float lr = __shfl_sync(FULL, lgv, r);
+      const W* rowp = reinterpret_cast<const W*>(mt + r * PITCH);
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int col = l * CPL + c;
+        if (col < kvalid) part[c] = fmaf(lr, to_f(rowp[col]), part[c]);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) wpart[w * EPT + l * CPL + c] = part[c];
+    __syncthreads();
+    for (int col = threadIdx.x; col < EPT; col += RM_RPB) {
+      const int kg = tI * EPT + col;
+      if (kg < a.ldx) {
+        float v = 0.0f;
+        for (int ww = 0; ww < RM_NWB; ++ww) v += wpart[ww * EPT + col];
+        a.dxpart[((int64_t)s * a.nchunk + chunk) * a.ldx + kg] = v;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void reduce_dx_kernel(const float* dxpart, int nchunk, int ld, int d,
+                                 const int32_t* cnt, float* dx) {
+  const int s = blockIdx.x;
+  const int nch = (int)ceil_div(cnt[s], RM_RPB);
+  for (int k = threadIdx.x; k < ld; k += blockDim.x) {
+    float v = 0.0f;
+    if (k < d)
+      for (int c = 0; c < nch; ++c) v += dxpart[((int64_t)s * nchunk + c) * ld + k];
+    dx[(int64_t)s * ld + k] = v;
+  }
+}
+
+// Softmax over the active set (layer.rs:286-308) and, with labels, the loss
+// gradient through the softmax Jacobian (layer.rs:141-176):
+// lg_i = sum_j g_j s_j (delta_ij - s_i) = s_i g_i - s_i * sum_j g_j s_j.
+__global__ void softmax_kernel(ActiveSet A, float* h, int ldh, const int32_t* lab_ptr,
+                               const uint32_t* labels, float* labprob) {
+  __shared__ float tmp[40];
+  const int s = blockIdx.x;
+  const int na = A.cnt[s];
+  const int64_t o = (int64_t)s * A.stride;
+  float mx = __int_as_float(0xff800000);
+  for (int a = threadIdx.x; a < na; a += blockDim.x) mx = fmaxf(mx, A.pre[o + a]);
+  mx = block_reduce_max_f(mx, tmp);
+  float sum = 0.0f;
+  for (int a = threadIdx.x; a < na; a += blockDim.x) {
+    const float e = expf(__fsub_rn(A.pre[o + a], mx));
+    A.post[o + a] = e;
+    sum += e;
+  }
+  sum = block_reduce_sum_f(sum, tmp);
+  float S = 0.0f;
+  for (int a = threadIdx.x; a < na; a += blockDim.x) {
+    const float sv = sum > 0.0f ? __fdiv_rn(A.post[o + a], sum) : __fdiv_rn(1.0f, (float)na);
+    A.post[o + a] = sv;
+    const uint32_t id = A.ids[o + a];
+    if (h) h[(int64_t)s * ldh + id] = sv;
+    if (lab_ptr) {
+      const int lb = lab_ptr[s], le = lab_ptr[s + 1];
+      float g = sv;
+      if (le == lb) {
+        g = 0.0f;
+      } else {
+        const float lw = __fdiv_rn(1.0f, (float)(le - lb));
+        for (int j = lb; j < le; ++j)
+          if (labels[j] == id) {
+            g = __fsub_rn(g, lw);
+            labprob[j] = sv;
+          }
+      }
+      A.lg[o + a] = g;  // temporarily the output gradient
+      S += g * sv;
+    }
+  }
+  if (!lab_ptr) return;
+  S = block_reduce_sum_f(S, tmp);
+  for (int a = threadIdx.x; a < na; a += blockDim.x) {
+    const float sv = A.post[o + a], g = A.lg[o + a];
+    A.lg[o + a] = __fsub_rn(__fmul_rn(sv, g), __fmul_rn(sv, S));
+  }
+}
+
+// Local gradients of a non-output layer (layer.rs:177-193).
+__global__ void local_grads_kernel(ActiveSet A, int act, const float* grad, int ldg, float* lgd,
+                                   int ldl, uint32_t* touched_mask) {
+  const int s = blockIdx.y;
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= A.cnt[s]) return;
+  const int64_t o = (int64_t)s * A.stride + a;
+  const uint32_t id = A.ids[o];
+  const float lg = __fmul_rn(grad[(int64_t)s * ldg + id], act_deriv(A.pre[o], A.post[o], act));
+  A.lg[o] = lg;
+  if (lgd) {
+    lgd[(int64_t)s * ldl + id] = lg;
+    atomicOr(&touched_mask[id >> 5], 1u << (id & 31));
+  }
+}
+// Softmax hidden layer: lg_i = s_i go_i - s_i sum_j go_j s_j.
+__global__ void local_grads_softmax_kernel(ActiveSet A, const float* grad, int ldg, float* lgd,
+                                           int ldl, uint32_t* touched_mask) {
+  __shared__ float tmp[40];
+  const int s = blockIdx.x;
+  const int na = A.cnt[s];
+  const int64_t o = (int64_t)s * A.stride;
+  float S = 0.0f;
+  for (int a = threadIdx.x; a < na; a += blockDim.x)
+    S += grad[(int64_t)s * ldg + A.ids[o + a]] * A.post[o + a];
+  S = block_reduce_sum_f(S, tmp);
+  for (int a = threadIdx.x; a < na; a += blockDim.x) {
+    const uint32_t id = A.ids[o + a];
+    const float sv = A.post[o + a];
+    const float lg = __fsub_rn(__fmul_rn(sv, grad[(int64_t)s * ldg + id]), __fmul_rn(sv, S));
+    A.lg[o + a] = lg;
+    if (lgd) {
+      lgd[(int64_t)s * ldl + id] = lg;
+      atomicOr(&touched_mask[id >> 5], 1u << (id & 31));
+    }
+  }
+}
+
+// compute_loss (net.rs:180-199): per sample, then summed in sample order.
+__global__ void loss_kernel(const int32_t* lab_ptr, const float* labprob, int nq, float* accum) {
+  extern __shared__ float ls[];
+  const float eps = 1e-7f;
+  for (int s = threadIdx.x; s < nq; s += blockDim.x) {
+    const int lb = lab_ptr[s], le = lab_ptr[s + 1];
+    float loss = 0.0f;
+    for (int j = lb; j < le; ++j) loss = __fsub_rn(loss, logf(fmaxf(labprob[j], eps)));
+    ls[s] = le > lb ? __fdiv_rn(loss, (float)(le - lb)) : 0.0f;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float acc = *accum;
+    for (int s = 0; s < nq; ++s) acc = __fadd_rn(acc, ls[s]);
+    *accum = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Segmented gradient reduction without float atomics.  (1) every (sample,
+// row) pair bumps a per-row counter; the first bump appends the row to the
+// touched list; (2) each touched row reserves a contiguous segment;
+// (3) pairs scatter (sample, coefficient) into their row's segment;
+// (4) one warp per touched row rebuilds the segment as a per-sample bitmask
+// in shared memory, so the gradient is summed in ascending sample order --
+// deterministic and identical to the batched oracle -- and applies the
+// optimizer to the row in the same pass (the gradient never touches HBM).
+// ---------------------------------------------------------------------------
+__global__ void rm_touch_kernel(ActiveSet A, uint32_t* hist, uint32_t* touched, uint32_t* ctr) {
+  const int s = blockIdx.y;
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  const bool valid = a < A.cnt[s];
+  uint32_t id = 0, old = 1;
+  if (valid) {
+    id = A.ids[(int64_t)s * A.stride + a];
+    old = atomicAdd(&hist[id], 1u);
+  }
+  const int pos = warp_append(valid && old == 0, &ctr[0]);
+  if (pos >= 0) touched[pos] = id;
+}
+__global__ void fm_touch_kernel(SparseIn in, uint32_t* hist, uint32_t* touched, uint32_t* ctr, int d) {
+  const int s = blockIdx.x;
+  const int beg = in.rowptr[s], end = in.rowptr[s + 1];
+  for (int base = beg; base < end; base += blockDim.x) {
+    const int e = base + threadIdx.x;
+    bool valid = e < end;
+    uint32_t f = 0, old = 1;
+    if (valid) {
+      f = in.idx[e];
+      valid = f < (uint32_t)d;
+      if (valid) old = atomicAdd(&hist[f], 1u);
+    }
+    const int pos = warp_append(valid && old == 0, &ctr[0]);
+    if (pos >= 0) touched[pos] = f;
+  }
+}
+__global__ void seg_alloc_kernel(const uint32_t* hist, const uint32_t* touched, uint32_t* cur,
+                                 uint32_t* ctr, int maxn) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  const int n = (int)ctr[0];
+  if (blockIdx.x * blockDim.x >= n) return;  // whole block idle
+  const bool valid = k < n && k < maxn;
+  const uint32_t row = valid ? touched[k] : 0u;
+  const int len = valid ? (int)hist[row] : 0;
+  const int inc = warp_incl_scan(len);
+  const int wtot = __shfl_sync(FULL, inc, 31);
+  uint32_t base = 0;
+  if ((threadIdx.x & 31) == 31) base = atomicAdd(&ctr[1], (uint32_t)wtot);
+  base = __shfl_sync(FULL, base, 31);
+  if (valid) cur[row] = base + inc - len;
+}
+__global__ void rm_scatter_kernel(ActiveSet A, uint32_t* cur, uint32_t* ent_s, float* ent_v) {
+  const int s = blockIdx.y;
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= A.cnt[s]) return;
+  const int64_t o = (int64_t)s * A.stride + a;
+  const uint32_t pos = atomicAdd(&cur[A.ids[o]], 1u);
+  ent_s[pos] = (uint32_t)s;
+  ent_v[pos] = A.lg[o];
+}
+__global__ void fm_scatter_kernel(SparseIn in, uint32_t* cur, uint32_t* ent_s, float* ent_v, int d) {
+  const int s = blockIdx.x;
+  for (int e = in.rowptr[s] + threadIdx.x; e < in.rowptr[s + 1]; e += blockDim.x) {
+    const uint32_t f = in.idx[e];
+    if (f >= (uint32_t)d) continue;
+    const uint32_t pos = atomicAdd(&cur[f], 1u);
+    ent_s[pos] = (uint32_t)s;
+    ent_v[pos] = in.val[e];
+  }
+}
+
+// Load one segment into the warp's (coefficient, sample-bitmask) buffers.
+__device__ __forceinline__ void seg_to_mask(const uint32_t* ent_s, const float* ent_v, uint32_t start,
+                                            uint32_t len, float* coef, uint32_t* mask) {
+  for (uint32_t e = threadIdx.x & 31; e < len; e += 32) {
+    const uint32_t s = ent_s[start + e];
+    coef[s] = ent_v[start + e];
+    atomicOr(&mask[s >> 5], 1u << (s & 31));
+  }
+  __syncwarp();
+}
+
+template <class W>
+__device__ __forceinline__ void load4(const void* Wm, int64_t off, float* w) {
+  if (sizeof(W) == 4) {
+    const float4 v = *reinterpret_cast<const float4*>(static_cast<const float*>(Wm) + off);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else {
+    const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(Wm) + off);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+    w[0] = to_f(e[0]); w[1] = to_f(e[1]); w[2] = to_f(e[2]); w[3] = to_f(e[3]);
+  }
+}
+template <class W>
+__device__ __forceinline__ void store4(void* Wm, int64_t off, const float* w) {
+  if (sizeof(W) == 4) {
+    *reinterpret_cast<float4*>(static_cast<float*>(Wm) + off) = make_float4(w[0], w[1], w[2], w[3]);
+  } else {
+    __nv_bfloat16 e[4] = {__float2bfloat16_rn(w[0]), __float2bfloat16_rn(w[1]),
+                          __float2bfloat16_rn(w[2]), __float2bfloat16_rn(w[3])};
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(Wm) + off) = *reinterpret_cast<uint2*>(e);
+  }
+}
+
+// Apply the optimizer to 4 consecutive elements; lanes with !upd[i] keep
+// their values (row padding, untouched neurons).
+template <class W>
+__device__ __forceinline__ void row_update4(void* Wm, float* m, float* v, int64_t off,
+                                            const float* g, const bool* upd, const OptStep& o) {
+  float w[4], mm[4], vv[4];
+  load4<W>(Wm, off, w);
+  const float4 m4 = *reinterpret_cast<const float4*>(m + off);
+  mm[0] = m4.x; mm[1] = m4.y; mm[2] = m4.z; mm[3] = m4.w;
+  float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (o.opt == KL_OPT_ADAM) v4 = *reinterpret_cast<const float4*>(v + off);
+  vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (upd[i]) opt_apply(w[i], mm[i], vv[i], g[i], o);
+  store4<W>(Wm, off, w);
+  *reinterpret_cast<float4*>(m + off) = make_float4(mm[0], mm[1], mm[2], mm[3]);
+  if (o.opt == KL_OPT_ADAM) *reinterpret_cast<float4*>(v + off) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+}
+
+__device__ __forceinline__ void bias_update(float* bias, float* mb, float* vb, uint32_t j, float gb,
+                                            const OptStep& o) {
+  float b = bias[j], m = mb[j], v = (o.opt == KL_OPT_ADAM) ? vb[j] : 0.0f;
+  opt_apply(b, m, v, gb, o);
+  bias[j] = b;
+  mb[j] = m;
+  if (o.opt == KL_OPT_ADAM) vb[j] = v;
+}
+
+constexpr int UPD_WARPS = 8;
+
+template <class W>
+__global__ void __launch_bounds__(UPD_WARPS * 32)
+    rm_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
+                     const float* X, int ldx, SegScratch S, int nwords, OptStep o,
+                     unsigned long long* stat_touched) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  uint32_t* mask = reinterpret_cast<uint32_t*>(dyn) + w * nwords;
+  float* coef = reinterpret_cast<float*>(dyn + (size_t)UPD_WARPS * nwords * 4) + (size_t)w * nwords * 32;
+  for (int i = l; i < nwords; i += 32) mask[i] = 0;
+  __syncwarp();
+  const int n = (int)S.ctr[0];
+  if (blockIdx.x == 0 && threadIdx.x == 0 && stat_touched) atomicAdd(stat_touched, (unsigned long long)n);
+  for (int k = blockIdx.x * UPD_WARPS + w; k < n; k += gridDim.x * UPD_WARPS) {
+    const uint32_t row = S.touched[k];
+    const uint32_t len = S.hist[row];
+    const uint32_t start = S.cur[row] - len;
+    seg_to_mask(S.ent_s, S.ent_v, start, len, coef, mask);
+    float gb = 0.0f;
+    for (int g0 = 0; g0 < d; g0 += 128) {
+      const int c = g0 + l * 4;
+      float g[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int wi = 0; wi < nwords; ++wi) {
+        uint32_t mw = mask[wi];
+        while (mw) {
+          const int b = __ffs(mw) - 1;
+          mw &= mw - 1;
+          const int s = wi * 32 + b;
+          const float cf = coef[s];
+          if (g0 == 0) gb = __fadd_rn(gb, cf);
+          if (c < d) {
+            const float4 xv = *reinterpret_cast<const float4*>(X + (int64_t)s * ldx + c);
+            g[0] = __fadd_rn(g[0], __fmul_rn(cf, xv.x));
+            g[1] = __fadd_rn(g[1], __fmul_rn(cf, xv.y));
+            g[2] = __fadd_rn(g[2], __fmul_rn(cf, xv.z));
+            g[3] = __fadd_rn(g[3], __fmul_rn(cf, xv.w));
+          }
+        }
+      }
+      if (c < d) {
+        const bool upd[4] = {c < d, c + 1 < d, c + 2 < d, c + 3 < d};
+        row_update4<W>(Wm, m, v, (int64_t)row * ldw + c, g, upd, o);
+      }
+    }
+    if (l == 0) {
+      bias_update(bias, mb, vb, row, gb, o);
+      S.hist[row] = 0;
+    }
+    for (int i = l; i < nwords; i += 32) mask[i] = 0;
+    __syncwarp();
+  }
+}
+
+// Feature-major update: warp per feature row f over ALL d features.  The
+// gradient of neuron j at feature f is sum over samples s containing f of
+// x_s[f] * lg_s[j] (ascending s); touched neurons are updated at every f.
+template <class W>
+__global__ void __launch_bounds__(UPD_WARPS * 32)
+    fm_update_kernel(void* Wm, int ldw, int d, int N, float* m, float* v, const float* lgd, int ldl,
+                     const uint32_t* tmask, SegScratch S, int nwords, OptStep o) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  uint32_t* mask = reinterpret_cast<uint32_t*>(dyn) + w * nwords;
+  float* coef = reinterpret_cast<float*>(dyn + (size_t)UPD_WARPS * nwords * 4) + (size_t)w * nwords * 32;
+  for (int i = l; i < nwords; i += 32) mask[i] = 0;
+  __syncwarp();
+  for (int64_t f = (int64_t)blockIdx.x * UPD_WARPS + w; f < d; f += (int64_t)gridDim.x * UPD_WARPS) {
+    const uint32_t len = S.hist[f];
+    if (len) seg_to_mask(S.ent_s, S.ent_v, S.cur[f] - len, len, coef, mask);
+    for (int g0 = 0; g0 < N; g0 += 128) {
+      const int c = g0 + l * 4;
+      if (c >= N) continue;
+      const uint32_t tw = tmask[c >> 5] >> (c & 31);
+      const bool upd[4] = {(tw & 1u) != 0, c + 1 < N && (tw & 2u), c + 2 < N && (tw & 4u),
+                           c + 3 < N && (tw & 8u)};
+      if (!(upd[0] | upd[1] | upd[2] | upd[3])) continue;
+      float g[4] = {0.f, 0.f, 0.f, 0.f};
+      if (len) {
+        for (int wi = 0; wi < nwords; ++wi) {
+          uint32_t mw = mask[wi];
+          while (mw) {
+            const int b = __ffs(mw) - 1;
+            mw &= mw - 1;
+            const int s = wi * 32 + b;
+            const float cf = coef[s];
+            const float4 lv = *reinterpret_cast<const float4*>(lgd + (int64_t)s * ldl + c);
+            g[0] = __fadd_rn(g[0], __fmul_rn(cf, lv.x));
+            g[1] = __fadd_rn(g[1], __fmul_rn(cf, lv.y));
+            g[2] = __fadd_rn(g[2], __fmul_rn(cf, lv.z));
+            g[3] = __fadd_rn(g[3], __fmul_rn(cf, lv.w));
+          }
+        }
+      }
+      row_update4<W>(Wm, m, v, f * ldw + c, g, upd, o);
+    }
+    if (len) {
+      if (l == 0) S.hist[f] = 0;
+      for (int i = l; i < nwords; i += 32) mask[i] = 0;
+      __syncwarp();
+    }
+  }
+}
+
+__global__ void fm_bias_kernel(float* bias, float* mb, float* vb, const float* lgd, int ldl, int nq,
+                               int N, const uint32_t* tmask, OptStep o,
+                               unsigned long long* stat_touched) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= N) return;
+  if (!((tmask[j >> 5] >> (j & 31)) & 1u)) return;
+  if (stat_touched) atomicAdd(stat_touched, 1ull);
+  float gb = 0.0f;
+  for (int s = 0; s < nq; ++s) gb = __fadd_rn(gb, lgd[(int64_t)s * ldl + j]);
+  bias_update(bias, mb, vb, (uint32_t)j, gb, o);
+}
+
+// Matrix conversion between reference f32 rows and device storage.
+template <class W>
+__global__ void f32_to_w_kernel(const float* src, int64_t n_rows, int d, int64_t ld_src, W* dst,
+                                int64_t ld_dst, bool transpose) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n_rows * d) return;
+  const int64_t r = g / d, c = g % d;
+  const W val = from_f<W>(src[r * ld_src + c]);
+  if (transpose) dst[c * ld_dst + r] = val;
+  else dst[r * ld_dst + c] = val;
+}
+
+template <class W>
+__global__ void w_to_f32_kernel(const W* src, int64_t ld_src, bool transpose, float* dst, int64_t n_rows,
+                                int d) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n_rows * d) return;
+  const int64_t r = g / d, c = g % d;
+  dst[g] = to_f(transpose ? src[c * ld_src + r] : src[r * ld_src + c]);
+}
+
+// Top-k of one sample: actives sorted by (score desc, id asc) with a bitonic
+// sort in shared memory; the score-0 tier merges active zeros with inactive
+// ids in id order.
+constexpr int TK_MAX = 4096;
+__global__ void __launch_bounds__(1024) topk_kernel(ActiveSet A, int N, int k, uint32_t* top_ids,
+                                                    float* top_scores) {
+  __shared__ float sc[TK_MAX];
+  __shared__ uint32_t id[TK_MAX];
+  const int s = blockIdx.x;
+  const int na = min(A.cnt[s], TK_MAX);
+  int P = 1;
+  while (P < na) P <<= 1;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    if (i < na) {
+      sc[i] = A.post[(int64_t)s * A.stride + i];
+      id[i] = A.ids[(int64_t)s * A.stride + i];
+    } else {
+      sc[i] = __int_as_float(0xff800000);
+      id[i] = 0xffffffffu;
+    }
+  }
+  __syncthreads();
+  // "a before b" if a.score > b.score or (== and a.id < b.id)
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const bool before_ji = sc[j] > sc[i] || (sc[j] == sc[i] && id[j] < id[i]);
+          if (before_ji == up) {
+            float t = sc[i]; sc[i] = sc[j]; sc[j] = t;
+            uint32_t u = id[i]; id[i] = id[j]; id[j] = u;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if (threadIdx.x != 0) return;
+  uint32_t* oi = top_ids + (int64_t)s * k;
+  float* os = top_scores ? top_scores + (int64_t)s * k : nullptr;
+  int o = 0, p = 0;
+  while (o < k && p < na && sc[p] > 0.0f) {
+    oi[o] = id[p];
+    if (os) os[o] = sc[p];
+    ++o; ++p;
+  }
+  // zero tier: ids (active with score 0, or inactive) ascending
+  const uint32_t* act_ids = A.ids + (int64_t)s * A.stride;  // sorted by id
+  int q = 0;
+  for (uint32_t cand = 0; o < k && cand < (uint32_t)N; ++cand) {
+    while (q < na && act_ids[q] < cand) ++q;
+    bool active = q < na && act_ids[q] == cand;
+    if (active) {
+      const float v = A.post[(int64_t)s * A.stride + q];
+      if (!(v == 0.0f)) continue;
+    }
+    oi[o] = cand;
+    if (os) os[o] = 0.0f;
+    ++o;
+  }
+  while (o < k && p < na) {
+    if (sc[p] < 0.0f) {
+      oi[o] = id[p];
+      if (os) os[o] = sc[p];
+      ++o;
+    }
+    ++p;
+  }
+}
+
+}  // namespace
+
+void launch_topk(ActiveSet A, int N, int k, uint32_t* top_ids, float* top_scores, int nq,
+                 cudaStream_t st) {
+  if (nq <= 0 || k <= 0) return;
+  topk_kernel<<<nq, 1024, 0, st>>>(A, N, k, top_ids, top_scores);
+  count_launch();
+}
+
+void launch_w_to_f32(const void* src, int wdtype, int64_t ld_src, bool transpose, float* dst,
+                     int64_t n_rows, int d, cudaStream_t st) {
+  const int64_t tot = n_rows * d;
+  if (tot <= 0) return;
+  const unsigned g = (unsigned)ceil_div(tot, 256);
+  if (wdtype == KL_DTYPE_BF16)
+    w_to_f32_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), ld_src,
+                                                       transpose, dst, n_rows, d);
+  else
+    w_to_f32_kernel<float><<<g, 256, 0, st>>>(static_cast<const float*>(src), ld_src, transpose, dst,
+                                              n_rows, d);
+  count_launch();
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+void launch_fm_forward(const void* W, int wdtype, int ldw, int d, const float* bias, int act,
+                       SparseIn in, ActiveSet A, float* h, int ldh, int* err, cudaStream_t st) {
+  if (in.n <= 0) return;
+  if (wdtype == KL_DTYPE_BF16)
+    fm_forward_kernel<__nv_bfloat16><<<in.n, 128, 0, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err);
+  else
+    fm_forward_kernel<float><<<in.n, 128, 0, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err);
+  count_launch();
+}
+
+template <class W, int MODE, int TILEB>
+static void rm_launch(const RmArgs& a, int nq, cudaStream_t st) {
+  constexpr int PITCH = TILEB + 16;
+  constexpr int EPT = TILEB / (int)sizeof(W);
+  const size_t sm = (size_t)round_up((int64_t)a.ldx * 4, 16) + (size_t)RM_NWB * 32 * PITCH +
+                    (size_t)RM_NWB * EPT * 4;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(rm_forward_kernel<W, MODE, TILEB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         200 * 1024);
+    attr = true;
+  }
+  dim3 grid(a.nchunk, nq);
+  rm_forward_kernel<W, MODE, TILEB><<<grid, RM_RPB, sm, st>>>(a);
+  count_launch();
+}
+template <class W, int MODE>
+static void rm_launch_t(const RmArgs& a, int nq, cudaStream_t st) {
+  if ((int64_t)a.ldw * (int64_t)sizeof(W) <= 256) rm_launch<W, MODE, 256>(a, nq, st);
+  else rm_launch<W, MODE, 512>(a, nq, st);
+}
+void launch_rm_forward(const RmArgs& a, int nq, int mode, cudaStream_t st) {
+  if (nq <= 0) return;
+  const bool bf = a.wdtype == KL_DTYPE_BF16;
+  switch (mode) {
+    case RM_FWD:
+      bf ? rm_launch_t<__nv_bfloat16, RM_FWD>(a, nq, st) : rm_launch_t<float, RM_FWD>(a, nq, st);
+      break;
+    case RM_FUSED:
+      bf ? rm_launch_t<__nv_bfloat16, RM_FUSED>(a, nq, st) : rm_launch_t<float, RM_FUSED>(a, nq, st);
+      break;
+    default:
+      bf ? rm_launch_t<__nv_bfloat16, RM_DX>(a, nq, st) : rm_launch_t<float, RM_DX>(a, nq, st);
+      break;
+  }
+}
+void launch_reduce_dx(const float* dxpart, int nchunk, int ld, int d, const int32_t* cnt, float* dx,
+                      int nq, cudaStream_t st) {
+  if (nq <= 0) return;
+  reduce_dx_kernel<<<nq, 256, 0, st>>>(dxpart, nchunk, ld, d, cnt, dx);
+  count_launch();
+}
+void launch_softmax(ActiveSet A, float* h, int ldh, const int32_t* lab_ptr, const uint32_t* labels,
+                    float* labprob, int nq, cudaStream_t st) {
+  if (nq <= 0) return;
+  softmax_kernel<<<nq, 256, 0, st>>>(A, h, ldh, lab_ptr, labels, labprob);
+  count_launch();
+}
+void launch_local_grads(ActiveSet A, int act, const float* grad, int ldg, float* lgd, int ldl,
+                        uint32_t* touched_mask, int nq, cudaStream_t st) {
+  if (nq <= 0) return;
+  if (act == KL_ACT_SOFTMAX) {
+    local_grads_softmax_kernel<<<nq, 256, 0, st>>>(A, grad, ldg, lgd, ldl, touched_mask);
+  count_launch();
+  } else {
+    dim3 grid((unsigned)ceil_div(A.stride, 128), nq);
+    local_grads_kernel<<<grid, 128, 0, st>>>(A, act, grad, ldg, lgd, ldl, touched_mask);
+  count_launch();
+  }
+}
+void launch_loss(const int32_t* lab_ptr, const float* labprob, int nq, float* accum, cudaStream_t st) {
+  if (nq <= 0) return;
+  loss_kernel<<<1, 1024, (size_t)nq * 4, st>>>(lab_ptr, labprob, nq, accum);
+  count_launch();
+}
+
+static int upd_grid() {
+  static int g = 0;
+  if (!g) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    g = sms * 8;
+  }
+  return g;
+}
+
+void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
+                      float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
+                      SegScratch S, const OptStep& o, unsigned long long* stat_touched,
+                      cudaStream_t st) {
+  if (nq <= 0) return;
+  dim3 g2((unsigned)ceil_div(A.stride, 256), nq);
+  rm_touch_kernel<<<g2, 256, 0, st>>>(A, S.hist, S.touched, S.ctr);
+  count_launch();
+  const int maxn = (int)std::min<int64_t>((int64_t)N, (int64_t)nq * A.stride);
+  seg_alloc_kernel<<<(unsigned)ceil_div(maxn, 256), 256, 0, st>>>(S.hist, S.touched, S.cur, S.ctr, maxn);
+  count_launch();
+  rm_scatter_kernel<<<g2, 256, 0, st>>>(A, S.cur, S.ent_s, S.ent_v);
+  count_launch();
+  const int nwords = (int)ceil_div(nq, 32);
+  const size_t sm = (size_t)UPD_WARPS * nwords * 4 * 33;
+  const int grid = (int)std::min<int64_t>(upd_grid(), ceil_div(maxn, UPD_WARPS));
+  if (wdtype == KL_DTYPE_BF16) {
+    cudaFuncSetAttribute(rm_update_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    rm_update_kernel<__nv_bfloat16><<<grid, UPD_WARPS * 32, sm, st>>>(
+        const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X, ldx, S, nwords, o, stat_touched);
+  count_launch();
+  } else {
+    cudaFuncSetAttribute(rm_update_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    rm_update_kernel<float><<<grid, UPD_WARPS * 32, sm, st>>>(
+        const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X, ldx, S, nwords, o, stat_touched);
+  count_launch();
+  }
+}
+
+void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
+                      float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
+                      const uint32_t* touched_mask, SegScratch S, const OptStep& o,
+                      unsigned long long* stat_touched, cudaStream_t st) {
+  const int nq = in.n;
+  if (nq <= 0) return;
+  fm_touch_kernel<<<nq, 256, 0, st>>>(in, S.hist, S.touched, S.ctr, d);
+  count_launch();
+  seg_alloc_kernel<<<(unsigned)ceil_div(d, 256), 256, 0, st>>>(S.hist, S.touched, S.cur, S.ctr, d);
+  count_launch();
+  fm_scatter_kernel<<<nq, 256, 0, st>>>(in, S.cur, S.ent_s, S.ent_v, d);
+  count_launch();
+  const int nwords = (int)ceil_div(nq, 32);
+  const size_t sm = (size_t)UPD_WARPS * nwords * 4 * 33;
+  const int grid = (int)std::min<int64_t>(upd_grid(), ceil_div(d, UPD_WARPS));
+  if (wdtype == KL_DTYPE_BF16) {
+    cudaFuncSetAttribute(fm_update_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    fm_update_kernel<__nv_bfloat16><<<grid, UPD_WARPS * 32, sm, st>>>(
+        const_cast<void*>(W), ldw, d, N, m, v, lgd, ldl, touched_mask, S, nwords, o);
+  count_launch();
+  } else {
+    cudaFuncSetAttribute(fm_update_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    fm_update_kernel<float><<<grid, UPD_WARPS * 32, sm, st>>>(
+        const_cast<void*>(W), ldw, d, N, m, v, lgd, ldl, touched_mask, S, nwords, o);
+  count_launch();
+  }
+  fm_bias_kernel<<<(unsigned)ceil_div(N, 128), 128, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask,
+                                                             o, stat_touched);
+  count_launch();
+}
+
+void launch_f32_to_w(const float* src, int64_t n_rows, int d, int64_t ld_src, void* dst, int wdtype,
+                     int64_t ld_dst, bool transpose, cudaStream_t st) {
+  const int64_t tot = n_rows * d;
+  if (tot <= 0) return;
+  const unsigned g = (unsigned)ceil_div(tot, 256);
+  if (wdtype == KL_DTYPE_BF16)
+    f32_to_w_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(src, n_rows, d, ld_src,
+                                                       static_cast<__nv_bfloat16*>(dst), ld_dst, transpose);
+  else
+    f32_to_w_kernel<float><<<g, 256, 0, st>>>(src, n_rows, d, ld_src, static_cast<float*>(dst), ld_dst,
+                                              transpose);
+  count_launch();
+}
+
+}  // namespace kl
