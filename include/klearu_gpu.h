@@ -212,6 +212,24 @@ KL_API kl_status kl_index_clear(kl_index_t ix);
 KL_API kl_status kl_index_query_batch(kl_index_t ix, const float* X, int n, int ldx, int mode,
                                uint32_t* out_ids, uint32_t* out_counts, int32_t* out_offsets,
                                int32_t capacity, int32_t* overflow);
+/* Allocation-free variant of kl_index_query_batch, for callers that cannot
+ * call cudaMalloc: a host runtime that owns all device memory, or a memory
+ * budget fixed at start-up.  No counterpart in the reference (its queries
+ * are CPU calls).  Same arguments, results and errors as
+ * kl_index_query_batch, but the call allocates nothing: its scratch is a
+ * fixed KL_NOALLOC_SCRATCH_BYTES array inside this library's device image,
+ * held by every GPU that loads the library until the process exits.
+ *  - n queries need about n * L * capacity * 8 bytes of it (plus L*n*2 and
+ *    n*4); a larger batch is refused with KL_ECAPACITY: split it.
+ *  - The first call on a device looks up the array's device address (no
+ *    allocation); make that first call before any stream capture.
+ *  - All calls on a device share the array; calls whose GPU work overlaps
+ *    (other streams, other contexts on the same device) race on it. */
+#define KL_NOALLOC_SCRATCH_BYTES (16u << 20)
+KL_API kl_status kl_index_query_batch_noalloc(kl_index_t ix, const float* X, int n, int ldx, int mode,
+                                              uint32_t* out_ids, uint32_t* out_counts,
+                                              int32_t* out_offsets, int32_t capacity,
+                                              int32_t* overflow);
 /* Batched query_sparse_union / query_sparse_with_counts (index.rs:290-300). */
 KL_API kl_status kl_index_query_sparse_batch(kl_index_t ix, const int32_t* rowptr,
                                       const uint32_t* idx, const float* val, int n, int mode,

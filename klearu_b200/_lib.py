@@ -95,6 +95,7 @@ _PROTOS = {
     "kl_index_rebuild": (_S, [_H, _P, _P, C.c_int, C.c_int, C.c_int]),
     "kl_index_clear": (_S, [_H]),
     "kl_index_query_batch": (_S, [_H, _P, C.c_int, C.c_int, C.c_int, _P, _P, _P, C.c_int32, _P]),
+    "kl_index_query_batch_noalloc": (_S, [_H, _P, C.c_int, C.c_int, C.c_int, _P, _P, _P, C.c_int32, _P]),
     "kl_index_query_sparse_batch": (_S, [_H, _P, _P, _P, C.c_int, C.c_int, _P, _P, _P, C.c_int32, _P]),
     "kl_index_export": (_S, [_H, _P, _P, _P]),
     "kl_index_import": (_S, [_H, _P, _P, _P]),

@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -1546,4 +1547,112 @@ extern "C" kl_status kl_net_create_sharded(kl_ctx_t ctx, const kl_net_config* cf
   if (out) *out = nullptr;
   if (ctx) ctx->last_error = "sharded networks are not built yet";
   return KL_EUNSUPPORTED;
+}
+
+// ===========================================================================
+// Allocation-free index query.
+//
+// Some callers cannot call cudaMalloc: an allocator-owning host runtime that
+// forbids allocations behind its back, a memory budget fixed before start-up,
+// or code already running under a pool that must not grow.  For them,
+// kl_index_query_batch_noalloc does the same work as kl_index_query_batch, but
+// its scratch (per-query bucket numbers and padded per-query (id, count)
+// lists) lives in the file-scope device array below instead of buffers that
+// the index allocates on demand.  The array is part of the loaded module, so
+// every GPU that loads this library holds its KL_NOALLOC_SCRATCH_BYTES until
+// the process exits.  Every call shares the array and it keeps the previous
+// call's contents; nothing in it must start at zero (the hash and probe
+// kernels write every element that the compaction later reads).  Calls whose
+// work overlaps on the GPU (different streams or contexts on the same device)
+// race on the array and must be serialised by the caller.
+// ===========================================================================
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)KL_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch per device.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per
+// device with that device current (the caller's DeviceGuard makes it so).
+std::mutex g_noalloc_mu;
+std::vector<void*> g_noalloc_addr;
+
+void* noalloc_scratch_for(int device) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if ((int)g_noalloc_addr.size() <= device) g_noalloc_addr.resize((size_t)device + 1, nullptr);
+  if (!g_noalloc_addr[(size_t)device]) {
+    void* p = nullptr;
+    ck(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)");
+    require(p != nullptr, "no-alloc scratch: null symbol address");
+    g_noalloc_addr[(size_t)device] = p;
+  }
+  return g_noalloc_addr[(size_t)device];
+}
+
+// Scratch carve for n queries: bucket numbers u16 [L][n], then padded
+// results qids / qcnt u32 [n][L*cap] and sizes qn i32 [n], each 256-aligned.
+size_t noalloc_query_bytes(int64_t n, int64_t L, int64_t stride) {
+  return (size_t)(round_up(L * n * 2, 256) + 2 * round_up(n * stride * 4, 256) + round_up(n * 4, 256));
+}
+
+}  // namespace
+
+extern "C" kl_status kl_index_query_batch_noalloc(kl_index_t ix, const float* X, int n, int ldx, int mode,
+                                                  uint32_t* out_ids, uint32_t* out_counts, int32_t* out_offsets,
+                                                  int32_t capacity, int32_t* overflow) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  require(mode == KL_QUERY_COUNTS || mode == KL_QUERY_UNION, "query: unknown mode");
+  require(n >= 0 && out_offsets && (n == 0 || (X && ldx >= I.hash->dh.d)), "query: bad arguments");
+  require(capacity >= 0 && (capacity == 0 || out_ids), "query: bad capacity");
+  const int64_t stride = (int64_t)I.T.L * I.T.cap;
+  const size_t need = noalloc_query_bytes(n, I.T.L, stride);
+  if (need > kNoAllocScratchBytes)
+    throw KlError{KL_ECAPACITY, "query_noalloc: " + std::to_string(n) + " queries need " + std::to_string(need) +
+                                    " scratch bytes, more than the fixed " +
+                                    std::to_string(kNoAllocScratchBytes) + " (KL_NOALLOC_SCRATCH_BYTES); "
+                                    "split the batch"};
+  void* base = noalloc_scratch_for(ctx__->device);
+  cudaStream_t st = ctx__->stream;
+  if (n == 0) {
+    ck(cudaMemsetAsync(out_offsets, 0, 4, st), "memset");
+    return KL_OK;
+  }
+  char* p = static_cast<char*>(base);
+  uint16_t* bkt = reinterpret_cast<uint16_t*>(p);
+  p += round_up((int64_t)I.T.L * n * 2, 256);
+  uint32_t* qids = reinterpret_cast<uint32_t*>(p);
+  p += round_up((int64_t)n * stride * 4, 256);
+  uint32_t* qcnt = reinterpret_cast<uint32_t*>(p);
+  p += round_up((int64_t)n * stride * 4, 256);
+  int32_t* qn = reinterpret_cast<int32_t*>(p);
+
+  HashOut o;
+  o.bkt = bkt;
+  o.bkt_ld = n;
+  o.nb_mask = (uint32_t)(I.T.nb - 1);
+  launch_hash_dense(I.hash->dh, dense_rows(X, KL_DTYPE_F32, n, ldx), o, st);
+  ck_launch("hash");
+  ProbeArgs a;
+  a.T = I.T;
+  a.bkt = bkt;
+  a.bkt_ld = n;
+  a.nq = n;
+  a.N = 0;
+  a.id_bits = 32;
+  a.out_ids = qids;
+  a.out_counts = qcnt;
+  a.out_stride = (int)stride;
+  a.out_n = qn;
+  a.err = ctx__->err.as<int>();
+  launch_probe(a, st);
+  ck_launch("probe");
+  if (overflow) ck(cudaMemsetAsync(overflow, 0, 4, st), "memset");
+  launch_scan(qn, out_offsets, n, nullptr, st);
+  ck_launch("scan");
+  launch_compact(qids, mode == KL_QUERY_COUNTS ? qcnt : nullptr, (int)stride, out_offsets, n, out_ids,
+                 mode == KL_QUERY_COUNTS ? out_counts : nullptr, capacity, overflow, ctx__->err.as<int>(), st);
+  ck_launch("compact");
+  KL_API_END
 }
