@@ -789,7 +789,9 @@ struct Layer {
   DBuf W, b, m, v, mb, vb;
   std::shared_ptr<IndexImpl> index;
   // per-step buffers
-  DBuf bkt, ids, cnt, pre, post, lg, h, dx_in, dxpart, lgd, tmask;
+  DBuf bkt, ids, cnt, pre, post, lg, h, dx_in, dxpart, lgd, tmask, gfeat;
+  DBuf dbits, dtouched, dslot, dlg;  // dense-collision update scratch (row-major layers)
+  int64_t dldu = 0;
   DBuf hist, cur, touched, ctr, ent_s, ent_v;
   size_t ent_cap = 0;
   DBuf stats;  // u64 [3]: active_sum, touched_rows, input_nnz
@@ -1088,28 +1090,42 @@ struct kl_net_s {
       if (L.fm) {
         launch_fm_update(L.W.p, wdtype, L.ldw, L.d, L.N, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
                          L.mb.as<float>(), L.vb.as<float>(), in, L.lgd.as<float>(), L.ldN, L.tmask.as<uint32_t>(),
-                         S, o, stat, st);
+                         S, L.gfeat.as<float>(), o, stat, st);
         ck_launch("fm update");
       } else {
         const Layer& P = *layers[l - 1];
-        launch_rm_update(L.W.p, wdtype, L.ldw, L.d, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
-                         L.mb.as<float>(), L.vb.as<float>(), P.h.as<float>(), P.ldN, L.act(), nq, L.N, S, o,
-                         stat, st);
+        if (L.dldu > 0) {
+          DenseScratch D{L.dbits.as<uint32_t>(), L.dtouched.as<uint32_t>(), L.dslot.as<uint32_t>(),
+                         L.ctr.as<uint32_t>(), L.dlg.as<float>(), L.dldu};
+          launch_rm_update_dense(L.W.p, wdtype, L.ldw, L.d, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
+                                 L.mb.as<float>(), L.vb.as<float>(), P.h.as<float>(), P.ldN, L.act(), nq, L.N, D,
+                                 o, stat, st);
+          launch_count_touched(L.ctr.as<uint32_t>(), stat, st);
+        } else {
+          launch_rm_update(L.W.p, wdtype, L.ldw, L.d, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
+                           L.mb.as<float>(), L.vb.as<float>(), P.h.as<float>(), P.ldN, L.act(), nq, L.N, S, o,
+                           stat, st);
+        }
         ck_launch("rm update");
       }
     }
   }
 
+  // Per-batch buffers grow geometrically (x1.5) so that a stream of batches
+  // with varying nnz / label counts reallocates O(log) times, not per batch.
   void ensure_batch_buffers(const kl_batch& b) {
     if ((size_t)b.nlabels > labprob_cap) {
-      labprob.alloc((size_t)std::max(b.nlabels, 1) * 4);
-      labprob_cap = (size_t)b.nlabels;
+      const size_t cap = std::max<size_t>((size_t)b.nlabels, labprob_cap * 3 / 2);
+      labprob.alloc(std::max<size_t>(cap, 1) * 4);
+      labprob_cap = cap;
     }
     Layer& L0 = *layers[0];
     if ((size_t)b.nnz > L0.ent_cap) {
-      L0.ent_s.alloc((size_t)std::max(b.nnz, 1) * 4);
-      L0.ent_v.alloc((size_t)std::max(b.nnz, 1) * 4);
-      L0.ent_cap = (size_t)b.nnz;
+      const size_t cap = std::max<size_t>((size_t)b.nnz, L0.ent_cap * 3 / 2);
+      L0.ent_s.alloc(std::max<size_t>(cap, 1) * 4);
+      L0.ent_v.alloc(std::max<size_t>(cap, 1) * 4);
+      L0.gfeat.alloc((size_t)std::min<int64_t>(std::max<int64_t>((int64_t)cap, 1), L0.d) * L0.ldN * 4);
+      L0.ent_cap = cap;
     }
   }
 };
@@ -1233,6 +1249,19 @@ void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_
   L.ctr.alloc(8);
   ck(cudaMemsetAsync(L.hist.p, 0, rows * 4, st), "memset");
   if (!L.fm) {
+    // dense-collision update scratch when its gradient matrix fits the budget
+    const int64_t drows = std::min<int64_t>((int64_t)L.N, (int64_t)B * L.stride);
+    const int64_t ldu = round_up(drows + 16, 32);  // + a tile of slack: update tiles read 16 slots at a time
+    if (rm_dense_fits(ldu, std::max(B, 1))) {
+      L.dldu = ldu;
+      const size_t nwords = (size_t)ceil_div(L.N, 32);
+      L.dbits.alloc(nwords * 4);
+      ck(cudaMemsetAsync(L.dbits.p, 0, nwords * 4, st), "memset");
+      L.dtouched.alloc((size_t)drows * 4);
+      L.dslot.alloc((size_t)L.N * 4);
+      L.dlg.alloc((size_t)ldu * B * 4);
+      ck(cudaMemsetAsync(L.dlg.p, 0, (size_t)ldu * B * 4, st), "memset");
+    }
     L.ent_s.alloc((size_t)B * L.stride * 4);
     L.ent_v.alloc((size_t)B * L.stride * 4);
     L.ent_cap = (size_t)B * L.stride;

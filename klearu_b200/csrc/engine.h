@@ -194,11 +194,30 @@ void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, fl
                       float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
                       SegScratch S, const OptStep& o, unsigned long long* stat_touched,
                       cudaStream_t st);
+// Dense-collision path of the row-major update: touched rows by a bitmap
+// (first setter appends), local gradients scattered sample-major into LGd
+// [max batch][ldu] (all zero between steps), tiled bit-exact reduction.
+struct DenseScratch {
+  uint32_t* bits;      // [ceil(N / 32)] bitmap, zero between steps
+  uint32_t* touched;   // [rows]
+  uint32_t* slot_of;   // [N]
+  uint32_t* ctr;       // [1] touched count (zeroed by the caller per step)
+  float* LGd;          // [max batch][ldu], zero between steps
+  int64_t ldu;         // >= rows, multiple of 32
+};
+bool rm_dense_fits(int64_t rows, int nb);
+// stat += ctr[0] (touched-row counter of the roofline statistics)
+void launch_count_touched(const uint32_t* ctr, unsigned long long* stat, cudaStream_t st);
+void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
+                            float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
+                            DenseScratch D, const OptStep& o, unsigned long long* stat_touched,
+                            cudaStream_t st);
 // Feature-major gradient + optimizer over ALL features of the touched neurons
-// (Adam decays every element of an active row, adam.rs:57-68).
+// (Adam decays every element of an active row, adam.rs:57-68).  G: gradient
+// rows of the touched features, [min(d, nnz)][ldl] f32 scratch.
 void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
                       float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
-                      const uint32_t* touched_mask, SegScratch S, const OptStep& o,
+                      const uint32_t* touched_mask, SegScratch S, float* G, const OptStep& o,
                       unsigned long long* stat_touched, cudaStream_t st);
 
 // Predict top-k over the final layer (net.rs:159-173): inactive neurons

@@ -62,6 +62,11 @@ __device__ __forceinline__ void opt_apply(float& w, float& m, float& v, float g,
   if (o.opt == KL_OPT_ADAM) {
     m = __fadd_rn(__fmul_rn(o.b1, m), __fmul_rn(o.omb1, g));
     v = __fadd_rn(__fmul_rn(o.b2, v), __fmul_rn(__fmul_rn(o.omb2, g), g));
+    // m == 0 makes the step lr * 0 / (sqrt(v_hat) + eps) a zero, so w keeps
+    // its value (up to the sign of a zero weight); skipping the IEEE divisions
+    // and sqrt is exact and keeps never-updated elements (m = v = 0) off the
+    // slow paths of division and square root by zero.
+    if (m == 0.0f) return;
     const float mh = __fdiv_rn(m, o.c1);
     const float vh = __fdiv_rn(v, o.c2);
     const float q = __fdiv_rn(__fmul_rn(o.lr, mh), __fadd_rn(__fsqrt_rn(vh), o.eps));
@@ -581,66 +586,313 @@ __global__ void __launch_bounds__(UPD_WARPS * 32)
   }
 }
 
-// Feature-major update: warp per feature row f over ALL d features.  The
-// gradient of neuron j at feature f is sum over samples s containing f of
-// x_s[f] * lg_s[j] (ascending s); touched neurons are updated at every f.
+// ---------------------------------------------------------------------------
+// Dense-collision path of the row-major update, used when the layer's dense
+// gradient matrix fits its memory budget.  In batched SLIDE steps many
+// samples share active rows (C1: ~6 K distinct rows behind 1.5 M (sample,
+// row) pairs), so instead of per-row segments built with contended atomics:
+//  (1) rm_mark_kernel: a bitmap over rows; a lane whose row bit is already
+//      set only reads it, the lane that sets it first appends the row to the
+//      touched list (slot = position) and records slot_of[row];
+//  (2) rm_dense_scatter_kernel: LGd[s][slot] = local gradient of the row in
+//      sample s (sample-major, LGd is all zero between steps);
+//  (3) rm_dense_update_kernel: a block owns RDU_ROWS consecutive slots (2 per
+//      warp, 4 columns per lane).  Chunks of RDU_S samples of X and LGd are
+//      double-buffered into shared memory with cp.async; each lane sums
+//      g = sum_s lg_s * x_s in ascending s with the non-fused f32 operations
+//      of the batched oracle (bit-exact), zeroes the consumed LGd tile,
+//      applies the optimizer to its rows and biases, and clears their bits.
+// ---------------------------------------------------------------------------
+__global__ void rm_mark_kernel(ActiveSet A, uint32_t* bits, uint32_t* touched, uint32_t* slot_of,
+                               uint32_t* ctr) {
+  const int s = blockIdx.y;
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= A.cnt[s]) return;
+  const uint32_t id = A.ids[(int64_t)s * A.stride + a];
+  const uint32_t b = 1u << (id & 31);
+  uint32_t* wp = bits + (id >> 5);
+  bool first = false;
+  if (!(*reinterpret_cast<volatile uint32_t*>(wp) & b)) first = !(atomicOr(wp, b) & b);
+  const int pos = warp_append(first, ctr);
+  if (pos >= 0) {
+    touched[pos] = id;
+    slot_of[id] = (uint32_t)pos;
+  }
+}
+
+__global__ void rm_dense_scatter_kernel(ActiveSet A, const uint32_t* slot_of, float* LGd, int64_t ldu) {
+  const int s = blockIdx.y;
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= A.cnt[s]) return;
+  const int64_t o = (int64_t)s * A.stride + a;
+  LGd[(int64_t)s * ldu + slot_of[A.ids[o]]] = A.lg[o];
+}
+
+constexpr int RDU_ROWS = 16;  // slots per block (8 warps x 2)
+constexpr int RDU_S = 32;     // samples per staged chunk
+
 template <class W>
-__global__ void __launch_bounds__(UPD_WARPS * 32)
-    fm_update_kernel(void* Wm, int ldw, int d, int N, float* m, float* v, const float* lgd, int ldl,
-                     const uint32_t* tmask, SegScratch S, int nwords, OptStep o) {
-  extern __shared__ __align__(16) unsigned char dyn[];
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  uint32_t* mask = reinterpret_cast<uint32_t*>(dyn) + w * nwords;
-  float* coef = reinterpret_cast<float*>(dyn + (size_t)UPD_WARPS * nwords * 4) + (size_t)w * nwords * 32;
-  for (int i = l; i < nwords; i += 32) mask[i] = 0;
-  __syncwarp();
-  for (int64_t f = (int64_t)blockIdx.x * UPD_WARPS + w; f < d; f += (int64_t)gridDim.x * UPD_WARPS) {
-    const uint32_t len = S.hist[f];
-    if (len) seg_to_mask(S.ent_s, S.ent_v, S.cur[f] - len, len, coef, mask);
-    for (int g0 = 0; g0 < N; g0 += 128) {
+__global__ void __launch_bounds__(256)
+    rm_dense_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
+                           const float* X, int ldx, uint32_t* bits, const uint32_t* touched, const uint32_t* ctr,
+                           float* LGd, int64_t ldu, int nq, OptStep o) {
+  __shared__ __align__(16) float xs[2][RDU_S][128];
+  __shared__ __align__(16) float ls[2][RDU_S][RDU_ROWS];
+  const int t = threadIdx.x, w = t >> 5, l = t & 31;
+  const int n = (int)ctr[0];
+  const int nch = (nq + RDU_S - 1) / RDU_S;
+  for (int k0 = blockIdx.x * RDU_ROWS; k0 < n; k0 += gridDim.x * RDU_ROWS) {
+    float gb[2] = {0.f, 0.f};
+    for (int g0 = 0; g0 < d; g0 += 128) {
       const int c = g0 + l * 4;
-      if (c >= N) continue;
-      const uint32_t tw = tmask[c >> 5] >> (c & 31);
-      const bool upd[4] = {(tw & 1u) != 0, c + 1 < N && (tw & 2u), c + 2 < N && (tw & 4u),
-                           c + 3 < N && (tw & 8u)};
-      if (!(upd[0] | upd[1] | upd[2] | upd[3])) continue;
-      float g[4] = {0.f, 0.f, 0.f, 0.f};
-      if (len) {
-        for (int wi = 0; wi < nwords; ++wi) {
-          uint32_t mw = mask[wi];
-          while (mw) {
-            const int b = __ffs(mw) - 1;
-            mw &= mw - 1;
-            const int s = wi * 32 + b;
-            const float cf = coef[s];
-            const float4 lv = *reinterpret_cast<const float4*>(lgd + (int64_t)s * ldl + c);
-            g[0] = __fadd_rn(g[0], __fmul_rn(cf, lv.x));
-            g[1] = __fadd_rn(g[1], __fmul_rn(cf, lv.y));
-            g[2] = __fadd_rn(g[2], __fmul_rn(cf, lv.z));
-            g[3] = __fadd_rn(g[3], __fmul_rn(cf, lv.w));
+      const bool last_pass = g0 + 128 >= d;
+      // stage chunk `ch` into buffer `bf`: X rows (4 x 16 B per thread), LGd tile (threads < 128)
+      auto stage = [&](int ch, int bf) {
+        const int s0 = ch * RDU_S;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int idx = t + 256 * q;
+          const int r = idx >> 5, c4 = (idx & 31) * 4;
+          float* dst = &xs[bf][r][c4];
+          if (s0 + r < nq && g0 + c4 < d)
+            cp_async16(dst, X + (int64_t)(s0 + r) * ldx + g0 + c4);
+          else
+            *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (t < RDU_S * RDU_ROWS / 4) {
+          const int r = t / (RDU_ROWS / 4), c4 = (t % (RDU_ROWS / 4)) * 4;
+          float* dst = &ls[bf][r][c4];
+          if (s0 + r < nq) cp_async16(dst, LGd + (int64_t)(s0 + r) * ldu + k0 + c4);
+          else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        cp_async_commit();
+      };
+      float g[2][4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) g[i][0] = g[i][1] = g[i][2] = g[i][3] = 0.f;
+      __syncthreads();  // previous users of both buffers are done
+      stage(0, 0);
+      for (int ch = 0; ch < nch; ++ch) {
+        const int bf = ch & 1;
+        if (ch + 1 < nch) {
+          stage(ch + 1, bf ^ 1);
+          cp_async_wait_group<1>();
+        } else {
+          cp_async_wait_group<0>();
+        }
+        __syncthreads();
+        if (last_pass && t < RDU_S * RDU_ROWS / 4) {
+          const int s0 = ch * RDU_S;
+          const int r = t / (RDU_ROWS / 4), c4 = (t % (RDU_ROWS / 4)) * 4;
+          if (s0 + r < nq)
+            *reinterpret_cast<float4*>(LGd + (int64_t)(s0 + r) * ldu + k0 + c4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const int ns = min(RDU_S, nq - ch * RDU_S);
+        for (int j = 0; j < ns; ++j) {
+          const float4 xv = *reinterpret_cast<const float4*>(&xs[bf][j][l * 4]);
+          const float2 l2 = *reinterpret_cast<const float2*>(&ls[bf][j][w * 2]);
+          const float lgv[2] = {l2.x, l2.y};
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            if (lgv[i] != 0.0f) {
+              if (g0 == 0) gb[i] = __fadd_rn(gb[i], lgv[i]);
+              g[i][0] = __fadd_rn(g[i][0], __fmul_rn(lgv[i], xv.x));
+              g[i][1] = __fadd_rn(g[i][1], __fmul_rn(lgv[i], xv.y));
+              g[i][2] = __fadd_rn(g[i][2], __fmul_rn(lgv[i], xv.z));
+              g[i][3] = __fadd_rn(g[i][3], __fmul_rn(lgv[i], xv.w));
+            }
           }
         }
+        __syncthreads();  // buffer bf is restaged two chunks later
       }
-      row_update4<W>(Wm, m, v, f * ldw + c, g, upd, o);
+      if (c < d) {
+        const bool upd[4] = {true, c + 1 < d, c + 2 < d, c + 3 < d};
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int k = k0 + w * 2 + i;
+          if (k < n) row_update4<W>(Wm, m, v, (int64_t)touched[k] * ldw + c, g[i], upd, o);
+        }
+      }
     }
-    if (len) {
-      if (l == 0) S.hist[f] = 0;
-      for (int i = l; i < nwords; i += 32) mask[i] = 0;
-      __syncwarp();
+    if (l < 2) {
+      const int k = k0 + w * 2 + l;
+      if (k < n) {
+        const uint32_t row = touched[k];
+        bias_update(bias, mb, vb, row, l == 0 ? gb[0] : gb[1], o);
+        atomicAnd(bits + (row >> 5), ~(1u << (row & 31)));
+      }
     }
   }
 }
 
+// Feature-major (layer 0) update, in two passes.
+//
+// (1) fm_grad_kernel: one warp per touched feature row f (a feature present in
+//     the batch).  The gradient of neuron j at f is sum over the samples s that
+//     contain f of x_s[f] * lg_s[j], in ascending s (the batched oracle's
+//     order).  The segment's (sample, value) pairs arrive unordered, so the
+//     warp marks them in a per-sample bitmask, compacts the set bits into an
+//     ascending sample list in shared memory, and then sums with FM_PF loads
+//     of lg rows in flight per lane.  The row goes to G[k] (k = position of f
+//     in the touched list) and hist[f] becomes k + 1.
+// (2) fm_adam_kernel: streams W, m, v of ALL d feature rows (Adam runs over
+//     every element of a touched neuron, optim/adam.rs:57-68), FM_UNROLL
+//     16-byte vectors in flight per thread; rows with hist[f] != 0 read their
+//     gradient from G, the rest use g = 0.  fm_hist_clear_kernel then zeroes
+//     hist for the next step.
+// ---------------------------------------------------------------------------
+constexpr int FM_PF = 8;
+constexpr int FM_UNROLL = 2;
+constexpr int FM_NT = 256;
+
+__global__ void __launch_bounds__(UPD_WARPS * 32)
+    fm_grad_kernel(int N, const float* lgd, int ldl, SegScratch S, int nwords, float* G, int ldg) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  // per warp: mask[nwords] u32, coef[32*nwords] f32, list[32*nwords] u32
+  uint32_t* mask = reinterpret_cast<uint32_t*>(dyn) + (size_t)w * nwords * 65;
+  float* coef = reinterpret_cast<float*>(mask + nwords);
+  uint32_t* list = mask + nwords + 32 * nwords;
+  for (int i = l; i < nwords; i += 32) mask[i] = 0;
+  __syncwarp();
+  const int n = (int)S.ctr[0];
+  for (int k = blockIdx.x * UPD_WARPS + w; k < n; k += gridDim.x * UPD_WARPS) {
+    const uint32_t f = S.touched[k];
+    const uint32_t len = S.hist[f];
+    seg_to_mask(S.ent_s, S.ent_v, S.cur[f] - len, len, coef, mask);
+    // ascending sample list: word i's bits go after the bits of words < i
+    int base = 0;
+    for (int w0 = 0; w0 < nwords; w0 += 32) {
+      const uint32_t mw = w0 + l < nwords ? mask[w0 + l] : 0u;
+      const int c = __popc(mw);
+      const int inc = warp_incl_scan(c);
+      int pos = base + inc - c;
+      uint32_t b = mw;
+      while (b) {
+        const int bit = __ffs(b) - 1;
+        b &= b - 1;
+        list[pos++] = (uint32_t)((w0 + l) * 32 + bit);
+      }
+      base += __shfl_sync(FULL, inc, 31);
+      if (w0 + l < nwords) mask[w0 + l] = 0;
+    }
+    __syncwarp();
+    float* grow = G + (int64_t)k * ldg;
+    for (int g0 = 0; g0 < N; g0 += 128) {
+      const int c = g0 + l * 4;
+      if (c >= N) continue;
+      float g[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int i0 = 0; i0 < base; i0 += FM_PF) {
+        float4 lv[FM_PF];
+        float cf[FM_PF];
+#pragma unroll
+        for (int u = 0; u < FM_PF; ++u) {
+          if (i0 + u < base) {
+            const uint32_t s = list[i0 + u];
+            cf[u] = coef[s];
+            lv[u] = *reinterpret_cast<const float4*>(lgd + (int64_t)s * ldl + c);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < FM_PF; ++u) {
+          if (i0 + u < base) {
+            g[0] = __fadd_rn(g[0], __fmul_rn(cf[u], lv[u].x));
+            g[1] = __fadd_rn(g[1], __fmul_rn(cf[u], lv[u].y));
+            g[2] = __fadd_rn(g[2], __fmul_rn(cf[u], lv[u].z));
+            g[3] = __fadd_rn(g[3], __fmul_rn(cf[u], lv[u].w));
+          }
+        }
+      }
+      *reinterpret_cast<float4*>(grow + c) = make_float4(g[0], g[1], g[2], g[3]);
+    }
+    __syncwarp();
+    if (l == 0) S.hist[f] = (uint32_t)k + 1u;
+  }
+}
+
+template <class W>
+__global__ void __launch_bounds__(FM_NT, 4)
+    fm_adam_kernel(void* Wm, int ldw, int64_t nvec, int vpr, int N, float* m, float* v,
+                   const uint32_t* tmask, const uint32_t* hist, const float* G, int ldg, OptStep o) {
+  // vector q = f * vpr + j covers elements [4j, 4j+4) of feature row f
+  const int64_t q0 = (int64_t)blockIdx.x * (FM_NT * FM_UNROLL) + threadIdx.x;
+  float w[FM_UNROLL][4], mm[FM_UNROLL][4], vv[FM_UNROLL][4];
+  uint32_t hv[FM_UNROLL];
+  bool live[FM_UNROLL], upd[FM_UNROLL][4];
+#pragma unroll
+  for (int u = 0; u < FM_UNROLL; ++u) {
+    const int64_t q = q0 + (int64_t)u * FM_NT;
+    live[u] = false;
+    hv[u] = 0;
+    if (q < nvec) {
+      const int64_t f = q / vpr;
+      const int c = (int)(q - f * vpr) * 4;
+      const uint32_t tw = c < N ? tmask[c >> 5] >> (c & 31) : 0u;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) upd[u][i] = c + i < N && ((tw >> i) & 1u);
+      live[u] = upd[u][0] | upd[u][1] | upd[u][2] | upd[u][3];
+      if (live[u]) {
+        const int64_t off = f * ldw + c;
+        load4<W>(Wm, off, w[u]);
+        const float4 m4 = *reinterpret_cast<const float4*>(m + off);
+        mm[u][0] = m4.x; mm[u][1] = m4.y; mm[u][2] = m4.z; mm[u][3] = m4.w;
+        if (o.opt == KL_OPT_ADAM) {
+          const float4 v4 = *reinterpret_cast<const float4*>(v + off);
+          vv[u][0] = v4.x; vv[u][1] = v4.y; vv[u][2] = v4.z; vv[u][3] = v4.w;
+        } else {
+          vv[u][0] = vv[u][1] = vv[u][2] = vv[u][3] = 0.f;
+        }
+        hv[u] = hist[f];
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < FM_UNROLL; ++u) {
+    if (!live[u]) continue;
+    const int64_t q = q0 + (int64_t)u * FM_NT;
+    const int64_t f = q / vpr;
+    const int c = (int)(q - f * vpr) * 4;
+    float g[4] = {0.f, 0.f, 0.f, 0.f};
+    if (hv[u]) {
+      const float4 g4 = *reinterpret_cast<const float4*>(G + (int64_t)(hv[u] - 1) * ldg + c);
+      g[0] = g4.x; g[1] = g4.y; g[2] = g4.z; g[3] = g4.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (upd[u][i]) opt_apply(w[u][i], mm[u][i], vv[u][i], g[i], o);
+    const int64_t off = f * ldw + c;
+    store4<W>(Wm, off, w[u]);
+    *reinterpret_cast<float4*>(m + off) = make_float4(mm[u][0], mm[u][1], mm[u][2], mm[u][3]);
+    if (o.opt == KL_OPT_ADAM)
+      *reinterpret_cast<float4*>(v + off) = make_float4(vv[u][0], vv[u][1], vv[u][2], vv[u][3]);
+  }
+}
+
+// hist[f] = 0 for the touched features (after fm_adam_kernel read them).
+__global__ void fm_hist_clear_kernel(SegScratch S) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k < (int)S.ctr[0]) S.hist[S.touched[k]] = 0;
+}
+
+// Bias gradient of every touched neuron: one warp per neuron loads 32
+// samples' gradients at a time and adds them in ascending sample order.
 __global__ void fm_bias_kernel(float* bias, float* mb, float* vb, const float* lgd, int ldl, int nq,
                                int N, const uint32_t* tmask, OptStep o,
                                unsigned long long* stat_touched) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int l = threadIdx.x & 31;
   if (j >= N) return;
   if (!((tmask[j >> 5] >> (j & 31)) & 1u)) return;
-  if (stat_touched) atomicAdd(stat_touched, 1ull);
   float gb = 0.0f;
-  for (int s = 0; s < nq; ++s) gb = __fadd_rn(gb, lgd[(int64_t)s * ldl + j]);
-  bias_update(bias, mb, vb, (uint32_t)j, gb, o);
+  for (int s0 = 0; s0 < nq; s0 += 32) {
+    const float mine = s0 + l < nq ? lgd[(int64_t)(s0 + l) * ldl + j] : 0.f;
+    const int ns = min(32, nq - s0);
+    for (int u = 0; u < ns; ++u) gb = __fadd_rn(gb, __shfl_sync(FULL, mine, u));
+  }
+  if (l == 0) {
+    if (stat_touched) atomicAdd(stat_touched, 1ull);
+    bias_update(bias, mb, vb, (uint32_t)j, gb, o);
+  }
 }
 
 // Matrix conversion between reference f32 rows and device storage.
@@ -849,6 +1101,39 @@ static int upd_grid() {
   return g;
 }
 
+__global__ void count_touched_kernel(const uint32_t* ctr, unsigned long long* stat) { *stat += ctr[0]; }
+void launch_count_touched(const uint32_t* ctr, unsigned long long* stat, cudaStream_t st) {
+  if (!stat) return;
+  count_touched_kernel<<<1, 1, 0, st>>>(ctr, stat);
+  count_launch();
+}
+
+bool rm_dense_fits(int64_t rows, int nb) {
+  return rows * (int64_t)nb * 4 <= ((int64_t)2 << 30);
+}
+
+void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
+                            float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
+                            DenseScratch D, const OptStep& o, unsigned long long* stat_touched,
+                            cudaStream_t st) {
+  (void)stat_touched;
+  if (nq <= 0) return;
+  dim3 g2((unsigned)ceil_div(A.stride, 256), nq);
+  rm_mark_kernel<<<g2, 256, 0, st>>>(A, D.bits, D.touched, D.slot_of, D.ctr);
+  count_launch();
+  rm_dense_scatter_kernel<<<g2, 256, 0, st>>>(A, D.slot_of, D.LGd, D.ldu);
+  count_launch();
+  const int64_t maxn = std::min<int64_t>((int64_t)N, (int64_t)nq * A.stride);
+  const int grid = (int)std::min<int64_t>(upd_grid() * 3 / 4, ceil_div(maxn, RDU_ROWS));
+  if (wdtype == KL_DTYPE_BF16)
+    rm_dense_update_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X,
+                                                                ldx, D.bits, D.touched, D.ctr, D.LGd, D.ldu, nq, o);
+  else
+    rm_dense_update_kernel<float><<<grid, 256, 0, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X, ldx,
+                                                        D.bits, D.touched, D.ctr, D.LGd, D.ldu, nq, o);
+  count_launch();
+}
+
 void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
                       float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
                       SegScratch S, const OptStep& o, unsigned long long* stat_touched,
@@ -880,7 +1165,7 @@ void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, fl
 
 void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
                       float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
-                      const uint32_t* touched_mask, SegScratch S, const OptStep& o,
+                      const uint32_t* touched_mask, SegScratch S, float* G, const OptStep& o,
                       unsigned long long* stat_touched, cudaStream_t st) {
   const int nq = in.n;
   if (nq <= 0) return;
@@ -891,21 +1176,29 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
   fm_scatter_kernel<<<nq, 256, 0, st>>>(in, S.cur, S.ent_s, S.ent_v, d);
   count_launch();
   const int nwords = (int)ceil_div(nq, 32);
-  const size_t sm = (size_t)UPD_WARPS * nwords * 4 * 33;
-  const int grid = (int)std::min<int64_t>(upd_grid(), ceil_div(d, UPD_WARPS));
-  if (wdtype == KL_DTYPE_BF16) {
-    cudaFuncSetAttribute(fm_update_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    fm_update_kernel<__nv_bfloat16><<<grid, UPD_WARPS * 32, sm, st>>>(
-        const_cast<void*>(W), ldw, d, N, m, v, lgd, ldl, touched_mask, S, nwords, o);
-  count_launch();
-  } else {
-    cudaFuncSetAttribute(fm_update_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    fm_update_kernel<float><<<grid, UPD_WARPS * 32, sm, st>>>(
-        const_cast<void*>(W), ldw, d, N, m, v, lgd, ldl, touched_mask, S, nwords, o);
-  count_launch();
+  const size_t sm = (size_t)UPD_WARPS * nwords * 4 * 65;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(fm_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
   }
-  fm_bias_kernel<<<(unsigned)ceil_div(N, 128), 128, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask,
-                                                             o, stat_touched);
+  const int ggrid = (int)std::min<int64_t>(upd_grid(), ceil_div(d, UPD_WARPS));
+  fm_grad_kernel<<<ggrid, UPD_WARPS * 32, sm, st>>>(N, lgd, ldl, S, nwords, G, ldl);
+  count_launch();
+  const int vpr = ldl / 4;  // vectors per feature row (ldw == ldl == pitch of N)
+  const int64_t nvec = (int64_t)d * vpr;
+  const unsigned agrid = (unsigned)ceil_div(nvec, (int64_t)FM_NT * FM_UNROLL);
+  if (wdtype == KL_DTYPE_BF16)
+    fm_adam_kernel<__nv_bfloat16><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, nvec, vpr, N, m, v,
+                                                           touched_mask, S.hist, G, ldl, o);
+  else
+    fm_adam_kernel<float><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, nvec, vpr, N, m, v, touched_mask,
+                                                   S.hist, G, ldl, o);
+  count_launch();
+  fm_hist_clear_kernel<<<(unsigned)ceil_div(d, 256), 256, 0, st>>>(S);
+  count_launch();
+  fm_bias_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask, o,
+                                                           stat_touched);
   count_launch();
 }
 
