@@ -172,7 +172,7 @@ struct kl_ctx_s {
 struct HashImpl {
   kl_ctx_t ctx;
   DevHash dh;
-  DBuf planes, planesT, windows, fallback, perms;
+  DBuf planes, planesT, windows, fallback, perms, plist, poff;
 };
 struct kl_hash_s {
   std::shared_ptr<HashImpl> h;
@@ -292,6 +292,26 @@ std::shared_ptr<HashImpl> make_hash(kl_ctx_t ctx, int kind, int d, int k, int L,
       }
       for (int tb = 0; tb < h.LK; ++tb)
         for (int i = 0; i < d; ++i) dT[(size_t)i * h.lkpad + tb] = dense[(size_t)tb * h.dpad + i];
+      h.nt = (int)ceil_div(d, PL_T);
+      std::vector<uint16_t> plist;
+      std::vector<uint32_t> poff((size_t)h.LK * (h.nt + 1), 0);
+      for (int tb = 0; tb < h.LK; ++tb) {
+        for (int ti = 0; ti < h.nt; ++ti) {
+          poff[(size_t)tb * (h.nt + 1) + ti] = (uint32_t)plist.size();
+          for (int i = ti * PL_T; i < std::min(d, (ti + 1) * PL_T); ++i) {
+            const int8_t v = dense[(size_t)tb * h.dpad + i];
+            if (v) plist.push_back((uint16_t)((i - ti * PL_T) | (v < 0 ? 0x8000 : 0)));
+          }
+        }
+        poff[(size_t)tb * (h.nt + 1) + h.nt] = (uint32_t)plist.size();
+      }
+      plist.resize(plist.size() + 128, 0);  // slack for the kernel's read-ahead (3 windows of 32)
+      H->plist.alloc(plist.size() * 2);
+      H->poff.alloc(poff.size() * 4);
+      ck(cudaMemcpyAsync(H->plist.p, plist.data(), plist.size() * 2, cudaMemcpyHostToDevice, st), "upload");
+      ck(cudaMemcpyAsync(H->poff.p, poff.data(), poff.size() * 4, cudaMemcpyHostToDevice, st), "upload");
+      h.plist = H->plist.as<uint16_t>();
+      h.poff = H->poff.as<uint32_t>();
       H->planes.alloc(dense.size());
       H->planesT.alloc(dT.size());
       ck(cudaMemcpyAsync(H->planes.p, dense.data(), dense.size(), cudaMemcpyHostToDevice, st), "upload");

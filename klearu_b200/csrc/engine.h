@@ -24,7 +24,15 @@ struct DevHash {
   uint32_t* windows = nullptr;  // [L][K][w]   (WTA, DWTA)
   uint8_t* fallback = nullptr;  // [L][K]      DWTA sparse fallback position
   uint32_t* perms = nullptr;    // [L][d]      (MINHASH)
+  // SIMHASH / SRP: non-zero entries of each projection in dimension order,
+  // for the tiled dense kernel.  Dimensions are cut into tiles of PL_T; an
+  // entry is (dim % PL_T) | 0x8000 when the coefficient is -1.  Projection tb owns plist[poff[tb*(nt+1)] ..
+  // poff[tb*(nt+1)+nt]) and tile ti starts at poff[tb*(nt+1)+ti].
+  uint16_t* plist = nullptr;
+  uint32_t* poff = nullptr;     // [LK][nt+1]
+  int nt = 0;                   // ceil(d / PL_T)
 };
+constexpr int PL_T = 640;       // dimensions per staged tile (< 2^15)
 
 // Dense input: element (i, j) of row i at X[i*ld_row + j*ld_elem], as f32 or bf16.
 struct DenseIn {

@@ -12,6 +12,8 @@
 //    window, strict `>` from -inf.
 //  * MinHash / DOPH (minhash.rs:67-153): per-bin minimum of permuted indices,
 //    circular densification, polynomial combine.
+#include <algorithm>
+
 #include "engine.h"
 
 namespace kl {
@@ -33,79 +35,171 @@ __device__ __forceinline__ void write_out(const HashOut& o, int L, int i, int t,
   if (o.bkt) o.bkt[(int64_t)t * o.bkt_ld + i] = (uint16_t)(code & o.nb_mask);
 }
 
-// ---------------------------------------------------------------------------
-// Projection hashing of dense rows.  Block = 32 rows x (TT tables x K bits);
-// thread (row r, projection tb) owns one sequential f32 chain over d.  Input
-// tiles of 64 columns are staged in shared memory (pitch 65 floats: lanes that
-// read different rows hit different banks); plane rows are read 16 bytes at a
-// time (all lanes of a warp share one projection -> broadcast).
-// ---------------------------------------------------------------------------
-constexpr int PJ_ROWS = 32;
-constexpr int PJ_DT = 64;
+// Stage a 32-row x `tw`-column tile of dense rows into shared memory as f32,
+// dst[rr * rs + dd * ds].  Loads are issued STG_U at a time before their
+// stores, so a thread keeps STG_U global loads in flight instead of one.
+constexpr int STG_U = 8;
+__device__ __forceinline__ void stage_rows(const DenseIn& in, int row0, int d0, int tw, float* dst, int rs, int ds) {
+  const bool rowfast = in.ld_elem != 1;  // consecutive rows are adjacent in memory
+  const int total = 32 * tw;
+  for (int base = threadIdx.x; base < total; base += blockDim.x * STG_U) {
+    float v[STG_U];
+    int rr[STG_U], dd[STG_U];
+#pragma unroll
+    for (int u = 0; u < STG_U; ++u) {
+      const int idx = base + u * blockDim.x;
+      if (rowfast) { rr[u] = idx & 31; dd[u] = idx >> 5; }
+      else { rr[u] = idx / tw; dd[u] = idx - rr[u] * tw; }
+      v[u] = 0.0f;
+      if (idx < total && row0 + rr[u] < in.n)
+        v[u] = ldx_dt(in.X, in.dtype, (int64_t)(row0 + rr[u]) * in.ld_row + (int64_t)(d0 + dd[u]) * in.ld_elem);
+    }
+#pragma unroll
+    for (int u = 0; u < STG_U; ++u)
+      if (base + u * blockDim.x < total) dst[rr[u] * rs + dd[u] * ds] = v[u];
+  }
+}
 
-__global__ void proj_dense_kernel(DevHash h, DenseIn in, HashOut out, int TT) {
-  __shared__ float xs[PJ_ROWS][PJ_DT + 1];
-  extern __shared__ unsigned char dyn[];
+// ---------------------------------------------------------------------------
+// Projection hashing of dense rows over the planes' non-zero lists.  The
+// reference's dot_ternary_dense (simhash.rs:75-85) adds x where the plane is
+// +1, subtracts it where it is -1 and skips zeros; walking each projection's
+// sorted non-zero list does exactly that, in the same order, with a third of
+// the work (acc + (-x) is IEEE-identical to acc - x).  Block = 32 rows (one
+// lane each) x TT*K projections (one warp each); the rows are staged in
+// tiles of PL_T dimensions as xs[dim][row]:
+//  * FMB (rows adjacent in memory, bf16 -- the feature-major layer-0 weights):
+//    raw bf16 tiles copied with cp.async into two buffers, the next tile in
+//    flight while the warps walk the current one;
+//  * otherwise: converted to f32 by stage_rows (pitch 33).
+// Each warp walks its list in windows of 32 entries (one per lane, broadcast
+// by shuffle), prefetched two windows ahead.
+// ---------------------------------------------------------------------------
+constexpr int PL_PITCH = 33;
+
+template <bool FMB>
+__global__ void proj_list_kernel(DevHash h, DenseIn in, HashOut out, int TT) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  const int tdim = min(h.d, PL_T);
+  // FMB: two bf16 buffers [tdim][32]; else one f32 buffer [tdim][PL_PITCH]
+  const size_t xbytes = FMB ? (size_t)2 * tdim * 32 * 2 : (size_t)tdim * PL_PITCH * 4;
+  float* sv = reinterpret_cast<float*>(dyn + round_up((int64_t)xbytes, 16));  // [TT*K][32]
   const int K = h.k;
-  const int nthr = blockDim.x;
   const int r = threadIdx.x & 31;
-  const int q = threadIdx.x >> 5;  // projection within the block: tt*K + b
+  const int q = threadIdx.x >> 5;
   const int tt = q / K, b = q % K;
   const int t = blockIdx.y * TT + tt;
-  const int row0 = blockIdx.x * PJ_ROWS;
-  const bool active = (t < h.L);
-  const int tb = t * K + b;
-  const int8_t* prow = h.planes + (int64_t)(active ? tb : 0) * h.dpad;
+  const int row0 = blockIdx.x * 32;
+  const bool active = t < h.L;
+  const uint32_t* toff = h.poff + (size_t)(active ? t * K + b : 0) * (h.nt + 1);
+  auto stage_async = [&](int ti, int bf) {  // FMB only
+    const int d0 = ti * PL_T, tw = min(PL_T, h.d - d0);
+    unsigned char* dst = dyn + (size_t)bf * tdim * 64;
+    const unsigned char* src = static_cast<const unsigned char*>(in.X);
+    for (int c = threadIdx.x; c < tw * 4; c += blockDim.x) {
+      const int dd = c >> 2, part = c & 3;  // 4 x 16 B = 32 bf16 rows per dimension
+      const int rr = row0 + part * 8;
+      if (rr + 8 <= in.ld_elem)
+        cp_async16(dst + dd * 64 + part * 16, src + ((int64_t)(d0 + dd) * in.ld_elem + rr) * 2);
+      else
+        *reinterpret_cast<uint4*>(dst + dd * 64 + part * 16) = make_uint4(0, 0, 0, 0);
+    }
+    cp_async_commit();
+  };
+  uint32_t pos = toff[0];
+  uint32_t wb = pos;
+  uint32_t c0 = h.plist[wb + r], c1 = h.plist[wb + 32 + r], c2 = h.plist[wb + 64 + r];
   float acc = 0.0f;
-  for (int d0 = 0; d0 < h.d; d0 += PJ_DT) {
-    // stage X[row0 .. row0+32)[d0 .. d0+64) as f32
-    for (int e = threadIdx.x; e < PJ_ROWS * PJ_DT; e += nthr) {
-      int rr, dd;
-      if (in.ld_elem == 1) {
-        rr = e / PJ_DT;
-        dd = e % PJ_DT;
+  if (FMB) stage_async(0, 0);
+  for (int ti = 0; ti < h.nt; ++ti) {
+    const int d0 = ti * PL_T;
+    const uint32_t E = active ? toff[ti + 1] : pos;
+    if (FMB) {
+      if (ti + 1 < h.nt) {
+        stage_async(ti + 1, (ti + 1) & 1);
+        cp_async_wait_group<1>();
       } else {
-        rr = e % PJ_ROWS;
-        dd = e / PJ_ROWS;
+        cp_async_wait_group<0>();
       }
-      float v = 0.0f;
-      if (row0 + rr < in.n && d0 + dd < h.d)
-        v = ldx_dt(in.X, in.dtype, (int64_t)(row0 + rr) * in.ld_row + (int64_t)(d0 + dd) * in.ld_elem);
-      xs[rr][dd] = v;
+    } else {
+      stage_rows(in, row0, d0, min(PL_T, h.d - d0), reinterpret_cast<float*>(dyn), 1, PL_PITCH);
     }
     __syncthreads();
-    if (active) {
-      const int dmax = min(PJ_DT, h.d - d0);
-#pragma unroll 1
-      for (int dd = 0; dd < dmax; dd += 16) {
-        int4 pv = *reinterpret_cast<const int4*>(prow + d0 + dd);
-        const int8_t* p8 = reinterpret_cast<const int8_t*>(&pv);
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          // columns beyond d are zero in both the plane padding and xs
-          acc = __fmaf_rn((float)p8[u], xs[r][dd + u], acc);
-        }
+    const uint16_t* xb = reinterpret_cast<const uint16_t*>(dyn + (size_t)(ti & 1) * tdim * 64) + r;
+    const float* xf = reinterpret_cast<const float*>(dyn) + r;
+    while (pos < E) {
+      const int u0 = (int)(pos - wb);
+      const int u1 = (int)min(32u, E - wb);
+#pragma unroll 4
+      for (int u = u0; u < u1; ++u) {
+        const uint32_t ent = __shfl_sync(FULL, c0, u);
+        const uint32_t dd = ent & 0x7fffu;
+        const float x = FMB ? __uint_as_float((uint32_t)xb[dd * 32] << 16) : xf[dd * PL_PITCH];
+        acc = __fadd_rn(acc, __int_as_float(__float_as_int(x) ^ (int)((ent & 0x8000u) << 16)));
+      }
+      pos = wb + (uint32_t)u1;
+      if (u1 == 32) {
+        c0 = c1;
+        c1 = c2;
+        wb += 32;
+        c2 = h.plist[wb + 64 + r];
       }
     }
     __syncthreads();
   }
-  // combine K sign bits per (row, table) through shared memory
-  float* sv = reinterpret_cast<float*>(dyn);  // [TT*K][32]
+  const int nthr = blockDim.x;
   sv[q * 32 + r] = acc;
   __syncthreads();
-  const int ncomb = TT * PJ_ROWS;
+  const int ncomb = TT * 32;
   for (int c = threadIdx.x; c < ncomb; c += nthr) {
-    const int ct = c / PJ_ROWS, cr = c % PJ_ROWS;
+    const int ct = c / 32, cr = c % 32;
     const int tab = blockIdx.y * TT + ct, i = row0 + cr;
     if (tab >= h.L || i >= in.n) continue;
     uint64_t code = 0;
     float mn = __int_as_float(0x7f800000);
     for (int bb = 0; bb < K; ++bb) {
-      float v = sv[(ct * K + bb) * 32 + cr];
+      const float v = sv[(ct * K + bb) * 32 + cr];
       if (v >= 0.0f) code |= 1ULL << bb;
       mn = fminf(mn, fabsf(v));
     }
     write_out(out, h.L, i, tab, code, mn, true);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// WTA / DWTA over dense rows, tiled: 32 rows staged as f32 in shared memory
+// (pitch d+1), one warp per table at a time, one lane per row.  When only the
+// bucket number is wanted (out.codes == NULL), only the windows whose bits
+// survive `code & nb_mask` are evaluated (K=8, w=8, 256 buckets: 3 of 8).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) wta_tile_kernel(DevHash h, DenseIn in, HashOut out, int nwin) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  float* xs = reinterpret_cast<float*>(dyn);  // [32][d+1]
+  const int pitch = h.d + 1;
+  const int row0 = blockIdx.x * 32;
+  const int nr = min(32, in.n - row0);
+  stage_rows(in, row0, 0, h.d, xs, pitch, 1);
+  __syncthreads();
+  const int w = threadIdx.x >> 5, r = threadIdx.x & 31;
+  const float* xr = xs + r * pitch;
+  for (int t = w; t < h.L; t += blockDim.x >> 5) {
+    uint64_t code = 0;
+    int shift = 0;
+    for (int kk = 0; kk < nwin; ++kk) {
+      const uint32_t* win = h.windows + ((int64_t)t * h.k + kk) * h.w;
+      int best_pos = 0;
+      float best = __int_as_float(0xff800000);
+      for (int p = 0; p < h.w; ++p) {
+        const float v = xr[__ldg(win + p)];
+        if (v > best) {
+          best = v;
+          best_pos = p;
+        }
+      }
+      code |= (uint64_t)best_pos << shift;
+      shift += h.bpw;
+    }
+    if (r < nr) write_out(out, h.L, row0 + r, t, code, 0.0f, false);
   }
 }
 
@@ -283,20 +377,45 @@ void launch_hash_dense(const DevHash& h, const DenseIn& in, const HashOut& out, 
   switch (h.kind) {
     case KL_HASH_SIMHASH:
     case KL_HASH_SRP: {
-      int TT = max(1, 512 / (32 * h.k));
-      TT = min(TT, h.L);
-      dim3 grid((unsigned)ceil_div(in.n, PJ_ROWS), (unsigned)ceil_div(h.L, TT));
+      const int TT = std::min(h.L, std::max(1, 12 / h.k));
+      dim3 grid((unsigned)ceil_div(in.n, 32), (unsigned)ceil_div(h.L, TT));
       dim3 block(32 * TT * h.k);
-      size_t sm = (size_t)TT * h.k * 32 * sizeof(float);
-      proj_dense_kernel<<<grid, block, sm, st>>>(h, in, out, TT);
-  count_launch();
+      const int tdim = std::min(h.d, PL_T);
+      const bool fmb = in.ld_row == 1 && in.dtype == KL_DTYPE_BF16 && in.ld_elem % 8 == 0 &&
+                       (reinterpret_cast<uintptr_t>(in.X) & 15) == 0;
+      const size_t xbytes = fmb ? (size_t)2 * tdim * 64 : (size_t)tdim * PL_PITCH * 4;
+      const size_t sm = (size_t)round_up((int64_t)xbytes, 16) + (size_t)TT * h.k * 32 * sizeof(float);
+      static bool attr = false;
+      if (!attr) {
+        cudaFuncSetAttribute(proj_list_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(proj_list_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+      }
+      if (fmb) proj_list_kernel<true><<<grid, block, sm, st>>>(h, in, out, TT);
+      else proj_list_kernel<false><<<grid, block, sm, st>>>(h, in, out, TT);
+      count_launch();
       break;
     }
     case KL_HASH_WTA:
     case KL_HASH_DWTA: {
-      int64_t tot = (int64_t)in.n * h.L;
-      wta_dense_kernel<<<(unsigned)ceil_div(tot, 256), 256, 0, st>>>(h, in, out);
-  count_launch();
+      const size_t sm = (size_t)32 * (h.d + 1) * sizeof(float);
+      if (sm <= 200 * 1024) {
+        int nwin = h.k;
+        if (!out.codes && !out.min_abs) {
+          const int bits = __builtin_popcount(out.nb_mask);
+          nwin = std::min(h.k, (bits + h.bpw - 1) / h.bpw);
+        }
+        static bool attr = false;
+        if (!attr) {
+          cudaFuncSetAttribute(wta_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+          attr = true;
+        }
+        wta_tile_kernel<<<(unsigned)ceil_div(in.n, 32), 256, sm, st>>>(h, in, out, nwin);
+      } else {
+        int64_t tot = (int64_t)in.n * h.L;
+        wta_dense_kernel<<<(unsigned)ceil_div(tot, 256), 256, 0, st>>>(h, in, out);
+      }
+      count_launch();
       break;
     }
     case KL_HASH_MINHASH: {
