@@ -203,16 +203,25 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
     for (int tI = 0; tI < ntiles; ++tI) {
       rm_load_tile<W, TILEB>(mt, Wb, rowbytes, tI, myid, nw);
       if (has) {
+        // Sequential f32 dot in element order (bit-exact).  The loop runs to a
+        // whole number of 16-byte vectors: row padding up to ldw is zero in W
+        // and the staged x is zero beyond d, so the extra terms add +0.
         const int k0 = tI * EPT;
-        const int kmax = min(EPT, a.d - k0);
-        const W* rowp = reinterpret_cast<const W*>(mt + l * PITCH);
         constexpr int VE = 16 / (int)sizeof(W);
+        const int kmax = (int)round_up(min(EPT, a.d - k0), VE);
+        const uint4* rowp = reinterpret_cast<const uint4*>(mt + l * PITCH);
+        const float4* x4 = reinterpret_cast<const float4*>(xs + k0);
         for (int kb = 0; kb < kmax; kb += VE) {
-          uint4 raw = *reinterpret_cast<const uint4*>(rowp + kb);
+          const uint4 raw = rowp[kb / VE];
           const W* e = reinterpret_cast<const W*>(&raw);
+          float xv[VE];
 #pragma unroll
-          for (int u = 0; u < VE; ++u)
-            if (kb + u < kmax) acc = __fadd_rn(acc, __fmul_rn(to_f(e[u]), xs[k0 + kb + u]));
+          for (int u4 = 0; u4 < VE / 4; ++u4) {
+            const float4 t4 = x4[kb / 4 + u4];
+            xv[4 * u4] = t4.x; xv[4 * u4 + 1] = t4.y; xv[4 * u4 + 2] = t4.z; xv[4 * u4 + 3] = t4.w;
+          }
+#pragma unroll
+          for (int u = 0; u < VE; ++u) acc = __fadd_rn(acc, __fmul_rn(to_f(e[u]), xv[u]));
         }
       }
       __syncwarp();
@@ -253,14 +262,20 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
     float part[CPL];
 #pragma unroll
     for (int c = 0; c < CPL; ++c) part[c] = 0.0f;
-    const int kvalid = a.d - tI * EPT;
+    // lane l owns the CPL consecutive columns l*CPL.. of the tile (columns
+    // beyond d see zero row padding and are not written back)
     for (int r = 0; r < nw; ++r) {
       const float lr = __shfl_sync(FULL, lgv, r);
-      const W* rowp = reinterpret_cast<const W*>(mt + r * PITCH);
+      const unsigned char* rowb = mt + r * PITCH + l * CPL * (int)sizeof(W);
+      if constexpr (sizeof(W) == 2 && CPL == 4) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(rowb);
+        const W* e = reinterpret_cast<const W*>(&raw);
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        const int col = l * CPL + c;
-        if (col < kvalid) part[c] = fmaf(lr, to_f(rowp[col]), part[c]);
+        for (int c = 0; c < 4; ++c) part[c] = fmaf(lr, to_f(e[c]), part[c]);
+      } else {
+        const W* rowp = reinterpret_cast<const W*>(rowb);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) part[c] = fmaf(lr, to_f(rowp[c]), part[c]);
       }
     }
 #pragma unroll
@@ -630,14 +645,16 @@ __global__ void rm_dense_scatter_kernel(ActiveSet A, const uint32_t* slot_of, fl
 
 constexpr int RDU_ROWS = 16;  // slots per block (8 warps x 2)
 constexpr int RDU_S = 32;     // samples per staged chunk
+constexpr int RDU_ST = 4;     // cp.async pipeline stages
 
 template <class W>
 __global__ void __launch_bounds__(256)
     rm_dense_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
                            const float* X, int ldx, uint32_t* bits, const uint32_t* touched, const uint32_t* ctr,
                            float* LGd, int64_t ldu, int nq, OptStep o) {
-  __shared__ __align__(16) float xs[2][RDU_S][128];
-  __shared__ __align__(16) float ls[2][RDU_S][RDU_ROWS];
+  extern __shared__ __align__(16) unsigned char dyn[];
+  float (*xs)[RDU_S][128] = reinterpret_cast<float (*)[RDU_S][128]>(dyn);
+  float (*ls)[RDU_S][RDU_ROWS] = reinterpret_cast<float (*)[RDU_S][RDU_ROWS]>(dyn + sizeof(float) * RDU_ST * RDU_S * 128);
   const int t = threadIdx.x, w = t >> 5, l = t & 31;
   const int n = (int)ctr[0];
   const int nch = (nq + RDU_S - 1) / RDU_S;
@@ -647,7 +664,8 @@ __global__ void __launch_bounds__(256)
       const int c = g0 + l * 4;
       const bool last_pass = g0 + 128 >= d;
       // stage chunk `ch` into buffer `bf`: X rows (4 x 16 B per thread), LGd tile (threads < 128)
-      auto stage = [&](int ch, int bf) {
+      auto stage = [&](int ch) {
+        const int bf = ch % RDU_ST;
         const int s0 = ch * RDU_S;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -665,21 +683,38 @@ __global__ void __launch_bounds__(256)
           if (s0 + r < nq) cp_async16(dst, LGd + (int64_t)(s0 + r) * ldu + k0 + c4);
           else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        cp_async_commit();
       };
+      // the optimizer state of this lane's two rows, loaded now and used after the sum
+      float wv[2][4], mv[2][4], vv[2][4];
+      int64_t roff[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int k = k0 + w * 2 + i;
+        roff[i] = -1;
+        if (k < n && c < d) {
+          roff[i] = (int64_t)touched[k] * ldw + c;
+          load4<W>(Wm, roff[i], wv[i]);
+          const float4 m4 = *reinterpret_cast<const float4*>(m + roff[i]);
+          mv[i][0] = m4.x; mv[i][1] = m4.y; mv[i][2] = m4.z; mv[i][3] = m4.w;
+          float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (o.opt == KL_OPT_ADAM) v4 = *reinterpret_cast<const float4*>(v + roff[i]);
+          vv[i][0] = v4.x; vv[i][1] = v4.y; vv[i][2] = v4.z; vv[i][3] = v4.w;
+        }
+      }
       float g[2][4];
 #pragma unroll
       for (int i = 0; i < 2; ++i) g[i][0] = g[i][1] = g[i][2] = g[i][3] = 0.f;
-      __syncthreads();  // previous users of both buffers are done
-      stage(0, 0);
+      __syncthreads();  // previous users of the buffers are done
+#pragma unroll
+      for (int p = 0; p < RDU_ST - 1; ++p) {
+        if (p < nch) stage(p);
+        cp_async_commit();  // one group per stage slot (possibly empty) keeps the wait count uniform
+      }
       for (int ch = 0; ch < nch; ++ch) {
-        const int bf = ch & 1;
-        if (ch + 1 < nch) {
-          stage(ch + 1, bf ^ 1);
-          cp_async_wait_group<1>();
-        } else {
-          cp_async_wait_group<0>();
-        }
+        const int bf = ch % RDU_ST;
+        if (ch + RDU_ST - 1 < nch) stage(ch + RDU_ST - 1);
+        cp_async_commit();
+        cp_async_wait_group<RDU_ST - 1>();
         __syncthreads();
         if (last_pass && t < RDU_S * RDU_ROWS / 4) {
           const int s0 = ch * RDU_S;
@@ -703,15 +738,19 @@ __global__ void __launch_bounds__(256)
             }
           }
         }
-        __syncthreads();  // buffer bf is restaged two chunks later
+        __syncthreads();  // buffer bf is restaged RDU_ST - 1 chunks later
       }
-      if (c < d) {
-        const bool upd[4] = {true, c + 1 < d, c + 2 < d, c + 3 < d};
+      cp_async_wait_group<0>();
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int k = k0 + w * 2 + i;
-          if (k < n) row_update4<W>(Wm, m, v, (int64_t)touched[k] * ldw + c, g[i], upd, o);
-        }
+      for (int i = 0; i < 2; ++i) {
+        if (roff[i] < 0) continue;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (c + e < d) opt_apply(wv[i][e], mv[i][e], vv[i][e], g[i][e], o);
+        store4<W>(Wm, roff[i], wv[i]);
+        *reinterpret_cast<float4*>(m + roff[i]) = make_float4(mv[i][0], mv[i][1], mv[i][2], mv[i][3]);
+        if (o.opt == KL_OPT_ADAM)
+          *reinterpret_cast<float4*>(v + roff[i]) = make_float4(vv[i][0], vv[i][1], vv[i][2], vv[i][3]);
       }
     }
     if (l < 2) {
@@ -1124,12 +1163,19 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
   rm_dense_scatter_kernel<<<g2, 256, 0, st>>>(A, D.slot_of, D.LGd, D.ldu);
   count_launch();
   const int64_t maxn = std::min<int64_t>((int64_t)N, (int64_t)nq * A.stride);
-  const int grid = (int)std::min<int64_t>(upd_grid() * 3 / 4, ceil_div(maxn, RDU_ROWS));
+  const int grid = (int)std::min<int64_t>(upd_grid() * 3 / 8, ceil_div(maxn, RDU_ROWS));
+  const size_t sm = sizeof(float) * RDU_ST * RDU_S * (128 + RDU_ROWS);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(rm_dense_update_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    cudaFuncSetAttribute(rm_dense_update_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    attr = true;
+  }
   if (wdtype == KL_DTYPE_BF16)
-    rm_dense_update_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X,
+    rm_dense_update_kernel<__nv_bfloat16><<<grid, 256, sm, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X,
                                                                 ldx, D.bits, D.touched, D.ctr, D.LGd, D.ldu, nq, o);
   else
-    rm_dense_update_kernel<float><<<grid, 256, 0, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X, ldx,
+    rm_dense_update_kernel<float><<<grid, 256, sm, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X, ldx,
                                                         D.bits, D.touched, D.ctr, D.LGd, D.ldu, nq, o);
   count_launch();
 }
