@@ -112,6 +112,7 @@ struct ProbeArgs {
   int* err = nullptr;
   unsigned long long* stat_active = nullptr;  // nullable: += sum of sizes
   int maxm = 0;       // set by launch_probe
+  int mode = 0;       // set by launch_probe: 0 radix sort, 1 small-N count array, 2 bitmap (all selected)
 };
 int probe_max_items();  // largest L*cap the probe kernel holds in shared memory
 void launch_probe(const ProbeArgs& a, cudaStream_t st);

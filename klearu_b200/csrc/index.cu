@@ -20,6 +20,8 @@
 // __match_any_sync.
 #include <cub/block/block_scan.cuh>
 
+#include <algorithm>
+
 #include "engine.h"
 
 namespace kl {
@@ -184,6 +186,8 @@ __global__ void remove_hashed_kernel(DevTables T, const uint32_t* ids, const uin
 constexpr int PB_NT = 512;
 constexpr int PB_NW = PB_NT / 32;
 constexpr int PB_MAXM = 16384;  // largest L*cap: 3 arrays of u32 => 192 KB of shared memory
+constexpr int PB_MAXWORDS = 3 * PB_MAXM;  // dynamic shared words beyond ProbeSmem
+constexpr int PB_SMALLN = 8192;            // neuron counts handled by the count-array path
 
 struct ProbeSmem {
   uint32_t hist[PB_NW][256];
@@ -269,53 +273,141 @@ __global__ void __launch_bounds__(PB_NT) probe_kernel(ProbeArgs a) {
     __syncthreads();
   }
   const int M = tot;
-  // 2. gather: warp w copies tables w, w+16, ...
-  {
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    for (int t = w; t < T.L; t += PB_NW) {
+  const int w_ = threadIdx.x >> 5, l_ = threadIdx.x & 31;
+  if (a.mode == 2) {
+    // Every candidate is selected and no counts are wanted (Vanilla, or TopK
+    // with top_k >= L*cap >= |union|): the union sorted by id is the set bits
+    // of a presence bitmap over the N neuron ids.  Ids >= N are dropped
+    // (retain, layer.rs:87); the network's own tables never hold them.
+    uint32_t* bm = A;
+    const int nwd = (a.N + 31) >> 5;
+    for (int i = threadIdx.x; i < nwd; i += PB_NT) bm[i] = 0;
+    __syncthreads();
+    for (int t = w_; t < T.L; t += PB_NW) {
       const int b = a.bkt[(int64_t)t * a.bkt_ld + q];
       const uint32_t* src = T.ids + ((int64_t)t * T.nb + b) * T.cap;
-      const int o = S.lens_off[t], n = S.lens_off[t + 1] - o;
-      for (int j = l; j < n; j += 32) A[o + j] = src[j];
+      const int n = S.lens_off[t + 1] - S.lens_off[t];
+      for (int j = l_; j < n; j += 32) {
+        const uint32_t id = src[j];
+        if (id < (uint32_t)a.N) atomicOr(&bm[id >> 5], 1u << (id & 31));
+      }
     }
+    __syncthreads();
+    const int wpt = (nwd + PB_NT - 1) / PB_NT;  // contiguous words per thread
+    const int w0 = threadIdx.x * wpt, w1 = min(nwd, w0 + wpt);
+    int c = 0;
+    for (int i = w0; i < w1; ++i) c += __popc(bm[i]);
+    int nsel;
+    int pos = block_excl_scan<PB_NT>(c, S.tmp, &nsel);
+    uint32_t* out_ids = a.out_ids + (int64_t)q * a.out_stride;
+    int nout;
+    if (nsel == 0) {
+      // fallback: every neuron (layer.rs:82-84)
+      nout = min(a.N, a.out_stride);
+      if (a.N > a.out_stride && threadIdx.x == 0) atomicOr(a.err, DERR_CAPACITY);
+      for (int j = threadIdx.x; j < nout; j += PB_NT) out_ids[j] = (uint32_t)j;
+    } else {
+      for (int i = w0; i < w1; ++i) {
+        uint32_t bits = bm[i];
+        while (bits) {
+          const int j = __ffs(bits) - 1;
+          bits &= bits - 1;
+          if (pos < a.out_stride) out_ids[pos] = (uint32_t)(i * 32 + j);
+          ++pos;
+        }
+      }
+      nout = min(nsel, a.out_stride);
+      if (nsel > a.out_stride && threadIdx.x == 0) atomicOr(a.err, DERR_CAPACITY);
+    }
+    if (threadIdx.x == 0) {
+      a.out_n[q] = nout;
+      if (a.stat_active) atomicAdd(a.stat_active, (unsigned long long)nout);
+    }
+    return;
   }
-  __syncthreads();
-  // 3. radix sort by id
-  uint32_t* cur = A;
-  uint32_t* oth = Bf;
-  for (int shift = 0; shift < a.id_bits; shift += 8) {
-    probe_radix_pass(cur, oth, M, shift, S.hist, S.tmp);
-    uint32_t* x = cur;
-    cur = oth;
-    oth = x;
-  }
-  // 4. run-length encode: heads -> unique ids (oth) and head positions (C)
-  const int IPT = (int)ceil_div(M, PB_NT);
-  int nheads = 0;
-  for (int j = 0; j < IPT; ++j) {
-    const int i = threadIdx.x * IPT + j;
-    if (i < M && (i == 0 || cur[i] != cur[i - 1])) ++nheads;
-  }
+  uint32_t* uid;
+  uint32_t* ucnt;
   int U;
-  int hoff = block_excl_scan<PB_NT>(nheads, S.tmp, &U);
-  for (int j = 0; j < IPT; ++j) {
-    const int i = threadIdx.x * IPT + j;
-    if (i < M && (i == 0 || cur[i] != cur[i - 1])) {
-      oth[hoff] = cur[i];
-      C[hoff] = (uint32_t)i;
-      ++hoff;
+  if (a.mode == 1) {
+    // Small N: per-id counts in shared memory, compacted in id order into
+    // (uid, ucnt) -- the union and collect_counts multiplicities
+    // (lsh/index.rs:219-234) without a sort.  Ids >= N are dropped before
+    // selection; the network's own tables never hold them.
+    // layout: uid = A, ucnt = Bf, selection flags C, counts after C (maxm >= N)
+    uint32_t* cntv = C + a.maxm;
+    uid = A;
+    ucnt = Bf;
+    for (int i = threadIdx.x; i < a.N; i += PB_NT) cntv[i] = 0;
+    __syncthreads();
+    for (int t = w_; t < T.L; t += PB_NW) {
+      const int b = a.bkt[(int64_t)t * a.bkt_ld + q];
+      const uint32_t* src = T.ids + ((int64_t)t * T.nb + b) * T.cap;
+      const int n = S.lens_off[t + 1] - S.lens_off[t];
+      for (int j = l_; j < n; j += 32) {
+        const uint32_t id = src[j];
+        if (id < (uint32_t)a.N) atomicAdd(&cntv[id], 1u);
+      }
     }
+    __syncthreads();
+    const int ipt = (a.N + PB_NT - 1) / PB_NT;
+    const int i0 = threadIdx.x * ipt, i1 = min(a.N, i0 + ipt);
+    int c = 0;
+    for (int i = i0; i < i1; ++i) c += cntv[i] != 0;
+    int pos = block_excl_scan<PB_NT>(c, S.tmp, &U);
+    for (int i = i0; i < i1; ++i)
+      if (cntv[i]) {
+        uid[pos] = (uint32_t)i;
+        ucnt[pos] = cntv[i];
+        ++pos;
+      }
+    __syncthreads();
+  } else {
+    // 2. gather: warp w copies tables w, w+16, ...
+    {
+      const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+      for (int t = w; t < T.L; t += PB_NW) {
+        const int b = a.bkt[(int64_t)t * a.bkt_ld + q];
+        const uint32_t* src = T.ids + ((int64_t)t * T.nb + b) * T.cap;
+        const int o = S.lens_off[t], n = S.lens_off[t + 1] - o;
+        for (int j = l; j < n; j += 32) A[o + j] = src[j];
+      }
+    }
+    __syncthreads();
+    // 3. radix sort by id
+    uint32_t* cur = A;
+    uint32_t* oth = Bf;
+    for (int shift = 0; shift < a.id_bits; shift += 8) {
+      probe_radix_pass(cur, oth, M, shift, S.hist, S.tmp);
+      uint32_t* x = cur;
+      cur = oth;
+      oth = x;
+    }
+    // 4. run-length encode: heads -> unique ids (oth) and head positions (C)
+    const int IPT = (int)ceil_div(M, PB_NT);
+    int nheads = 0;
+    for (int j = 0; j < IPT; ++j) {
+      const int i = threadIdx.x * IPT + j;
+      if (i < M && (i == 0 || cur[i] != cur[i - 1])) ++nheads;
+    }
+    int hoff = block_excl_scan<PB_NT>(nheads, S.tmp, &U);
+    for (int j = 0; j < IPT; ++j) {
+      const int i = threadIdx.x * IPT + j;
+      if (i < M && (i == 0 || cur[i] != cur[i - 1])) {
+        oth[hoff] = cur[i];
+        C[hoff] = (uint32_t)i;
+        ++hoff;
+      }
+    }
+    __syncthreads();
+    // counts into `cur` (no longer needed): count[u] = pos[u+1] - pos[u]
+    for (int u = threadIdx.x; u < U; u += PB_NT) {
+      const uint32_t nxt = (u + 1 < U) ? C[u + 1] : (uint32_t)M;
+      cur[u] = nxt - C[u];
+    }
+    __syncthreads();
+    uid = oth;
+    ucnt = cur;
   }
-  __syncthreads();
-  // counts into `cur` (no longer needed): count[u] = pos[u+1] - pos[u]
-  for (int u = threadIdx.x; u < U; u += PB_NT) {
-    const uint32_t nxt = (u + 1 < U) ? C[u + 1] : (uint32_t)M;
-    cur[u] = nxt - C[u];
-  }
-  __syncthreads();
-  uint32_t* uid = oth;
-  uint32_t* ucnt = cur;
-
   // 5. selection -> flags in C (1 = selected)
   const bool net = a.N > 0;
   int cstar = -1, need = 0;  // TopK threshold
@@ -557,12 +649,27 @@ int probe_max_items() { return PB_MAXM; }
 void launch_probe(const ProbeArgs& a, cudaStream_t st) {
   if (a.nq <= 0) return;
   ProbeArgs b = a;
-  b.maxm = (int)round_up(max(1, a.T.L * a.T.cap), 32);
-  const size_t sm = sizeof(ProbeSmem) + 3 * (size_t)b.maxm * 4;
+  const int M = max(1, a.T.L * a.T.cap);
+  b.maxm = (int)round_up(M, 32);
+  size_t words = 3 * (size_t)b.maxm;
+  b.mode = 0;
+  if (a.N > 0) {
+    const bool all = a.sampling == KL_SAMPLING_VANILLA || (a.sampling == KL_SAMPLING_TOPK && a.top_k >= M);
+    if (all && !a.out_counts && a.N > PB_SMALLN && (size_t)(a.N + 31) / 32 <= (size_t)PB_MAXWORDS) {
+      b.mode = 2;
+      words = std::max(words, (size_t)(a.N + 31) / 32);
+    } else if (a.N <= PB_SMALLN) {
+      // uid, ucnt, selection flags and counts: [N] each
+      b.mode = 1;
+      b.maxm = (int)round_up(a.N, 32);
+      words = 4 * (size_t)b.maxm;
+    }
+  }
+  const size_t sm = sizeof(ProbeSmem) + words * 4;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)(sizeof(ProbeSmem) + 3 * (size_t)PB_MAXM * 4));
+                         (int)(sizeof(ProbeSmem) + (size_t)PB_MAXWORDS * 4));
     attr = true;
   }
   probe_kernel<<<a.nq, PB_NT, sm, st>>>(b);
