@@ -193,6 +193,7 @@ struct ProbeSmem {
   uint32_t hist[PB_NW][256];
   int tmp[40];
   int lens_off[1025];
+  int bsel[1024];  // bucket probed in each table
 };
 
 __device__ void probe_radix_pass(const uint32_t* in, uint32_t* out, int M, int shift,
@@ -261,6 +262,7 @@ __global__ void __launch_bounds__(PB_NT) probe_kernel(ProbeArgs a) {
       int len = 0;
       if (t < T.L) {
         const int b = a.bkt[(int64_t)t * a.bkt_ld + q];
+        S.bsel[t] = b;
         len = (int)min(T.len[(int64_t)t * T.nb + b], (uint32_t)T.cap);
       }
       int chunk_tot;
@@ -284,12 +286,16 @@ __global__ void __launch_bounds__(PB_NT) probe_kernel(ProbeArgs a) {
     for (int i = threadIdx.x; i < nwd; i += PB_NT) bm[i] = 0;
     __syncthreads();
     for (int t = w_; t < T.L; t += PB_NW) {
-      const int b = a.bkt[(int64_t)t * a.bkt_ld + q];
+      const int b = S.bsel[t];
       const uint32_t* src = T.ids + ((int64_t)t * T.nb + b) * T.cap;
       const int n = S.lens_off[t + 1] - S.lens_off[t];
-      for (int j = l_; j < n; j += 32) {
-        const uint32_t id = src[j];
-        if (id < (uint32_t)a.N) atomicOr(&bm[id >> 5], 1u << (id & 31));
+      for (int j0 = 0; j0 < n; j0 += 128) {  // 4 loads in flight per lane
+        uint32_t id[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) id[u] = j0 + u * 32 + l_ < n ? src[j0 + u * 32 + l_] : 0xffffffffu;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (id[u] < (uint32_t)a.N) atomicOr(&bm[id[u] >> 5], 1u << (id[u] & 31));
       }
     }
     __syncthreads();
@@ -340,12 +346,16 @@ __global__ void __launch_bounds__(PB_NT) probe_kernel(ProbeArgs a) {
     for (int i = threadIdx.x; i < a.N; i += PB_NT) cntv[i] = 0;
     __syncthreads();
     for (int t = w_; t < T.L; t += PB_NW) {
-      const int b = a.bkt[(int64_t)t * a.bkt_ld + q];
+      const int b = S.bsel[t];
       const uint32_t* src = T.ids + ((int64_t)t * T.nb + b) * T.cap;
       const int n = S.lens_off[t + 1] - S.lens_off[t];
-      for (int j = l_; j < n; j += 32) {
-        const uint32_t id = src[j];
-        if (id < (uint32_t)a.N) atomicAdd(&cntv[id], 1u);
+      for (int j0 = 0; j0 < n; j0 += 128) {  // 4 loads in flight per lane
+        uint32_t id[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) id[u] = j0 + u * 32 + l_ < n ? src[j0 + u * 32 + l_] : 0xffffffffu;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (id[u] < (uint32_t)a.N) atomicAdd(&cntv[id[u]], 1u);
       }
     }
     __syncthreads();
@@ -366,7 +376,7 @@ __global__ void __launch_bounds__(PB_NT) probe_kernel(ProbeArgs a) {
     {
       const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
       for (int t = w; t < T.L; t += PB_NW) {
-        const int b = a.bkt[(int64_t)t * a.bkt_ld + q];
+        const int b = S.bsel[t];
         const uint32_t* src = T.ids + ((int64_t)t * T.nb + b) * T.cap;
         const int o = S.lens_off[t], n = S.lens_off[t + 1] - o;
         for (int j = l; j < n; j += 32) A[o + j] = src[j];

@@ -780,7 +780,7 @@ __global__ void __launch_bounds__(256)
 //     gradient from G, the rest use g = 0.  fm_hist_clear_kernel then zeroes
 //     hist for the next step.
 // ---------------------------------------------------------------------------
-constexpr int FM_PF = 8;
+constexpr int FM_PF = 16;
 constexpr int FM_UNROLL = 2;
 constexpr int FM_NT = 256;
 
@@ -852,7 +852,7 @@ __global__ void __launch_bounds__(UPD_WARPS * 32)
 template <class W>
 __global__ void __launch_bounds__(FM_NT, 4)
     fm_adam_kernel(void* Wm, int ldw, int64_t nvec, int vpr, int N, float* m, float* v,
-                   const uint32_t* tmask, const uint32_t* hist, const float* G, int ldg, OptStep o) {
+                   const uint32_t* tmask, uint32_t* hist, const float* G, int ldg, OptStep o) {
   // vector q = f * vpr + j covers elements [4j, 4j+4) of feature row f
   const int64_t q0 = (int64_t)blockIdx.x * (FM_NT * FM_UNROLL) + threadIdx.x;
   float w[FM_UNROLL][4], mm[FM_UNROLL][4], vv[FM_UNROLL][4];
@@ -881,16 +881,19 @@ __global__ void __launch_bounds__(FM_NT, 4)
         } else {
           vv[u][0] = vv[u][1] = vv[u][2] = vv[u][3] = 0.f;
         }
-        hv[u] = hist[f];
       }
+      hv[u] = hist[f];  // read for every row: its first lane clears it below
     }
   }
+  __syncwarp();  // every lane has read hist before the row's first lane clears it
 #pragma unroll
   for (int u = 0; u < FM_UNROLL; ++u) {
-    if (!live[u]) continue;
     const int64_t q = q0 + (int64_t)u * FM_NT;
+    if (q >= nvec) continue;
     const int64_t f = q / vpr;
     const int c = (int)(q - f * vpr) * 4;
+    if (c == 0 && hv[u]) hist[f] = 0;  // ready for the next step
+    if (!live[u]) continue;
     float g[4] = {0.f, 0.f, 0.f, 0.f};
     if (hv[u]) {
       const float4 g4 = *reinterpret_cast<const float4*>(G + (int64_t)(hv[u] - 1) * ldg + c);
@@ -923,10 +926,19 @@ __global__ void fm_bias_kernel(float* bias, float* mb, float* vb, const float* l
   if (j >= N) return;
   if (!((tmask[j >> 5] >> (j & 31)) & 1u)) return;
   float gb = 0.0f;
-  for (int s0 = 0; s0 < nq; s0 += 32) {
-    const float mine = s0 + l < nq ? lgd[(int64_t)(s0 + l) * ldl + j] : 0.f;
-    const int ns = min(32, nq - s0);
-    for (int u = 0; u < ns; ++u) gb = __fadd_rn(gb, __shfl_sync(FULL, mine, u));
+  constexpr int R = 8;  // rounds of 32 samples loaded before they are summed
+  for (int s00 = 0; s00 < nq; s00 += 32 * R) {
+    float mine[R];
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      const int sidx = s00 + u * 32 + l;
+      mine[u] = sidx < nq ? lgd[(int64_t)sidx * ldl + j] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      const int ns = min(32, nq - (s00 + u * 32));
+      for (int v = 0; v < ns; ++v) gb = __fadd_rn(gb, __shfl_sync(FULL, mine[u], v));
+    }
   }
   if (l == 0) {
     if (stat_touched) atomicAdd(stat_touched, 1ull);
@@ -1241,8 +1253,11 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
     fm_adam_kernel<float><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, nvec, vpr, N, m, v, touched_mask,
                                                    S.hist, G, ldl, o);
   count_launch();
-  fm_hist_clear_kernel<<<(unsigned)ceil_div(d, 256), 256, 0, st>>>(S);
-  count_launch();
+  if (!(vpr == 32 || vpr == 8 || vpr == 16 || vpr == 4 || vpr == 2 || vpr == 1) || (vpr >= 32 && vpr % 32)) {
+    // a feature row does not sit inside one warp: clear hist separately
+    fm_hist_clear_kernel<<<(unsigned)ceil_div(d, 256), 256, 0, st>>>(S);
+    count_launch();
+  }
   fm_bias_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask, o,
                                                            stat_touched);
   count_launch();
