@@ -396,15 +396,39 @@ KL_API kl_status kl_launch_count(uint64_t* count_host);
 KL_API int kl_dist_unique_id_size(void);
 /* Rank 0 creates the id; it is shared with all ranks out of band. */
 KL_API kl_status kl_dist_get_unique_id(void* id_host);
-/* Like kl_net_create, but the output layer's neurons are split into `nranks`
- * contiguous slices; this rank owns slice `rank` (its rows, optimizer state
- * and LSH tables).  Hidden layers are replicated.  `init` holds the FULL
- * parameters (every rank passes the same).  Collectives per step: broadcast
- * of the batch's hidden activations' input, all-gather of per-rank candidate
- * lists, all-reduce of the output layer's input gradient and of the loss. */
+/* Like kl_net_create, but for one rank of an `nranks`-process job (one GPU
+ * each).  No reference counterpart: the reference's only parallelism is
+ * HOGWILD threads (crates/klearu-core/src/optim/hogwild.rs:65-95).
+ *  - The output (last) layer's neurons are split into contiguous slices
+ *    [r*N/P, (r+1)*N/P); this rank owns slice `rank`: its rows, optimizer
+ *    state and LSH tables, whose buckets hold bucket_capacity / nranks ids so
+ *    that an example's candidates over all shards stay num_tables *
+ *    bucket_capacity, as in the unsharded network.
+ *  - The sparse-input hidden layer is replicated and data parallel: in
+ *    kl_net_train_step each rank passes its own `max_batch`-bounded batch
+ *    (every rank the same number of examples); the step trains on the global
+ *    batch of all ranks' examples in rank order (KL_MODE_BATCHED only).
+ *  - Collectives per step (NCCL, on the context stream): all-gather of the
+ *    batches and of the hidden activations, all-reduce of per-example
+ *    selection counts, all-reduce of the label probabilities with a
+ *    reduce-scatter of the output layer's input gradient, all-gather of the
+ *    hidden local gradients and touched masks.
+ *  - Supported shapes: two layers, non-softmax output, output sampling that
+ *    selects every candidate (Vanilla, or TopK with top_k >= num_tables *
+ *    bucket_capacity).  Per example at most 512 input nnz and 32 labels.
+ *  - kl_net_forward / kl_net_predict_topk / KL_MODE_EXACT_SEQUENTIAL return
+ *    KL_EUNSUPPORTED; kl_net_get_layer / set_layer / layer_output address the
+ *    rank's slice of the output layer with local row ids (see kl_net_shard_info).
+ * `init` holds the FULL parameters (every rank passes the same);
+ * `unique_id_host` is kl_dist_get_unique_id's output from rank 0. */
 KL_API kl_status kl_net_create_sharded(kl_ctx_t ctx, const kl_net_config* cfg_host,
                                 const kl_layer_init* init_host, const void* unique_id_host,
                                 int rank, int nranks, kl_net_t* out);
+/* This rank's place in a sharded network: rank, number of ranks, global id of
+ * its first output neuron and its number of output neurons (1, 0, N for an
+ * unsharded network). */
+KL_API kl_status kl_net_shard_info(kl_net_t net, int* rank_host, int* nranks_host, uint32_t* id_base_host,
+                            int* num_local_host);
 
 #ifdef __cplusplus
 }

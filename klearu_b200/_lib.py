@@ -119,6 +119,7 @@ _PROTOS = {
     "kl_dist_unique_id_size": (C.c_int, []),
     "kl_dist_get_unique_id": (_S, [_P]),
     "kl_net_create_sharded": (_S, [_H, C.POINTER(NetConfigC), _P, _P, C.c_int, C.c_int, C.POINTER(_H)]),
+    "kl_net_shard_info": (_S, [_H, _P, _P, _P, _P]),
 }
 
 _lib = None

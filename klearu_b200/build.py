@@ -22,13 +22,29 @@ PKG = ROOT / "klearu_b200"
 CSRC = PKG / "csrc"
 BUILD = ROOT / "_build" / "gpu"
 LIB = PKG / "libklearu_gpu.so"
-SOURCES = ["hash.cu", "index.cu", "layer.cu", "api.cu"]
+SOURCES = ["hash.cu", "index.cu", "layer.cu", "shard.cu", "api.cu"]
+
+def _nccl_dirs() -> tuple[str, str]:
+    """NCCL headers and library: the copy PyTorch itself loads (nvidia-nccl
+    wheel), so one process never holds two NCCL builds."""
+    try:
+        import nvidia.nccl as _n  # noqa: PLC0415
+
+        base = Path(list(_n.__path__)[0])
+        if (base / "include" / "nccl.h").exists() and (base / "lib" / "libnccl.so.2").exists():
+            return str(base / "include"), str(base / "lib")
+    except ImportError:
+        pass
+    return "/usr/include", "/usr/lib/x86_64-linux-gnu"
+
+
+NCCL_INC, NCCL_LIB = _nccl_dirs()
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo", "-O3", "-std=c++17",
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-    "-I", str(ROOT / "include"),
+    "-I", str(ROOT / "include"), "-I", NCCL_INC,
 ]
 
 
@@ -66,7 +82,8 @@ def build_gpu(verbose: bool = False, force: bool = False) -> Path:
                 raise RuntimeError("nvcc failed: " + " ".join(cmd))
     if force or _stale(LIB, objs):
         cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(LIB),
-               *map(str, objs), "-lcudart"]
+               *map(str, objs), "-lcudart", "-L", NCCL_LIB, "-l:libnccl.so.2",
+               "-Xlinker", "-rpath=" + NCCL_LIB]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode:
             sys.stderr.write(res.stdout + res.stderr)

@@ -380,7 +380,10 @@ class Network:
     """
 
     def __init__(self, config: SlideConfig, init=None, weight_dtype: str = "f32", max_batch: int = 256,
-                 ctx: Context | None = None):
+                 ctx: Context | None = None, shard: tuple[bytes, int, int] | None = None):
+        """``shard=(unique_id, rank, nranks)`` builds this rank's part of a
+        neuron-sharded network (kl_net_create_sharded); ``unique_id`` comes from
+        klearu_b200.dist.share_unique_id."""
         self.ctx = ctx or default_context()
         self.lib = self.ctx.lib
         self.config = config
@@ -406,7 +409,14 @@ class Network:
                 keep.append(k2)
                 init_arr[i].hash = hp
         h = C.c_void_p()
-        check(self.lib.kl_net_create(self.ctx.h, C.byref(cfg), init_arr, C.byref(h)), self.ctx.h, "kl_net_create")
+        if shard is None:
+            check(self.lib.kl_net_create(self.ctx.h, C.byref(cfg), init_arr, C.byref(h)), self.ctx.h,
+                  "kl_net_create")
+        else:
+            uid, rank, nranks = shard
+            idbuf = C.create_string_buffer(bytes(uid), len(uid))
+            check(self.lib.kl_net_create_sharded(self.ctx.h, C.byref(cfg), init_arr, idbuf, int(rank), int(nranks),
+                                                 C.byref(h)), self.ctx.h, "kl_net_create_sharded")
         self.h = h
         self.num_layers = len(config.network.layers)
 
@@ -417,6 +427,13 @@ class Network:
     @property
     def _dev(self) -> str:
         return f"cuda:{self.ctx.device}"
+
+    def shard_info(self) -> tuple[int, int, int, int]:
+        """(rank, nranks, global id of the first local output neuron, local output neurons)."""
+        r, n, nl = C.c_int(), C.c_int(), C.c_int()
+        base = C.c_uint32()
+        check(self.lib.kl_net_shard_info(self.h, C.byref(r), C.byref(n), C.byref(base), C.byref(nl)))
+        return r.value, n.value, base.value, nl.value
 
     @property
     def step(self) -> int:
@@ -446,6 +463,14 @@ class Network:
         out = C.c_float()
         m = _lib.MODE_EXACT_SEQUENTIAL if mode == "exact" else _lib.MODE_BATCHED
         check(self.lib.kl_net_train_step(self.h, C.byref(db.c), float(lr), m, None, C.byref(out)),
+              self.ctx.h, "kl_net_train_step")
+        return out.value
+
+    def train_step_host(self, hb: HostBatch, lr: float, mode=_lib.MODE_BATCHED) -> float:
+        """One train step on a host CSR batch; returns the mean loss."""
+        db = self.device_batch(hb)
+        out = C.c_float()
+        check(self.lib.kl_net_train_step(self.h, C.byref(db.c), float(lr), mode, None, C.byref(out)),
               self.ctx.h, "kl_net_train_step")
         return out.value
 

@@ -16,6 +16,10 @@
 #include <string>
 #include <vector>
 
+#include <nccl.h>
+
+#include <functional>
+
 #include "engine.h"
 
 using namespace kl;
@@ -806,6 +810,7 @@ struct Layer {
   int stride = 0;    // max active per example
   int nchunk = 0;
   int id_bits = 0;
+  uint32_t id_base = 0;  // global id of row 0 (the rank's slice of a sharded output layer)
   DBuf W, b, m, v, mb, vb;
   std::shared_ptr<IndexImpl> index;
   // per-step buffers
@@ -825,6 +830,11 @@ struct Layer {
 
 }  // namespace
 
+// Per-example capacities of the sharded batch exchange (input nnz, labels).
+#define KL_SHARD_NNZ_PER_EXAMPLE_H 512
+#define KL_SHARD_LABELS_PER_EXAMPLE_H 32
+void nccl_ck(ncclResult_t r, const char* what);
+
 struct kl_net_s {
   kl_ctx_t ctx;
   kl_net_config cfg{};
@@ -836,6 +846,13 @@ struct kl_net_s {
   Scheduler sched;
   DBuf labprob, loss_acc, rb_bkt, rb_scratch;
   size_t labprob_cap = 0;
+  // neuron sharding of the output layer (kl_net_create_sharded)
+  int rank = 0, nranks = 1;
+  ncclComm_t comm = nullptr;
+  int rank_batch = 0;             // examples per rank per step (cfg max_batch)
+  int nnz_cap = 0, lab_cap = 0;   // per-rank capacities of the batch exchange
+  ShardLayout shl{};
+  DBuf dsend, drecv, g_rowptr, g_idx, g_val, g_lptr, g_labels, gcnt, tmask_all;
   std::vector<std::unique_ptr<kl_index_s>> index_handles;
 
   // Phase profiler: CUDA events on the context stream around each phase of
@@ -886,6 +903,7 @@ struct kl_net_s {
     ~Phase() { n->prof_end(i); }
   };
   ~kl_net_s() {
+    if (comm) ncclCommDestroy(comm);
     for (auto& e : pending) pool.emplace_back(e.a, e.b);
     for (auto& e : pool) {
       cudaEventDestroy(e.first);
@@ -952,10 +970,20 @@ struct kl_net_s {
   // pointer offset: CSR offsets stay absolute).  train=true also computes
   // the loss gradient in the output layer.
   void forward(const kl_batch& b, int s0, int nq, bool train) {
+    for (int l = 0; l < (int)layers.size(); ++l) forward_layer(l, b, s0, nq, train);
+  }
+
+  // One layer of the forward.  Layer 0 reads examples [s0, s0+nq) of the batch
+  // and writes its activations to rows [hrow0, hrow0+nq) of its h; later
+  // layers read rows [0, nq) of the previous layer's h.  `after_probe` runs
+  // between the probe and the active-row kernels (the sharded step's global
+  // empty-selection fallback).
+  void forward_layer(int l, const kl_batch& b, int s0, int nq, bool train, int hrow0 = 0,
+                     const std::function<void(Layer&)>& after_probe = nullptr) {
     cudaStream_t st = ctx->stream;
     const int nL = (int)layers.size();
     SparseIn in{b.rowptr + s0, b.idx, b.val, nq};
-    for (int l = 0; l < nL; ++l) {
+    {
       Layer& L = *layers[l];
       const bool last = l == nL - 1;
       IndexImpl& I = *L.index;
@@ -994,14 +1022,16 @@ struct kl_net_s {
       pa.out_n = L.cnt.as<int32_t>();
       pa.err = ctx->err.as<int>();
       pa.stat_active = L.stats.as<unsigned long long>();
+      pa.fallback = !(last && nranks > 1);
       launch_probe(pa, st);
       ck_launch("probe");
+      if (after_probe) after_probe(L);
       ph_hash.~Phase();
       new (&ph_hash) Phase(this, l, KL_PHASE_FORWARD);
       float* hout = nullptr;
       if (!last) {
-        ck(cudaMemsetAsync(L.h.p, 0, (size_t)nq * L.ldN * 4, st), "memset");
-        hout = L.h.as<float>();
+        hout = L.h.as<float>() + (size_t)hrow0 * L.ldN;
+        ck(cudaMemsetAsync(hout, 0, (size_t)nq * L.ldN * 4, st), "memset");
       }
       const ActiveSet A = L.act();
       if (L.fm) {
@@ -1032,6 +1062,7 @@ struct kl_net_s {
         ra.labels = b.labels;
         ra.labprob = labprob.as<float>();
         ra.err = ctx->err.as<int>();
+        ra.id_base = L.id_base;
         const bool softmax = L.cfg.activation == KL_ACT_SOFTMAX;
         const bool fused = last && train && !softmax;
         launch_rm_forward(ra, nq, fused ? RM_FUSED : RM_FWD, st);
@@ -1100,6 +1131,15 @@ struct kl_net_s {
       }
     }
     // optimizer updates (every gradient above used the pre-update weights)
+    update_layers(b, s0, nq, lr);
+  }
+
+  // Optimizer updates of every layer for examples [s0, s0+nq) of the batch.
+  void update_layers(const kl_batch& b, int s0, int nq, double lr) {
+    cudaStream_t st = ctx->stream;
+    const int nL = (int)layers.size();
+    const OptStep o = opt_step(lr);
+    SparseIn in{b.rowptr + s0, b.idx, b.val, nq};
     for (int l = nL - 1; l >= 0; --l) {
       Phase ph(this, l, KL_PHASE_UPDATE);
       Layer& L = *layers[l];
@@ -1129,6 +1169,94 @@ struct kl_net_s {
         ck_launch("rm update");
       }
     }
+  }
+
+  // One batched train step of a neuron-sharded network (nranks > 1).  `lb`
+  // holds this rank's B examples; the global batch is the P*B examples of all
+  // ranks in rank order.  Collectives, all on the context stream:
+  //  (1) all-gather of the packed batches (inputs and labels);
+  //  (2) all-gather of the hidden activations (data-parallel hidden forward);
+  //  (3) all-reduce of each example's number of selected candidates (global
+  //      empty-selection fallback);
+  //  (4) one group: all-reduce of the label probabilities (the loss) and
+  //      reduce-scatter of the output layer's input gradient;
+  //  (5) one group: all-gather of the hidden local gradients and touched masks.
+  // The replicated hidden layer then applies the same update on every rank.
+  void train_sharded(const kl_batch& lb, double lr) {
+    cudaStream_t st = ctx->stream;
+    const int P = nranks, B = lb.batch, PB = P * B;
+    if (lb.nnz > nnz_cap || lb.nlabels > lab_cap)
+      raise(KL_ECAPACITY, "sharded train_step: batch exceeds the exchange capacity (" +
+                              std::to_string(KL_SHARD_NNZ_PER_EXAMPLE_H) + " nnz and " +
+                              std::to_string(KL_SHARD_LABELS_PER_EXAMPLE_H) + " labels per example)");
+    Layer& H = *layers[0];
+    Layer& O = *layers[1];
+    // (1) the global batch
+    launch_shard_pack(dsend.as<uint32_t>(), shl, lb, st);
+    ck_launch("shard pack");
+    nccl_ck(ncclAllGather(dsend.p, drecv.p, (size_t)shl.words, ncclUint32, comm, st), "all-gather batches");
+    launch_shard_unpack(drecv.as<uint32_t>(), shl, P, B, g_rowptr.as<int32_t>(), g_idx.as<uint32_t>(),
+                        g_val.as<float>(), g_lptr.as<int32_t>(), g_labels.as<uint32_t>(), ctx->err.as<int>(), st);
+    ck_launch("shard unpack");
+    kl_batch gb{};
+    gb.batch = PB;
+    gb.rowptr = g_rowptr.as<int32_t>();
+    gb.idx = g_idx.as<uint32_t>();
+    gb.val = g_val.as<float>();
+    gb.label_ptr = g_lptr.as<int32_t>();
+    gb.labels = g_labels.as<uint32_t>();
+    gb.nnz = P * nnz_cap;
+    gb.nlabels = P * lab_cap;
+    ck(cudaMemsetAsync(loss_acc.p, 0, 4, st), "memset");
+    ck(cudaMemsetAsync(labprob.p, 0, (size_t)P * lab_cap * 4, st), "memset");
+    // (2) hidden forward of this rank's examples, then every rank's activations
+    forward_layer(0, gb, rank * B, B, true, rank * B);
+    {
+      float* h = H.h.as<float>();
+      nccl_ck(ncclAllGather(h + (size_t)rank * B * H.ldN, h, (size_t)B * H.ldN, ncclFloat32, comm, st),
+              "all-gather hidden activations");
+    }
+    // output forward over the global batch; (3) between probe and forward
+    forward_layer(1, gb, 0, PB, true, 0, [&](Layer& L) {
+      ck(cudaMemcpyAsync(gcnt.p, L.cnt.p, (size_t)PB * 4, cudaMemcpyDeviceToDevice, st), "copy counts");
+      nccl_ck(ncclAllReduce(gcnt.p, gcnt.p, (size_t)PB, ncclInt32, ncclSum, comm, st), "all-reduce selections");
+      launch_shard_fallback(L.act(), gcnt.as<int32_t>(), L.N, PB, ctx->err.as<int>(), st);
+      ck_launch("shard fallback");
+    });
+    // (4) loss probabilities and the output layer's input gradient
+    {
+      Phase ph(this, 1, KL_PHASE_BACKWARD);
+      launch_reduce_dx(O.dxpart.as<float>(), O.nchunk, O.ldd, O.d, O.cnt.as<int32_t>(), O.dx_in.as<float>(), PB, st);
+      ck_launch("reduce dx");
+      float* dx = O.dx_in.as<float>();
+      nccl_ck(ncclGroupStart(), "group");
+      nccl_ck(ncclAllReduce(labprob.p, labprob.p, (size_t)P * lab_cap, ncclFloat32, ncclSum, comm, st),
+              "all-reduce label probabilities");
+      nccl_ck(ncclReduceScatter(dx, dx + (size_t)rank * B * O.ldd, (size_t)B * O.ldd, ncclFloat32, ncclSum, comm, st),
+              "reduce-scatter input gradient");
+      nccl_ck(ncclGroupEnd(), "group");
+    }
+    launch_loss(gb.label_ptr, labprob.as<float>(), PB, loss_acc.as<float>(), st);
+    ck_launch("loss");
+    // hidden local gradients of this rank's examples; (5) everyone's
+    {
+      Phase ph(this, 0, KL_PHASE_BACKWARD);
+      const int nw = (int)ceil_div(H.N, 32);
+      ck(cudaMemsetAsync(H.lgd.p, 0, (size_t)PB * H.ldN * 4, st), "memset");
+      ck(cudaMemsetAsync(H.tmask.p, 0, (size_t)nw * 4, st), "memset");
+      float* lgd = H.lgd.as<float>();
+      launch_local_grads(H.act(), H.cfg.activation, O.dx_in.as<float>() + (size_t)rank * B * O.ldd, O.ldd,
+                         lgd + (size_t)rank * B * H.ldN, H.ldN, H.tmask.as<uint32_t>(), B, st);
+      ck_launch("local grads");
+      nccl_ck(ncclGroupStart(), "group");
+      nccl_ck(ncclAllGather(lgd + (size_t)rank * B * H.ldN, lgd, (size_t)B * H.ldN, ncclFloat32, comm, st),
+              "all-gather hidden gradients");
+      nccl_ck(ncclAllGather(H.tmask.p, tmask_all.p, (size_t)nw, ncclUint32, comm, st), "all-gather touched masks");
+      nccl_ck(ncclGroupEnd(), "group");
+      launch_shard_or_masks(H.tmask.as<uint32_t>(), tmask_all.as<uint32_t>(), P, nw, st);
+      ck_launch("or masks");
+    }
+    update_layers(gb, 0, PB, lr);
   }
 
   // Per-batch buffers grow geometrically (x1.5) so that a stream of batches
@@ -1162,7 +1290,10 @@ void validate_batch(const kl_net_s* net, const kl_batch* b) {
   if (b->nlabels > 0) require(b->labels != nullptr, "batch labels required");
 }
 
-void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_init* init) {
+// `id_base`: global id of this layer's first neuron (the rank's slice of a
+// sharded output layer; 0 otherwise).  Explicit init rows are the slice's own.
+void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_init* init,
+                 uint32_t id_base = 0) {
   kl_ctx_t ctx = net->ctx;
   cudaStream_t st = ctx->stream;
   auto Lp = std::make_unique<Layer>();
@@ -1224,7 +1355,7 @@ void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_
       rows.resize((size_t)L.N * L.d);
       const double sd = std::sqrt(2.0 / (double)L.d);
       for (int n = 0; n < L.N; ++n) {
-        SplitMix rng{lseed + (uint64_t)n};
+        SplitMix rng{lseed + (uint64_t)id_base + (uint64_t)n};
         for (int i = 0; i < L.d; ++i) rows[(size_t)n * L.d + i] = (float)(rng.normal() * sd);
       }
       src = rows.data();
@@ -1288,16 +1419,24 @@ void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_
   }
   L.stats.alloc(3 * 8);
   ck(cudaMemsetAsync(L.stats.p, 0, 24, st), "memset");
+  L.id_base = id_base;
   net->layers.push_back(std::move(Lp));
 }
 
 }  // namespace
 
-extern "C" kl_status kl_net_create(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init* init,
-                                   kl_net_t* out) {
-  if (!ctx || !cfg || !out) return KL_EINVAL;
-  KL_API_BEGIN(ctx)
-  *out = nullptr;
+void nccl_ck(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) raise(KL_ENCCL, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+namespace {
+constexpr int KL_SHARD_NNZ_PER_EXAMPLE = KL_SHARD_NNZ_PER_EXAMPLE_H;
+constexpr int KL_SHARD_LABELS_PER_EXAMPLE = KL_SHARD_LABELS_PER_EXAMPLE_H;
+
+// Shared body of kl_net_create (nranks == 1, no communicator) and
+// kl_net_create_sharded.
+kl_net_s* create_net(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init* init, const void* unique_id,
+                     int rank, int nranks) {
   require(cfg->num_layers >= 1 && cfg->layers, "net: at least one layer required");
   support(cfg->num_layers >= 2, "net: single-layer networks are not supported (layer 0 is the sparse-input layer)");
   require(cfg->optimizer == KL_OPT_SGD || cfg->optimizer == KL_OPT_ADAM, "net: unknown optimizer");
@@ -1306,14 +1445,50 @@ extern "C" kl_status kl_net_create(kl_ctx_t ctx, const kl_net_config* cfg, const
   for (int l = 1; l < cfg->num_layers; ++l)
     require(cfg->layers[l].input_dim == cfg->layers[l - 1].num_neurons,
             "net: layer input_dim must equal the previous layer's num_neurons");
+  require(nranks >= 1 && rank >= 0 && rank < nranks, "sharded net: rank must be in [0, nranks)");
+  const int nl = cfg->num_layers;
+  if (nranks > 1) {
+    const kl_layer_config& o = cfg->layers[nl - 1];
+    support(nl == 2, "sharded net: exactly two layers (sparse-input hidden layer + sharded output layer)");
+    support(o.activation != KL_ACT_SOFTMAX, "sharded net: softmax output layers are not supported");
+    support(o.num_neurons >= nranks, "sharded net: fewer output neurons than ranks");
+    const int cap_shard = std::max(1, o.lsh.bucket_capacity / nranks);
+    const int64_t M = (int64_t)o.lsh.num_tables * cap_shard * nranks;  // candidates per example, all shards
+    support(o.sampling == KL_SAMPLING_VANILLA || (o.sampling == KL_SAMPLING_TOPK && o.top_k >= M),
+            "sharded net: output sampling must select every candidate (Vanilla, or TopK with top_k >= "
+            "num_tables * bucket_capacity)");
+    require(cfg->max_batch <= 4096 / nranks, "sharded net: nranks * max_batch must be <= 4096");
+  }
   std::unique_ptr<kl_net_s> net(new kl_net_s());
   net->ctx = ctx;
   net->cfg = *cfg;
-  net->layer_cfgs.assign(cfg->layers, cfg->layers + cfg->num_layers);
+  net->layer_cfgs.assign(cfg->layers, cfg->layers + nl);
   net->cfg.layers = net->layer_cfgs.data();
   net->wdtype = cfg->weight_dtype;
-  net->max_batch = cfg->max_batch;
-  for (int l = 0; l < cfg->num_layers; ++l) build_layer(net.get(), l, cfg->layers[l], init ? &init[l] : nullptr);
+  net->rank = rank;
+  net->nranks = nranks;
+  net->rank_batch = cfg->max_batch;
+  net->max_batch = cfg->max_batch * nranks;  // per-step buffers hold the global batch
+  for (int l = 0; l < nl; ++l) {
+    const kl_layer_init* li = init ? &init[l] : nullptr;
+    if (nranks > 1 && l == nl - 1) {
+      // this rank's contiguous slice [lo, hi) of the output neurons, buckets of cap / P ids
+      kl_layer_config c = cfg->layers[l];
+      const uint32_t lo = (uint32_t)(((uint64_t)rank * c.num_neurons) / nranks);
+      const uint32_t hi = (uint32_t)(((uint64_t)(rank + 1) * c.num_neurons) / nranks);
+      c.num_neurons = (int32_t)(hi - lo);
+      c.lsh.bucket_capacity = std::max(1, c.lsh.bucket_capacity / nranks);
+      kl_layer_init sl{};
+      if (li) {
+        sl = *li;
+        if (li->weights) sl.weights = li->weights + (size_t)lo * c.input_dim;
+        if (li->bias) sl.bias = li->bias + lo;
+      }
+      build_layer(net.get(), l, c, li ? &sl : nullptr, lo);
+    } else {
+      build_layer(net.get(), l, cfg->layers[l], li);
+    }
+  }
   // Layer::new inserts every neuron in id order (layer.rs:42-44)
   for (auto& L : net->layers) {
     net->rebuild_layer(*L);
@@ -1325,8 +1500,40 @@ extern "C" kl_status kl_net_create(kl_ctx_t ctx, const kl_net_config* cfg, const
   net->sched.next = net->sched.base;
   net->loss_acc.alloc(4);
   net->labprob.alloc(4);
+  if (nranks > 1) {
+    const int B = net->rank_batch, P = nranks;
+    net->nnz_cap = B * KL_SHARD_NNZ_PER_EXAMPLE;
+    net->lab_cap = B * KL_SHARD_LABELS_PER_EXAMPLE;
+    net->shl = shard_layout(B, net->nnz_cap, net->lab_cap);
+    net->dsend.alloc((size_t)net->shl.words * 4);
+    net->drecv.alloc((size_t)net->shl.words * 4 * P);
+    net->g_rowptr.alloc((size_t)(P * B + 1) * 4);
+    net->g_lptr.alloc((size_t)(P * B + 1) * 4);
+    net->g_idx.alloc((size_t)P * net->nnz_cap * 4);
+    net->g_val.alloc((size_t)P * net->nnz_cap * 4);
+    net->g_labels.alloc((size_t)P * net->lab_cap * 4);
+    net->gcnt.alloc((size_t)P * B * 4);
+    net->tmask_all.alloc((size_t)P * ceil_div(net->layers[0]->N, 32) * 4);
+    kl_batch cap_b{};
+    cap_b.batch = P * B;
+    cap_b.nnz = P * net->nnz_cap;
+    cap_b.nlabels = P * net->lab_cap;
+    net->ensure_batch_buffers(cap_b);
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof(id));
+    nccl_ck(ncclCommInitRank(&net->comm, nranks, id, rank), "ncclCommInitRank");
+  }
   ck(cudaStreamSynchronize(ctx->stream), "sync");
-  *out = net.release();
+  return net.release();
+}
+}  // namespace
+
+extern "C" kl_status kl_net_create(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init* init,
+                                   kl_net_t* out) {
+  if (!ctx || !cfg || !out) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  *out = nullptr;
+  *out = create_net(ctx, cfg, init, nullptr, 0, 1);
   KL_API_END
 }
 
@@ -1360,6 +1567,13 @@ extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double l
     if (loss_host) *loss_host = 0.0f;
     return KL_OK;
   }
+  int loss_div = b->batch;
+  if (net->nranks > 1) {
+    support(mode == KL_MODE_BATCHED, "sharded net: only KL_MODE_BATCHED train steps");
+    require(b->batch <= net->rank_batch, "sharded train_step: batch exceeds max_batch");
+    net->train_sharded(*b, lr);
+    loss_div = b->batch * net->nranks;
+  } else {
   net->ensure_batch_buffers(*b);
   ck(cudaMemsetAsync(net->loss_acc.p, 0, 4, st), "memset");
   ck(cudaMemsetAsync(net->labprob.p, 0, (size_t)std::max(b->nlabels, 1) * 4, st), "memset");
@@ -1376,7 +1590,8 @@ extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double l
       net->backward(*b, s, 1, lr);
     }
   }
-  loss_final_kernel<<<1, 1, 0, st>>>(net->loss_acc.as<float>(), b->batch, loss, net->loss_acc.as<float>());
+  }
+  loss_final_kernel<<<1, 1, 0, st>>>(net->loss_acc.as<float>(), loss_div, loss, net->loss_acc.as<float>());
   ck_launch("loss final");
   for (auto& L : net->layers) {
     L->examples += (uint64_t)b->batch;
@@ -1396,6 +1611,7 @@ extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double l
 extern "C" kl_status kl_net_forward(kl_net_t net, const kl_batch* b) {
   if (!net) return KL_EINVAL;
   KL_API_BEGIN(net->ctx)
+  support(net->nranks == 1, "sharded net: forward without a train step is not supported");
   validate_batch(net, b);
   if (b->batch == 0) return KL_OK;
   net->ensure_batch_buffers(*b);
@@ -1432,6 +1648,7 @@ extern "C" kl_status kl_net_predict_topk(kl_net_t net, const kl_batch* b, int k,
                                          float* top_scores) {
   if (!net) return KL_EINVAL;
   KL_API_BEGIN(net->ctx)
+  support(net->nranks == 1, "sharded net: predict_top_k is not supported");
   validate_batch(net, b);
   require(k >= 0 && (k == 0 || top_ids), "predict_topk: bad arguments");
   if (b->batch == 0 || k == 0) return KL_OK;
@@ -1581,21 +1798,30 @@ extern "C" kl_status kl_launch_count(uint64_t* count_host) {
 // ===========================================================================
 // Neuron sharding over NCCL: not available in this build configuration.
 // ===========================================================================
-extern "C" int kl_dist_unique_id_size(void) { return 128; }
+extern "C" int kl_dist_unique_id_size(void) { return (int)sizeof(ncclUniqueId); }
 extern "C" kl_status kl_dist_get_unique_id(void* id_host) {
-  (void)id_host;
-  return KL_EUNSUPPORTED;
+  if (!id_host) return KL_EINVAL;
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return KL_ENCCL;
+  std::memcpy(id_host, &id, sizeof(id));
+  return KL_OK;
 }
 extern "C" kl_status kl_net_create_sharded(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init* init,
                                            const void* unique_id, int rank, int nranks, kl_net_t* out) {
-  (void)cfg;
-  (void)init;
-  (void)unique_id;
-  (void)rank;
-  (void)nranks;
-  if (out) *out = nullptr;
-  if (ctx) ctx->last_error = "sharded networks are not built yet";
-  return KL_EUNSUPPORTED;
+  if (!ctx || !cfg || !out || !unique_id) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  *out = nullptr;
+  *out = create_net(ctx, cfg, init, unique_id, rank, nranks);
+  KL_API_END
+}
+extern "C" kl_status kl_net_shard_info(kl_net_t net, int* rank_host, int* nranks_host, uint32_t* id_base_host,
+                                       int* num_local_host) {
+  if (!net) return KL_EINVAL;
+  if (rank_host) *rank_host = net->rank;
+  if (nranks_host) *nranks_host = net->nranks;
+  if (id_base_host) *id_base_host = net->layers.back()->id_base;
+  if (num_local_host) *num_local_host = net->layers.back()->N;
+  return KL_OK;
 }
 
 // ===========================================================================

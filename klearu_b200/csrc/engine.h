@@ -112,6 +112,7 @@ struct ProbeArgs {
   int* err = nullptr;
   unsigned long long* stat_active = nullptr;  // nullable: += sum of sizes
   int maxm = 0;       // set by launch_probe
+  bool fallback = true;  // empty selection -> every neuron (layer.rs:82-84); off on a shard
   int mode = 0;       // set by launch_probe: 0 radix sort, 1 small-N count array, 2 bitmap (all selected)
 };
 int probe_max_items();  // largest L*cap the probe kernel holds in shared memory
@@ -171,6 +172,7 @@ struct RmArgs {
   const uint32_t* labels;
   float* labprob;
   int* err;
+  uint32_t id_base;   // global id of local row 0 (neuron-sharded output layer; labels are global)
 };
 void launch_rm_forward(const RmArgs& a, int nq, int mode, cudaStream_t st);
 // dX[s][k] = sum over chunks of dxpart (chunk order).
@@ -240,5 +242,21 @@ void launch_w_to_f32(const void* src, int wdtype, int64_t ld_src, bool transpose
                      int64_t n_rows, int d, cudaStream_t st);
 void launch_f32_to_w(const float* src, int64_t n_rows, int d, int64_t ld_src, void* dst,
                      int wdtype, int64_t ld_dst, bool transpose, cudaStream_t st);
+
+
+// ---------------------------------------------------------------------------
+// Neuron-sharded train step (shard.cu).  A rank's batch is packed into a
+// fixed layout of 32-bit words so that NCCL can all-gather equal-size blocks.
+// ---------------------------------------------------------------------------
+struct ShardLayout {
+  int rowptr = 0, lptr = 0, idx = 0, val = 0, labels = 0, words = 0;  // word offsets / block size
+};
+ShardLayout shard_layout(int max_batch, int nnz_cap, int lab_cap);
+void launch_shard_pack(uint32_t* send, const ShardLayout& Ly, const kl_batch& b, cudaStream_t st);
+void launch_shard_unpack(const uint32_t* recv, const ShardLayout& Ly, int P, int B, int32_t* g_rowptr,
+                         uint32_t* g_idx, float* g_val, int32_t* g_lptr, uint32_t* g_labels, int* err,
+                         cudaStream_t st);
+void launch_shard_fallback(ActiveSet A, const int32_t* gcnt, int n_local, int nq, int* err, cudaStream_t st);
+void launch_shard_or_masks(uint32_t* tmask, const uint32_t* all, int P, int nw, cudaStream_t st);
 
 }  // namespace kl

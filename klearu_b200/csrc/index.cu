@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(PB_NT) probe_kernel(ProbeArgs a) {
     int pos = block_excl_scan<PB_NT>(c, S.tmp, &nsel);
     uint32_t* out_ids = a.out_ids + (int64_t)q * a.out_stride;
     int nout;
-    if (nsel == 0) {
+    if (nsel == 0 && a.fallback) {
       // fallback: every neuron (layer.rs:82-84)
       nout = min(a.N, a.out_stride);
       if (a.N > a.out_stride && threadIdx.x == 0) atomicOr(a.err, DERR_CAPACITY);
@@ -509,7 +509,7 @@ __global__ void __launch_bounds__(PB_NT) probe_kernel(ProbeArgs a) {
   uint32_t* out_ids = a.out_ids + (int64_t)q * a.out_stride;
   uint32_t* out_cnt = a.out_counts ? a.out_counts + (int64_t)q * a.out_stride : nullptr;
   int nout = 0;
-  if (net && nsel == 0) {
+  if (net && nsel == 0 && a.fallback) {
     // fallback: every neuron (layer.rs:82-84)
     nout = a.N;
     if (nout > a.out_stride) {

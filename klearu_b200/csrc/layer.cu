@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
         } else {
           const float lw = __fdiv_rn(1.0f, (float)(le - lb));
           for (int j = lb; j < le; ++j) {
-            if (a.labels[j] == myid) {
+            if (a.labels[j] == myid + a.id_base) {
               g = __fsub_rn(g, lw);
               a.labprob[j] = post;
             }

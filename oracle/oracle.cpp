@@ -1060,7 +1060,8 @@ void orc_optimizer_update(int opt, float* w, const float* g, int d, float* bias,
 
 // ---- network ----
 // nshards > 1: the LAST layer's index is split into nshards indices over
-// contiguous neuron slices [r*N/P, (r+1)*N/P) sharing one hash family.
+// contiguous neuron slices [r*N/P, (r+1)*N/P) sharing one hash family, each
+// with bucket capacity cap / P.
 void* orc_net_create(const kl_net_config* cfg, const kl_layer_init* init, int nshards, int sparse_input) {
   auto* net = new Net();
   net->opt = cfg->optimizer;
@@ -1092,7 +1093,10 @@ void* orc_net_create(const kl_net_config* cfg, const kl_layer_init* init, int ns
     int P = (l == cfg->num_layers - 1) ? std::max(1, nshards) : 1;
     for (int r = 0; r <= P; ++r) L.shard_lo.push_back((uint32_t)(((uint64_t)r * L.N) / P));
     L.shards.reserve(P);
-    for (int r = 0; r < P; ++r) L.shards.emplace_back(h, lc.bucket_type, lc.bucket_capacity);
+    // Sharded: each shard's buckets hold cap / P ids (at least 1), so a
+    // sample's candidate budget over all shards stays L * cap, as unsharded.
+    const int shard_cap = P > 1 ? std::max(1, lc.bucket_capacity / P) : lc.bucket_capacity;
+    for (int r = 0; r < P; ++r) L.shards.emplace_back(h, lc.bucket_type, shard_cap);
     L.build_index();
   }
   const kl_lsh_config& l0 = cfg->layers[0].lsh;

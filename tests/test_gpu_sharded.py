@@ -1,0 +1,106 @@
+"""Neuron-sharded network on 2 GPUs (one process each) vs the CPU oracle's
+2-shard network trained on the same global batch.
+
+Bar: the per-step loss within 1e-4 relative on every rank; the replicated
+hidden layer and each rank's slice of the output layer within the network
+tests' tolerance (1e-3 relative, 1e-6 absolute; one bf16 ulp for weights).
+Needs two GPUs: skipped on a one-GPU box.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-3, 1e-6
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cfg():
+    from klearu_b200 import synthetic as S
+    from klearu_b200.config import LshConfig
+
+    # output TopK = n_out / 10 = 500 >= num_tables * bucket_capacity = 320: every candidate is selected
+    return S.config_xc(d_in=2000, hidden=64, n_out=5000, out_l=10, cap=32,
+                       hidden_lsh=LshConfig(num_tables=10, num_hashes=6), rebuild_base=2, rebuild_decay=0.1)
+
+
+def _close(a, b, bf16_weights=False):
+    if bf16_weights:
+        return not (np.abs(a - b) > np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -7 + ATOL).any()
+    return not (np.abs(a - b) > RTOL * np.abs(b) + ATOL).any()
+
+
+def _worker(rank, world, port, dtype, out):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from klearu_b200 import synthetic as S
+        from klearu_b200.core import Context, Network
+        from klearu_b200.dist import rank_slice, share_unique_id
+
+        cfg = _cfg()
+        init = S.make_init(cfg, 42)
+        uid = share_unique_id(rank, world)
+        net = Network(cfg, init, weight_dtype=dtype, max_batch=24, ctx=Context(rank), shard=(uid, rank, world))
+        gen = S.XcGenerator(2000, 5000, seed=3, mean_nnz=20)
+        batches = [gen.batch(24 * world) for _ in range(4)]
+        losses = [net.train_step_host(rank_slice(hb, rank, world), 1e-3) for hb in batches]
+        r, n, base, nloc = net.shard_info()
+        res = {"losses": losses, "hidden": net.get_layer(0), "out": net.get_layer(1), "base": base, "n": nloc,
+               "step": net.step}
+        gathered = [None] * world
+        dist.all_gather_object(gathered, res)
+        if rank == 0:
+            import oracle
+
+            o = oracle.Net(cfg, init, weight_dtype=dtype, nshards=world)
+            ol = [o.train_step(hb, 1e-3, mode="batched") for hb in batches]
+            msgs = []
+            oh, oo = o.get_layer(0), o.get_layer(1)
+            for rr, g in enumerate(gathered):
+                if g["step"] != 4:
+                    msgs.append(f"rank {rr}: step {g['step']}")
+                for i, (a, b) in enumerate(zip(g["losses"], ol)):
+                    if abs(a - b) > 1e-4 * abs(b) + 1e-6:
+                        msgs.append(f"rank {rr} step {i}: loss {a} vs oracle {b}")
+                lo, hi = g["base"], g["base"] + g["n"]
+                for k in ("weights", "bias", "m", "v", "mb", "vb"):
+                    if not _close(g["hidden"][k], oh[k], dtype == "bf16" and k == "weights"):
+                        msgs.append(f"rank {rr}: hidden {k} differs")
+                    if not _close(g["out"][k], oo[k][lo:hi], dtype == "bf16" and k == "weights"):
+                        msgs.append(f"rank {rr}: output {k} [{lo}, {hi}) differs")
+            out.put(msgs)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_sharded_two_gpus_match_oracle(dtype):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, dtype, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    msgs = q.get(timeout=600)
+    for p in ps:
+        p.join(120)
+        assert p.exitcode == 0
+    assert not msgs, "\n".join(msgs)
