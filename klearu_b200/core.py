@@ -532,8 +532,10 @@ class Network:
 
     # -- state ------------------------------------------------------------
     def get_layer(self, layer: int) -> dict:
-        lc = self.config.network.layers[layer]
-        N, d = lc.num_neurons, lc.input_dim
+        """Parameters and optimizer state of `layer` (a sharded output layer: this rank's slice)."""
+        dd, nn, ma = C.c_int(), C.c_int(), C.c_int()
+        check(self.lib.kl_net_layer_info(self.h, layer, C.byref(dd), C.byref(nn), C.byref(ma)), self.ctx.h)
+        N, d = nn.value, dd.value
         out = {k: np.empty((N, d), np.float32) for k in ("weights", "m", "v")}
         out.update({k: np.empty(N, np.float32) for k in ("bias", "mb", "vb")})
         check(self.lib.kl_net_get_layer(self.h, layer, *(out[k].ctypes.data for k in

@@ -49,44 +49,55 @@ def _worker(rank, world, port, dtype, out):
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        from klearu_b200 import synthetic as S
-        from klearu_b200.core import Context, Network
-        from klearu_b200.dist import rank_slice, share_unique_id
+        _run(rank, world, dtype, out)
+    except Exception:  # report instead of leaving the parent waiting
+        import traceback
 
-        cfg = _cfg()
-        init = S.make_init(cfg, 42)
-        uid = share_unique_id(rank, world)
-        net = Network(cfg, init, weight_dtype=dtype, max_batch=24, ctx=Context(rank), shard=(uid, rank, world))
-        gen = S.XcGenerator(2000, 5000, seed=3, mean_nnz=20)
-        batches = [gen.batch(24 * world) for _ in range(4)]
-        losses = [net.train_step_host(rank_slice(hb, rank, world), 1e-3) for hb in batches]
-        r, n, base, nloc = net.shard_info()
-        res = {"losses": losses, "hidden": net.get_layer(0), "out": net.get_layer(1), "base": base, "n": nloc,
-               "step": net.step}
-        gathered = [None] * world
-        dist.all_gather_object(gathered, res)
-        if rank == 0:
-            import oracle
-
-            o = oracle.Net(cfg, init, weight_dtype=dtype, nshards=world)
-            ol = [o.train_step(hb, 1e-3, mode="batched") for hb in batches]
-            msgs = []
-            oh, oo = o.get_layer(0), o.get_layer(1)
-            for rr, g in enumerate(gathered):
-                if g["step"] != 4:
-                    msgs.append(f"rank {rr}: step {g['step']}")
-                for i, (a, b) in enumerate(zip(g["losses"], ol)):
-                    if abs(a - b) > 1e-4 * abs(b) + 1e-6:
-                        msgs.append(f"rank {rr} step {i}: loss {a} vs oracle {b}")
-                lo, hi = g["base"], g["base"] + g["n"]
-                for k in ("weights", "bias", "m", "v", "mb", "vb"):
-                    if not _close(g["hidden"][k], oh[k], dtype == "bf16" and k == "weights"):
-                        msgs.append(f"rank {rr}: hidden {k} differs")
-                    if not _close(g["out"][k], oo[k][lo:hi], dtype == "bf16" and k == "weights"):
-                        msgs.append(f"rank {rr}: output {k} [{lo}, {hi}) differs")
-            out.put(msgs)
+        out.put([f"rank {rank}: " + traceback.format_exc()])
+        raise
     finally:
         dist.destroy_process_group()
+
+
+def _run(rank, world, dtype, out):
+    import torch.distributed as dist
+
+    from klearu_b200 import synthetic as S
+    from klearu_b200.core import Context, Network
+    from klearu_b200.dist import rank_slice, share_unique_id
+
+    cfg = _cfg()
+    init = S.make_init(cfg, 42)
+    uid = share_unique_id(rank, world)
+    net = Network(cfg, init, weight_dtype=dtype, max_batch=24, ctx=Context(rank), shard=(uid, rank, world))
+    gen = S.XcGenerator(2000, 5000, seed=3, mean_nnz=20)
+    batches = [gen.batch(24 * world) for _ in range(4)]
+    losses = [net.train_step_host(rank_slice(hb, rank, world), 1e-3) for hb in batches]
+    r, n, base, nloc = net.shard_info()
+    res = {"losses": losses, "hidden": net.get_layer(0), "out": net.get_layer(1), "base": base, "n": nloc,
+           "step": net.step}
+    gathered = [None] * world
+    dist.all_gather_object(gathered, res)
+    if rank == 0:
+        import oracle
+
+        o = oracle.Net(cfg, init, weight_dtype=dtype, nshards=world)
+        ol = [o.train_step(hb, 1e-3, mode="batched") for hb in batches]
+        msgs = []
+        oh, oo = o.get_layer(0), o.get_layer(1)
+        for rr, g in enumerate(gathered):
+            if g["step"] != 4:
+                msgs.append(f"rank {rr}: step {g['step']}")
+            for i, (a, b) in enumerate(zip(g["losses"], ol)):
+                if abs(a - b) > 1e-4 * abs(b) + 1e-6:
+                    msgs.append(f"rank {rr} step {i}: loss {a} vs oracle {b}")
+            lo, hi = g["base"], g["base"] + g["n"]
+            for k in ("weights", "bias", "m", "v", "mb", "vb"):
+                if not _close(g["hidden"][k], oh[k], dtype == "bf16" and k == "weights"):
+                    msgs.append(f"rank {rr}: hidden {k} differs")
+                if not _close(g["out"][k], oo[k][lo:hi], dtype == "bf16" and k == "weights"):
+                    msgs.append(f"rank {rr}: output {k} [{lo}, {hi}) differs")
+        out.put(msgs)
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
@@ -99,7 +110,7 @@ def test_sharded_two_gpus_match_oracle(dtype):
     ps = [ctx.Process(target=_worker, args=(r, 2, port, dtype, q)) for r in range(2)]
     for p in ps:
         p.start()
-    msgs = q.get(timeout=600)
+    msgs = q.get(timeout=240)
     for p in ps:
         p.join(120)
         assert p.exitcode == 0
