@@ -18,8 +18,13 @@ synthetic C1 examples.  Prints ONE JSON line on rank 0.
   host threads) on a bounded sample of the same workload.
 * ``--impl reference``: that CPU path alone, as the reference arm.
 
-Multi-GPU (torchrun, one rank per GPU): every rank trains its own replica on
-its own batches (weak scaling); no data-path collective.
+Multi-GPU (torchrun, one rank per GPU): ONE network, neuron-sharded over the
+ranks (kl_net_create_sharded): each rank owns 1/N of the 670K output neurons
+(rows, Adam state, LSH tables with bucket capacity 128/N) and contributes its
+own B=256 examples to a global batch of N*256 (weak scaling).  The hidden layer
+is replicated and data parallel; NCCL all-gathers the batches, hidden
+activations and hidden gradients, and all-reduces / reduce-scatters the loss
+probabilities and the output layer's input gradient.
 """
 
 from __future__ import annotations
@@ -63,7 +68,7 @@ def workload(cfg, B):
             "input_dim": lo[0].input_dim, "hidden": lo[0].num_neurons, "output": lo[1].num_neurons,
             "hidden_lsh": "SimHash K6 L50 TopK12 FIFO128", "output_lsh": "DWTA K8 L50 FIFO128 (union<=6400)",
             "per_gpu_batch": B, "weights": "bf16 storage, fp32 Adam state",
-            "l2": "working set > L2 (1.03 GB output weights+Adam state per replica)"}
+            "l2": "working set > L2 (1.03 GB of output weights + Adam state in total)"}
 
 
 def measured_peaks():
@@ -181,7 +186,7 @@ def main():
 
     from klearu_b200 import _lib
     from klearu_b200 import synthetic as S
-    from klearu_b200.core import Network
+    from klearu_b200.core import Network, default_context
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -192,7 +197,12 @@ def main():
     B = args.batch
     cfg = S.config_c1()
     init = S.make_init(cfg, 42)
-    net = Network(cfg, init, weight_dtype="bf16", max_batch=B)
+    shard = None
+    if world > 1:
+        from klearu_b200.dist import share_unique_id
+
+        shard = (share_unique_id(rank, world), rank, world)
+    net = Network(cfg, init, weight_dtype="bf16", max_batch=B, shard=shard, ctx=default_context(local))
     del init
     gen = S.XcGenerator(135909, 670091, seed=1234 + rank)
     pool_host = [gen.batch(B) for _ in range(args.pool)]
@@ -201,7 +211,7 @@ def main():
     # allocation happens inside the timed region
     from klearu_b200 import _lib as _L
     import ctypes as _C
-    for db in sorted(pool, key=lambda db: -db.c.nnz)[:1]:
+    for db in (sorted(pool, key=lambda db: -db.c.nnz)[:1] if world == 1 else []):  # sharded nets pre-size
         _L.check(net.lib.kl_net_forward(net.h, _C.byref(db.c)), net.ctx.h)
     torch.cuda.synchronize()
 
@@ -339,7 +349,8 @@ def main():
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {**workload(cfg, B), "global_batch": B * world,
-                           "parallelism": "replicas" if world > 1 else "single"},
+                           "parallelism": f"output neurons sharded over {world} GPUs, hidden layer data parallel"
+                           if world > 1 else "single"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": int(lc1.value - lc0.value), "clocks": clk}
         print(json.dumps(line), flush=True)

@@ -61,7 +61,10 @@ class Context:
             pass
 
 
-def default_context(device: int = 0) -> Context:
+def default_context(device: int | None = None) -> Context:
+    """One shared context per device; `device` None = torch's current device."""
+    if device is None:
+        device = torch.cuda.current_device() if torch.cuda.is_available() else 0
     if device not in _DEFAULT_CTX:
         _DEFAULT_CTX[device] = Context(device)
     return _DEFAULT_CTX[device]
