@@ -245,6 +245,34 @@ KL_API kl_status kl_index_import(kl_index_t ix, const uint32_t* ids, const uint3
                           const uint64_t* counts);
 
 /* ------------------------------------------------------------------------ */
+/* Adaptive rebuild scheduling -- replaces klearu_mongoose::AdaptiveScheduler */
+/* (crates/klearu-mongoose/src/scheduler.rs:44-213)                          */
+/* ------------------------------------------------------------------------ */
+typedef struct kl_adaptive_s* kl_adaptive_t;
+/* AdaptiveScheduler::new (scheduler.rs:53-87); EMA alpha 0.3. */
+KL_API kl_status kl_adaptive_create(kl_ctx_t ctx, uint64_t min_interval, uint64_t max_interval,
+                             float sample_fraction, float drift_threshold, kl_adaptive_t* out);
+KL_API kl_status kl_adaptive_destroy(kl_adaptive_t a);
+/* record_baseline (scheduler.rs:96-129): hash the sampled rows of `rows`
+ * ([n][ld] of `dtype`, device) with `h` and keep their codes.  Sampled row
+ * indices are explicit (`sampled_host`, n_sampled) or, when NULL, the first
+ * ceil(n * sample_fraction) of a shuffle seeded by `seed` (this library's
+ * SplitMix64 stream: rand 0.8.5's StdRng is not reproduced).  Synchronises. */
+KL_API kl_status kl_adaptive_record_baseline(kl_adaptive_t a, kl_hash_t h, const void* rows, int n, int ld,
+                                      int dtype, const uint32_t* sampled_host, int n_sampled,
+                                      uint64_t seed);
+/* should_rebuild (scheduler.rs:133-159) on the current rows; a drift check
+ * (every min_interval steps) hashes the sampled rows on the GPU and
+ * synchronises to read the changed count. */
+KL_API kl_status kl_adaptive_should_rebuild(kl_adaptive_t a, const void* rows, int n, int ld, int dtype,
+                                     int* rebuild_host);
+/* notify_rebuild / drift_estimate / steps_since_rebuild (scheduler.rs:198-211);
+ * n_sampled_host: number of rows in the baseline (baseline_codes.len()). */
+KL_API kl_status kl_adaptive_notify_rebuild(kl_adaptive_t a);
+KL_API kl_status kl_adaptive_state(kl_adaptive_t a, float* drift_ema_host, uint64_t* steps_since_rebuild_host,
+                            int* n_sampled_host);
+
+/* ------------------------------------------------------------------------ */
 /* Network -- replaces klearu_core::network::Network (network/net.rs:10-173) */
 /* ------------------------------------------------------------------------ */
 

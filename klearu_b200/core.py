@@ -349,6 +349,65 @@ def create_lsh_index(config: LshConfig, input_dim: int, seed: int, ctx: Context 
 # Network
 # ---------------------------------------------------------------------------
 @dataclass
+class AdaptiveScheduler:
+    """klearu_mongoose::AdaptiveScheduler (scheduler.rs:44-213): rebuild the
+    LSH tables when the hash codes of sampled neurons have drifted.  Rows are
+    a device tensor [n][d] (f32 or bf16); the drift check runs on the GPU."""
+
+    def __init__(self, min_interval: int, max_interval: int, sample_fraction: float, drift_threshold: float,
+                 ctx: Context | None = None):
+        self.ctx = ctx or default_context()
+        self.lib = self.ctx.lib
+        h = C.c_void_p()
+        check(self.lib.kl_adaptive_create(self.ctx.h, int(min_interval), int(max_interval), float(sample_fraction),
+                                          float(drift_threshold), C.byref(h)), self.ctx.h, "kl_adaptive_create")
+        self.h = h
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.lib.kl_adaptive_destroy(self.h)
+
+    @staticmethod
+    def _rows(rows):
+        dt = _lib.DTYPE_BF16 if rows.dtype == torch.bfloat16 else _lib.DTYPE_F32
+        rows = (rows if dt == _lib.DTYPE_BF16 else rows.float()).contiguous()
+        n = rows.shape[0]
+        ld = rows.shape[1] if rows.dim() == 2 and n else 0
+        return rows, n, ld, dt
+
+    def record_baseline(self, rows: torch.Tensor, hash_fn: HashFamily, seed: int = 0, sampled=None) -> None:
+        rows, n, ld, dt = self._rows(torch.as_tensor(rows).to(f"cuda:{self.ctx.device}"))
+        idx = None if sampled is None else np.ascontiguousarray(np.asarray(sampled, np.uint32))
+        check(self.lib.kl_adaptive_record_baseline(self.h, hash_fn.h, _ptr(rows) if n else None, n, ld, dt,
+                                                   None if idx is None else idx.ctypes.data,
+                                                   0 if idx is None else len(idx), int(seed)),
+              self.ctx.h, "kl_adaptive_record_baseline")
+
+    def should_rebuild(self, rows: torch.Tensor) -> bool:
+        rows, n, ld, dt = self._rows(torch.as_tensor(rows).to(f"cuda:{self.ctx.device}"))
+        out = C.c_int()
+        check(self.lib.kl_adaptive_should_rebuild(self.h, _ptr(rows) if n else None, n, ld, dt, C.byref(out)),
+              self.ctx.h, "kl_adaptive_should_rebuild")
+        return bool(out.value)
+
+    def notify_rebuild(self) -> None:
+        check(self.lib.kl_adaptive_notify_rebuild(self.h))
+
+    def _state(self):
+        e, st, ns = C.c_float(), C.c_uint64(), C.c_int()
+        check(self.lib.kl_adaptive_state(self.h, C.byref(e), C.byref(st), C.byref(ns)))
+        return e.value, st.value, ns.value
+
+    def drift_estimate(self) -> float:
+        return self._state()[0]
+
+    def steps_since_rebuild(self) -> int:
+        return self._state()[1]
+
+    def num_sampled(self) -> int:
+        return self._state()[2]
+
+
 class LayerOutput:  # network/layer.rs:19-26
     activations: np.ndarray
     active_neurons: list

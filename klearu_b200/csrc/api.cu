@@ -6,6 +6,7 @@
 //   Network::train_step -> kl_net_train_step (net.rs:81-119)
 //   Network::forward    -> kl_net_forward  (net.rs:62-78)
 //   RebuildScheduler    -> Scheduler below (lsh/maintenance.rs:70-82)
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -776,6 +777,192 @@ extern "C" kl_status kl_index_import(kl_index_t ix, const uint32_t* ids, const u
   if (counts) ck(cudaMemcpyAsync(I.T.cnt, counts, LB * 8, cudaMemcpyDeviceToDevice, st), "import");
   else ck(cudaMemsetAsync(I.T.cnt, 0, LB * 8, st), "import");
   KL_API_END
+}
+
+// ===========================================================================
+// AdaptiveScheduler (crates/klearu-mongoose/src/scheduler.rs:44-213): the
+// drift check hashes the sampled rows on the GPU and counts, on the GPU, the
+// rows whose code changed in any table; counters, drift and EMA are the
+// reference's host arithmetic (f32).
+// ===========================================================================
+struct kl_adaptive_s {
+  kl_ctx_t ctx;
+  std::shared_ptr<HashImpl> hash;
+  size_t min_interval = 0, max_interval = 0;
+  float sample_fraction = 0.f, drift_threshold = 0.f;
+  float drift_ema = 0.f, ema_alpha = 0.3f;
+  size_t steps_since_rebuild = 0, steps_since_check = 0;
+  int S = 0;  // sampled rows
+  DBuf idx, base, cur, rows, changed;
+};
+
+namespace {
+// rows[i] = f32 copy of row idx[i] (zeros for indices >= n)
+__global__ void adaptive_gather_kernel(const void* X, int dtype, int64_t ld, int n, const uint32_t* idx, int S,
+                                       int d, float* out) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= (int64_t)S * d) return;
+  const int i = (int)(g / d), c = (int)(g % d);
+  const uint32_t r = idx[i];
+  float v = 0.f;
+  if (r < (uint32_t)n) {
+    const int64_t o = (int64_t)r * ld + c;
+    v = dtype == KL_DTYPE_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(X)[o])
+                               : static_cast<const float*>(X)[o];
+  }
+  out[g] = v;
+}
+// changed += number of sampled rows (< n) whose code differs in any table
+__global__ void adaptive_compare_kernel(const uint64_t* cur, const uint64_t* base, const uint32_t* idx, int S,
+                                        int L, int n, int* changed) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= S || idx[i] >= (uint32_t)n) return;
+  bool any = false;
+  for (int t = 0; t < L && !any; ++t) any = cur[(int64_t)i * L + t] != base[(int64_t)i * L + t];
+  if (any) atomicAdd(changed, 1);
+}
+
+void adaptive_hash(kl_adaptive_s* a, const void* rows, int n, int ld, int dtype, DBuf& codes) {
+  cudaStream_t st = a->ctx->stream;
+  const DevHash& h = a->hash->dh;
+  adaptive_gather_kernel<<<(unsigned)ceil_div((int64_t)a->S * h.d, 256), 256, 0, st>>>(
+      rows, dtype, ld, n, a->idx.as<uint32_t>(), a->S, h.d, a->rows.as<float>());
+  count_launch();
+  ck_launch("adaptive gather");
+  DenseIn in;
+  in.X = a->rows.p;
+  in.dtype = KL_DTYPE_F32;
+  in.ld_row = h.d;
+  in.ld_elem = 1;
+  in.n = a->S;
+  HashOut o;
+  o.codes = codes.as<uint64_t>();
+  launch_hash_dense(h, in, o, st);
+  ck_launch("adaptive hash");
+}
+}  // namespace
+
+extern "C" kl_status kl_adaptive_create(kl_ctx_t ctx, uint64_t min_interval, uint64_t max_interval,
+                                        float sample_fraction, float drift_threshold, kl_adaptive_t* out) {
+  if (!ctx || !out) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  *out = nullptr;
+  require(min_interval <= max_interval, "adaptive: min_interval must be <= max_interval (scheduler.rs:61-64)");
+  require(sample_fraction >= 0.f && sample_fraction <= 1.f, "adaptive: sample_fraction must be in [0, 1]");
+  require(drift_threshold >= 0.f && drift_threshold <= 1.f, "adaptive: drift_threshold must be in [0, 1]");
+  auto* a = new kl_adaptive_s();
+  a->ctx = ctx;
+  a->min_interval = (size_t)min_interval;
+  a->max_interval = (size_t)max_interval;
+  a->sample_fraction = sample_fraction;
+  a->drift_threshold = drift_threshold;
+  a->changed.alloc(4);
+  *out = a;
+  KL_API_END
+}
+extern "C" kl_status kl_adaptive_destroy(kl_adaptive_t a) {
+  if (!a) return KL_EINVAL;
+  {
+    DeviceGuard g(a->ctx->device);
+    cudaStreamSynchronize(a->ctx->stream);
+    delete a;
+  }
+  return KL_OK;
+}
+extern "C" kl_status kl_adaptive_record_baseline(kl_adaptive_t a, kl_hash_t h, const void* rows, int n, int ld,
+                                                 int dtype, const uint32_t* sampled_host, int n_sampled,
+                                                 uint64_t seed) {
+  if (!a || !h) return KL_EINVAL;
+  KL_API_BEGIN(a->ctx)
+  require(n >= 0 && (n == 0 || (rows && ld >= h->h->dh.d)), "adaptive: bad rows");
+  require(dtype == KL_DTYPE_F32 || dtype == KL_DTYPE_BF16, "adaptive: dtype must be F32 or BF16");
+  std::vector<uint32_t> idx;
+  if (sampled_host) {
+    require(n_sampled >= 0, "adaptive: n_sampled must be >= 0");
+    idx.assign(sampled_host, sampled_host + n_sampled);
+  } else {
+    // scheduler.rs:104-110: ceil(n * fraction) clamped to [1, n] indices of a
+    // seeded shuffle, sorted (this library's SplitMix64 stream, not StdRng)
+    const size_t S = std::min<size_t>((size_t)n, std::max<size_t>(1, (size_t)std::ceil((float)n * a->sample_fraction)));
+    std::vector<uint32_t> perm((size_t)n);
+    for (int i = 0; i < n; ++i) perm[(size_t)i] = (uint32_t)i;
+    SplitMix rng{seed};
+    for (size_t i = (size_t)n - 1; i > 0; --i) std::swap(perm[i], perm[(size_t)(rng.next() % (uint64_t)(i + 1))]);
+    idx.assign(perm.begin(), perm.begin() + S);
+  }
+  std::sort(idx.begin(), idx.end());
+  a->hash = h->h;
+  a->S = (int)idx.size();
+  const int L = a->hash->dh.L;
+  a->steps_since_rebuild = 0;
+  a->steps_since_check = 0;
+  a->drift_ema = 0.f;
+  if (idx.empty()) return KL_OK;  // no neurons: nothing to watch (scheduler.rs tests: empty_neurons)
+  a->idx.alloc(idx.size() * 4);
+  a->base.alloc(idx.size() * L * 8);
+  a->cur.alloc(idx.size() * L * 8);
+  a->rows.alloc(idx.size() * (size_t)a->hash->dh.d * 4);
+  cudaStream_t st = ctx__->stream;
+  ck(cudaMemcpyAsync(a->idx.p, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice, st), "upload");
+  adaptive_hash(a, rows, n, ld, dtype, a->base);
+  ck(cudaStreamSynchronize(st), "sync");
+  a->steps_since_rebuild = 0;
+  a->steps_since_check = 0;
+  a->drift_ema = 0.f;
+  KL_API_END
+}
+extern "C" kl_status kl_adaptive_should_rebuild(kl_adaptive_t a, const void* rows, int n, int ld, int dtype,
+                                                int* rebuild_host) {
+  if (!a || !rebuild_host) return KL_EINVAL;
+  KL_API_BEGIN(a->ctx)
+  *rebuild_host = 0;
+  a->steps_since_rebuild += 1;
+  a->steps_since_check += 1;
+  if (a->steps_since_rebuild >= a->max_interval) {  // forced (scheduler.rs:141-145)
+    a->steps_since_rebuild = 0;
+    a->steps_since_check = 0;
+    *rebuild_host = 1;
+    return KL_OK;
+  }
+  if (a->steps_since_check < a->min_interval) return KL_OK;
+  float drift = 0.f;
+  if (a->hash && a->S > 0) {  // estimate_drift (scheduler.rs:163-195)
+    require(rows && ld >= a->hash->dh.d, "adaptive: bad rows");
+    require(dtype == KL_DTYPE_F32 || dtype == KL_DTYPE_BF16, "adaptive: dtype must be F32 or BF16");
+    cudaStream_t st = ctx__->stream;
+    adaptive_hash(a, rows, n, ld, dtype, a->cur);
+    ck(cudaMemsetAsync(a->changed.p, 0, 4, st), "memset");
+    adaptive_compare_kernel<<<(unsigned)ceil_div(a->S, 256), 256, 0, st>>>(
+        a->cur.as<uint64_t>(), a->base.as<uint64_t>(), a->idx.as<uint32_t>(), a->S, a->hash->dh.L, n,
+        a->changed.as<int>());
+    count_launch();
+    ck_launch("adaptive compare");
+    int changed = 0;
+    ck(cudaMemcpyAsync(&changed, a->changed.p, 4, cudaMemcpyDeviceToHost, st), "copy");
+    ck(cudaStreamSynchronize(st), "sync");
+    drift = (float)changed / (float)a->S;
+  }
+  a->drift_ema = a->ema_alpha * drift + (1.0f - a->ema_alpha) * a->drift_ema;
+  a->steps_since_check = 0;
+  if (a->drift_ema >= a->drift_threshold) {
+    a->steps_since_rebuild = 0;
+    *rebuild_host = 1;
+  }
+  KL_API_END
+}
+extern "C" kl_status kl_adaptive_notify_rebuild(kl_adaptive_t a) {
+  if (!a) return KL_EINVAL;
+  a->steps_since_rebuild = 0;
+  a->steps_since_check = 0;
+  return KL_OK;
+}
+extern "C" kl_status kl_adaptive_state(kl_adaptive_t a, float* drift_ema_host, uint64_t* steps_since_rebuild_host,
+                                       int* n_sampled_host) {
+  if (!a) return KL_EINVAL;
+  if (n_sampled_host) *n_sampled_host = a->S;
+  if (drift_ema_host) *drift_ema_host = a->drift_ema;
+  if (steps_since_rebuild_host) *steps_since_rebuild_host = (uint64_t)a->steps_since_rebuild;
+  return KL_OK;
 }
 
 // ===========================================================================

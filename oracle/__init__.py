@@ -60,6 +60,13 @@ def lib() -> C.CDLL:
             "orc_index_query_sparse": (C.c_int, [_P, _P, _P, C.c_int, _P, _P, C.c_int]),
             "orc_index_export": (None, [_P, _P, _P, _P]),
             "orc_sample": (C.c_int, [C.c_int, C.c_int, C.c_int, _P, _P, C.c_int, _P]),
+            "orc_adaptive_create": (_P, [C.c_uint64, C.c_uint64, C.c_float, C.c_float]),
+            "orc_adaptive_destroy": (None, [_P]),
+            "orc_adaptive_record_baseline": (None, [_P, _P, _P, C.c_int, C.c_int, _P, C.c_int]),
+            "orc_adaptive_should_rebuild": (C.c_int, [_P, _P, _P, C.c_int, C.c_int]),
+            "orc_adaptive_notify_rebuild": (None, [_P]),
+            "orc_adaptive_drift": (C.c_float, [_P]),
+            "orc_adaptive_steps": (C.c_uint64, [_P]),
             "orc_sched_create": (_P, [C.c_uint64, C.c_double]),
             "orc_sched_destroy": (None, [_P]),
             "orc_sched_should_rebuild": (C.c_int, [_P, C.c_uint64]),
@@ -249,6 +256,36 @@ class Scheduler:
 
     def rebuild_count(self) -> int:
         return int(lib().orc_sched_count(self.h))
+
+
+class AdaptiveScheduler:
+    """mongoose AdaptiveScheduler (scheduler.rs:44-213) with explicit sampled indices."""
+
+    def __init__(self, min_interval: int, max_interval: int, sample_fraction: float, drift_threshold: float):
+        self.h = lib().orc_adaptive_create(min_interval, max_interval, sample_fraction, drift_threshold)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().orc_adaptive_destroy(self.h)
+
+    def record_baseline(self, rows, hash_fn: Hash, sampled) -> None:
+        rows = np.ascontiguousarray(rows, np.float32)
+        idx = np.ascontiguousarray(np.sort(np.asarray(sampled, np.uint32)))
+        self._keep = idx
+        lib().orc_adaptive_record_baseline(self.h, hash_fn.h, _p(rows), rows.shape[0], rows.shape[1], _p(idx), len(idx))
+
+    def should_rebuild(self, rows, hash_fn: Hash) -> bool:
+        rows = np.ascontiguousarray(rows, np.float32)
+        return bool(lib().orc_adaptive_should_rebuild(self.h, hash_fn.h, _p(rows), rows.shape[0], rows.shape[1]))
+
+    def notify_rebuild(self) -> None:
+        lib().orc_adaptive_notify_rebuild(self.h)
+
+    def drift_estimate(self) -> float:
+        return float(lib().orc_adaptive_drift(self.h))
+
+    def steps_since_rebuild(self) -> int:
+        return int(lib().orc_adaptive_steps(self.h))
 
 
 def compute_loss(activations, active, labels) -> float:

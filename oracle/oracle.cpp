@@ -521,6 +521,70 @@ struct Scheduler {
 };
 
 // ---------------------------------------------------------------------------
+// AdaptiveScheduler (crates/klearu-mongoose/src/scheduler.rs:44-213).  The
+// reference samples ceil(n * sample_fraction) neurons with rand 0.8.5's
+// StdRng shuffle; that stream is not available here, so the sampled indices
+// (sorted) are an input.  Everything else -- counters, the drift fraction in
+// f32, the EMA with alpha 0.3 -- follows the reference line by line.
+// ---------------------------------------------------------------------------
+struct Adaptive {
+  size_t min_interval, max_interval;
+  float sample_fraction, drift_threshold;
+  float drift_ema = 0.0f, ema_alpha = 0.3f;
+  size_t steps_since_rebuild = 0, steps_since_check = 0;
+  std::vector<uint32_t> sampled;               // indices into the neuron rows
+  std::vector<std::vector<uint64_t>> baseline;  // [sampled][L]
+
+  // record_baseline (scheduler.rs:96-129) with explicit sampled indices.
+  void record_baseline(const Hash& h, const float* rows, int n, int ld, const uint32_t* idx, int ns) {
+    sampled.assign(idx, idx + ns);
+    baseline.assign(ns, std::vector<uint64_t>(h.L));
+    for (int i = 0; i < ns; ++i)
+      for (int t = 0; t < h.L; ++t) baseline[i][t] = h.hash_dense(rows + (size_t)idx[i] * ld, t, nullptr);
+    (void)n;
+    steps_since_rebuild = 0;
+    steps_since_check = 0;
+    drift_ema = 0.0f;
+  }
+  // estimate_drift (scheduler.rs:163-195)
+  float estimate_drift(const Hash& h, const float* rows, int n, int ld) const {
+    if (baseline.empty() || sampled.empty()) return 0.0f;
+    size_t changed = 0;
+    for (size_t b = 0; b < sampled.size(); ++b) {
+      if ((int)sampled[b] >= n) continue;
+      bool any = false;
+      for (int t = 0; t < h.L && !any; ++t)
+        any = (size_t)t < baseline[b].size() && h.hash_dense(rows + (size_t)sampled[b] * ld, t, nullptr) != baseline[b][t];
+      if (any) ++changed;
+    }
+    return (float)changed / (float)sampled.size();
+  }
+  // should_rebuild (scheduler.rs:133-159)
+  bool should_rebuild(const Hash& h, const float* rows, int n, int ld) {
+    steps_since_rebuild += 1;
+    steps_since_check += 1;
+    if (steps_since_rebuild >= max_interval) {
+      steps_since_rebuild = 0;
+      steps_since_check = 0;
+      return true;
+    }
+    if (steps_since_check < min_interval) return false;
+    const float drift = estimate_drift(h, rows, n, ld);
+    drift_ema = ema_alpha * drift + (1.0f - ema_alpha) * drift_ema;
+    steps_since_check = 0;
+    if (drift_ema >= drift_threshold) {
+      steps_since_rebuild = 0;
+      return true;
+    }
+    return false;
+  }
+  void notify_rebuild() {  // scheduler.rs:198-201
+    steps_since_rebuild = 0;
+    steps_since_check = 0;
+  }
+};
+
+// ---------------------------------------------------------------------------
 // Activations (layer.rs:250-308)
 // ---------------------------------------------------------------------------
 float activate(float x, int act) {
@@ -1013,6 +1077,24 @@ int orc_sample(int type, int top_k, int threshold, const uint32_t* ids, const ui
 }
 
 // ---- scheduler ----
+void* orc_adaptive_create(uint64_t min_interval, uint64_t max_interval, float sample_fraction, float drift_threshold) {
+  auto* a = new Adaptive();
+  a->min_interval = min_interval;
+  a->max_interval = max_interval;
+  a->sample_fraction = sample_fraction;
+  a->drift_threshold = drift_threshold;
+  return a;
+}
+void orc_adaptive_destroy(void* p) { delete static_cast<Adaptive*>(p); }
+void orc_adaptive_record_baseline(void* p, void* hp, const float* rows, int n, int ld, const uint32_t* idx, int ns) {
+  static_cast<Adaptive*>(p)->record_baseline(**static_cast<std::shared_ptr<Hash>*>(hp), rows, n, ld, idx, ns);
+}
+int orc_adaptive_should_rebuild(void* p, void* hp, const float* rows, int n, int ld) {
+  return static_cast<Adaptive*>(p)->should_rebuild(**static_cast<std::shared_ptr<Hash>*>(hp), rows, n, ld) ? 1 : 0;
+}
+void orc_adaptive_notify_rebuild(void* p) { static_cast<Adaptive*>(p)->notify_rebuild(); }
+float orc_adaptive_drift(void* p) { return static_cast<Adaptive*>(p)->drift_ema; }
+uint64_t orc_adaptive_steps(void* p) { return static_cast<Adaptive*>(p)->steps_since_rebuild; }
 void* orc_sched_create(uint64_t base, double decay) { return new Scheduler(base, decay); }
 void orc_sched_destroy(void* p) { delete static_cast<Scheduler*>(p); }
 int orc_sched_should_rebuild(void* p, uint64_t step) { return static_cast<Scheduler*>(p)->should_rebuild(step) ? 1 : 0; }
