@@ -348,7 +348,6 @@ def create_lsh_index(config: LshConfig, input_dim: int, seed: int, ctx: Context 
 # ---------------------------------------------------------------------------
 # Network
 # ---------------------------------------------------------------------------
-@dataclass
 class AdaptiveScheduler:
     """klearu_mongoose::AdaptiveScheduler (scheduler.rs:44-213): rebuild the
     LSH tables when the hash codes of sampled neurons have drifted.  Rows are
@@ -408,6 +407,7 @@ class AdaptiveScheduler:
         return self._state()[2]
 
 
+@dataclass
 class LayerOutput:  # network/layer.rs:19-26
     activations: np.ndarray
     active_neurons: list
