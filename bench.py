@@ -273,21 +273,22 @@ def main():
     U_h = stats[0].touched_rows / K          # hidden neurons updated per step
     nnz = stats[0].input_nnz / K
     A_h = stats[0].active_sum / K
-    phases = {
-        ("output", "forward"): (A * (2 * d_h + 16), prof[1]["forward"]),   # fused gather: fwd + loss grad + dX
-        ("output", "update"): (U_o * (20 * d_h + 24) + A * 24, prof[1]["update"]),
-        ("hidden", "update"): (U_h * (20 * d_in + 24) + nnz * 24, prof[0]["update"]),
-        ("hidden", "forward"): (A_h * nnz / max(B, 1) * 2 + nnz * 8, prof[0]["forward"]),
-        ("output", "probe"): (A * 8, prof[1]["probe"]),
-    }
-    dom = max(phases, key=lambda k: phases[k][1][0])
-    bytes_dom, (ms_dom, calls_dom) = phases[dom]
+    # The roofline kernel: layer 0's streaming Adam pass (fm_adam_kernel), the step's HBM-bound
+    # kernel: W (bf16), m, v (f32) of all 135909 feature rows x U_h touched neurons, read and
+    # written = 20 B per element.  Timed alone by the library's KL_PHASE_STREAM events.  The
+    # output-layer kernels take more time but read rows resident in L2 (issue-bound, see
+    # phase_ms_per_step and profiles/).
+    bytes_dom = 20.0 * d_in * U_h
+    ms_dom = prof[0]["stream"][0]
     peak, peak_kind = measured_peaks()
-    achieved = bytes_dom / (ms_dom / K / 1e3) / 1e9 if ms_dom > 0 else 0.0  # one launch of the phase per step
+    achieved = bytes_dom / (ms_dom / K / 1e3) / 1e9 if ms_dom > 0 else 0.0  # one launch per step
     step_bytes_formula = (2 * d_h * A) * 2 + 20 * d_h * U_o + 16 * U_o + 4 * 50 * 128 * B + 2 * d_h * nnz + \
         20 * d_in * U_h + nnz * 8
-    roofline = {"bound": "hbm", "kernel": f"{dom[0]} {dom[1]}", "achieved": achieved, "peak": peak,
-                "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+    roofline = {"bound": "hbm", "kernel": "fm_adam_kernel (hidden-layer Adam over all 135909 feature rows)",
+                "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                # dram__bytes_read.sum + dram__bytes_write.sum of one launch, ncu --set full, C1
+                # (profiles/slide_step_c1_kernels_ncu.md): part of W/m/v is served from L2
+                "traffic": 295.8e6,
                 "bytes_per_launch": bytes_dom / 1.0, "ms_per_launch": ms_dom / K,
                 "step_bytes_formula": step_bytes_formula,
                 "step_frac_of_peak": step_bytes_formula / (ms_max / K / 1e3) / 1e9 / peak,

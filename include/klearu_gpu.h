@@ -405,7 +405,9 @@ typedef enum {
   KL_PHASE_BACKWARD = 3, /* local gradients, input gradients                  */
   KL_PHASE_UPDATE = 4,   /* segmented gradient reduction + optimizer          */
   KL_PHASE_REBUILD = 5,  /* table rebuild                                     */
-  KL_NPHASES = 6
+  KL_PHASE_STREAM = 6,   /* layer 0 only: the streaming Adam pass over all     */
+                         /* feature rows (inside KL_PHASE_UPDATE)              */
+  KL_NPHASES = 7
 } kl_phase;
 KL_API kl_status kl_net_profile(kl_net_t net, int enable);
 /* Accumulated milliseconds and call counts per phase of `layer` since the last

@@ -26,7 +26,7 @@ OPT_SGD, OPT_ADAM = range(2)
 DTYPE_F32, DTYPE_BF16 = range(2)
 QUERY_COUNTS, QUERY_UNION = range(2)
 MODE_EXACT_SEQUENTIAL, MODE_BATCHED = range(2)
-PHASES = ["hash", "probe", "forward", "backward", "update", "rebuild"]
+PHASES = ["hash", "probe", "forward", "backward", "update", "rebuild", "stream"]
 
 
 class HashParams(C.Structure):

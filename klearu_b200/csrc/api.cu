@@ -1053,6 +1053,13 @@ struct kl_net_s {
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pool;
   std::vector<double> prof_ms;
   std::vector<uint64_t> prof_calls;
+  // events around layer 0's streaming Adam launch (KL_PHASE_STREAM)
+  int stream_ev = -1;
+  static void stream_hook(void* self, int after) {
+    auto* n = static_cast<kl_net_s*>(self);
+    if (!after) n->stream_ev = n->prof_begin(0, KL_PHASE_STREAM);
+    else n->prof_end(n->stream_ev);
+  }
   int prof_begin(int layer, int phase) {
     if (!prof) return -1;
     std::pair<cudaEvent_t, cudaEvent_t> e;
@@ -1337,7 +1344,7 @@ struct kl_net_s {
       if (L.fm) {
         launch_fm_update(L.W.p, wdtype, L.ldw, L.d, L.N, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
                          L.mb.as<float>(), L.vb.as<float>(), in, L.lgd.as<float>(), L.ldN, L.tmask.as<uint32_t>(),
-                         S, L.gfeat.as<float>(), o, stat, st);
+                         S, L.gfeat.as<float>(), o, stat, st, &kl_net_s::stream_hook, this);
         ck_launch("fm update");
       } else {
         const Layer& P = *layers[l - 1];

@@ -1224,7 +1224,8 @@ void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, fl
 void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
                       float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
                       const uint32_t* touched_mask, SegScratch S, float* G, const OptStep& o,
-                      unsigned long long* stat_touched, cudaStream_t st) {
+                      unsigned long long* stat_touched, cudaStream_t st, void (*around_adam)(void*, int),
+                      void* hook_arg) {
   const int nq = in.n;
   if (nq <= 0) return;
   fm_touch_kernel<<<nq, 256, 0, st>>>(in, S.hist, S.touched, S.ctr, d);
@@ -1246,6 +1247,7 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
   const int vpr = ldl / 4;  // vectors per feature row (ldw == ldl == pitch of N)
   const int64_t nvec = (int64_t)d * vpr;
   const unsigned agrid = (unsigned)ceil_div(nvec, (int64_t)FM_NT * FM_UNROLL);
+  if (around_adam) around_adam(hook_arg, 0);
   if (wdtype == KL_DTYPE_BF16)
     fm_adam_kernel<__nv_bfloat16><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, nvec, vpr, N, m, v,
                                                            touched_mask, S.hist, G, ldl, o);
@@ -1253,6 +1255,7 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
     fm_adam_kernel<float><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, nvec, vpr, N, m, v, touched_mask,
                                                    S.hist, G, ldl, o);
   count_launch();
+  if (around_adam) around_adam(hook_arg, 1);
   if (!(vpr == 32 || vpr == 8 || vpr == 16 || vpr == 4 || vpr == 2 || vpr == 1) || (vpr >= 32 && vpr % 32)) {
     // a feature row does not sit inside one warp: clear hist separately
     fm_hist_clear_kernel<<<(unsigned)ceil_div(d, 256), 256, 0, st>>>(S);
