@@ -10,6 +10,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -1019,8 +1020,23 @@ struct Layer {
 
 // Per-example capacities of the sharded batch exchange (input nnz, labels).
 #define KL_SHARD_NNZ_PER_EXAMPLE_H 512
+// Per-example capacities of the graph-captured step's batch buffers.
+#define KL_GRAPH_NNZ_PER_EXAMPLE 512
+#define KL_GRAPH_LABELS_PER_EXAMPLE 32
 #define KL_SHARD_LABELS_PER_EXAMPLE_H 32
 void nccl_ck(ncclResult_t r, const char* what);
+
+namespace {
+__global__ void loss_final_kernel(const float* acc, int B, float* out1, float* out2) {
+  const float v = B > 0 ? __fdiv_rn(*acc, (float)B) : 0.0f;
+  if (out1) *out1 = v;
+  if (out2) *out2 = v;
+}
+void launch_loss_final(const float* acc, int B, float* out1, float* out2, cudaStream_t st) {
+  loss_final_kernel<<<1, 1, 0, st>>>(acc, B, out1, out2);
+  count_launch();
+}
+}  // namespace
 
 struct kl_net_s {
   kl_ctx_t ctx;
@@ -1097,6 +1113,8 @@ struct kl_net_s {
     ~Phase() { n->prof_end(i); }
   };
   ~kl_net_s() {
+    if (gexec) cudaGraphExecDestroy(gexec);
+    if (cap_stream) cudaStreamDestroy(cap_stream);
     if (comm) ncclCommDestroy(comm);
     for (auto& e : pending) pool.emplace_back(e.a, e.b);
     for (auto& e : pool) {
@@ -1144,6 +1162,14 @@ struct kl_net_s {
     for (auto& L : layers) rebuild_layer(*L);
   }
 
+  // Optimizer constants of the current step, copied to the device before
+  // the step's kernels (they read them from dopt).
+  DBuf dopt;
+  OptStep opt_host{};
+  void upload_opt(double lr) {
+    opt_host = opt_step(lr);
+    ck(cudaMemcpyAsync(dopt.p, &opt_host, sizeof(OptStep), cudaMemcpyHostToDevice, ctx->stream), "upload optimizer step");
+  }
   OptStep opt_step(double lr) const {
     OptStep o;
     o.opt = cfg.optimizer;
@@ -1278,8 +1304,6 @@ struct kl_net_s {
   void backward(const kl_batch& b, int s0, int nq, double lr) {
     cudaStream_t st = ctx->stream;
     const int nL = (int)layers.size();
-    const OptStep o = opt_step(lr);
-    SparseIn in{b.rowptr + s0, b.idx, b.val, nq};
     // input gradient of the output layer
     {
       Phase ph(this, nL - 1, KL_PHASE_BACKWARD);
@@ -1330,9 +1354,10 @@ struct kl_net_s {
 
   // Optimizer updates of every layer for examples [s0, s0+nq) of the batch.
   void update_layers(const kl_batch& b, int s0, int nq, double lr) {
+    (void)lr;  // the step's optimizer constants are in dopt (upload_opt)
     cudaStream_t st = ctx->stream;
     const int nL = (int)layers.size();
-    const OptStep o = opt_step(lr);
+    const OptStep* o = dopt.as<OptStep>();
     SparseIn in{b.rowptr + s0, b.idx, b.val, nq};
     for (int l = nL - 1; l >= 0; --l) {
       Phase ph(this, l, KL_PHASE_UPDATE);
@@ -1451,6 +1476,114 @@ struct kl_net_s {
       ck_launch("or masks");
     }
     update_layers(gb, 0, PB, lr);
+  }
+
+  // ---- CUDA graph of the batched single-GPU train step ------------------
+  // The step's ~30 kernel launches and memsets are captured once per batch
+  // size and replayed with one cudaGraphLaunch.  The graph reads the batch
+  // from fixed buffers (the caller's arrays are copied in first) and the
+  // optimizer constants from dopt; the rebuild check stays on the host.
+  bool graph_disabled = false;
+  bool graph_warm = false;
+  int graph_B = -1;
+  cudaGraphExec_t gexec = nullptr;
+  cudaStream_t cap_stream = nullptr;
+  int g_nnz_cap = 0, g_lab_cap = 0;
+  unsigned long long graph_kernels = 0;  // kernels in the captured graph (launch accounting)
+  DBuf gi_rowptr, gi_idx, gi_val, gi_lptr, gi_labels, loss_out;
+
+  bool graph_usable(const kl_batch& b) const {
+    return !graph_disabled && !prof && nranks == 1 && b.batch > 0 && b.nnz <= max_batch * KL_GRAPH_NNZ_PER_EXAMPLE &&
+           b.nlabels <= max_batch * KL_GRAPH_LABELS_PER_EXAMPLE;
+  }
+  void batched_body(const kl_batch& ib) {
+    cudaStream_t st = ctx->stream;
+    ck(cudaMemsetAsync(loss_acc.p, 0, 4, st), "memset");
+    ck(cudaMemsetAsync(labprob.p, 0, (size_t)g_lab_cap * 4, st), "memset");
+    forward(ib, 0, ib.batch, true);
+    launch_loss(ib.label_ptr, labprob.as<float>(), ib.batch, loss_acc.as<float>(), st);
+    ck_launch("loss");
+    backward(ib, 0, ib.batch, 0.0);
+    launch_loss_final(loss_acc.as<float>(), ib.batch, loss_out.as<float>(), loss_acc.as<float>(), st);
+    ck_launch("loss final");
+  }
+  void graph_step(const kl_batch& b, float* loss) {
+    cudaStream_t st = ctx->stream;
+    const int B = b.batch;
+    if (g_nnz_cap == 0) {
+      g_nnz_cap = max_batch * KL_GRAPH_NNZ_PER_EXAMPLE;
+      g_lab_cap = max_batch * KL_GRAPH_LABELS_PER_EXAMPLE;
+      gi_rowptr.alloc((size_t)(max_batch + 1) * 4);
+      gi_lptr.alloc((size_t)(max_batch + 1) * 4);
+      gi_idx.alloc((size_t)g_nnz_cap * 4);
+      gi_val.alloc((size_t)g_nnz_cap * 4);
+      gi_labels.alloc((size_t)g_lab_cap * 4);
+      loss_out.alloc(4);
+      kl_batch cap_b{};
+      cap_b.batch = max_batch;
+      cap_b.nnz = g_nnz_cap;
+      cap_b.nlabels = g_lab_cap;
+      ensure_batch_buffers(cap_b);
+      ck(cudaStreamCreateWithFlags(&cap_stream, cudaStreamNonBlocking), "capture stream");
+    }
+    ck(cudaMemcpyAsync(gi_rowptr.p, b.rowptr, (size_t)(B + 1) * 4, cudaMemcpyDeviceToDevice, st), "batch copy");
+    ck(cudaMemcpyAsync(gi_lptr.p, b.label_ptr, (size_t)(B + 1) * 4, cudaMemcpyDeviceToDevice, st), "batch copy");
+    if (b.nnz > 0) {
+      ck(cudaMemcpyAsync(gi_idx.p, b.idx, (size_t)b.nnz * 4, cudaMemcpyDeviceToDevice, st), "batch copy");
+      ck(cudaMemcpyAsync(gi_val.p, b.val, (size_t)b.nnz * 4, cudaMemcpyDeviceToDevice, st), "batch copy");
+    }
+    if (b.nlabels > 0)
+      ck(cudaMemcpyAsync(gi_labels.p, b.labels, (size_t)b.nlabels * 4, cudaMemcpyDeviceToDevice, st), "batch copy");
+    kl_batch ib{};
+    ib.batch = B;
+    ib.rowptr = gi_rowptr.as<int32_t>();
+    ib.idx = gi_idx.as<uint32_t>();
+    ib.val = gi_val.as<float>();
+    ib.label_ptr = gi_lptr.as<int32_t>();
+    ib.labels = gi_labels.as<uint32_t>();
+    ib.nnz = g_nnz_cap;
+    ib.nlabels = g_lab_cap;
+    if (!graph_warm || (gexec && graph_B != B)) {
+      // first use (or a new batch size): run eagerly; capture on the next call
+      if (gexec) {
+        cudaGraphExecDestroy(gexec);
+        gexec = nullptr;
+      }
+      graph_warm = true;
+      batched_body(ib);
+    } else {
+      if (!gexec) {
+        cudaGraph_t g = nullptr;
+        ctx->stream = cap_stream;
+        bool ok = cudaStreamBeginCapture(cap_stream, cudaStreamCaptureModeRelaxed) == cudaSuccess;
+        const unsigned long long n0 = g_launches.load();
+        if (ok) {
+          try {
+            batched_body(ib);
+          } catch (...) {
+            ok = false;
+          }
+          ok = cudaStreamEndCapture(cap_stream, &g) == cudaSuccess && ok && g;
+        }
+        ctx->stream = st;
+        if (ok) ok = cudaGraphInstantiate(&gexec, g, 0) == cudaSuccess;
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        if (!ok) {
+          gexec = nullptr;
+          graph_disabled = true;  // stay eager from now on
+          batched_body(ib);
+          if (loss) ck(cudaMemcpyAsync(loss, loss_out.p, 4, cudaMemcpyDeviceToDevice, st), "loss copy");
+          return;
+        }
+        graph_B = B;
+        graph_kernels = g_launches.load() - n0;
+        g_launches.fetch_sub(graph_kernels);  // counted again per replay below
+      }
+      ck(cudaGraphLaunch(gexec, st), "graph launch");
+      count_launch((unsigned)graph_kernels);
+    }
+    if (loss) ck(cudaMemcpyAsync(loss, loss_out.p, 4, cudaMemcpyDeviceToDevice, st), "loss copy");
   }
 
   // Per-batch buffers grow geometrically (x1.5) so that a stream of batches
@@ -1661,6 +1794,8 @@ kl_net_s* create_net(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init
   net->wdtype = cfg->weight_dtype;
   net->rank = rank;
   net->nranks = nranks;
+  if (const char* gv = std::getenv("KL_GRAPH"))
+    if (!std::strcmp(gv, "0")) net->graph_disabled = true;
   net->rank_batch = cfg->max_batch;
   net->max_batch = cfg->max_batch * nranks;  // per-step buffers hold the global batch
   for (int l = 0; l < nl; ++l) {
@@ -1694,6 +1829,7 @@ kl_net_s* create_net(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init
   net->sched.next = net->sched.base;
   net->loss_acc.alloc(4);
   net->labprob.alloc(4);
+  net->dopt.alloc(sizeof(OptStep));
   if (nranks > 1) {
     const int B = net->rank_batch, P = nranks;
     net->nnz_cap = B * KL_SHARD_NNZ_PER_EXAMPLE;
@@ -1741,13 +1877,6 @@ extern "C" kl_status kl_net_destroy(kl_net_t net) {
   return KL_OK;
 }
 
-namespace {
-__global__ void loss_final_kernel(const float* acc, int B, float* out1, float* out2) {
-  const float v = B > 0 ? __fdiv_rn(*acc, (float)B) : 0.0f;
-  if (out1) *out1 = v;
-  if (out2) *out2 = v;
-}
-}  // namespace
 
 extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double lr, int mode, float* loss,
                                        float* loss_host) {
@@ -1762,11 +1891,15 @@ extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double l
     return KL_OK;
   }
   int loss_div = b->batch;
+  net->upload_opt(lr);
   if (net->nranks > 1) {
     support(mode == KL_MODE_BATCHED, "sharded net: only KL_MODE_BATCHED train steps");
     require(b->batch <= net->rank_batch, "sharded train_step: batch exceeds max_batch");
     net->train_sharded(*b, lr);
     loss_div = b->batch * net->nranks;
+  } else if (mode == KL_MODE_BATCHED && net->graph_usable(*b)) {
+    net->graph_step(*b, loss);
+    loss_div = -1;  // the captured body wrote the loss
   } else {
   net->ensure_batch_buffers(*b);
   ck(cudaMemsetAsync(net->loss_acc.p, 0, 4, st), "memset");
@@ -1785,7 +1918,7 @@ extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double l
     }
   }
   }
-  loss_final_kernel<<<1, 1, 0, st>>>(net->loss_acc.as<float>(), loss_div, loss, net->loss_acc.as<float>());
+  if (loss_div >= 0) launch_loss_final(net->loss_acc.as<float>(), loss_div, loss, net->loss_acc.as<float>(), st);
   ck_launch("loss final");
   for (auto& L : net->layers) {
     L->examples += (uint64_t)b->batch;

@@ -132,6 +132,9 @@ void launch_compact(const uint32_t* ids, const uint32_t* counts, int stride, con
 // Optimizer constants for one step, computed on the host exactly as the
 // reference does in f32 (adam.rs:38-55: t = max(step,1), powi via
 // square-and-multiply).
+// Optimizer constants of one step.  The update kernels read them from device
+// memory (written by the host before each train step), so a captured step
+// graph stays valid as the step count changes.
 struct OptStep {
   int opt;           // KL_OPT_*
   float lr, b1, b2, eps, omb1, omb2, c1, c2, mom;
@@ -203,7 +206,7 @@ struct SegScratch {
 };
 void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
                       float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
-                      SegScratch S, const OptStep& o, unsigned long long* stat_touched,
+                      SegScratch S, const OptStep* o, unsigned long long* stat_touched,
                       cudaStream_t st);
 // Dense-collision path of the row-major update: touched rows by a bitmap
 // (first setter appends), local gradients scattered sample-major into LGd
@@ -221,7 +224,7 @@ bool rm_dense_fits(int64_t rows, int nb);
 void launch_count_touched(const uint32_t* ctr, unsigned long long* stat, cudaStream_t st);
 void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
                             float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
-                            DenseScratch D, const OptStep& o, unsigned long long* stat_touched,
+                            DenseScratch D, const OptStep* o, unsigned long long* stat_touched,
                             cudaStream_t st);
 // Feature-major gradient + optimizer over ALL features of the touched neurons
 // (Adam decays every element of an active row, adam.rs:57-68).  G: gradient
@@ -229,7 +232,7 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
 // (nullable) is called with 0 before and 1 after the streaming Adam launch.
 void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
                       float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
-                      const uint32_t* touched_mask, SegScratch S, float* G, const OptStep& o,
+                      const uint32_t* touched_mask, SegScratch S, float* G, const OptStep* o,
                       unsigned long long* stat_touched, cudaStream_t st, void (*around_adam)(void*, int) = nullptr,
                       void* hook_arg = nullptr);
 

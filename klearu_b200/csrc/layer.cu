@@ -551,8 +551,9 @@ constexpr int UPD_WARPS = 8;
 template <class W>
 __global__ void __launch_bounds__(UPD_WARPS * 32)
     rm_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
-                     const float* X, int ldx, SegScratch S, int nwords, OptStep o,
+                     const float* X, int ldx, SegScratch S, int nwords, const OptStep* op,
                      unsigned long long* stat_touched) {
+  const OptStep o = *op;
   extern __shared__ __align__(16) unsigned char dyn[];
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   uint32_t* mask = reinterpret_cast<uint32_t*>(dyn) + w * nwords;
@@ -651,7 +652,8 @@ template <class W>
 __global__ void __launch_bounds__(256)
     rm_dense_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
                            const float* X, int ldx, uint32_t* bits, const uint32_t* touched, const uint32_t* ctr,
-                           float* LGd, int64_t ldu, int nq, OptStep o) {
+                           float* LGd, int64_t ldu, int nq, const OptStep* op) {
+  const OptStep o = *op;
   extern __shared__ __align__(16) unsigned char dyn[];
   float (*xs)[RDU_S][128] = reinterpret_cast<float (*)[RDU_S][128]>(dyn);
   float (*ls)[RDU_S][RDU_ROWS] = reinterpret_cast<float (*)[RDU_S][RDU_ROWS]>(dyn + sizeof(float) * RDU_ST * RDU_S * 128);
@@ -852,7 +854,8 @@ __global__ void __launch_bounds__(UPD_WARPS * 32)
 template <class W>
 __global__ void __launch_bounds__(FM_NT, 4)
     fm_adam_kernel(void* Wm, int ldw, int64_t nvec, int vpr, int N, float* m, float* v,
-                   const uint32_t* tmask, uint32_t* hist, const float* G, int ldg, OptStep o) {
+                   const uint32_t* tmask, uint32_t* hist, const float* G, int ldg, const OptStep* op) {
+  const OptStep o = *op;
   // vector q = f * vpr + j covers elements [4j, 4j+4) of feature row f
   const int64_t q0 = (int64_t)blockIdx.x * (FM_NT * FM_UNROLL) + threadIdx.x;
   float w[FM_UNROLL][4], mm[FM_UNROLL][4], vv[FM_UNROLL][4];
@@ -919,8 +922,9 @@ __global__ void fm_hist_clear_kernel(SegScratch S) {
 // Bias gradient of every touched neuron: one warp per neuron loads 32
 // samples' gradients at a time and adds them in ascending sample order.
 __global__ void fm_bias_kernel(float* bias, float* mb, float* vb, const float* lgd, int ldl, int nq,
-                               int N, const uint32_t* tmask, OptStep o,
+                               int N, const uint32_t* tmask, const OptStep* op,
                                unsigned long long* stat_touched) {
+  const OptStep o = *op;
   const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int l = threadIdx.x & 31;
   if (j >= N) return;
@@ -1165,7 +1169,7 @@ bool rm_dense_fits(int64_t rows, int nb) {
 
 void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
                             float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
-                            DenseScratch D, const OptStep& o, unsigned long long* stat_touched,
+                            DenseScratch D, const OptStep* o, unsigned long long* stat_touched,
                             cudaStream_t st) {
   (void)stat_touched;
   if (nq <= 0) return;
@@ -1194,7 +1198,7 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
 
 void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
                       float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
-                      SegScratch S, const OptStep& o, unsigned long long* stat_touched,
+                      SegScratch S, const OptStep* o, unsigned long long* stat_touched,
                       cudaStream_t st) {
   if (nq <= 0) return;
   dim3 g2((unsigned)ceil_div(A.stride, 256), nq);
@@ -1223,7 +1227,7 @@ void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, fl
 
 void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
                       float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
-                      const uint32_t* touched_mask, SegScratch S, float* G, const OptStep& o,
+                      const uint32_t* touched_mask, SegScratch S, float* G, const OptStep* o,
                       unsigned long long* stat_touched, cudaStream_t st, void (*around_adam)(void*, int),
                       void* hook_arg) {
   const int nq = in.n;
