@@ -182,7 +182,10 @@ __global__ void __launch_bounds__(256) wta_tile_kernel(DevHash h, DenseIn in, Ha
   __syncthreads();
   const int w = threadIdx.x >> 5, r = threadIdx.x & 31;
   const float* xr = xs + r * pitch;
-  for (int t = w; t < h.L; t += blockDim.x >> 5) {
+  // tables of this block: [blockIdx.y * tpb, ...), one warp per table at a time
+  const int tpb = (h.L + gridDim.y - 1) / gridDim.y;
+  const int t0 = blockIdx.y * tpb, t1 = min(h.L, t0 + tpb);
+  for (int t = t0 + w; t < t1; t += blockDim.x >> 5) {
     uint64_t code = 0;
     int shift = 0;
     for (int kk = 0; kk < nwin; ++kk) {
@@ -204,28 +207,49 @@ __global__ void __launch_bounds__(256) wta_tile_kernel(DevHash h, DenseIn in, Ha
 }
 
 // Projection hashing of CSR rows: one block per row, one thread per projection.
+// Chunks of PS_CH nonzeros: the plane bytes of their columns are staged in
+// shared memory first, then each projection sums its chain in index order.
+constexpr int PS_CH = 64;
 __global__ void proj_sparse_kernel(DevHash h, SparseIn in, HashOut out) {
   extern __shared__ unsigned char dyn[];
   float* sv = reinterpret_cast<float*>(dyn);  // [LK]
-  __shared__ uint32_t sidx[256];
-  __shared__ float sval[256];
+  __shared__ uint32_t sidx[PS_CH];
+  __shared__ float sval[PS_CH];
+  uint32_t* spl = reinterpret_cast<uint32_t*>(dyn) + round_up(h.LK, 4);  // [PS_CH][lkpad] plane bytes
   const int i = blockIdx.x;
   const int tb = threadIdx.x;
   const int beg = in.rowptr[i], end = in.rowptr[i + 1];
   float acc = 0.0f;
-  for (int c0 = beg; c0 < end; c0 += 256) {
-    const int m = min(256, end - c0);
+  for (int c0 = beg; c0 < end; c0 += PS_CH) {
+    const int m = min(PS_CH, end - c0);
     for (int e = threadIdx.x; e < m; e += blockDim.x) {
       sidx[e] = in.idx[c0 + e];
       sval[e] = in.val[c0 + e];
     }
     __syncthreads();
-    if (tb < h.LK) {
-      for (int e = 0; e < m; ++e) {
-        uint32_t col = sidx[e];
-        float p = (col < (uint32_t)h.d) ? (float)h.planesT[(int64_t)col * h.lkpad + tb] : 0.0f;
-        acc = __fmaf_rn(p, sval[e], acc);
+    // stage the plane bytes of this chunk's columns ([m][lkpad] int8, one
+    // independent 4-byte load per thread at a time), then walk them in order
+    const int wpc = h.lkpad / 4;  // 32-bit words per column
+    for (int q0 = threadIdx.x; q0 < m * wpc; q0 += 4 * blockDim.x) {
+      uint32_t v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int q = q0 + u * blockDim.x;
+        v[u] = 0u;
+        if (q < m * wpc) {
+          const int e = q / wpc, wq = q - e * wpc;
+          const uint32_t col = sidx[e];
+          if (col < (uint32_t)h.d) v[u] = reinterpret_cast<const uint32_t*>(h.planesT + (int64_t)col * h.lkpad)[wq];
+        }
       }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (q0 + u * blockDim.x < m * wpc) spl[q0 + u * blockDim.x] = v[u];
+    }
+    __syncthreads();
+    if (tb < h.LK) {
+      const int8_t* pl = reinterpret_cast<const int8_t*>(spl);
+      for (int e = 0; e < m; ++e) acc = __fmaf_rn((float)pl[e * h.lkpad + tb], sval[e], acc);
     }
     __syncthreads();
   }
@@ -410,7 +434,10 @@ void launch_hash_dense(const DevHash& h, const DenseIn& in, const HashOut& out, 
           cudaFuncSetAttribute(wta_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
           attr = true;
         }
-        wta_tile_kernel<<<(unsigned)ceil_div(in.n, 32), 256, sm, st>>>(h, in, out, nwin);
+        // few row tiles (a query batch): spread the tables over more blocks
+        const int rt = (int)ceil_div(in.n, 32);
+        const int tg = std::max(1, std::min(h.L / 8, 296 / std::max(rt, 1)));
+        wta_tile_kernel<<<dim3((unsigned)rt, (unsigned)tg), 256, sm, st>>>(h, in, out, nwin);
       } else {
         int64_t tot = (int64_t)in.n * h.L;
         wta_dense_kernel<<<(unsigned)ceil_div(tot, 256), 256, 0, st>>>(h, in, out);
@@ -433,7 +460,13 @@ void launch_hash_sparse(const DevHash& h, const SparseIn& in, const HashOut& out
     case KL_HASH_SIMHASH:
     case KL_HASH_SRP: {
       int nt = (int)round_up(h.LK, 32);
-      proj_sparse_kernel<<<in.n, nt, (size_t)h.LK * sizeof(float), st>>>(h, in, out);
+      const size_t sm = ((size_t)round_up(h.LK, 4) + (size_t)PS_CH * h.lkpad / 4) * sizeof(float);
+      static bool attr = false;
+      if (!attr) {
+        cudaFuncSetAttribute(proj_sparse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+      }
+      proj_sparse_kernel<<<in.n, nt, sm, st>>>(h, in, out);
   count_launch();
       break;
     }

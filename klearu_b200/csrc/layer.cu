@@ -85,10 +85,16 @@ __device__ __forceinline__ void opt_apply(float& w, float& m, float& v, float g,
 template <class W>
 __global__ void __launch_bounds__(128) fm_forward_kernel(const void* Wm, int ldw, int d,
                                                          const float* bias, int act, SparseIn in,
-                                                         ActiveSet A, float* h, int ldh, int* err) {
-  constexpr int NT = 128, MAXJ = 8, CH = 256;
-  __shared__ uint32_t sidx[CH];
-  __shared__ float sval[CH];
+                                                         ActiveSet A, float* h, int ldh, int* err, int ch) {
+  // chunks of `ch` nonzeros: their whole feature rows (ldw weights each, one
+  // contiguous line per nonzero) are staged in shared memory with coalesced,
+  // independent 16-byte loads; then each active neuron's thread sums its
+  // chain in nonzero order (bit-exact) from shared memory.
+  constexpr int NT = 128, MAXJ = 8;
+  extern __shared__ __align__(16) unsigned char dyn[];
+  uint32_t* sidx = reinterpret_cast<uint32_t*>(dyn);
+  float* sval = reinterpret_cast<float*>(sidx + ch);
+  W* wt = reinterpret_cast<W*>(dyn + round_up((int64_t)ch * 8, 16));  // [ch][ldw]
   const int s = blockIdx.x;
   const int na = min(A.cnt[s], NT * MAXJ);
   const uint32_t* ids = A.ids + (int64_t)s * A.stride;
@@ -101,8 +107,9 @@ __global__ void __launch_bounds__(128) fm_forward_kernel(const void* Wm, int ldw
     acc[j] = 0.0f;
   }
   const int beg = in.rowptr[s], end = in.rowptr[s + 1];
-  for (int c0 = beg; c0 < end; c0 += CH) {
-    const int m = min(CH, end - c0);
+  const int vpr = (int)(((int64_t)ldw * sizeof(W)) / 16);  // 16-byte vectors per feature row
+  for (int c0 = beg; c0 < end; c0 += ch) {
+    const int m = min(ch, end - c0);
     for (int e = threadIdx.x; e < m; e += NT) {
       uint32_t col = in.idx[c0 + e];
       if (col >= (uint32_t)d) {
@@ -113,15 +120,31 @@ __global__ void __launch_bounds__(128) fm_forward_kernel(const void* Wm, int ldw
       sval[e] = in.val[c0 + e];
     }
     __syncthreads();
+    for (int q0 = threadIdx.x; q0 < m * vpr; q0 += 4 * NT) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int q = q0 + u * NT;
+        v[u] = make_uint4(0, 0, 0, 0);
+        if (q < m * vpr) {
+          const int e = q / vpr, c = q - e * vpr;
+          const uint32_t col = sidx[e];
+          if (col != 0xffffffffu) v[u] = reinterpret_cast<const uint4*>(static_cast<const W*>(Wm) + (int64_t)col * ldw)[c];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (q0 + u * NT < m * vpr) reinterpret_cast<uint4*>(wt)[q0 + u * NT] = v[u];
+    }
+    __syncthreads();
 #pragma unroll
     for (int j = 0; j < MAXJ; ++j) {
       const int a = threadIdx.x + j * NT;
       if (a < na) {
         float x = acc[j];
         for (int e = 0; e < m; ++e) {
-          const uint32_t col = sidx[e];
-          if (col == 0xffffffffu) continue;
-          x = __fadd_rn(x, __fmul_rn(wload<W>(Wm, (int64_t)col * ldw + myid[j]), sval[e]));
+          if (sidx[e] == 0xffffffffu) continue;
+          x = __fadd_rn(x, __fmul_rn(to_f(wt[(int64_t)e * ldw + myid[j]]), sval[e]));
         }
         acc[j] = x;
       }
@@ -1072,10 +1095,19 @@ void launch_w_to_f32(const void* src, int wdtype, int64_t ld_src, bool transpose
 void launch_fm_forward(const void* W, int wdtype, int ldw, int d, const float* bias, int act,
                        SparseIn in, ActiveSet A, float* h, int ldh, int* err, cudaStream_t st) {
   if (in.n <= 0) return;
+  const size_t rowb = (size_t)ldw * (wdtype == KL_DTYPE_BF16 ? 2 : 4);
+  const int ch = (int)std::max<size_t>(8, std::min<size_t>(64, (size_t)(48 * 1024) / rowb));
+  const size_t sm = (size_t)round_up((int64_t)ch * 8, 16) + (size_t)ch * rowb;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(fm_forward_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(fm_forward_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
   if (wdtype == KL_DTYPE_BF16)
-    fm_forward_kernel<__nv_bfloat16><<<in.n, 128, 0, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err);
+    fm_forward_kernel<__nv_bfloat16><<<in.n, 128, sm, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err, ch);
   else
-    fm_forward_kernel<float><<<in.n, 128, 0, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err);
+    fm_forward_kernel<float><<<in.n, 128, sm, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err, ch);
   count_launch();
 }
 
