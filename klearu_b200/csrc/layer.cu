@@ -668,142 +668,140 @@ __global__ void rm_dense_scatter_kernel(ActiveSet A, const uint32_t* slot_of, fl
 }
 
 constexpr int RDU_ROWS = 16;  // slots per block (8 warps x 2)
+constexpr int RDU_COLS = 32;  // columns per block (one per lane)
 constexpr int RDU_S = 32;     // samples per staged chunk
 constexpr int RDU_ST = 4;     // cp.async pipeline stages
 
+// Block = (16 slots, 32 columns): warp w owns slots 2w and 2w+1, lane l column
+// cb*32 + l.  Column blocks multiply the parallelism when few rows meet many
+// samples (a shard's union over a large global batch).  The gradient matrix
+// is left as read; rm_lg_zero_kernel restores its zeros afterwards.
 template <class W>
 __global__ void __launch_bounds__(256)
     rm_dense_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
                            const float* X, int ldx, uint32_t* bits, const uint32_t* touched, const uint32_t* ctr,
                            float* LGd, int64_t ldu, int nq, const OptStep* op) {
   const OptStep o = *op;
-  extern __shared__ __align__(16) unsigned char dyn[];
-  float (*xs)[RDU_S][128] = reinterpret_cast<float (*)[RDU_S][128]>(dyn);
-  float (*ls)[RDU_S][RDU_ROWS] = reinterpret_cast<float (*)[RDU_S][RDU_ROWS]>(dyn + sizeof(float) * RDU_ST * RDU_S * 128);
+  __shared__ __align__(16) float xs[RDU_ST][RDU_S][RDU_COLS];
+  __shared__ __align__(16) float ls[RDU_ST][RDU_S][RDU_ROWS];
   const int t = threadIdx.x, w = t >> 5, l = t & 31;
   const int n = (int)ctr[0];
   const int nch = (nq + RDU_S - 1) / RDU_S;
-  for (int k0 = blockIdx.x * RDU_ROWS; k0 < n; k0 += gridDim.x * RDU_ROWS) {
-    float gb[2] = {0.f, 0.f};
-    for (int g0 = 0; g0 < d; g0 += 128) {
-      const int c = g0 + l * 4;
-      const bool last_pass = g0 + 128 >= d;
-      // stage chunk `ch` into buffer `bf`: X rows (4 x 16 B per thread), LGd tile (threads < 128)
-      auto stage = [&](int ch) {
-        const int bf = ch % RDU_ST;
-        const int s0 = ch * RDU_S;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int idx = t + 256 * q;
-          const int r = idx >> 5, c4 = (idx & 31) * 4;
-          float* dst = &xs[bf][r][c4];
-          if (s0 + r < nq && g0 + c4 < d)
-            cp_async16(dst, X + (int64_t)(s0 + r) * ldx + g0 + c4);
-          else
-            *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        if (t < RDU_S * RDU_ROWS / 4) {
-          const int r = t / (RDU_ROWS / 4), c4 = (t % (RDU_ROWS / 4)) * 4;
-          float* dst = &ls[bf][r][c4];
-          if (s0 + r < nq) cp_async16(dst, LGd + (int64_t)(s0 + r) * ldu + k0 + c4);
-          else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      };
-      // the optimizer state of this lane's two rows, loaded now and used after the sum
-      float wv[2][4], mv[2][4], vv[2][4];
-      int64_t roff[2];
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int k = k0 + w * 2 + i;
-        roff[i] = -1;
-        if (k < n && c < d) {
-          roff[i] = (int64_t)touched[k] * ldw + c;
-          load4<W>(Wm, roff[i], wv[i]);
-          const float4 m4 = *reinterpret_cast<const float4*>(m + roff[i]);
-          mv[i][0] = m4.x; mv[i][1] = m4.y; mv[i][2] = m4.z; mv[i][3] = m4.w;
-          float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (o.opt == KL_OPT_ADAM) v4 = *reinterpret_cast<const float4*>(v + roff[i]);
-          vv[i][0] = v4.x; vv[i][1] = v4.y; vv[i][2] = v4.z; vv[i][3] = v4.w;
-        }
+  const int ncb = (d + RDU_COLS - 1) / RDU_COLS;
+  const int ngroups = (n + RDU_ROWS - 1) / RDU_ROWS;
+  for (int item = blockIdx.x; item < ngroups * ncb; item += gridDim.x) {
+    const int k0 = (item / ncb) * RDU_ROWS, cb = item % ncb;
+    const int c = cb * RDU_COLS + l;
+    const bool cin = c < d;
+    auto stage = [&](int ch) {
+      const int bf = ch % RDU_ST;
+      const int s0 = ch * RDU_S;
+      {  // 32 samples x 32 columns = 256 float4, one per thread
+        const int r = t >> 3, c4 = (t & 7) * 4;
+        float* dst = &xs[bf][r][c4];
+        if (s0 + r < nq && cb * RDU_COLS + c4 < d)
+          cp_async16(dst, X + (int64_t)(s0 + r) * ldx + cb * RDU_COLS + c4);
+        else
+          *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      float g[2][4];
-#pragma unroll
-      for (int i = 0; i < 2; ++i) g[i][0] = g[i][1] = g[i][2] = g[i][3] = 0.f;
-      __syncthreads();  // previous users of the buffers are done
-#pragma unroll
-      for (int p = 0; p < RDU_ST - 1; ++p) {
-        if (p < nch) stage(p);
-        cp_async_commit();  // one group per stage slot (possibly empty) keeps the wait count uniform
+      if (t < RDU_S * RDU_ROWS / 4) {
+        const int r = t / (RDU_ROWS / 4), c4 = (t % (RDU_ROWS / 4)) * 4;
+        float* dst = &ls[bf][r][c4];
+        if (s0 + r < nq) cp_async16(dst, LGd + (int64_t)(s0 + r) * ldu + k0 + c4);
+        else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      for (int ch = 0; ch < nch; ++ch) {
-        const int bf = ch % RDU_ST;
-        if (ch + RDU_ST - 1 < nch) stage(ch + RDU_ST - 1);
-        cp_async_commit();
-        cp_async_wait_group<RDU_ST - 1>();
-        __syncthreads();
-        if (last_pass && t < RDU_S * RDU_ROWS / 4) {
-          const int s0 = ch * RDU_S;
-          const int r = t / (RDU_ROWS / 4), c4 = (t % (RDU_ROWS / 4)) * 4;
-          if (s0 + r < nq)
-            *reinterpret_cast<float4*>(LGd + (int64_t)(s0 + r) * ldu + k0 + c4) = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        const int ns = min(RDU_S, nq - ch * RDU_S);
-        for (int j = 0; j < ns; ++j) {
-          const float4 xv = *reinterpret_cast<const float4*>(&xs[bf][j][l * 4]);
-          const float2 l2 = *reinterpret_cast<const float2*>(&ls[bf][j][w * 2]);
-          const float lgv[2] = {l2.x, l2.y};
+    };
+    // optimizer state of this lane's two elements, loaded now and used after the sum
+    float wv[2], mv[2], vv[2];
+    int64_t roff[2];
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            if (lgv[i] != 0.0f) {
-              if (g0 == 0) gb[i] = __fadd_rn(gb[i], lgv[i]);
-              g[i][0] = __fadd_rn(g[i][0], __fmul_rn(lgv[i], xv.x));
-              g[i][1] = __fadd_rn(g[i][1], __fmul_rn(lgv[i], xv.y));
-              g[i][2] = __fadd_rn(g[i][2], __fmul_rn(lgv[i], xv.z));
-              g[i][3] = __fadd_rn(g[i][3], __fmul_rn(lgv[i], xv.w));
-            }
-          }
-        }
-        __syncthreads();  // buffer bf is restaged RDU_ST - 1 chunks later
-      }
-      cp_async_wait_group<0>();
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        if (roff[i] < 0) continue;
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (c + e < d) opt_apply(wv[i][e], mv[i][e], vv[i][e], g[i][e], o);
-        store4<W>(Wm, roff[i], wv[i]);
-        *reinterpret_cast<float4*>(m + roff[i]) = make_float4(mv[i][0], mv[i][1], mv[i][2], mv[i][3]);
-        if (o.opt == KL_OPT_ADAM)
-          *reinterpret_cast<float4*>(v + roff[i]) = make_float4(vv[i][0], vv[i][1], vv[i][2], vv[i][3]);
+    for (int i = 0; i < 2; ++i) {
+      const int k = k0 + w * 2 + i;
+      roff[i] = -1;
+      if (k < n && cin) {
+        roff[i] = (int64_t)touched[k] * ldw + c;
+        wv[i] = to_f(static_cast<const W*>(Wm)[roff[i]]);
+        mv[i] = m[roff[i]];
+        vv[i] = o.opt == KL_OPT_ADAM ? v[roff[i]] : 0.f;
       }
     }
-    if (l < 2) {
+    float g[2] = {0.f, 0.f}, gb[2] = {0.f, 0.f};
+    __syncthreads();  // previous users of the buffers are done
+#pragma unroll
+    for (int p = 0; p < RDU_ST - 1; ++p) {
+      if (p < nch) stage(p);
+      cp_async_commit();  // one group per stage slot (possibly empty) keeps the wait count uniform
+    }
+    for (int ch = 0; ch < nch; ++ch) {
+      const int bf = ch % RDU_ST;
+      if (ch + RDU_ST - 1 < nch) stage(ch + RDU_ST - 1);
+      cp_async_commit();
+      cp_async_wait_group<RDU_ST - 1>();
+      __syncthreads();
+      const int ns = min(RDU_S, nq - ch * RDU_S);
+      for (int j = 0; j < ns; ++j) {
+        const float xv = xs[bf][j][l];
+        const float2 l2 = *reinterpret_cast<const float2*>(&ls[bf][j][w * 2]);
+        if (l2.x != 0.0f) {
+          gb[0] = __fadd_rn(gb[0], l2.x);
+          g[0] = __fadd_rn(g[0], __fmul_rn(l2.x, xv));
+        }
+        if (l2.y != 0.0f) {
+          gb[1] = __fadd_rn(gb[1], l2.y);
+          g[1] = __fadd_rn(g[1], __fmul_rn(l2.y, xv));
+        }
+      }
+      __syncthreads();  // buffer bf is restaged RDU_ST - 1 chunks later
+    }
+    cp_async_wait_group<0>();
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      if (roff[i] < 0) continue;
+      opt_apply(wv[i], mv[i], vv[i], g[i], o);
+      static_cast<W*>(Wm)[roff[i]] = from_f<W>(wv[i]);
+      m[roff[i]] = mv[i];
+      if (o.opt == KL_OPT_ADAM) v[roff[i]] = vv[i];
+    }
+    if (cb == 0 && l < 2) {
       const int k = k0 + w * 2 + l;
       if (k < n) {
         const uint32_t row = touched[k];
         bias_update(bias, mb, vb, row, l == 0 ? gb[0] : gb[1], o);
-        atomicAnd(bits + (row >> 5), ~(1u << (row & 31)));
+        atomicAnd(bits + (row >> 5), ~(1u << (row & 31)));  // ready for the next step's mark
       }
     }
   }
 }
 
+// LGd[s][slot] = 0 for the slots the update read (restores the zero invariant).
+__global__ void rm_lg_zero_kernel(float* LGd, int64_t ldu, const uint32_t* ctr, int nq) {
+  const int s = blockIdx.x;
+  if (s >= nq) return;
+  const int n = (int)ctr[0];
+  float* row = LGd + (int64_t)s * ldu;
+  for (int k = threadIdx.x * 4; k < n; k += blockDim.x * 4) {
+    if (k + 4 <= n) *reinterpret_cast<float4*>(row + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+    else
+      for (int q = k; q < n; ++q) row[q] = 0.f;
+  }
+}
+
 // Feature-major (layer 0) update, in two passes.
 //
-// (1) fm_grad_kernel: one warp per touched feature row f (a feature present in
-//     the batch).  The gradient of neuron j at f is sum over the samples s that
-//     contain f of x_s[f] * lg_s[j], in ascending s (the batched oracle's
-//     order).  The segment's (sample, value) pairs arrive unordered, so the
-//     warp marks them in a per-sample bitmask, compacts the set bits into an
-//     ascending sample list in shared memory, and then sums with FM_PF loads
-//     of lg rows in flight per lane.  The row goes to G[k] (k = position of f
-//     in the touched list) and hist[f] becomes k + 1.
+// (1) fm_grad_kernel: one warp per (touched feature row f, 32 neurons).  The
+//     gradient of neuron j at f is sum over the samples s that contain f of
+//     x_s[f] * lg_s[j], in ascending s (the batched oracle's order).  The
+//     segment's (sample, value) pairs arrive unordered, so the warp marks them
+//     in a per-sample bitmask, compacts the set bits into an ascending sample
+//     list in shared memory, and then sums with FM_PF lg loads in flight per
+//     lane.  The row goes to G[k] (k = position of f in the touched list) and
+//     slot[f] becomes k + 1.
 // (2) fm_adam_kernel: streams W, m, v of ALL d feature rows (Adam runs over
 //     every element of a touched neuron, optim/adam.rs:57-68), FM_UNROLL
-//     16-byte vectors in flight per thread; rows with hist[f] != 0 read their
-//     gradient from G, the rest use g = 0.  fm_hist_clear_kernel then zeroes
-//     hist for the next step.
+//     16-byte vectors in flight per thread; rows with slot[f] != 0 read their
+//     gradient from G, the rest use g = 0.  The row's first lane then zeroes
+//     slot[f] and hist[f] for the next step (fm_hist_clear_kernel does it when
+//     a feature row spans several warps).
 // ---------------------------------------------------------------------------
 constexpr int FM_PF = 16;
 constexpr int FM_UNROLL = 2;
@@ -811,6 +809,7 @@ constexpr int FM_NT = 256;
 
 __global__ void __launch_bounds__(UPD_WARPS * 32)
     fm_grad_kernel(int N, const float* lgd, int ldl, SegScratch S, int nwords, float* G, int ldg) {
+  // one warp per (touched feature, 32 neurons): lane l sums column cb*32 + l
   extern __shared__ __align__(16) unsigned char dyn[];
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   // per warp: mask[nwords] u32, coef[32*nwords] f32, list[32*nwords] u32
@@ -820,7 +819,9 @@ __global__ void __launch_bounds__(UPD_WARPS * 32)
   for (int i = l; i < nwords; i += 32) mask[i] = 0;
   __syncwarp();
   const int n = (int)S.ctr[0];
-  for (int k = blockIdx.x * UPD_WARPS + w; k < n; k += gridDim.x * UPD_WARPS) {
+  const int ncb = (N + 31) / 32;
+  for (int item = blockIdx.x * UPD_WARPS + w; item < n * ncb; item += gridDim.x * UPD_WARPS) {
+    const int k = item / ncb, cb = item % ncb;
     const uint32_t f = S.touched[k];
     const uint32_t len = S.hist[f];
     seg_to_mask(S.ent_s, S.ent_v, S.cur[f] - len, len, coef, mask);
@@ -841,43 +842,34 @@ __global__ void __launch_bounds__(UPD_WARPS * 32)
       if (w0 + l < nwords) mask[w0 + l] = 0;
     }
     __syncwarp();
-    float* grow = G + (int64_t)k * ldg;
-    for (int g0 = 0; g0 < N; g0 += 128) {
-      const int c = g0 + l * 4;
-      if (c >= N) continue;
-      float g[4] = {0.f, 0.f, 0.f, 0.f};
+    const int c = cb * 32 + l;
+    float g = 0.f;
+    if (c < N) {
       for (int i0 = 0; i0 < base; i0 += FM_PF) {
-        float4 lv[FM_PF];
-        float cf[FM_PF];
+        float lv[FM_PF], cf[FM_PF];
 #pragma unroll
         for (int u = 0; u < FM_PF; ++u) {
           if (i0 + u < base) {
             const uint32_t s = list[i0 + u];
             cf[u] = coef[s];
-            lv[u] = *reinterpret_cast<const float4*>(lgd + (int64_t)s * ldl + c);
+            lv[u] = lgd[(int64_t)s * ldl + c];
           }
         }
 #pragma unroll
-        for (int u = 0; u < FM_PF; ++u) {
-          if (i0 + u < base) {
-            g[0] = __fadd_rn(g[0], __fmul_rn(cf[u], lv[u].x));
-            g[1] = __fadd_rn(g[1], __fmul_rn(cf[u], lv[u].y));
-            g[2] = __fadd_rn(g[2], __fmul_rn(cf[u], lv[u].z));
-            g[3] = __fadd_rn(g[3], __fmul_rn(cf[u], lv[u].w));
-          }
-        }
+        for (int u = 0; u < FM_PF; ++u)
+          if (i0 + u < base) g = __fadd_rn(g, __fmul_rn(cf[u], lv[u]));
       }
-      *reinterpret_cast<float4*>(grow + c) = make_float4(g[0], g[1], g[2], g[3]);
     }
+    if (c < ldg) G[(int64_t)k * ldg + c] = g;  // the row pitch may end before the last 32-column block
     __syncwarp();
-    if (l == 0) S.hist[f] = (uint32_t)k + 1u;
+    if (cb == 0 && l == 0) S.slot[f] = (uint32_t)k + 1u;
   }
 }
 
 template <class W>
 __global__ void __launch_bounds__(FM_NT, 4)
     fm_adam_kernel(void* Wm, int ldw, int64_t nvec, int vpr, int N, float* m, float* v,
-                   const uint32_t* tmask, uint32_t* hist, const float* G, int ldg, const OptStep* op) {
+                   const uint32_t* tmask, uint32_t* hist, uint32_t* slot, const float* G, int ldg, const OptStep* op) {
   const OptStep o = *op;
   // vector q = f * vpr + j covers elements [4j, 4j+4) of feature row f
   const int64_t q0 = (int64_t)blockIdx.x * (FM_NT * FM_UNROLL) + threadIdx.x;
@@ -908,7 +900,7 @@ __global__ void __launch_bounds__(FM_NT, 4)
           vv[u][0] = vv[u][1] = vv[u][2] = vv[u][3] = 0.f;
         }
       }
-      hv[u] = hist[f];  // read for every row: its first lane clears it below
+      hv[u] = slot[f];  // read for every row: its first lane clears it below
     }
   }
   __syncwarp();  // every lane has read hist before the row's first lane clears it
@@ -918,7 +910,10 @@ __global__ void __launch_bounds__(FM_NT, 4)
     if (q >= nvec) continue;
     const int64_t f = q / vpr;
     const int c = (int)(q - f * vpr) * 4;
-    if (c == 0 && hv[u]) hist[f] = 0;  // ready for the next step
+    if (c == 0 && hv[u]) {  // ready for the next step
+      slot[f] = 0;
+      hist[f] = 0;
+    }
     if (!live[u]) continue;
     float g[4] = {0.f, 0.f, 0.f, 0.f};
     if (hv[u]) {
@@ -939,7 +934,10 @@ __global__ void __launch_bounds__(FM_NT, 4)
 // hist[f] = 0 for the touched features (after fm_adam_kernel read them).
 __global__ void fm_hist_clear_kernel(SegScratch S) {
   const int k = blockIdx.x * blockDim.x + threadIdx.x;
-  if (k < (int)S.ctr[0]) S.hist[S.touched[k]] = 0;
+  if (k < (int)S.ctr[0]) {
+    S.hist[S.touched[k]] = 0;
+    S.slot[S.touched[k]] = 0;
+  }
 }
 
 // Bias gradient of every touched neuron: one warp per neuron loads 32
@@ -1211,20 +1209,16 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
   rm_dense_scatter_kernel<<<g2, 256, 0, st>>>(A, D.slot_of, D.LGd, D.ldu);
   count_launch();
   const int64_t maxn = std::min<int64_t>((int64_t)N, (int64_t)nq * A.stride);
-  const int grid = (int)std::min<int64_t>(upd_grid() * 3 / 8, ceil_div(maxn, RDU_ROWS));
-  const size_t sm = sizeof(float) * RDU_ST * RDU_S * (128 + RDU_ROWS);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(rm_dense_update_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    cudaFuncSetAttribute(rm_dense_update_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    attr = true;
-  }
+  const int ncb = (int)ceil_div(d, RDU_COLS);
+  const int grid = (int)std::min<int64_t>((int64_t)upd_grid() * 2, ceil_div(maxn, RDU_ROWS) * ncb);
   if (wdtype == KL_DTYPE_BF16)
-    rm_dense_update_kernel<__nv_bfloat16><<<grid, 256, sm, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X,
+    rm_dense_update_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X,
                                                                 ldx, D.bits, D.touched, D.ctr, D.LGd, D.ldu, nq, o);
   else
-    rm_dense_update_kernel<float><<<grid, 256, sm, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X, ldx,
+    rm_dense_update_kernel<float><<<grid, 256, 0, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X, ldx,
                                                         D.bits, D.touched, D.ctr, D.LGd, D.ldu, nq, o);
+  count_launch();
+  rm_lg_zero_kernel<<<nq, 256, 0, st>>>(D.LGd, D.ldu, D.ctr, nq);
   count_launch();
 }
 
@@ -1277,7 +1271,7 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
     cudaFuncSetAttribute(fm_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr = true;
   }
-  const int ggrid = (int)std::min<int64_t>(upd_grid(), ceil_div(d, UPD_WARPS));
+  const int ggrid = (int)std::min<int64_t>((int64_t)upd_grid() * 2, ceil_div((int64_t)d * ceil_div(N, 32), UPD_WARPS));
   fm_grad_kernel<<<ggrid, UPD_WARPS * 32, sm, st>>>(N, lgd, ldl, S, nwords, G, ldl);
   count_launch();
   const int vpr = ldl / 4;  // vectors per feature row (ldw == ldl == pitch of N)
@@ -1286,10 +1280,10 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
   if (around_adam) around_adam(hook_arg, 0);
   if (wdtype == KL_DTYPE_BF16)
     fm_adam_kernel<__nv_bfloat16><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, nvec, vpr, N, m, v,
-                                                           touched_mask, S.hist, G, ldl, o);
+                                                           touched_mask, S.hist, S.slot, G, ldl, o);
   else
     fm_adam_kernel<float><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, nvec, vpr, N, m, v, touched_mask,
-                                                   S.hist, G, ldl, o);
+                                                   S.hist, S.slot, G, ldl, o);
   count_launch();
   if (around_adam) around_adam(hook_arg, 1);
   if (!(vpr == 32 || vpr == 8 || vpr == 16 || vpr == 4 || vpr == 2 || vpr == 1) || (vpr >= 32 && vpr % 32)) {
