@@ -1005,7 +1005,7 @@ struct Layer {
   DBuf bkt, ids, cnt, pre, post, lg, h, dx_in, dxpart, lgd, tmask, gfeat;
   DBuf dbits, dtouched, dslot, dlg;  // dense-collision update scratch (row-major layers)
   int64_t dldu = 0;
-  DBuf hist, cur, touched, ctr, ent_s, ent_v, fslot;
+  DBuf hist, cur, touched, ctr, ent_s, ent_v, fslot, flong;
   size_t ent_cap = 0;
   DBuf stats;  // u64 [3]: active_sum, touched_rows, input_nnz
   uint64_t examples = 0, steps = 0, rebuilds = 0, input_nnz = 0;
@@ -1363,9 +1363,9 @@ struct kl_net_s {
       Phase ph(this, l, KL_PHASE_UPDATE);
       Layer& L = *layers[l];
       unsigned long long* stat = L.stats.as<unsigned long long>() + 1;
-      ck(cudaMemsetAsync(L.ctr.p, 0, 8, st), "memset");
+      ck(cudaMemsetAsync(L.ctr.p, 0, 16, st), "memset");
       SegScratch S{L.hist.as<uint32_t>(), L.cur.as<uint32_t>(), L.touched.as<uint32_t>(), L.ctr.as<uint32_t>(),
-                   L.ent_s.as<uint32_t>(), L.ent_v.as<float>(), L.fslot.as<uint32_t>()};
+                   L.ent_s.as<uint32_t>(), L.ent_v.as<float>(), L.fslot.as<uint32_t>(), L.flong.as<uint32_t>()};
       if (L.fm) {
         launch_fm_update(L.W.p, wdtype, L.ldw, L.d, L.N, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
                          L.mb.as<float>(), L.vb.as<float>(), in, L.lgd.as<float>(), L.ldN, L.tmask.as<uint32_t>(),
@@ -1724,10 +1724,11 @@ void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_
   L.hist.alloc(rows * 4);
   L.cur.alloc(rows * 4);
   L.touched.alloc(rows * 4);
-  L.ctr.alloc(8);
+  L.ctr.alloc(16);
   ck(cudaMemsetAsync(L.hist.p, 0, rows * 4, st), "memset");
   if (L.fm) {
     L.fslot.alloc(rows * 4);
+    L.flong.alloc(rows * 4);
     ck(cudaMemsetAsync(L.fslot.p, 0, rows * 4, st), "memset");
   }
   if (!L.fm) {

@@ -200,10 +200,11 @@ struct SegScratch {
   uint32_t* hist;     // [rows] zero between uses
   uint32_t* cur;      // [rows]
   uint32_t* touched;  // [rows]
-  uint32_t* ctr;      // [2]: touched count, entry total (zeroed per use)
+  uint32_t* ctr;      // [4]: touched count, entry total, long-segment count (zeroed per use)
   uint32_t* ent_s;    // [entries]
   float* ent_v;       // [entries]
   uint32_t* slot;     // [rows] feature-major update: gradient row + 1 (0 = none), zero between uses
+  uint32_t* longk;    // [rows] feature-major update: touched positions of long segments (count in ctr[2])
 };
 void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
                       float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,

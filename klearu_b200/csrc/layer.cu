@@ -788,14 +788,15 @@ __global__ void rm_lg_zero_kernel(float* LGd, int64_t ldu, const uint32_t* ctr, 
 
 // Feature-major (layer 0) update, in two passes.
 //
-// (1) fm_grad_kernel: one warp per (touched feature row f, 32 neurons).  The
-//     gradient of neuron j at f is sum over the samples s that contain f of
+// (1) fm_grad_short_kernel / fm_grad_long_kernel: the gradient of neuron j
+//     at feature row f is sum over the samples s that contain f of
 //     x_s[f] * lg_s[j], in ascending s (the batched oracle's order).  The
-//     segment's (sample, value) pairs arrive unordered, so the warp marks them
-//     in a per-sample bitmask, compacts the set bits into an ascending sample
-//     list in shared memory, and then sums with FM_PF lg loads in flight per
-//     lane.  The row goes to G[k] (k = position of f in the touched list) and
-//     slot[f] becomes k + 1.
+//     segment's (sample, value) pairs arrive unordered.  Segments of at most
+//     FM_SHORT pairs (nearly all of them) are put in order by ranking the
+//     pairs inside one warp, which then sums 4 neurons per lane; longer ones
+//     are queued and a block per feature orders them through a per-sample
+//     bitmask.  The row goes to G[k] (k = position of f in the touched list)
+//     and slot[f] becomes k + 1.
 // (2) fm_adam_kernel: streams W, m, v of ALL d feature rows (Adam runs over
 //     every element of a touched neuron, optim/adam.rs:57-68), FM_UNROLL
 //     16-byte vectors in flight per thread; rows with slot[f] != 0 read their
@@ -807,62 +808,141 @@ constexpr int FM_PF = 16;
 constexpr int FM_UNROLL = 2;
 constexpr int FM_NT = 256;
 
-__global__ void __launch_bounds__(UPD_WARPS * 32)
-    fm_grad_kernel(int N, const float* lgd, int ldl, SegScratch S, int nwords, float* G, int ldg) {
-  // one warp per (touched feature, 32 neurons): lane l sums column cb*32 + l
-  extern __shared__ __align__(16) unsigned char dyn[];
+constexpr int FM_SHORT = 32;  // segments up to this length are ranked inside one warp
+constexpr int FM_GW = 8;      // warps per fm_grad_short block
+
+__global__ void __launch_bounds__(FM_GW * 32)
+    fm_grad_short_kernel(int N, const float* lgd, int ldl, SegScratch S, float* G, int ldg) {
+  // one warp per touched feature.  Lane e holds the segment's e-th (sample,
+  // value) pair; its rank among the pairs (sample id, then lane on a tie) is
+  // its place in the ascending list.  Lane l then sums neurons [4l, 4l + 4)
+  // of each 128-neuron chunk over the list.  Longer segments are queued for
+  // fm_grad_long_kernel.
+  __shared__ uint32_t ls[FM_GW][FM_SHORT];
+  __shared__ float lv[FM_GW][FM_SHORT];
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  // per warp: mask[nwords] u32, coef[32*nwords] f32, list[32*nwords] u32
-  uint32_t* mask = reinterpret_cast<uint32_t*>(dyn) + (size_t)w * nwords * 65;
-  float* coef = reinterpret_cast<float*>(mask + nwords);
-  uint32_t* list = mask + nwords + 32 * nwords;
-  for (int i = l; i < nwords; i += 32) mask[i] = 0;
-  __syncwarp();
   const int n = (int)S.ctr[0];
-  const int ncb = (N + 31) / 32;
-  for (int item = blockIdx.x * UPD_WARPS + w; item < n * ncb; item += gridDim.x * UPD_WARPS) {
-    const int k = item / ncb, cb = item % ncb;
+  for (int k = blockIdx.x * FM_GW + w; k < n; k += gridDim.x * FM_GW) {
     const uint32_t f = S.touched[k];
-    const uint32_t len = S.hist[f];
-    seg_to_mask(S.ent_s, S.ent_v, S.cur[f] - len, len, coef, mask);
-    // ascending sample list: word i's bits go after the bits of words < i
-    int base = 0;
-    for (int w0 = 0; w0 < nwords; w0 += 32) {
-      const uint32_t mw = w0 + l < nwords ? mask[w0 + l] : 0u;
-      const int c = __popc(mw);
-      const int inc = warp_incl_scan(c);
-      int pos = base + inc - c;
-      uint32_t b = mw;
-      while (b) {
-        const int bit = __ffs(b) - 1;
-        b &= b - 1;
-        list[pos++] = (uint32_t)((w0 + l) * 32 + bit);
-      }
-      base += __shfl_sync(FULL, inc, 31);
-      if (w0 + l < nwords) mask[w0 + l] = 0;
+    const int len = (int)S.hist[f];
+    if (l == 0) S.slot[f] = (uint32_t)k + 1u;
+    if (len > FM_SHORT) {
+      if (l == 0) S.longk[atomicAdd(&S.ctr[2], 1u)] = (uint32_t)k;
+      continue;
+    }
+    const uint32_t start = S.cur[f] - (uint32_t)len;
+    uint32_t s = 0xffffffffu;
+    float v = 0.f;
+    if (l < len) {
+      s = S.ent_s[start + l];
+      v = S.ent_v[start + l];
+    }
+    int r = 0;
+    for (int j = 0; j < len; ++j) {
+      const uint32_t sj = __shfl_sync(FULL, s, j);
+      r += (sj < s) | ((sj == s) & (j < l));
+    }
+    if (l < len) {
+      ls[w][r] = s;
+      lv[w][r] = v;
     }
     __syncwarp();
-    const int c = cb * 32 + l;
-    float g = 0.f;
-    if (c < N) {
-      for (int i0 = 0; i0 < base; i0 += FM_PF) {
-        float lv[FM_PF], cf[FM_PF];
+    for (int c0 = 0; c0 < ldg; c0 += 128) {
+      const int c = c0 + 4 * l;
+      float g[4] = {0.f, 0.f, 0.f, 0.f};
+      if (c < N) {
+        for (int i0 = 0; i0 < len; i0 += 8) {
+          float4 q[8];
 #pragma unroll
-        for (int u = 0; u < FM_PF; ++u) {
-          if (i0 + u < base) {
-            const uint32_t s = list[i0 + u];
-            cf[u] = coef[s];
-            lv[u] = lgd[(int64_t)s * ldl + c];
+          for (int u = 0; u < 8; ++u)
+            if (i0 + u < len) q[u] = *reinterpret_cast<const float4*>(lgd + (int64_t)ls[w][i0 + u] * ldl + c);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            if (i0 + u < len) {
+              const float x = lv[w][i0 + u];
+              g[0] = __fadd_rn(g[0], __fmul_rn(x, q[u].x));
+              g[1] = __fadd_rn(g[1], __fmul_rn(x, q[u].y));
+              g[2] = __fadd_rn(g[2], __fmul_rn(x, q[u].z));
+              g[3] = __fadd_rn(g[3], __fmul_rn(x, q[u].w));
+            }
           }
         }
 #pragma unroll
-        for (int u = 0; u < FM_PF; ++u)
-          if (i0 + u < base) g = __fadd_rn(g, __fmul_rn(cf[u], lv[u]));
+        for (int j = 0; j < 4; ++j)
+          if (c + j >= N) g[j] = 0.f;
       }
+      if (c < ldg) *reinterpret_cast<float4*>(G + (int64_t)k * ldg + c) = make_float4(g[0], g[1], g[2], g[3]);
     }
-    if (c < ldg) G[(int64_t)k * ldg + c] = g;  // the row pitch may end before the last 32-column block
-    __syncwarp();
-    if (cb == 0 && l == 0) S.slot[f] = (uint32_t)k + 1u;
+    __syncwarp();  // ls / lv reused by the warp's next feature
+  }
+}
+
+__global__ void __launch_bounds__(1024)
+    fm_grad_long_kernel(int N, const float* lgd, int ldl, SegScratch S, int nwords, float* G, int ldg) {
+  // one block per queued feature (segment longer than FM_SHORT): the block
+  // marks the samples in a bitmask, warp 0 compacts the set bits into an
+  // ascending list, then warp w sums neuron 32w + lane over it
+  extern __shared__ __align__(16) unsigned char dyn[];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  uint32_t* mask = reinterpret_cast<uint32_t*>(dyn);   // [nwords]
+  float* coef = reinterpret_cast<float*>(mask + nwords);  // [32*nwords]
+  uint32_t* list = mask + nwords + 32 * nwords;          // [32*nwords]
+  __shared__ int base_s;
+  for (int i = threadIdx.x; i < nwords; i += blockDim.x) mask[i] = 0;
+  __syncthreads();
+  const int n = (int)S.ctr[2];
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const uint32_t k = S.longk[i];
+    const uint32_t f = S.touched[k];
+    const uint32_t len = S.hist[f];
+    const uint32_t start = S.cur[f] - len;
+    for (uint32_t e = threadIdx.x; e < len; e += blockDim.x) {
+      const uint32_t s = S.ent_s[start + e];
+      coef[s] = S.ent_v[start + e];
+      atomicOr(&mask[s >> 5], 1u << (s & 31));
+    }
+    __syncthreads();
+    if (w == 0) {
+      int base = 0;
+      for (int w0 = 0; w0 < nwords; w0 += 32) {
+        const uint32_t mw = w0 + l < nwords ? mask[w0 + l] : 0u;
+        const int c = __popc(mw);
+        const int inc = warp_incl_scan(c);
+        int pos = base + inc - c;
+        uint32_t b = mw;
+        while (b) {
+          const int bit = __ffs(b) - 1;
+          b &= b - 1;
+          list[pos++] = (uint32_t)((w0 + l) * 32 + bit);
+        }
+        base += __shfl_sync(FULL, inc, 31);
+        if (w0 + l < nwords) mask[w0 + l] = 0;
+      }
+      if (l == 0) base_s = base;
+    }
+    __syncthreads();
+    const int base = base_s;
+    for (int c = threadIdx.x; c < ldg; c += blockDim.x) {
+      float g = 0.f;
+      if (c < N) {
+        for (int i0 = 0; i0 < base; i0 += FM_PF) {
+          float lv[FM_PF], cf[FM_PF];
+#pragma unroll
+          for (int u = 0; u < FM_PF; ++u) {
+            if (i0 + u < base) {
+              const uint32_t s = list[i0 + u];
+              cf[u] = coef[s];
+              lv[u] = lgd[(int64_t)s * ldl + c];
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < FM_PF; ++u)
+            if (i0 + u < base) g = __fadd_rn(g, __fmul_rn(cf[u], lv[u]));
+        }
+      }
+      G[(int64_t)k * ldg + c] = g;
+    }
+    __syncthreads();  // list / coef reused by the next feature
   }
 }
 
@@ -1264,15 +1344,18 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
   count_launch();
   fm_scatter_kernel<<<nq, 256, 0, st>>>(in, S.cur, S.ent_s, S.ent_v, d);
   count_launch();
+  const int ggrid = (int)std::min<int64_t>((int64_t)upd_grid() * 2, ceil_div(d, FM_GW));
+  fm_grad_short_kernel<<<ggrid, FM_GW * 32, 0, st>>>(N, lgd, ldl, S, G, ldl);
+  count_launch();
   const int nwords = (int)ceil_div(nq, 32);
-  const size_t sm = (size_t)UPD_WARPS * nwords * 4 * 65;
+  const size_t sm = (size_t)nwords * 4 * 65;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(fm_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(fm_grad_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr = true;
   }
-  const int ggrid = (int)std::min<int64_t>((int64_t)upd_grid() * 2, ceil_div((int64_t)d * ceil_div(N, 32), UPD_WARPS));
-  fm_grad_kernel<<<ggrid, UPD_WARPS * 32, sm, st>>>(N, lgd, ldl, S, nwords, G, ldl);
+  const int lthreads = std::min(1024, 32 * (int)ceil_div(N, 32));
+  fm_grad_long_kernel<<<upd_grid(), lthreads, sm, st>>>(N, lgd, ldl, S, nwords, G, ldl);
   count_launch();
   const int vpr = ldl / 4;  // vectors per feature row (ldw == ldl == pitch of N)
   const int64_t nvec = (int64_t)d * vpr;
