@@ -798,14 +798,13 @@ __global__ void rm_lg_zero_kernel(float* LGd, int64_t ldu, const uint32_t* ctr, 
 //     bitmask.  The row goes to G[k] (k = position of f in the touched list)
 //     and slot[f] becomes k + 1.
 // (2) fm_adam_kernel: streams W, m, v of ALL d feature rows (Adam runs over
-//     every element of a touched neuron, optim/adam.rs:57-68), FM_UNROLL
-//     16-byte vectors in flight per thread; rows with slot[f] != 0 read their
+//     every element of a touched neuron, optim/adam.rs:57-68) with persistent
+//     warps that prefetch their next item; rows with slot[f] != 0 read their
 //     gradient from G, the rest use g = 0.  The row's first lane then zeroes
 //     slot[f] and hist[f] for the next step (fm_hist_clear_kernel does it when
-//     a feature row spans several warps).
+//     a feature row spans several items).
 // ---------------------------------------------------------------------------
 constexpr int FM_PF = 16;
-constexpr int FM_UNROLL = 2;
 constexpr int FM_NT = 256;
 
 constexpr int FM_SHORT = 32;  // segments up to this length are ranked inside one warp
@@ -946,68 +945,112 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
+// One work item = rpw whole feature rows (vpr <= 32 vectors each: lane l
+// holds vector l % vpr of row l / vpr) or, for vpr > 32, the k-th 32-vector
+// slice of one row (nk slices per row).
+struct FmItem {
+  float w[4], m[4], v[4], g[4];
+  int64_t off;
+  int f;
+  uint32_t hv, upd;  // gradient slot + 1 (0: no gradient), per-element update bits
+  bool valid;
+};
+
+__device__ __forceinline__ bool fm_item_pos(int i, int rpw, int nk, int vpr, int d, int r_l, int j_l, int& f,
+                                            int& c) {
+  int j;
+  if (nk == 1) {
+    f = i * rpw + r_l;
+    j = j_l;
+  } else {
+    f = i / nk;
+    j = (i - f * nk) * 32 + (int)(threadIdx.x & 31);
+  }
+  c = 4 * j;
+  return r_l < rpw && f < d && j < vpr;
+}
+
+template <class W>
+__device__ __forceinline__ void fm_item_load(FmItem& it, int i, uint32_t hv, const void* Wm, int ldw, int d, int vpr,
+                                             int rpw, int nk, int N, const float* m, const float* v,
+                                             const uint32_t* tmask, const float* G, int ldg, int opt, int r_l,
+                                             int j_l) {
+  int c;
+  it.valid = fm_item_pos(i, rpw, nk, vpr, d, r_l, j_l, it.f, c);
+  it.hv = hv;
+  it.upd = 0;
+  if (!it.valid) return;
+  const uint32_t tw = c < N ? tmask[c >> 5] >> (c & 31) : 0u;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    if (c + q < N && ((tw >> q) & 1u)) it.upd |= 1u << q;
+  it.off = (int64_t)it.f * ldw + c;
+  if (!it.upd) return;
+  load4<W>(Wm, it.off, it.w);
+  const float4 m4 = *reinterpret_cast<const float4*>(m + it.off);
+  it.m[0] = m4.x; it.m[1] = m4.y; it.m[2] = m4.z; it.m[3] = m4.w;
+  if (opt == KL_OPT_ADAM) {
+    const float4 v4 = *reinterpret_cast<const float4*>(v + it.off);
+    it.v[0] = v4.x; it.v[1] = v4.y; it.v[2] = v4.z; it.v[3] = v4.w;
+  } else {
+    it.v[0] = it.v[1] = it.v[2] = it.v[3] = 0.f;
+  }
+  if (hv) {
+    const float4 g4 = *reinterpret_cast<const float4*>(G + (int64_t)(hv - 1) * ldg + c);
+    it.g[0] = g4.x; it.g[1] = g4.y; it.g[2] = g4.z; it.g[3] = g4.w;
+  } else {
+    it.g[0] = it.g[1] = it.g[2] = it.g[3] = 0.f;
+  }
+}
+
+// Persistent: warp w walks items w, w + nwarps, ...  While it updates item i
+// it already has the W/m/v/G loads of its next item and the slot load of the
+// one after in flight, so every warp keeps memory requests outstanding
+// through its arithmetic.
 template <class W>
 __global__ void __launch_bounds__(FM_NT, 4)
-    fm_adam_kernel(void* Wm, int ldw, int64_t nvec, int vpr, int N, float* m, float* v,
+    fm_adam_kernel(void* Wm, int ldw, int d, int vpr, int rpw, int nk, int N, float* m, float* v,
                    const uint32_t* tmask, uint32_t* hist, uint32_t* slot, const float* G, int ldg, const OptStep* op) {
   const OptStep o = *op;
-  // vector q = f * vpr + j covers elements [4j, 4j+4) of feature row f
-  const int64_t q0 = (int64_t)blockIdx.x * (FM_NT * FM_UNROLL) + threadIdx.x;
-  float w[FM_UNROLL][4], mm[FM_UNROLL][4], vv[FM_UNROLL][4];
-  uint32_t hv[FM_UNROLL];
-  bool live[FM_UNROLL], upd[FM_UNROLL][4];
-#pragma unroll
-  for (int u = 0; u < FM_UNROLL; ++u) {
-    const int64_t q = q0 + (int64_t)u * FM_NT;
-    live[u] = false;
-    hv[u] = 0;
-    if (q < nvec) {
-      const int64_t f = q / vpr;
-      const int c = (int)(q - f * vpr) * 4;
-      const uint32_t tw = c < N ? tmask[c >> 5] >> (c & 31) : 0u;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) upd[u][i] = c + i < N && ((tw >> i) & 1u);
-      live[u] = upd[u][0] | upd[u][1] | upd[u][2] | upd[u][3];
-      if (live[u]) {
-        const int64_t off = f * ldw + c;
-        load4<W>(Wm, off, w[u]);
-        const float4 m4 = *reinterpret_cast<const float4*>(m + off);
-        mm[u][0] = m4.x; mm[u][1] = m4.y; mm[u][2] = m4.z; mm[u][3] = m4.w;
-        if (o.opt == KL_OPT_ADAM) {
-          const float4 v4 = *reinterpret_cast<const float4*>(v + off);
-          vv[u][0] = v4.x; vv[u][1] = v4.y; vv[u][2] = v4.z; vv[u][3] = v4.w;
-        } else {
-          vv[u][0] = vv[u][1] = vv[u][2] = vv[u][3] = 0.f;
-        }
+  const int lane = threadIdx.x & 31;
+  const int nwarps = gridDim.x * (FM_NT / 32);
+  const int i0 = blockIdx.x * (FM_NT / 32) + (threadIdx.x >> 5);
+  const int nitems = nk == 1 ? (int)ceil_div(d, rpw) : d * nk;
+  const int r_l = nk == 1 ? lane / vpr : 0;
+  const int j_l = nk == 1 ? lane - r_l * vpr : lane;
+  int f, c;
+  FmItem cur, nxt;
+  uint32_t hv = 0;
+  if (i0 < nitems && fm_item_pos(i0, rpw, nk, vpr, d, r_l, j_l, f, c)) hv = slot[f];
+  fm_item_load<W>(cur, i0, hv, Wm, ldw, d, vpr, rpw, nk, N, m, v, tmask, G, ldg, o.opt, r_l, j_l);
+  uint32_t hv_n = 0;
+  if (i0 + nwarps < nitems && fm_item_pos(i0 + nwarps, rpw, nk, vpr, d, r_l, j_l, f, c)) hv_n = slot[f];
+  for (int i = i0; i < nitems; i += nwarps) {
+    const int in = i + nwarps;
+    if (in < nitems)
+      fm_item_load<W>(nxt, in, hv_n, Wm, ldw, d, vpr, rpw, nk, N, m, v, tmask, G, ldg, o.opt, r_l, j_l);
+    uint32_t hv_nn = 0;
+    if (in + nwarps < nitems && fm_item_pos(in + nwarps, rpw, nk, vpr, d, r_l, j_l, f, c)) hv_nn = slot[f];
+    __syncwarp();  // every lane of the item's rows has used its slot value
+    if (cur.valid) {
+      // a row inside one warp is cleared by its first lane, ready for the
+      // next step (rows split over several items: fm_hist_clear_kernel)
+      if (nk == 1 && j_l == 0 && cur.hv) {
+        slot[cur.f] = 0;
+        hist[cur.f] = 0;
       }
-      hv[u] = slot[f];  // read for every row: its first lane clears it below
-    }
-  }
-  __syncwarp();  // every lane has read hist before the row's first lane clears it
+      if (cur.upd) {
 #pragma unroll
-  for (int u = 0; u < FM_UNROLL; ++u) {
-    const int64_t q = q0 + (int64_t)u * FM_NT;
-    if (q >= nvec) continue;
-    const int64_t f = q / vpr;
-    const int c = (int)(q - f * vpr) * 4;
-    if (c == 0 && hv[u]) {  // ready for the next step
-      slot[f] = 0;
-      hist[f] = 0;
+        for (int q = 0; q < 4; ++q)
+          if ((cur.upd >> q) & 1u) opt_apply(cur.w[q], cur.m[q], cur.v[q], cur.g[q], o);
+        store4<W>(Wm, cur.off, cur.w);
+        *reinterpret_cast<float4*>(m + cur.off) = make_float4(cur.m[0], cur.m[1], cur.m[2], cur.m[3]);
+        if (o.opt == KL_OPT_ADAM)
+          *reinterpret_cast<float4*>(v + cur.off) = make_float4(cur.v[0], cur.v[1], cur.v[2], cur.v[3]);
+      }
     }
-    if (!live[u]) continue;
-    float g[4] = {0.f, 0.f, 0.f, 0.f};
-    if (hv[u]) {
-      const float4 g4 = *reinterpret_cast<const float4*>(G + (int64_t)(hv[u] - 1) * ldg + c);
-      g[0] = g4.x; g[1] = g4.y; g[2] = g4.z; g[3] = g4.w;
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (upd[u][i]) opt_apply(w[u][i], mm[u][i], vv[u][i], g[i], o);
-    const int64_t off = f * ldw + c;
-    store4<W>(Wm, off, w[u]);
-    *reinterpret_cast<float4*>(m + off) = make_float4(mm[u][0], mm[u][1], mm[u][2], mm[u][3]);
-    if (o.opt == KL_OPT_ADAM)
-      *reinterpret_cast<float4*>(v + off) = make_float4(vv[u][0], vv[u][1], vv[u][2], vv[u][3]);
+    cur = nxt;
+    hv_n = hv_nn;
   }
 }
 
@@ -1358,19 +1401,26 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
   fm_grad_long_kernel<<<upd_grid(), lthreads, sm, st>>>(N, lgd, ldl, S, nwords, G, ldl);
   count_launch();
   const int vpr = ldl / 4;  // vectors per feature row (ldw == ldl == pitch of N)
-  const int64_t nvec = (int64_t)d * vpr;
-  const unsigned agrid = (unsigned)ceil_div(nvec, (int64_t)FM_NT * FM_UNROLL);
+  const int rpw = vpr <= 32 ? 32 / vpr : 1;
+  const int nk = vpr <= 32 ? 1 : (int)ceil_div(vpr, 32);
+  static int agrid = 0;
+  if (!agrid) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    agrid = sms * 4;  // resident blocks per SM under the kernel's launch bounds
+  }
   if (around_adam) around_adam(hook_arg, 0);
   if (wdtype == KL_DTYPE_BF16)
-    fm_adam_kernel<__nv_bfloat16><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, nvec, vpr, N, m, v,
+    fm_adam_kernel<__nv_bfloat16><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, d, vpr, rpw, nk, N, m, v,
                                                            touched_mask, S.hist, S.slot, G, ldl, o);
   else
-    fm_adam_kernel<float><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, nvec, vpr, N, m, v, touched_mask,
-                                                   S.hist, S.slot, G, ldl, o);
+    fm_adam_kernel<float><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, d, vpr, rpw, nk, N, m, v,
+                                                   touched_mask, S.hist, S.slot, G, ldl, o);
   count_launch();
   if (around_adam) around_adam(hook_arg, 1);
-  if (!(vpr == 32 || vpr == 8 || vpr == 16 || vpr == 4 || vpr == 2 || vpr == 1) || (vpr >= 32 && vpr % 32)) {
-    // a feature row does not sit inside one warp: clear hist separately
+  if (nk > 1) {
+    // a feature row spans several items: clear slot / hist separately
     fm_hist_clear_kernel<<<(unsigned)ceil_div(d, 256), 256, 0, st>>>(S);
     count_launch();
   }

@@ -259,3 +259,19 @@ def test_device_batch_and_stats(gpu_ctx):
     assert st.examples == 32 and st.steps == 1 and 0 < st.active_sum <= 32 * 320 and st.touched_rows > 0
     st0 = g.stats(0)
     assert st0.input_nnz == hb.rowptr[-1]
+
+
+@pytest.mark.parametrize("hidden", [24, 200])
+def test_hidden_widths(gpu_ctx, hidden):
+    # 24 neurons: several feature rows per warp in the streaming update;
+    # 200 neurons: one feature row split over two warps
+    cfg = S.config_xc(d_in=2000, hidden=hidden, n_out=3000, out_hash=HF.DwtaHash, out_k=8, out_l=10,
+                      bucket=BucketType.Fifo, cap=32, hidden_lsh=LshConfig(num_tables=10, num_hashes=6),
+                      rebuild_base=100, rebuild_decay=0.1)
+    for dtype in ("f32", "bf16"):
+        g, o = pair(cfg, dtype)
+        for hb in xc_batches(3, 32, n_out=3000, seed=23):
+            lg = g.train_step(_examples(hb), 1e-3, mode="batched")
+            lo = o.train_step(hb, 1e-3, mode="batched")
+            assert abs(lg - lo) <= 1e-4 * abs(lo) + 1e-6
+        assert_layers_close(g, o, 2, dtype)
