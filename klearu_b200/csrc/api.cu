@@ -1369,7 +1369,7 @@ struct kl_net_s {
       if (L.fm) {
         launch_fm_update(L.W.p, wdtype, L.ldw, L.d, L.N, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
                          L.mb.as<float>(), L.vb.as<float>(), in, L.lgd.as<float>(), L.ldN, L.tmask.as<uint32_t>(),
-                         S, L.gfeat.as<float>(), o, stat, st, &kl_net_s::stream_hook, this);
+                         S, L.gfeat.as<float>(), o, stat, ctx->err.as<int>(), st, &kl_net_s::stream_hook, this);
         ck_launch("fm update");
       } else {
         const Layer& P = *layers[l - 1];
@@ -1727,9 +1727,9 @@ void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_
   L.ctr.alloc(16);
   ck(cudaMemsetAsync(L.hist.p, 0, rows * 4, st), "memset");
   if (L.fm) {
-    L.fslot.alloc(rows * 4);
+    L.fslot.alloc((round_up(rows, 4) + 4) * 4);  // read in 16-byte units by the streaming update
     L.flong.alloc(rows * 4);
-    ck(cudaMemsetAsync(L.fslot.p, 0, rows * 4, st), "memset");
+    ck(cudaMemsetAsync(L.fslot.p, 0, (round_up(rows, 4) + 4) * 4, st), "memset");
   }
   if (!L.fm) {
     // dense-collision update scratch when its gradient matrix fits the budget

@@ -232,11 +232,12 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
 // (Adam decays every element of an active row, adam.rs:57-68).  G: gradient
 // rows of the touched features, [min(d, nnz)][ldl] f32 scratch.  around_adam
 // (nullable) is called with 0 before and 1 after the streaming Adam launch.
+// S.slot must hold round_up(d, 4) + 4 entries (stages copy it in 16-byte units).
 void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
                       float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
                       const uint32_t* touched_mask, SegScratch S, float* G, const OptStep* o,
-                      unsigned long long* stat_touched, cudaStream_t st, void (*around_adam)(void*, int) = nullptr,
-                      void* hook_arg = nullptr);
+                      unsigned long long* stat_touched, int* err, cudaStream_t st,
+                      void (*around_adam)(void*, int) = nullptr, void* hook_arg = nullptr);
 
 // Predict top-k over the final layer (net.rs:159-173): inactive neurons
 // score 0; order by score descending, ties by lower id.

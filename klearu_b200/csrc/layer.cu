@@ -799,10 +799,10 @@ __global__ void rm_lg_zero_kernel(float* LGd, int64_t ldu, const uint32_t* ctr, 
 //     and slot[f] becomes k + 1.
 // (2) fm_adam_kernel: streams W, m, v of ALL d feature rows (Adam runs over
 //     every element of a touched neuron, optim/adam.rs:57-68) with persistent
-//     warps that prefetch their next item; rows with slot[f] != 0 read their
-//     gradient from G, the rest use g = 0.  The row's first lane then zeroes
-//     slot[f] and hist[f] for the next step (fm_hist_clear_kernel does it when
-//     a feature row spans several items).
+//     warps that keep their next items' loads in flight through a per-warp
+//     shared-memory ring; rows with slot[f] != 0 read their gradient from G,
+//     the rest use g = 0.  slot[f] and hist[f] are zeroed for the next step
+//     (by fm_hist_clear_kernel when a row spans several items).
 // ---------------------------------------------------------------------------
 constexpr int FM_PF = 16;
 constexpr int FM_NT = 256;
@@ -948,14 +948,6 @@ __global__ void __launch_bounds__(1024)
 // One work item = rpw whole feature rows (vpr <= 32 vectors each: lane l
 // holds vector l % vpr of row l / vpr) or, for vpr > 32, the k-th 32-vector
 // slice of one row (nk slices per row).
-struct FmItem {
-  float w[4], m[4], v[4], g[4];
-  int64_t off;
-  int f;
-  uint32_t hv, upd;  // gradient slot + 1 (0: no gradient), per-element update bits
-  bool valid;
-};
-
 __device__ __forceinline__ bool fm_item_pos(int i, int rpw, int nk, int vpr, int d, int r_l, int j_l, int& f,
                                             int& c) {
   int j;
@@ -970,91 +962,117 @@ __device__ __forceinline__ bool fm_item_pos(int i, int rpw, int nk, int vpr, int
   return r_l < rpw && f < d && j < vpr;
 }
 
-template <class W>
-__device__ __forceinline__ void fm_item_load(FmItem& it, int i, uint32_t hv, const void* Wm, int ldw, int d, int vpr,
-                                             int rpw, int nk, int N, const float* m, const float* v,
-                                             const uint32_t* tmask, const float* G, int ldg, int opt, int r_l,
-                                             int j_l) {
-  int c;
-  it.valid = fm_item_pos(i, rpw, nk, vpr, d, r_l, j_l, it.f, c);
-  it.hv = hv;
-  it.upd = 0;
-  if (!it.valid) return;
-  const uint32_t tw = c < N ? tmask[c >> 5] >> (c & 31) : 0u;
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-    if (c + q < N && ((tw >> q) & 1u)) it.upd |= 1u << q;
-  it.off = (int64_t)it.f * ldw + c;
-  if (!it.upd) return;
-  load4<W>(Wm, it.off, it.w);
-  const float4 m4 = *reinterpret_cast<const float4*>(m + it.off);
-  it.m[0] = m4.x; it.m[1] = m4.y; it.m[2] = m4.z; it.m[3] = m4.w;
-  if (opt == KL_OPT_ADAM) {
-    const float4 v4 = *reinterpret_cast<const float4*>(v + it.off);
-    it.v[0] = v4.x; it.v[1] = v4.y; it.v[2] = v4.z; it.v[3] = v4.w;
-  } else {
-    it.v[0] = it.v[1] = it.v[2] = it.v[3] = 0.f;
-  }
-  if (hv) {
-    const float4 g4 = *reinterpret_cast<const float4*>(G + (int64_t)(hv - 1) * ldg + c);
-    it.g[0] = g4.x; it.g[1] = g4.y; it.g[2] = g4.z; it.g[3] = g4.w;
-  } else {
-    it.g[0] = it.g[1] = it.g[2] = it.g[3] = 0.f;
-  }
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(gmem));
 }
 
-// Persistent: warp w walks items w, w + nwarps, ...  While it updates item i
-// it already has the W/m/v/G loads of its next item and the slot load of the
-// one after in flight, so every warp keeps memory requests outstanding
-// through its arithmetic.
+// Persistent warps walk items w, w + nwarps, ...  Each lane copies its own
+// W / m / v / G vectors of the item FA_D - 1 items ahead into its warp's ring
+// of FA_D stages in shared memory with cp.async, and reads back only what it
+// copied itself, so a per-thread wait_group is the only synchronisation.
+// The slot value that decides the G copy is loaded one item earlier still.
+constexpr int FA_NT = 256;
+constexpr int FA_D = 3;
+constexpr int FA_STG = 32 * 16 * 4;  // one stage of one warp: W, m, v, G, 16 bytes per lane each
+
 template <class W>
-__global__ void __launch_bounds__(FM_NT, 4)
+__global__ void __launch_bounds__(FA_NT, 4)
     fm_adam_kernel(void* Wm, int ldw, int d, int vpr, int rpw, int nk, int N, float* m, float* v,
                    const uint32_t* tmask, uint32_t* hist, uint32_t* slot, const float* G, int ldg, const OptStep* op) {
+  extern __shared__ __align__(16) unsigned char dyn[];
   const OptStep o = *op;
-  const int lane = threadIdx.x & 31;
-  const int nwarps = gridDim.x * (FM_NT / 32);
-  const int i0 = blockIdx.x * (FM_NT / 32) + (threadIdx.x >> 5);
+  const bool adam = o.opt == KL_OPT_ADAM;
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  unsigned char* ring = dyn + (size_t)wib * FA_D * FA_STG;
+  const int nwarps = gridDim.x * (FA_NT / 32);
+  const int i0 = blockIdx.x * (FA_NT / 32) + wib;
   const int nitems = nk == 1 ? (int)ceil_div(d, rpw) : d * nk;
   const int r_l = nk == 1 ? lane / vpr : 0;
   const int j_l = nk == 1 ? lane - r_l * vpr : lane;
-  int f, c;
-  FmItem cur, nxt;
-  uint32_t hv = 0;
-  if (i0 < nitems && fm_item_pos(i0, rpw, nk, vpr, d, r_l, j_l, f, c)) hv = slot[f];
-  fm_item_load<W>(cur, i0, hv, Wm, ldw, d, vpr, rpw, nk, N, m, v, tmask, G, ldg, o.opt, r_l, j_l);
-  uint32_t hv_n = 0;
-  if (i0 + nwarps < nitems && fm_item_pos(i0 + nwarps, rpw, nk, vpr, d, r_l, j_l, f, c)) hv_n = slot[f];
-  for (int i = i0; i < nitems; i += nwarps) {
-    const int in = i + nwarps;
-    if (in < nitems)
-      fm_item_load<W>(nxt, in, hv_n, Wm, ldw, d, vpr, rpw, nk, N, m, v, tmask, G, ldg, o.opt, r_l, j_l);
-    uint32_t hv_nn = 0;
-    if (in + nwarps < nitems && fm_item_pos(in + nwarps, rpw, nk, vpr, d, r_l, j_l, f, c)) hv_nn = slot[f];
-    __syncwarp();  // every lane of the item's rows has used its slot value
-    if (cur.valid) {
-      // a row inside one warp is cleared by its first lane, ready for the
-      // next step (rows split over several items: fm_hist_clear_kernel)
-      if (nk == 1 && j_l == 0 && cur.hv) {
-        slot[cur.f] = 0;
-        hist[cur.f] = 0;
-      }
-      if (cur.upd) {
+  auto upd_bits = [&](int c) {
+    if (c >= N) return 0u;
+    const uint32_t tw = tmask[c >> 5] >> (c & 31);
+    uint32_t u = 0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if ((cur.upd >> q) & 1u) opt_apply(cur.w[q], cur.m[q], cur.v[q], cur.g[q], o);
-        store4<W>(Wm, cur.off, cur.w);
-        *reinterpret_cast<float4*>(m + cur.off) = make_float4(cur.m[0], cur.m[1], cur.m[2], cur.m[3]);
-        if (o.opt == KL_OPT_ADAM)
-          *reinterpret_cast<float4*>(v + cur.off) = make_float4(cur.v[0], cur.v[1], cur.v[2], cur.v[3]);
-      }
+    for (int q = 0; q < 4; ++q)
+      if (c + q < N && ((tw >> q) & 1u)) u |= 1u << q;
+    return u;
+  };
+  auto slot_of = [&](int t) -> uint32_t {
+    const int i = i0 + t * nwarps;
+    int f, c;
+    if (i < nitems && fm_item_pos(i, rpw, nk, vpr, d, r_l, j_l, f, c)) return slot[f];
+    return 0u;
+  };
+  // copies item t (slot value hv) into stage t % FA_D; always commits a group
+  auto issue = [&](int t, uint32_t hv) {
+    const int i = i0 + t * nwarps;
+    int f, c;
+    if (i < nitems && fm_item_pos(i, rpw, nk, vpr, d, r_l, j_l, f, c) && upd_bits(c)) {
+      unsigned char* st = ring + (t % FA_D) * FA_STG + lane * 16;
+      const int64_t off = (int64_t)f * ldw + c;
+      if (sizeof(W) == 2) cp_async8(st, static_cast<const W*>(Wm) + off);
+      else cp_async16(st, static_cast<const W*>(Wm) + off);
+      cp_async16(st + 512, m + off);
+      if (adam) cp_async16(st + 1024, v + off);
+      if (hv) cp_async16(st + 1536, G + (int64_t)(hv - 1) * ldg + c);
     }
-    cur = nxt;
-    hv_n = hv_nn;
+    cp_async_commit();
+  };
+  uint32_t hvq[FA_D];  // slot values of items t .. t + FA_D - 1 (ring of registers)
+#pragma unroll
+  for (int u = 0; u < FA_D; ++u) hvq[u] = slot_of(u);
+#pragma unroll
+  for (int u = 0; u < FA_D - 1; ++u) issue(u, hvq[u]);
+  for (int t = 0; i0 + t * nwarps < nitems; ++t) {
+    // hvq[u] holds the slot of item t + u; fetch item t + FA_D - 1 and the
+    // slot of item t + FA_D
+    issue(t + FA_D - 1, hvq[FA_D - 1]);
+    const uint32_t hv = hvq[0];
+#pragma unroll
+    for (int u = 0; u < FA_D - 1; ++u) hvq[u] = hvq[u + 1];
+    hvq[FA_D - 1] = slot_of(t + FA_D);
+    cp_async_wait_group<FA_D - 1>();  // item t's copies of this lane have landed
+    const int i = i0 + t * nwarps;
+    int f, c;
+    const bool valid = fm_item_pos(i, rpw, nk, vpr, d, r_l, j_l, f, c);
+    __syncwarp();  // every lane of the item's rows has used its slot value
+    if (!valid) continue;
+    if (nk == 1 && j_l == 0 && hv) {  // ready for the next step
+      slot[f] = 0;
+      hist[f] = 0;
+    }
+    const uint32_t upd = upd_bits(c);
+    if (!upd) continue;
+    const unsigned char* st = ring + (t % FA_D) * FA_STG + lane * 16;
+    float w[4], mm[4], vv[4], g[4] = {0.f, 0.f, 0.f, 0.f};
+    load4<W>(st, 0, w);
+    const float4 m4 = *reinterpret_cast<const float4*>(st + 512);
+    mm[0] = m4.x; mm[1] = m4.y; mm[2] = m4.z; mm[3] = m4.w;
+    if (adam) {
+      const float4 v4 = *reinterpret_cast<const float4*>(st + 1024);
+      vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
+    } else {
+      vv[0] = vv[1] = vv[2] = vv[3] = 0.f;
+    }
+    if (hv) {
+      const float4 g4 = *reinterpret_cast<const float4*>(st + 1536);
+      g[0] = g4.x; g[1] = g4.y; g[2] = g4.z; g[3] = g4.w;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if ((upd >> q) & 1u) opt_apply(w[q], mm[q], vv[q], g[q], o);
+    const int64_t off = (int64_t)f * ldw + c;
+    store4<W>(Wm, off, w);
+    *reinterpret_cast<float4*>(m + off) = make_float4(mm[0], mm[1], mm[2], mm[3]);
+    if (adam) *reinterpret_cast<float4*>(v + off) = make_float4(vv[0], vv[1], vv[2], vv[3]);
   }
+  cp_async_wait_group<0>();
 }
 
-// hist[f] = 0 for the touched features (after fm_adam_kernel read them).
+// hist[f] = slot[f] = 0 for the touched features (rows split over several
+// items of fm_adam_kernel, which cannot clear them in place).
 __global__ void fm_hist_clear_kernel(SegScratch S) {
   const int k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k < (int)S.ctr[0]) {
@@ -1377,8 +1395,8 @@ void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, fl
 void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
                       float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
                       const uint32_t* touched_mask, SegScratch S, float* G, const OptStep* o,
-                      unsigned long long* stat_touched, cudaStream_t st, void (*around_adam)(void*, int),
-                      void* hook_arg) {
+                      unsigned long long* stat_touched, int* err, cudaStream_t st,
+                      void (*around_adam)(void*, int), void* hook_arg) {
   const int nq = in.n;
   if (nq <= 0) return;
   fm_touch_kernel<<<nq, 256, 0, st>>>(in, S.hist, S.touched, S.ctr, d);
@@ -1404,23 +1422,26 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
   const int rpw = vpr <= 32 ? 32 / vpr : 1;
   const int nk = vpr <= 32 ? 1 : (int)ceil_div(vpr, 32);
   static int agrid = 0;
+  const size_t smem = (size_t)(FA_NT / 32) * FA_D * FA_STG;
   if (!agrid) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     agrid = sms * 4;  // resident blocks per SM under the kernel's launch bounds
+    cudaFuncSetAttribute(fm_adam_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(fm_adam_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   }
+  (void)err;
   if (around_adam) around_adam(hook_arg, 0);
   if (wdtype == KL_DTYPE_BF16)
-    fm_adam_kernel<__nv_bfloat16><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, d, vpr, rpw, nk, N, m, v,
-                                                           touched_mask, S.hist, S.slot, G, ldl, o);
+    fm_adam_kernel<__nv_bfloat16><<<agrid, FA_NT, smem, st>>>(const_cast<void*>(W), ldw, d, vpr, rpw, nk, N, m, v,
+                                                              touched_mask, S.hist, S.slot, G, ldl, o);
   else
-    fm_adam_kernel<float><<<agrid, FM_NT, 0, st>>>(const_cast<void*>(W), ldw, d, vpr, rpw, nk, N, m, v,
-                                                   touched_mask, S.hist, S.slot, G, ldl, o);
+    fm_adam_kernel<float><<<agrid, FA_NT, smem, st>>>(const_cast<void*>(W), ldw, d, vpr, rpw, nk, N, m, v,
+                                                      touched_mask, S.hist, S.slot, G, ldl, o);
   count_launch();
   if (around_adam) around_adam(hook_arg, 1);
   if (nk > 1) {
-    // a feature row spans several items: clear slot / hist separately
     fm_hist_clear_kernel<<<(unsigned)ceil_div(d, 256), 256, 0, st>>>(S);
     count_launch();
   }
