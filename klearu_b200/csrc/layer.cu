@@ -642,6 +642,13 @@ __global__ void __launch_bounds__(UPD_WARPS * 32)
 //      of the batched oracle (bit-exact), zeroes the consumed LGd tile,
 //      applies the optimizer to its rows and biases, and clears their bits.
 // ---------------------------------------------------------------------------
+// rm_dense_scatter_kernel gives each thread RM_PK pairs of one sample (stride
+// blockDim), with the loads of all of them issued before any is used.
+constexpr int RM_PK = 8;
+
+// One pair per thread: blocks run in waves, and the plain read lets pairs of
+// later waves skip the atomic on rows an earlier wave already set (batching
+// pairs per thread puts them all in one wave and every pair then contends).
 __global__ void rm_mark_kernel(ActiveSet A, uint32_t* bits, uint32_t* touched, uint32_t* slot_of,
                                uint32_t* ctr) {
   const int s = blockIdx.y;
@@ -661,10 +668,23 @@ __global__ void rm_mark_kernel(ActiveSet A, uint32_t* bits, uint32_t* touched, u
 
 __global__ void rm_dense_scatter_kernel(ActiveSet A, const uint32_t* slot_of, float* LGd, int64_t ldu) {
   const int s = blockIdx.y;
-  const int a = blockIdx.x * blockDim.x + threadIdx.x;
-  if (a >= A.cnt[s]) return;
-  const int64_t o = (int64_t)s * A.stride + a;
-  LGd[(int64_t)s * ldu + slot_of[A.ids[o]]] = A.lg[o];
+  const int n = A.cnt[s];
+  const int a0 = blockIdx.x * blockDim.x * RM_PK + threadIdx.x;
+  if (blockIdx.x * blockDim.x * RM_PK >= n) return;
+  uint32_t id[RM_PK], sl[RM_PK];
+  float lg[RM_PK];
+#pragma unroll
+  for (int u = 0; u < RM_PK; ++u) {
+    const int a = a0 + u * blockDim.x;
+    const int64_t o = (int64_t)s * A.stride + a;
+    id[u] = a < n ? A.ids[o] : 0xffffffffu;
+    lg[u] = a < n ? A.lg[o] : 0.0f;
+  }
+#pragma unroll
+  for (int u = 0; u < RM_PK; ++u) sl[u] = id[u] != 0xffffffffu ? slot_of[id[u]] : 0u;
+#pragma unroll
+  for (int u = 0; u < RM_PK; ++u)
+    if (id[u] != 0xffffffffu) LGd[(int64_t)s * ldu + sl[u]] = lg[u];
 }
 
 constexpr int RDU_ROWS = 16;  // slots per block (8 warps x 2)
@@ -1344,10 +1364,10 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
                             cudaStream_t st) {
   (void)stat_touched;
   if (nq <= 0) return;
-  dim3 g2((unsigned)ceil_div(A.stride, 256), nq);
-  rm_mark_kernel<<<g2, 256, 0, st>>>(A, D.bits, D.touched, D.slot_of, D.ctr);
+  rm_mark_kernel<<<dim3((unsigned)ceil_div(A.stride, 256), nq), 256, 0, st>>>(A, D.bits, D.touched, D.slot_of,
+                                                                           D.ctr);
   count_launch();
-  rm_dense_scatter_kernel<<<g2, 256, 0, st>>>(A, D.slot_of, D.LGd, D.ldu);
+  rm_dense_scatter_kernel<<<dim3((unsigned)ceil_div(A.stride, 256 * RM_PK), nq), 256, 0, st>>>(A, D.slot_of, D.LGd, D.ldu);
   count_launch();
   const int64_t maxn = std::min<int64_t>((int64_t)N, (int64_t)nq * A.stride);
   const int ncb = (int)ceil_div(d, RDU_COLS);
