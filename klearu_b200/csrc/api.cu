@@ -1734,7 +1734,7 @@ void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_
   if (!L.fm) {
     // dense-collision update scratch when its gradient matrix fits the budget
     const int64_t drows = std::min<int64_t>((int64_t)L.N, (int64_t)B * L.stride);
-    const int64_t ldu = round_up(drows + 16, 32);  // + a tile of slack: update tiles read 16 slots at a time
+    const int64_t ldu = round_up(drows + 16, 32);  // update tiles read whole 32-slot groups below ldu
     if (rm_dense_fits(ldu, std::max(B, 1))) {
       L.dldu = ldu;
       const size_t nwords = (size_t)ceil_div(L.N, 32);

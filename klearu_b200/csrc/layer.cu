@@ -687,15 +687,35 @@ __global__ void rm_dense_scatter_kernel(ActiveSet A, const uint32_t* slot_of, fl
     if (id[u] != 0xffffffffu) LGd[(int64_t)s * ldu + sl[u]] = lg[u];
 }
 
-constexpr int RDU_ROWS = 16;  // slots per block (8 warps x 2)
-constexpr int RDU_COLS = 32;  // columns per block (one per lane)
-constexpr int RDU_S = 32;     // samples per staged chunk
-constexpr int RDU_ST = 4;     // cp.async pipeline stages
+constexpr int RDU_RPW = 4;               // slots per warp
+constexpr int RDU_ROWS = 8 * RDU_RPW;    // slots per block (8 warps)
+constexpr int RDU_COLS = 32;             // columns per block (one per lane)
+constexpr int RDU_S = 32;                // samples per staged chunk
+constexpr int RDU_ST = 4;                // cp.async pipeline stages
 
-// Block = (16 slots, 32 columns): warp w owns slots 2w and 2w+1, lane l column
+// Block = (32 slots, 32 columns): warp w owns slots 4w .. 4w+3, lane l column
 // cb*32 + l.  Column blocks multiply the parallelism when few rows meet many
-// samples (a shard's union over a large global batch).  The gradient matrix
-// is left as read; rm_lg_zero_kernel restores its zeros afterwards.
+// samples (a shard's union over a large global batch).  Every sample's term
+// is added, zero or not: the sums start at +0 and a round-to-nearest sum is
+// -0 only when both operands are, so a +-0 term (a sample where the row is
+// not active) leaves a sum unchanged and the result equals the sum over the
+// active samples in ascending order (finite activations assumed).  The
+// gradient matrix is left as read; rm_lg_zero_kernel restores its zeros.
+template <class W, bool BIAS>
+__device__ __forceinline__ void rdu_sum_chunk(const float (*xs)[RDU_COLS], const float (*ls)[RDU_ROWS], int ns,
+                                              int w, int l, float* g, float* gb) {
+  for (int j = 0; j < ns; ++j) {
+    const float xv = xs[j][l];
+    const float4 l4 = *reinterpret_cast<const float4*>(&ls[j][w * RDU_RPW]);
+    const float lv[RDU_RPW] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+    for (int i = 0; i < RDU_RPW; ++i) {
+      g[i] = __fadd_rn(g[i], __fmul_rn(lv[i], xv));
+      if (BIAS) gb[i] = __fadd_rn(gb[i], lv[i]);
+    }
+  }
+}
+
 template <class W>
 __global__ void __launch_bounds__(256)
     rm_dense_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
@@ -713,30 +733,25 @@ __global__ void __launch_bounds__(256)
     const int k0 = (item / ncb) * RDU_ROWS, cb = item % ncb;
     const int c = cb * RDU_COLS + l;
     const bool cin = c < d;
-    auto stage = [&](int ch) {
+    auto stage = [&](int ch) {  // 32 samples x 32 columns of X and x 32 slots of LGd: one float4 each per thread
       const int bf = ch % RDU_ST;
       const int s0 = ch * RDU_S;
-      {  // 32 samples x 32 columns = 256 float4, one per thread
-        const int r = t >> 3, c4 = (t & 7) * 4;
-        float* dst = &xs[bf][r][c4];
-        if (s0 + r < nq && cb * RDU_COLS + c4 < d)
-          cp_async16(dst, X + (int64_t)(s0 + r) * ldx + cb * RDU_COLS + c4);
-        else
-          *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      if (t < RDU_S * RDU_ROWS / 4) {
-        const int r = t / (RDU_ROWS / 4), c4 = (t % (RDU_ROWS / 4)) * 4;
-        float* dst = &ls[bf][r][c4];
-        if (s0 + r < nq) cp_async16(dst, LGd + (int64_t)(s0 + r) * ldu + k0 + c4);
-        else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+      const int r = t >> 3, c4 = (t & 7) * 4;
+      float* dx = &xs[bf][r][c4];
+      if (s0 + r < nq && cb * RDU_COLS + c4 < d)
+        cp_async16(dx, X + (int64_t)(s0 + r) * ldx + cb * RDU_COLS + c4);
+      else
+        *reinterpret_cast<float4*>(dx) = make_float4(0.f, 0.f, 0.f, 0.f);
+      float* dl = &ls[bf][r][c4];
+      if (s0 + r < nq) cp_async16(dl, LGd + (int64_t)(s0 + r) * ldu + k0 + c4);
+      else *reinterpret_cast<float4*>(dl) = make_float4(0.f, 0.f, 0.f, 0.f);
     };
-    // optimizer state of this lane's two elements, loaded now and used after the sum
-    float wv[2], mv[2], vv[2];
-    int64_t roff[2];
+    // optimizer state of this lane's elements, loaded now and used after the sum
+    float wv[RDU_RPW], mv[RDU_RPW], vv[RDU_RPW];
+    int64_t roff[RDU_RPW];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int k = k0 + w * 2 + i;
+    for (int i = 0; i < RDU_RPW; ++i) {
+      const int k = k0 + w * RDU_RPW + i;
       roff[i] = -1;
       if (k < n && cin) {
         roff[i] = (int64_t)touched[k] * ldw + c;
@@ -745,7 +760,7 @@ __global__ void __launch_bounds__(256)
         vv[i] = o.opt == KL_OPT_ADAM ? v[roff[i]] : 0.f;
       }
     }
-    float g[2] = {0.f, 0.f}, gb[2] = {0.f, 0.f};
+    float g[RDU_RPW] = {0.f, 0.f, 0.f, 0.f}, gb[RDU_RPW] = {0.f, 0.f, 0.f, 0.f};
     __syncthreads();  // previous users of the buffers are done
 #pragma unroll
     for (int p = 0; p < RDU_ST - 1; ++p) {
@@ -759,34 +774,25 @@ __global__ void __launch_bounds__(256)
       cp_async_wait_group<RDU_ST - 1>();
       __syncthreads();
       const int ns = min(RDU_S, nq - ch * RDU_S);
-      for (int j = 0; j < ns; ++j) {
-        const float xv = xs[bf][j][l];
-        const float2 l2 = *reinterpret_cast<const float2*>(&ls[bf][j][w * 2]);
-        if (l2.x != 0.0f) {
-          gb[0] = __fadd_rn(gb[0], l2.x);
-          g[0] = __fadd_rn(g[0], __fmul_rn(l2.x, xv));
-        }
-        if (l2.y != 0.0f) {
-          gb[1] = __fadd_rn(gb[1], l2.y);
-          g[1] = __fadd_rn(g[1], __fmul_rn(l2.y, xv));
-        }
-      }
+      if (cb == 0) rdu_sum_chunk<W, true>(xs[bf], ls[bf], ns, w, l, g, gb);
+      else rdu_sum_chunk<W, false>(xs[bf], ls[bf], ns, w, l, g, gb);
       __syncthreads();  // buffer bf is restaged RDU_ST - 1 chunks later
     }
     cp_async_wait_group<0>();
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < RDU_RPW; ++i) {
       if (roff[i] < 0) continue;
       opt_apply(wv[i], mv[i], vv[i], g[i], o);
       static_cast<W*>(Wm)[roff[i]] = from_f<W>(wv[i]);
       m[roff[i]] = mv[i];
       if (o.opt == KL_OPT_ADAM) v[roff[i]] = vv[i];
     }
-    if (cb == 0 && l < 2) {
-      const int k = k0 + w * 2 + l;
+    if (cb == 0 && l < RDU_RPW) {
+      const int k = k0 + w * RDU_RPW + l;
       if (k < n) {
         const uint32_t row = touched[k];
-        bias_update(bias, mb, vb, row, l == 0 ? gb[0] : gb[1], o);
+        const float gbl = l == 0 ? gb[0] : l == 1 ? gb[1] : l == 2 ? gb[2] : gb[3];
+        bias_update(bias, mb, vb, row, gbl, o);
         atomicAnd(bits + (row >> 5), ~(1u << (row & 31)));  // ready for the next step's mark
       }
     }

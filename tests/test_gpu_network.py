@@ -275,3 +275,26 @@ def test_hidden_widths(gpu_ctx, hidden):
             lo = o.train_step(hb, 1e-3, mode="batched")
             assert abs(lg - lo) <= 1e-4 * abs(lo) + 1e-6
         assert_layers_close(g, o, 2, dtype)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_first_step_output_gradients_bit_exact(gpu_ctx, dtype):
+    # Adam's first moment starts at zero, so after one step m = (1 - b1) * g
+    # exactly: equal m means the GPU's per-row output-layer gradient sums
+    # (weights and biases) are bit-identical to the oracle's ordered sums.
+    # An identity output makes the local gradients (post - label weight)
+    # exact arithmetic on both sides, so only the summation is under test
+    # (softmax and sigmoid go through exp, whose CPU and GPU results may
+    # differ in the last place).  The hidden layer's local gradients come from
+    # dX, accumulated in another order than the oracle's: tolerance there.
+    cfg = xc_small()
+    cfg.network.layers[1].activation = ActivationType.Identity
+    g, o = pair(cfg, dtype)
+    hb = xc_batches(1, 64, seed=29)[0]
+    g.train_step(_examples(hb), 1e-3, mode="batched")
+    o.train_step(hb, 1e-3, mode="batched")
+    gl, ol = g.get_layer(1), o.get_layer(1)
+    for k in ("m", "mb"):
+        diff = int((gl[k] != ol[k]).sum())
+        assert diff == 0, f"output {k}: {diff} of {gl[k].size} differ"
+    assert_layers_close(g, o, 2, dtype)
