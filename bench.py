@@ -10,8 +10,9 @@ synthetic C1 examples.  Prints ONE JSON line on rank 0.
 
 * ``value``: samples/s of the whole job with the batches already resident in
   HBM, timed with CUDA events (max over ranks).
-* ``e2e``: the same metric through the C-ABI train step with each batch copied
-  from pinned host memory inside the timed region and the loss read back.
+* ``e2e``: the same metric through the C-ABI host-batch train step
+  (kl_net_train_step_host), each batch uploaded from pinned host memory inside
+  the timed region and the loss read back every step.
 * ``roofline``: the dominant phase's algorithmic bytes / its event-timed
   duration, against MEASURED_PEAKS.json's HBM copy bandwidth.
 * ``cpu_baseline``: the CPU restatement of the reference path (HOGWILD, all
@@ -313,22 +314,18 @@ def main():
                 np.int32 if k != "val" else np.float32)).pin_memory()
                     for k in ("rowptr", "idx", "val", "label_ptr", "labels")}
             hosts.append((hb, arrs))
-        dev = {k: torch.empty(int(max(h[1][k].numel() for h in hosts)) + 1, dtype=hosts[0][1][k].dtype,
-                              device="cuda") for k in hosts[0][1]}
-        loss_d = torch.zeros(1, device="cuda")
         loss_h = torch.zeros(1).pin_memory()
         bi = sum(int(a.numel()) * 4 for a in hosts[0][1].values())
 
         def e2e_step(i):
+            # the public host-batch call: it packs the pinned CSR arrays,
+            # uploads them on its copy stream and enqueues the loss readback
             hb, arrs = hosts[i % len(hosts)]
-            for k, a in arrs.items():
-                dev[k][: a.numel()].copy_(a, non_blocking=True)
-            c = _lib.BatchC(hb.batch, dev["rowptr"].data_ptr(), dev["idx"].data_ptr(), dev["val"].data_ptr(),
-                            dev["label_ptr"].data_ptr(), dev["labels"].data_ptr(), int(hb.rowptr[-1]),
+            c = _lib.BatchC(hb.batch, arrs["rowptr"].data_ptr(), arrs["idx"].data_ptr(), arrs["val"].data_ptr(),
+                            arrs["label_ptr"].data_ptr(), arrs["labels"].data_ptr(), int(hb.rowptr[-1]),
                             int(hb.label_ptr[-1]))
-            _lib.check(lib.kl_net_train_step(net.h, C.byref(c), 1e-3, _lib.MODE_BATCHED, loss_d.data_ptr(), None),
+            _lib.check(lib.kl_net_train_step_host(net.h, C.byref(c), 1e-3, _lib.MODE_BATCHED, loss_h.data_ptr()),
                        net.ctx.h)
-            loss_h.copy_(loss_d, non_blocking=True)
 
         for i in range(3):
             e2e_step(i)
@@ -346,7 +343,7 @@ def main():
             dist.all_reduce(t2, op=dist.ReduceOp.MAX)
         e2e = {"value": world * B * args.steps / (float(t2.item()) / 1e3), "unit": "samples/s",
                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4,
-               "api": "kl_net_train_step (C ABI) with per-step pinned-host CSR upload and loss readback"}
+               "api": "kl_net_train_step_host (C ABI): per-step upload of the pinned host CSR batch and loss readback"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

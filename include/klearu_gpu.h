@@ -349,6 +349,16 @@ KL_API kl_status kl_net_destroy(kl_net_t net);
  * Increments step once and runs the rebuild check, as the reference does. */
 KL_API kl_status kl_net_train_step(kl_net_t net, const kl_batch* batch_host, double lr, int mode,
                             float* loss, float* loss_host);
+/* Network::train_step (net.rs:81-119) on a batch in HOST memory (every
+ * pointer of `batch_host` is host memory; nnz / nlabels are taken from
+ * rowptr[batch] / label_ptr[batch]).  The arrays are copied into an internal
+ * pinned buffer and uploaded with one copy on a separate stream, so the call
+ * returns without waiting for the GPU and the next batch's upload overlaps
+ * this step.  The mean loss is copied to `loss_host` (nullable) in stream
+ * order: it is valid after kl_ctx_sync, and the copy only stays
+ * asynchronous when `loss_host` is pinned memory. */
+KL_API kl_status kl_net_train_step_host(kl_net_t net, const kl_batch* batch_host, double lr, int mode,
+                                        float* loss_host);
 /* Network::forward (net.rs:62-78) for every example of the batch, without any
  * update.  Per-layer results are read with kl_net_layer_output. */
 KL_API kl_status kl_net_forward(kl_net_t net, const kl_batch* batch_host);

@@ -102,6 +102,7 @@ _PROTOS = {
     "kl_net_create": (_S, [_H, C.POINTER(NetConfigC), _P, C.POINTER(_H)]),
     "kl_net_destroy": (_S, [_H]),
     "kl_net_train_step": (_S, [_H, C.POINTER(BatchC), C.c_double, C.c_int, _P, C.POINTER(C.c_float)]),
+    "kl_net_train_step_host": (_S, [_H, C.POINTER(BatchC), C.c_double, C.c_int, _P]),
     "kl_net_forward": (_S, [_H, C.POINTER(BatchC)]),
     "kl_net_layer_output": (_S, [_H, C.c_int, _P, _P, _P, _P]),
     "kl_net_layer_info": (_S, [_H, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]),

@@ -528,13 +528,27 @@ class Network:
               self.ctx.h, "kl_net_train_step")
         return out.value
 
-    def train_step_host(self, hb: HostBatch, lr: float, mode=_lib.MODE_BATCHED) -> float:
-        """One train step on a host CSR batch; returns the mean loss."""
-        db = self.device_batch(hb)
-        out = C.c_float()
-        check(self.lib.kl_net_train_step(self.h, C.byref(db.c), float(lr), mode, None, C.byref(out)),
-              self.ctx.h, "kl_net_train_step")
-        return out.value
+    def train_step_host(self, hb: HostBatch, lr: float, mode=_lib.MODE_BATCHED, loss_out=None) -> float | None:
+        """One train step on a host CSR batch through kl_net_train_step_host.
+
+        With ``loss_out`` None the call waits for the step and returns the mean
+        loss.  Otherwise ``loss_out`` is a 1-element pinned float32 CPU tensor
+        that receives the loss in stream order (valid after ``ctx.sync()``), and
+        the call returns None without waiting, so consecutive calls overlap the
+        next batch's upload with the current step."""
+        arrs = [np.ascontiguousarray(getattr(hb, k)) for k in ("rowptr", "idx", "val", "label_ptr", "labels")]
+        rp, idx, val, lp, lab = arrs
+        c = _lib.BatchC(hb.batch, rp.ctypes.data, idx.ctypes.data, val.ctypes.data, lp.ctypes.data,
+                        lab.ctypes.data, int(rp[-1]) if hb.batch else 0, int(lp[-1]) if hb.batch else 0)
+        if loss_out is None:
+            out = torch.zeros(1, dtype=torch.float32).pin_memory()
+            check(self.lib.kl_net_train_step_host(self.h, C.byref(c), float(lr), mode, out.data_ptr()),
+                  self.ctx.h, "kl_net_train_step_host")
+            self.ctx.sync()
+            return float(out[0])
+        check(self.lib.kl_net_train_step_host(self.h, C.byref(c), float(lr), mode, loss_out.data_ptr()),
+              self.ctx.h, "kl_net_train_step_host")
+        return None
 
     # -- inference --------------------------------------------------------
     def forward_batch(self, examples) -> list[list[LayerOutput]]:

@@ -1049,6 +1049,18 @@ struct kl_net_s {
   Scheduler sched;
   DBuf labprob, loss_acc, rb_bkt, rb_scratch;
   size_t labprob_cap = 0;
+  // host-batch ingestion (kl_net_train_step_host): two slots, each a pinned
+  // host buffer and a device buffer holding one packed CSR batch.  h2d marks
+  // the slot's upload done, used the end of the step that read it.
+  struct HostSlot {
+    void* pinned = nullptr;
+    DBuf dev;
+    size_t cap = 0;
+    cudaEvent_t h2d = nullptr, used = nullptr;
+  };
+  HostSlot hslots[2];
+  int hnext = 0;
+  cudaStream_t copy_stream = nullptr;
   // neuron sharding of the output layer (kl_net_create_sharded)
   int rank = 0, nranks = 1;
   ncclComm_t comm = nullptr;
@@ -1113,6 +1125,13 @@ struct kl_net_s {
     ~Phase() { n->prof_end(i); }
   };
   ~kl_net_s() {
+    for (auto& h : hslots) {
+      if (h.h2d) cudaEventSynchronize(h.h2d);
+      if (h.pinned) cudaFreeHost(h.pinned);
+      if (h.h2d) cudaEventDestroy(h.h2d);
+      if (h.used) cudaEventDestroy(h.used);
+    }
+    if (copy_stream) cudaStreamDestroy(copy_stream);
     if (gexec) cudaGraphExecDestroy(gexec);
     if (cap_stream) cudaStreamDestroy(cap_stream);
     if (comm) ncclCommDestroy(comm);
@@ -1883,17 +1902,16 @@ extern "C" kl_status kl_net_destroy(kl_net_t net) {
 }
 
 
-extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double lr, int mode, float* loss,
-                                       float* loss_host) {
-  if (!net) return KL_EINVAL;
-  KL_API_BEGIN(net->ctx)
+// The body of Network::train_step (net.rs:81-119) on a validated device
+// batch; the mean loss ends in net->loss_acc (and `loss` when non-null).
+static void train_step_body(kl_net_t net, const kl_batch* b, double lr, int mode, float* loss) {
   validate_batch(net, b);
   require(mode == KL_MODE_EXACT_SEQUENTIAL || mode == KL_MODE_BATCHED, "train_step: unknown mode");
-  cudaStream_t st = ctx__->stream;
+  cudaStream_t st = net->ctx->stream;
   if (b->batch == 0) {  // net.rs:82-84
+    ck(cudaMemsetAsync(net->loss_acc.p, 0, 4, st), "memset");
     if (loss) ck(cudaMemsetAsync(loss, 0, 4, st), "memset");
-    if (loss_host) *loss_host = 0.0f;
-    return KL_OK;
+    return;
   }
   int loss_div = b->batch;
   net->upload_opt(lr);
@@ -1933,10 +1951,91 @@ extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double l
   // net.rs:109-116
   net->step += 1;
   if (net->sched.should_rebuild(net->step)) net->rebuild_all();
+}
+
+extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double lr, int mode, float* loss,
+                                       float* loss_host) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  train_step_body(net, b, lr, mode, loss);
   if (loss_host) {
-    ck(cudaMemcpyAsync(loss_host, net->loss_acc.p, 4, cudaMemcpyDeviceToHost, st), "loss copy");
+    ck(cudaMemcpyAsync(loss_host, net->loss_acc.p, 4, cudaMemcpyDeviceToHost, ctx__->stream), "loss copy");
     check_device_errors(ctx__);
   }
+  KL_API_END
+}
+
+// The batch's arrays are packed into one pinned slot, uploaded with a single
+// copy on the net's copy stream, and the step runs on the device copy; the
+// compute stream waits only for that upload, so the upload of the next batch
+// overlaps this step's kernels.  A slot is reused two calls later, after the
+// step that read it (device side) and its own upload (host side) are done.
+extern "C" kl_status kl_net_train_step_host(kl_net_t net, const kl_batch* hb, double lr, int mode,
+                                            float* loss_host) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  require(hb != nullptr, "batch is NULL");
+  require(hb->batch >= 0 && hb->batch <= net->max_batch, "batch size outside [0, max_batch]");
+  const int B = hb->batch;
+  if (B > 0) require(hb->rowptr && hb->label_ptr, "batch rowptr / label_ptr required");
+  const int32_t nnz = B > 0 ? hb->rowptr[B] : 0, nlab = B > 0 ? hb->label_ptr[B] : 0;
+  require(nnz >= 0 && nlab >= 0, "batch rowptr / label_ptr must end at >= 0");
+  if (nnz > 0) require(hb->idx && hb->val, "batch idx / val required");
+  if (nlab > 0) require(hb->labels != nullptr, "batch labels required");
+  cudaStream_t st = ctx__->stream;
+  if (!net->copy_stream) {
+    ck(cudaStreamCreateWithFlags(&net->copy_stream, cudaStreamNonBlocking), "copy stream");
+    for (auto& h : net->hslots) {
+      ck(cudaEventCreateWithFlags(&h.h2d, cudaEventDisableTiming), "event");
+      ck(cudaEventCreateWithFlags(&h.used, cudaEventDisableTiming), "event");
+      ck(cudaEventRecord(h.h2d, net->copy_stream), "event");
+      ck(cudaEventRecord(h.used, st), "event");
+    }
+  }
+  auto a16 = [](size_t n) { return (n + 15) & ~size_t(15); };
+  const size_t o_rp = 0, o_lp = o_rp + a16((size_t)(B + 1) * 4), o_idx = o_lp + a16((size_t)(B + 1) * 4),
+               o_val = o_idx + a16((size_t)nnz * 4), o_lab = o_val + a16((size_t)nnz * 4),
+               total = o_lab + a16((size_t)nlab * 4);
+  auto& h = net->hslots[net->hnext];
+  net->hnext ^= 1;
+  ck(cudaEventSynchronize(h.h2d), "event sync");  // the slot's previous upload has left the pinned buffer
+  if (total > h.cap) {
+    ck(cudaEventSynchronize(h.used), "event sync");
+    if (h.pinned) ck(cudaFreeHost(h.pinned), "cudaFreeHost");
+    h.pinned = nullptr;
+    h.cap = 0;
+    const size_t cap = a16(total + total / 2);
+    ck(cudaHostAlloc(&h.pinned, cap, cudaHostAllocDefault), "cudaHostAlloc");
+    h.dev.alloc(cap);
+    h.cap = cap;
+  }
+  unsigned char* hp = static_cast<unsigned char*>(h.pinned);
+  if (B > 0) {
+    std::memcpy(hp + o_rp, hb->rowptr, (size_t)(B + 1) * 4);
+    std::memcpy(hp + o_lp, hb->label_ptr, (size_t)(B + 1) * 4);
+  }
+  if (nnz > 0) {
+    std::memcpy(hp + o_idx, hb->idx, (size_t)nnz * 4);
+    std::memcpy(hp + o_val, hb->val, (size_t)nnz * 4);
+  }
+  if (nlab > 0) std::memcpy(hp + o_lab, hb->labels, (size_t)nlab * 4);
+  ck(cudaStreamWaitEvent(net->copy_stream, h.used, 0), "stream wait");  // the step that read this slot is done
+  ck(cudaMemcpyAsync(h.dev.p, h.pinned, total, cudaMemcpyHostToDevice, net->copy_stream), "batch upload");
+  ck(cudaEventRecord(h.h2d, net->copy_stream), "event");
+  ck(cudaStreamWaitEvent(st, h.h2d, 0), "stream wait");
+  unsigned char* dp = static_cast<unsigned char*>(h.dev.p);
+  kl_batch db{};
+  db.batch = B;
+  db.rowptr = reinterpret_cast<const int32_t*>(dp + o_rp);
+  db.label_ptr = reinterpret_cast<const int32_t*>(dp + o_lp);
+  db.idx = reinterpret_cast<const uint32_t*>(dp + o_idx);
+  db.val = reinterpret_cast<const float*>(dp + o_val);
+  db.labels = reinterpret_cast<const uint32_t*>(dp + o_lab);
+  db.nnz = nnz;
+  db.nlabels = nlab;
+  train_step_body(net, &db, lr, mode, nullptr);
+  ck(cudaEventRecord(h.used, st), "event");
+  if (loss_host) ck(cudaMemcpyAsync(loss_host, net->loss_acc.p, 4, cudaMemcpyDeviceToHost, st), "loss copy");
   KL_API_END
 }
 

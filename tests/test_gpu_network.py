@@ -298,3 +298,24 @@ def test_first_step_output_gradients_bit_exact(gpu_ctx, dtype):
         diff = int((gl[k] != ol[k]).sum())
         assert diff == 0, f"output {k}: {diff} of {gl[k].size} differ"
     assert_layers_close(g, o, 2, dtype)
+
+
+def test_host_batch_train_step_matches_device_batches(gpu_ctx):
+    # kl_net_train_step_host (host CSR arrays, pipelined upload, loss read in
+    # stream order) against kl_net_train_step on device batches: the same
+    # deterministic steps, so identical losses and weights
+    cfg = xc_small()
+    init = S.make_init(cfg, 31)
+    a, b = Network(cfg, init, max_batch=64), Network(cfg, init, max_batch=64)
+    batches = xc_batches(6, 40, seed=37) + [xc_batches(1, 64, seed=41)[0]]  # last one grows the staging slots
+    la = [a.train_step(_examples(hb), 1e-3, mode="batched") for hb in batches]
+    outs = [torch.zeros(1, dtype=torch.float32).pin_memory() for _ in batches]
+    for hb, o in zip(batches, outs):
+        assert b.train_step_host(hb, 1e-3, loss_out=o) is None  # no wait between calls
+    b.ctx.sync()
+    assert [float(o[0]) for o in outs] == la
+    for l in range(2):
+        x, y = a.get_layer(l), b.get_layer(l)
+        for k in x:
+            assert (x[k] == y[k]).all(), (l, k)
+    assert b.train_step_host(HostBatch.from_examples([]), 1e-3) == 0.0
