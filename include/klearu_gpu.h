@@ -470,6 +470,46 @@ KL_API kl_status kl_net_create_sharded(kl_ctx_t ctx, const kl_net_config* cfg_ho
 KL_API kl_status kl_net_shard_info(kl_net_t net, int* rank_host, int* nranks_host, uint32_t* id_base_host,
                             int* num_local_host);
 
+/* ---------------------------------------------------------------------------
+ * Deja Vu sparse FFN.
+ * --------------------------------------------------------------------------- */
+typedef struct kl_predictor_s* kl_predictor_t;
+typedef struct kl_sparse_mlp_s* kl_sparse_mlp_t;
+
+/* SparsityPredictor::from_weights (klearu-dejavu predictor/mlp_predictor.rs:65-84):
+ * w1 [hidden_dim][input_dim], w2 [output_dim][hidden_dim] row-major f32 (host),
+ * stored as bf16 (round to nearest even); b1 / b2 f32 (NULL = zeros). */
+KL_API kl_status kl_predictor_create(kl_ctx_t ctx, int input_dim, int hidden_dim, int output_dim,
+                                     const float* w1_host, const float* b1_host, const float* w2_host,
+                                     const float* b2_host, kl_predictor_t* out);
+KL_API kl_status kl_predictor_destroy(kl_predictor_t p);
+KL_API kl_status kl_predictor_info(kl_predictor_t p, int* input_dim_host, int* hidden_dim_host,
+                                   int* output_dim_host);
+/* SparsityPredictor::predict (mlp_predictor.rs:102-123) for n_tokens inputs:
+ * x [n_tokens][input_dim] -> scores [n_tokens][output_dim] (device, f32). */
+KL_API kl_status kl_predictor_predict(kl_predictor_t p, const float* x, int n_tokens, float* scores);
+/* SparsityPredictor::select_top_k (mlp_predictor.rs:126-132): per token the
+ * min(k, output_dim) indices of the largest scores, in descending score order
+ * with ties in ascending index order (the reference's stable sort).
+ * idx [n_tokens][min(k, output_dim)] (device); scores (device, nullable)
+ * receives the predict() output.  Scores must be finite. */
+KL_API kl_status kl_predictor_select_topk(kl_predictor_t p, const float* x, int n_tokens, int k, uint32_t* idx,
+                                          float* scores);
+
+/* SwiGLU MLP weights (klearu-llm model/mlp.rs): gate / up [intermediate][hidden],
+ * down [hidden][intermediate] row-major f32 (host), stored bf16; down_bias
+ * (nullable, klearu-dejavu mlp.rs:50-53) f32 [hidden]. */
+KL_API kl_status kl_sparse_mlp_create(kl_ctx_t ctx, int hidden, int intermediate, const float* gate_host,
+                                      const float* up_host, const float* down_host, const float* down_bias_host,
+                                      kl_sparse_mlp_t* out);
+KL_API kl_status kl_sparse_mlp_destroy(kl_sparse_mlp_t m);
+/* sparse_mlp::forward_sparse (klearu-llm sparse/sparse_mlp.rs:4-37) for each
+ * token: out[t] = down[:, sel[t]] . (silu(gate[sel[t]] . x[t]) * (up[sel[t]] . x[t]))
+ * (+ bias).  x [n_tokens][hidden], sel [n_tokens][k] (uint32 neuron ids),
+ * out [n_tokens][hidden]; all device. */
+KL_API kl_status kl_sparse_mlp_forward(kl_sparse_mlp_t m, const float* x, int n_tokens, const uint32_t* sel, int k,
+                                       float* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -122,6 +122,14 @@ _PROTOS = {
     "kl_net_create_sharded": (_S, [_H, C.POINTER(NetConfigC), _P, _P, C.c_int, C.c_int, C.POINTER(_H)]),
     "kl_net_shard_info": (_S, [_H, _P, _P, _P, _P]),
     "kl_adaptive_create": (_S, [_H, C.c_uint64, C.c_uint64, C.c_float, C.c_float, C.POINTER(_H)]),
+    "kl_predictor_create": (_S, [_H, C.c_int, C.c_int, C.c_int, _P, _P, _P, _P, C.POINTER(_H)]),
+    "kl_predictor_destroy": (_S, [_H]),
+    "kl_predictor_info": (_S, [_H, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "kl_predictor_predict": (_S, [_H, _P, C.c_int, _P]),
+    "kl_predictor_select_topk": (_S, [_H, _P, C.c_int, C.c_int, _P, _P]),
+    "kl_sparse_mlp_create": (_S, [_H, C.c_int, C.c_int, _P, _P, _P, _P, C.POINTER(_H)]),
+    "kl_sparse_mlp_destroy": (_S, [_H]),
+    "kl_sparse_mlp_forward": (_S, [_H, _P, C.c_int, _P, C.c_int, _P]),
     "kl_adaptive_destroy": (_S, [_H]),
     "kl_adaptive_record_baseline": (_S, [_H, _H, _P, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_uint64]),
     "kl_adaptive_should_rebuild": (_S, [_H, _P, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)]),

@@ -2362,3 +2362,194 @@ extern "C" kl_status kl_index_query_batch_noalloc(kl_index_t ix, const float* X,
   ck_launch("compact");
   KL_API_END
 }
+
+// ===========================================================================
+// Deja Vu sparse FFN: SparsityPredictor (klearu-dejavu
+// predictor/mlp_predictor.rs:11-132) and the sparse SwiGLU MLP (klearu-llm
+// sparse/sparse_mlp.rs:4-37, klearu-dejavu mlp.rs:23-58).
+// ===========================================================================
+struct kl_predictor_s {
+  kl_ctx_t ctx;
+  int in = 0, hid = 0, out = 0, ld_in = 0, ld_hid = 0;
+  DBuf w1, b1, w2, b2, xs, P, h, sc;
+};
+
+struct kl_sparse_mlp_s {
+  kl_ctx_t ctx;
+  int hid = 0, inter = 0, ldw = 0;
+  DBuf gate, up, downT, bias, a, part;
+  bool has_bias = false;
+};
+
+namespace {
+
+// Host f32 rows [n][d] -> device bf16 [n][ld] (zero padded), or transposed.
+void upload_bf16(kl_ctx_t ctx, DBuf& dst, const float* host, int64_t n, int d, int64_t ld_dst, int64_t rows_dst,
+                 bool transpose) {
+  cudaStream_t st = ctx->stream;
+  dst.alloc((size_t)rows_dst * ld_dst * 2);
+  ck(cudaMemsetAsync(dst.p, 0, (size_t)rows_dst * ld_dst * 2, st), "memset");
+  DBuf tmp;
+  tmp.alloc((size_t)n * d * 4);
+  ck(cudaMemcpyAsync(tmp.p, host, (size_t)n * d * 4, cudaMemcpyHostToDevice, st), "upload");
+  launch_f32_to_w(tmp.as<float>(), n, d, d, dst.p, KL_DTYPE_BF16, ld_dst, transpose, st);
+  ck_launch("convert");
+  ck(cudaStreamSynchronize(st), "sync");  // tmp is freed on return
+}
+
+void upload_f32(kl_ctx_t ctx, DBuf& dst, const float* host, int64_t n) {
+  dst.alloc((size_t)std::max<int64_t>(n, 1) * 4);
+  if (host) ck(cudaMemcpyAsync(dst.p, host, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream), "upload");
+  else ck(cudaMemsetAsync(dst.p, 0, (size_t)std::max<int64_t>(n, 1) * 4, ctx->stream), "memset");
+}
+
+void predictor_scores(kl_predictor_t p, const float* x, int T, float* scores, cudaStream_t st) {
+  kl_ctx_t ctx = p->ctx;
+  for (int t0 = 0; t0 < T; t0 += TC_LINEAR_MAX_T) {
+    const int tn = std::min(TC_LINEAR_MAX_T, T - t0);
+    launch_tc_linear(x + (int64_t)t0 * p->in, tn, p->in, p->in, p->w1.as<__nv_bfloat16>(), p->hid, p->ld_in,
+                     p->b1.as<float>(), 0, p->h.as<float>(), p->hid, p->xs.as<__nv_bfloat16>(), p->P.as<float>(), 16,
+                     ctx->err.as<int>(), st);
+    ck_launch("predictor layer 1");
+    launch_tc_linear(p->h.as<float>(), tn, p->hid, p->hid, p->w2.as<__nv_bfloat16>(), p->out, p->ld_hid,
+                     p->b2.as<float>(), 1, scores + (int64_t)t0 * p->out, p->out, p->xs.as<__nv_bfloat16>(),
+                     p->P.as<float>(), 16, ctx->err.as<int>(), st);
+    ck_launch("predictor layer 2");
+  }
+}
+
+}  // namespace
+
+extern "C" kl_status kl_predictor_create(kl_ctx_t ctx, int input_dim, int hidden_dim, int output_dim,
+                                         const float* w1_host, const float* b1_host, const float* w2_host,
+                                         const float* b2_host, kl_predictor_t* out) {
+  if (!ctx || !out) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  require(input_dim >= 1 && hidden_dim >= 1 && output_dim >= 1, "predictor: dimensions must be >= 1");
+  require(w1_host && w2_host, "predictor: w1 and w2 are required");
+  auto p = std::make_unique<kl_predictor_s>();
+  p->ctx = ctx;
+  p->in = input_dim;
+  p->hid = hidden_dim;
+  p->out = output_dim;
+  p->ld_in = (int)round_up(input_dim, TC_LINEAR_KPAD);
+  p->ld_hid = (int)round_up(hidden_dim, TC_LINEAR_KPAD);
+  upload_bf16(ctx, p->w1, w1_host, hidden_dim, input_dim, p->ld_in, hidden_dim, false);
+  upload_bf16(ctx, p->w2, w2_host, output_dim, hidden_dim, p->ld_hid, output_dim, false);
+  upload_f32(ctx, p->b1, b1_host, hidden_dim);
+  upload_f32(ctx, p->b2, b2_host, output_dim);
+  p->xs.alloc((size_t)3 * TC_LINEAR_MAX_T * std::max(p->ld_in, p->ld_hid) * 2);
+  p->P.alloc(std::max(tc_linear_scratch_floats(hidden_dim, p->ld_in), tc_linear_scratch_floats(output_dim, p->ld_hid)) *
+             4);
+  p->h.alloc((size_t)TC_LINEAR_MAX_T * hidden_dim * 4);
+  ck(cudaStreamSynchronize(ctx->stream), "sync");
+  *out = p.release();
+  KL_API_END
+}
+
+extern "C" kl_status kl_predictor_destroy(kl_predictor_t p) {
+  if (!p) return KL_EINVAL;
+  KL_API_BEGIN(p->ctx)
+  ck(cudaStreamSynchronize(p->ctx->stream), "sync");
+  delete p;
+  KL_API_END
+}
+
+extern "C" kl_status kl_predictor_info(kl_predictor_t p, int* input_dim, int* hidden_dim, int* output_dim) {
+  if (!p) return KL_EINVAL;
+  if (input_dim) *input_dim = p->in;
+  if (hidden_dim) *hidden_dim = p->hid;
+  if (output_dim) *output_dim = p->out;
+  return KL_OK;
+}
+
+extern "C" kl_status kl_predictor_predict(kl_predictor_t p, const float* x, int n_tokens, float* scores) {
+  if (!p) return KL_EINVAL;
+  KL_API_BEGIN(p->ctx)
+  require(n_tokens >= 0, "predict: n_tokens must be >= 0");
+  if (n_tokens == 0) return KL_OK;
+  require(x && scores, "predict: x and scores are required");
+  predictor_scores(p, x, n_tokens, scores, ctx__->stream);
+  KL_API_END
+}
+
+extern "C" kl_status kl_predictor_select_topk(kl_predictor_t p, const float* x, int n_tokens, int k, uint32_t* idx,
+                                              float* scores) {
+  if (!p) return KL_EINVAL;
+  KL_API_BEGIN(p->ctx)
+  require(n_tokens >= 0 && k >= 0, "select_topk: n_tokens and k must be >= 0");
+  const int kk = std::min(k, p->out);
+  if (n_tokens == 0 || kk == 0) return KL_OK;
+  require(x && idx, "select_topk: x and idx are required");
+  support(kk <= 16384, "select_topk: k above 16384 is not supported");
+  cudaStream_t st = ctx__->stream;
+  float* sc = scores;
+  if (!sc) {
+    p->sc.alloc((size_t)n_tokens * p->out * 4);
+    sc = p->sc.as<float>();
+  }
+  predictor_scores(p, x, n_tokens, sc, st);
+  launch_topk(sc, n_tokens, p->out, p->out, kk, idx, kk, st);
+  ck_launch("topk");
+  KL_API_END
+}
+
+extern "C" kl_status kl_sparse_mlp_create(kl_ctx_t ctx, int hidden, int intermediate, const float* gate_host,
+                                          const float* up_host, const float* down_host, const float* down_bias_host,
+                                          kl_sparse_mlp_t* out) {
+  if (!ctx || !out) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  require(hidden >= 1 && intermediate >= 1, "sparse_mlp: dimensions must be >= 1");
+  require(gate_host && up_host && down_host, "sparse_mlp: gate, up and down are required");
+  auto m = std::make_unique<kl_sparse_mlp_s>();
+  m->ctx = ctx;
+  m->hid = hidden;
+  m->inter = intermediate;
+  m->ldw = (int)round_up(hidden, 8);
+  upload_bf16(ctx, m->gate, gate_host, intermediate, hidden, m->ldw, intermediate, false);
+  upload_bf16(ctx, m->up, up_host, intermediate, hidden, m->ldw, intermediate, false);
+  // down [hidden][intermediate] stored transposed: a neuron's weights are one row
+  upload_bf16(ctx, m->downT, down_host, hidden, intermediate, m->ldw, intermediate, true);
+  m->has_bias = down_bias_host != nullptr;
+  if (m->has_bias) upload_f32(ctx, m->bias, down_bias_host, hidden);
+  ck(cudaStreamSynchronize(ctx->stream), "sync");
+  *out = m.release();
+  KL_API_END
+}
+
+extern "C" kl_status kl_sparse_mlp_destroy(kl_sparse_mlp_t m) {
+  if (!m) return KL_EINVAL;
+  KL_API_BEGIN(m->ctx)
+  ck(cudaStreamSynchronize(m->ctx->stream), "sync");
+  delete m;
+  KL_API_END
+}
+
+extern "C" kl_status kl_sparse_mlp_forward(kl_sparse_mlp_t m, const float* x, int n_tokens, const uint32_t* sel, int k,
+                                           float* out) {
+  if (!m) return KL_EINVAL;
+  KL_API_BEGIN(m->ctx)
+  require(n_tokens >= 0 && k >= 0, "sparse_mlp_forward: n_tokens and k must be >= 0");
+  if (n_tokens == 0) return KL_OK;
+  require(x && out, "sparse_mlp_forward: x and out are required");
+  cudaStream_t st = ctx__->stream;
+  if (k == 0) {  // no neuron selected: the output is the bias (or zero)
+    if (m->has_bias)
+      for (int t = 0; t < n_tokens; ++t)
+        ck(cudaMemcpyAsync(out + (int64_t)t * m->hid, m->bias.p, (size_t)m->hid * 4, cudaMemcpyDeviceToDevice, st),
+           "copy");
+    else ck(cudaMemsetAsync(out, 0, (size_t)n_tokens * m->hid * 4, st), "memset");
+    return KL_OK;
+  }
+  require(sel != nullptr, "sparse_mlp_forward: sel is required");
+  // enough blocks for the down projection: (hidden / 256) x splits x tokens
+  const int cols = (int)ceil_div(m->hid, 256);
+  const int splits = std::max(1, std::min(k, (int)ceil_div(296, (int64_t)cols * n_tokens)));
+  m->a.alloc((size_t)n_tokens * k * 4);
+  m->part.alloc((size_t)n_tokens * splits * m->ldw * 4);
+  launch_sparse_mlp(m->gate.as<__nv_bfloat16>(), m->up.as<__nv_bfloat16>(), m->downT.as<__nv_bfloat16>(), m->hid,
+                    m->ldw, m->inter, m->has_bias ? m->bias.as<float>() : nullptr, x, n_tokens, sel, k,
+                    m->a.as<float>(), m->part.as<float>(), splits, out, ctx__->err.as<int>(), st);
+  ck_launch("sparse mlp");
+  KL_API_END
+}

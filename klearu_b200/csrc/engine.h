@@ -267,4 +267,26 @@ void launch_shard_unpack(const uint32_t* recv, const ShardLayout& Ly, int P, int
 void launch_shard_fallback(ActiveSet A, const int32_t* gcnt, int n_local, int nq, int* err, cudaStream_t st);
 void launch_shard_or_masks(uint32_t* tmask, const uint32_t* all, int P, int nw, cudaStream_t st);
 
+// ---- Deja Vu sparse FFN (dejavu.cu) ----
+// Rows per tcgen05 linear call (tokens); K pitch granularity of its weights.
+constexpr int TC_LINEAR_MAX_T = 128;
+constexpr int TC_LINEAR_KPAD = 64;
+int tc_linear_splits(int n, int ldw, int* per);
+size_t tc_linear_scratch_floats(int n, int ldw);
+// y[T][n] = act(x[T][d] . W^T + bias), act 0 = ReLU, 1 = sigmoid; T <= 128;
+// W [n][ldw] bf16 zero beyond d; xs scratch [3][128][ldw] bf16; P scratch of
+// tc_linear_scratch_floats(n, ldw) floats.
+void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16* W, int n, int ldw,
+                      const float* bias, int act, float* y, int ldy, __nv_bfloat16* xs, float* P, int max_splits,
+                      int* err, cudaStream_t st);
+// idx[t][0, k) = the k largest of scores[t][0, n) in (score desc, index asc)
+// order; scores non-negative; k <= n.
+void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* idx, int ldi, cudaStream_t st);
+// out[T][hid] = SwiGLU MLP over the selected neurons sel[T][k]; gate/up
+// [inter][ldw], downT [inter][ldw] bf16; a scratch [T][k], part scratch
+// [T][splits][ldw] f32.
+void launch_sparse_mlp(const __nv_bfloat16* gate, const __nv_bfloat16* up, const __nv_bfloat16* downT, int hid,
+                       int ldw, int inter, const float* bias, const float* x, int T, const uint32_t* sel, int k,
+                       float* a, float* part, int splits, float* out, int* err, cudaStream_t st);
+
 }  // namespace kl

@@ -61,6 +61,9 @@ def lib() -> C.CDLL:
             "orc_index_export": (None, [_P, _P, _P, _P]),
             "orc_sample": (C.c_int, [C.c_int, C.c_int, C.c_int, _P, _P, C.c_int, _P]),
             "orc_adaptive_create": (_P, [C.c_uint64, C.c_uint64, C.c_float, C.c_float]),
+            "orc_pred_predict": (None, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, _P, C.c_int, _P]),
+            "orc_pred_topk": (C.c_int, [_P, C.c_int, C.c_int, _P]),
+            "orc_sparse_mlp": (None, [_P, _P, _P, _P, C.c_int, C.c_int, _P, _P, C.c_int, _P]),
             "orc_adaptive_destroy": (None, [_P]),
             "orc_adaptive_record_baseline": (None, [_P, _P, _P, C.c_int, C.c_int, _P, C.c_int]),
             "orc_adaptive_should_rebuild": (C.c_int, [_P, _P, _P, C.c_int, C.c_int]),
@@ -402,3 +405,37 @@ class Net:
         cnt = np.zeros((L, nb), np.uint64)
         lib().orc_net_export_index(self.h, l, shard, _p(ids), _p(lens), _p(cnt))
         return ids, lens, cnt
+
+
+# ---- Deja Vu sparse FFN (oracle/dejavu.cpp) ----------------------------------
+
+def pred_predict(w1, b1, w2, b2, x) -> np.ndarray:
+    """SparsityPredictor::predict (mlp_predictor.rs:102-123) for each row of x."""
+    w1, b1, w2, b2 = (np.ascontiguousarray(a, np.float32) for a in (w1, b1, w2, b2))
+    x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+    hid, d = w1.shape
+    out = w2.shape[0]
+    scores = np.empty((x.shape[0], out), np.float32)
+    lib().orc_pred_predict(_p(w1), _p(b1), _p(w2), _p(b2), d, hid, out, _p(x), x.shape[0], _p(scores))
+    return scores
+
+
+def pred_topk(scores, k: int) -> np.ndarray:
+    """select_top_k (mlp_predictor.rs:126-132) on one score vector."""
+    scores = np.ascontiguousarray(scores, np.float32)
+    idx = np.empty(min(k, scores.size), np.uint32)
+    n = lib().orc_pred_topk(_p(scores), scores.size, k, _p(idx))
+    return idx[:n]
+
+
+def sparse_mlp(gate, up, down, bias, x, sel) -> np.ndarray:
+    """forward_sparse (sparse_mlp.rs:4-37) for one token; bias may be None."""
+    gate, up, down = (np.ascontiguousarray(a, np.float32) for a in (gate, up, down))
+    inter, hid = gate.shape
+    x = np.ascontiguousarray(x, np.float32)
+    sel = np.ascontiguousarray(sel, np.uint32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    out = np.empty(hid, np.float32)
+    lib().orc_sparse_mlp(_p(gate), _p(up), _p(down), None if b is None else _p(b), hid, inter, _p(x), _p(sel),
+                         sel.size, _p(out))
+    return out

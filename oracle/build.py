@@ -1,6 +1,6 @@
 """Build recipe of the CPU oracle (test infrastructure only).
 
-Compiles ``oracle/oracle.cpp`` into ``oracle/liboracle.so`` with the flags the
+Compiles ``oracle/oracle.cpp`` and ``oracle/dejavu.cpp`` into ``oracle/liboracle.so`` with the flags the
 parity argument depends on: ``-ffp-contract=off`` (the Rust reference never
 fuses a*b+c) and no fast-math.  ``-march=x86-64-v3`` (AVX2/FMA level) keeps the
 library loadable on the GPU box's host CPU.  OpenMP drives the HOGWILD
@@ -18,6 +18,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 SRC = HERE / "oracle.cpp"
+SRCS = [SRC, HERE / "dejavu.cpp"]
 LIB = HERE / "liboracle.so"
 HDR = HERE.parent / "include" / "klearu_gpu.h"
 FLAGS = ["-O3", "-march=x86-64-v3", "-ffp-contract=off", "-fno-fast-math", "-fopenmp",
@@ -25,9 +26,10 @@ FLAGS = ["-O3", "-march=x86-64-v3", "-ffp-contract=off", "-fno-fast-math", "-fop
 
 
 def build_oracle(force: bool = False) -> Path:
-    if not force and LIB.exists() and LIB.stat().st_mtime > max(SRC.stat().st_mtime, HDR.stat().st_mtime):
+    newest = max(max(p.stat().st_mtime for p in SRCS), HDR.stat().st_mtime)
+    if not force and LIB.exists() and LIB.stat().st_mtime > newest:
         return LIB
-    cmd = ["g++", *FLAGS, str(SRC), "-o", str(LIB)]
+    cmd = ["g++", *FLAGS, *map(str, SRCS), "-o", str(LIB)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode:
         sys.stderr.write(res.stdout + res.stderr)

@@ -1,0 +1,115 @@
+"""GPU parity of the Deja Vu path (tcgen05 predictor GEMMs, top-k select,
+sparse SwiGLU MLP) against the oracle (oracle/dejavu.cpp), on the weights
+the engine stores (bf16-rounded).
+
+Tolerances (north_star: 1e-3 relative in f32): predictor scores within 1e-4
+relative (the products are exact; only the f32 accumulation order and exp
+differ); MLP outputs within 1e-3 of the output scale.  Top-k indices are
+bit-exact given the same scores, and against the oracle's own scores they
+may differ only where two scores are within the score tolerance of the k-th
+one."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from klearu_b200.dejavu import SparseMlp, SparsityPredictor
+
+pytestmark = pytest.mark.gpu
+
+
+def bf16(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).bfloat16().float().numpy()
+
+
+def predictor_weights(rng, d, hid, out, std=0.02):  # configs[3]: N(0, 0.02)
+    w1 = rng.normal(0, std, (hid, d)).astype(np.float32)
+    w2 = rng.normal(0, std, (out, hid)).astype(np.float32)
+    b1 = rng.normal(0, 0.01, hid).astype(np.float32)
+    b2 = rng.normal(0, 0.01, out).astype(np.float32)
+    return w1, b1, w2, b2
+
+
+@pytest.mark.parametrize("shape,T", [((96, 40, 200), 1), ((130, 70, 300), 5), ((4096, 1000, 11008), 3),
+                                     ((256, 128, 512), 130)])
+def test_predictor_scores_match_oracle(gpu_ctx, shape, T):
+    d, hid, out = shape
+    rng = np.random.default_rng(d + T)
+    w1, b1, w2, b2 = predictor_weights(rng, d, hid, out, std=0.05 if d < 1000 else 0.02)
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    p = SparsityPredictor(w1, b1, w2, b2, ctx=gpu_ctx)
+    got = p.predict(x).cpu().numpy()
+    ref = oracle.pred_predict(bf16(w1), b1, bf16(w2), b2, x)
+    assert got.shape == ref.shape
+    err = np.abs(got - ref) / np.maximum(np.abs(ref), 1e-6)
+    assert err.max() < 1e-4, err.max()
+
+
+def test_select_top_k_matches_oracle(gpu_ctx):
+    d, hid, out, T, k = 4096, 1000, 11008, 4, 1101  # configs[3]: keep ceil(0.1 * 11008)
+    rng = np.random.default_rng(7)
+    w1, b1, w2, b2 = predictor_weights(rng, d, hid, out)
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    p = SparsityPredictor(w1, b1, w2, b2, ctx=gpu_ctx)
+    idx = p.select_top_k(x, k).cpu().numpy()
+    sc = p.predict(x).cpu().numpy()
+    ref_sc = oracle.pred_predict(bf16(w1), b1, bf16(w2), b2, x)
+    for t in range(T):
+        # the same scores give the same order, bit for bit
+        assert (idx[t] == oracle.pred_topk(sc[t], k)).all()
+        # against the oracle's scores: differences only at the k-th score
+        ref = oracle.pred_topk(ref_sc[t], k)
+        kth = ref_sc[t][ref[-1]]
+        diff = set(idx[t].tolist()) ^ set(ref.tolist())
+        assert all(abs(ref_sc[t][i] - kth) <= 1e-4 * kth for i in diff), len(diff)
+
+
+def test_select_top_k_ties_and_clamp(gpu_ctx):
+    rng = np.random.default_rng(9)
+    d, hid, out = 64, 32, 40
+    w1, b1, w2, b2 = predictor_weights(rng, d, hid, out, std=0.2)
+    w2[10:20] = w2[5]  # equal rows: equal scores, ties broken by lower index
+    b2[10:20] = b2[5]
+    p = SparsityPredictor(w1, b1, w2, b2, ctx=gpu_ctx)
+    x = rng.standard_normal((2, d)).astype(np.float32)
+    sc = p.predict(x).cpu().numpy()
+    for k in (1, 7, 15, 40, 100):
+        idx = p.select_top_k(x, k).cpu().numpy()
+        assert idx.shape == (2, min(k, out))
+        for t in range(2):
+            assert (idx[t] == oracle.pred_topk(sc[t], k)).all()
+
+
+def mlp_weights(rng, hid, inter, std=0.02):
+    gate = rng.normal(0, std, (inter, hid)).astype(np.float32)
+    up = rng.normal(0, std, (inter, hid)).astype(np.float32)
+    down = rng.normal(0, std, (hid, inter)).astype(np.float32)
+    return gate, up, down
+
+
+@pytest.mark.parametrize("hid,inter,k,T,bias", [(64, 128, 128, 1, False), (96, 200, 37, 3, True),
+                                                (4096, 11008, 1101, 2, False)])
+def test_sparse_mlp_matches_oracle(gpu_ctx, hid, inter, k, T, bias):
+    rng = np.random.default_rng(hid + k)
+    gate, up, down = mlp_weights(rng, hid, inter, std=0.02 if hid >= 1000 else 0.1)
+    b = rng.standard_normal(hid).astype(np.float32) if bias else None
+    m = SparseMlp(gate, up, down, b, ctx=gpu_ctx)
+    x = rng.standard_normal((T, hid)).astype(np.float32)
+    sel = np.stack([rng.permutation(inter)[:k] for _ in range(T)]).astype(np.uint32)
+    got = m.forward_sparse(x, sel.astype(np.int32)).cpu().numpy()
+    for t in range(T):
+        ref = oracle.sparse_mlp(bf16(gate), bf16(up), bf16(down), b, x[t], sel[t])
+        scale = np.abs(ref).max()
+        assert np.abs(got[t] - ref).max() <= 1e-3 * scale, (np.abs(got[t] - ref).max(), scale)
+
+
+def test_sparse_mlp_no_selection_is_bias(gpu_ctx):
+    rng = np.random.default_rng(4)
+    gate, up, down = mlp_weights(rng, 32, 64)
+    b = rng.standard_normal(32).astype(np.float32)
+    x = rng.standard_normal((2, 32)).astype(np.float32)
+    out = SparseMlp(gate, up, down, b, ctx=gpu_ctx).forward_sparse(x, np.zeros((2, 0), np.int32)).cpu().numpy()
+    assert (out == b).all()
+    out0 = SparseMlp(gate, up, down, None, ctx=gpu_ctx).forward_sparse(x, np.zeros((2, 0), np.int32)).cpu().numpy()
+    assert (out0 == 0).all()
