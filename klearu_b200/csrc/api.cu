@@ -2371,7 +2371,7 @@ extern "C" kl_status kl_index_query_batch_noalloc(kl_index_t ix, const float* X,
 struct kl_predictor_s {
   kl_ctx_t ctx;
   int in = 0, hid = 0, out = 0, ld_in = 0, ld_hid = 0;
-  DBuf w1, b1, w2, b2, xs, P, h, sc;
+  DBuf w1, b1, w2, b2, xs, xs2, P, h, sc;
 };
 
 struct kl_sparse_mlp_s {
@@ -2407,13 +2407,14 @@ void predictor_scores(kl_predictor_t p, const float* x, int T, float* scores, cu
   kl_ctx_t ctx = p->ctx;
   for (int t0 = 0; t0 < T; t0 += TC_LINEAR_MAX_T) {
     const int tn = std::min(TC_LINEAR_MAX_T, T - t0);
+    // layer 1 reads x's pieces from xs and writes h's pieces to xs2 for layer 2
     launch_tc_linear(x + (int64_t)t0 * p->in, tn, p->in, p->in, p->w1.as<__nv_bfloat16>(), p->hid, p->ld_in,
-                     p->b1.as<float>(), 0, p->h.as<float>(), p->hid, p->xs.as<__nv_bfloat16>(), p->P.as<float>(), 16,
-                     ctx->err.as<int>(), st);
+                     p->b1.as<float>(), 0, p->h.as<float>(), p->hid, p->xs.as<__nv_bfloat16>(), p->P.as<float>(),
+                     p->xs2.as<__nv_bfloat16>(), p->ld_hid, ctx->err.as<int>(), st);
     ck_launch("predictor layer 1");
-    launch_tc_linear(p->h.as<float>(), tn, p->hid, p->hid, p->w2.as<__nv_bfloat16>(), p->out, p->ld_hid,
-                     p->b2.as<float>(), 1, scores + (int64_t)t0 * p->out, p->out, p->xs.as<__nv_bfloat16>(),
-                     p->P.as<float>(), 16, ctx->err.as<int>(), st);
+    launch_tc_linear(nullptr, tn, p->hid, p->hid, p->w2.as<__nv_bfloat16>(), p->out, p->ld_hid, p->b2.as<float>(), 1,
+                     scores + (int64_t)t0 * p->out, p->out, p->xs2.as<__nv_bfloat16>(), p->P.as<float>(), nullptr, 0,
+                     ctx->err.as<int>(), st);
     ck_launch("predictor layer 2");
   }
 }
@@ -2438,7 +2439,8 @@ extern "C" kl_status kl_predictor_create(kl_ctx_t ctx, int input_dim, int hidden
   upload_bf16(ctx, p->w2, w2_host, output_dim, hidden_dim, p->ld_hid, output_dim, false);
   upload_f32(ctx, p->b1, b1_host, hidden_dim);
   upload_f32(ctx, p->b2, b2_host, output_dim);
-  p->xs.alloc((size_t)3 * TC_LINEAR_MAX_T * std::max(p->ld_in, p->ld_hid) * 2);
+  p->xs.alloc((size_t)3 * TC_LINEAR_MAX_T * p->ld_in * 2);
+  p->xs2.alloc((size_t)3 * TC_LINEAR_MAX_T * p->ld_hid * 2);
   p->P.alloc(std::max(tc_linear_scratch_floats(hidden_dim, p->ld_in), tc_linear_scratch_floats(output_dim, p->ld_hid)) *
              4);
   p->h.alloc((size_t)TC_LINEAR_MAX_T * hidden_dim * 4);
@@ -2481,7 +2483,10 @@ extern "C" kl_status kl_predictor_select_topk(kl_predictor_t p, const float* x, 
   const int kk = std::min(k, p->out);
   if (n_tokens == 0 || kk == 0) return KL_OK;
   require(x && idx, "select_topk: x and idx are required");
-  support(kk <= 16384, "select_topk: k above 16384 is not supported");
+  int pow2 = 1;
+  while (pow2 < kk) pow2 <<= 1;
+  support((size_t)pow2 * 8 + (size_t)p->out * 4 <= 190 * 1024,
+          "select_topk: k and output_dim too large for one block's shared memory");
   cudaStream_t st = ctx__->stream;
   float* sc = scores;
   if (!sc) {
@@ -2543,8 +2548,11 @@ extern "C" kl_status kl_sparse_mlp_forward(kl_sparse_mlp_t m, const float* x, in
   }
   require(sel != nullptr, "sparse_mlp_forward: sel is required");
   // enough blocks for the down projection: (hidden / 256) x splits x tokens
+  // K splits of the down projection: at most ~32 selected rows per thread,
+  // and enough blocks ((hidden / 256) x splits x tokens) to fill the SMs
   const int cols = (int)ceil_div(m->hid, 256);
-  const int splits = std::max(1, std::min(k, (int)ceil_div(296, (int64_t)cols * n_tokens)));
+  const int splits = std::max(1, std::min(k, std::max((int)ceil_div(k, 32),
+                                                      (int)ceil_div(592, (int64_t)cols * n_tokens))));
   m->a.alloc((size_t)n_tokens * k * 4);
   m->part.alloc((size_t)n_tokens * splits * m->ldw * 4);
   launch_sparse_mlp(m->gate.as<__nv_bfloat16>(), m->up.as<__nv_bfloat16>(), m->downT.as<__nv_bfloat16>(), m->hid,

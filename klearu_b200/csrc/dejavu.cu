@@ -19,13 +19,12 @@
 namespace kl {
 namespace {
 
-constexpr int TC_M = 128;                  // accumulator rows (tokens, zero padded)
-constexpr int TC_N = 128;                  // accumulator columns (output features per tile)
+constexpr int TC_M = 128;                  // accumulator rows: output features (weight rows) per tile
 constexpr int TC_K = 64;                   // K elements per stage: 128-byte rows
-constexpr int TC_ST = 3;                   // pipeline stages
 constexpr int TC_NP = 3;                   // bf16 pieces of the f32 activations
-constexpr int TC_TILE = TC_M * TC_K * 2;   // bytes of one 128 x 64 bf16 tile
-constexpr int TC_STAGE = (TC_NP + 1) * TC_TILE;
+constexpr int TC_TMAX = 85;                // tokens per call: 3 piece rows each, <= 256 accumulator columns
+constexpr int TC_WTILE = TC_M * TC_K * 2;  // bytes of one 128 x 64 bf16 weight tile
+constexpr int TC_SMEM = 200 * 1024;        // shared-memory budget of the stage ring
 
 // Canonical K-major layout without swizzle: 8-row x 16-byte core matrices,
 // stored contiguously (128 B); the next 16 bytes of K are the next core
@@ -40,147 +39,171 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
          (1ull << 46);
 }
 // Instruction descriptor: f32 accumulator, bf16 A and B, both K-major,
-// N = TC_N, M = TC_M.
-constexpr uint32_t TC_IDESC =
-    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_N >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+// M = TC_M, N = n (a multiple of 16 up to 256).
+__host__ __device__ constexpr uint32_t tc_idesc(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+}
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 
-__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t accumulate) {
+__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-      "l"(da), "l"(db), "r"(TC_IDESC), "r"(accumulate)
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];\n"
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
-// P[split][TC_M][ldp] (f32 partial sums) = A . B^T over the split's K tiles.
-// A: TC_NP pieces, each [TC_M][lda] bf16 (rows past the token count are zero);
-// B: [nb][ldb] bf16, rows >= nb read as zero.  lda, ldb: multiples of TC_K.
-// One CTA per (128-column tile, K split); 128 threads; warp 0 owns the
-// tensor-memory allocation, thread 0 issues the MMAs.
+// P[split][t][n0 + m] (f32 partial sums, t < T) = sum over the split's K tiles
+// of W[n0 + m] . x[t]: the weights are the MMA's A operand (M = 128 rows per
+// tile), the token pieces its B operand: row 3t + p of X is piece p of token
+// t, so one MMA per 16-wide K step covers every piece of every token, and the
+// epilogue adds a token's three accumulator columns (hi + mid + lo).
+// A: [nw][ldw] bf16, rows >= nw read as zero.  X: [3 * TC_TMAX][ldw] bf16;
+// rows 3T .. NT-1 are zeroed in every stage once and never loaded.  NST stages of
+// (weight tile + token pieces) stream through shared memory (cp.async); the
+// MMAs of a stage release it through tcgen05.commit on its mbarrier.  One CTA
+// per (128-row tile, K split); 128 threads; warp 0 owns the tensor memory,
+// thread 0 issues the MMAs; the epilogue reads row m = lane of warp m / 32.
+template <int NT>
+struct TcCfg {
+  static constexpr int XTILE = NT * TC_K * 2;  // the token-piece rows
+  static constexpr int STAGE = TC_WTILE + XTILE;
+  static constexpr int NST = (TC_SMEM / STAGE) < 8 ? (TC_SMEM / STAGE) : 8;
+  static_assert(NST >= 3, "the ring needs a prefetch distance of at least one stage");
+  static constexpr int TMEM_COLS = NT < 32 ? 32 : NT;
+};
+
+template <int NT>
 __global__ void __launch_bounds__(128, 1)
-    tc_gemm_kernel(const __nv_bfloat16* __restrict__ A, int64_t a_piece, int lda, const __nv_bfloat16* __restrict__ B,
-                   int ldb, int nb, int ktiles, int kt_per_split, float* __restrict__ P, int ldp, int* err) {
+    tc_gemm_kernel(const __nv_bfloat16* __restrict__ W, int ldw, int nw, const __nv_bfloat16* __restrict__ X, int T,
+                   int ktiles, int kt_per_split, float* __restrict__ P, int ldp, int* err) {
+  using Cfg = TcCfg<NT>;
+  constexpr int NST = Cfg::NST;
   extern __shared__ __align__(1024) unsigned char tc_smem[];
-  __shared__ uint64_t bar_mma[TC_ST];
+  __shared__ uint64_t bar_mma[NST];
   __shared__ uint64_t bar_done;
   __shared__ uint32_t tmem_s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * TC_N;
+  const int n0 = blockIdx.x * TC_M;
   const int kt0 = blockIdx.y * kt_per_split;
   const int nk = max(0, min(ktiles, kt0 + kt_per_split) - kt0);
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(&tmem_s)),
-                 "r"(TC_N)
+                 "r"(Cfg::TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
   }
   if (tid == 0) {
-    for (int s = 0; s < TC_ST; ++s) mbar_init(&bar_mma[s], 1);
+    for (int s = 0; s < NST; ++s) mbar_init(&bar_mma[s], 1);
     mbar_init(&bar_done, 1);
     fence_mbar_init();
   }
+  const int xr = TC_NP * T;  // token-piece rows
+  // rows xr .. NT-1 of the token tile are zero in every stage
+  for (int s = 0; s < NST; ++s)
+    for (int q = xr * 8 + tid; q < NT * 8; q += 128)
+      *reinterpret_cast<uint4*>(tc_smem + s * Cfg::STAGE + TC_WTILE + canon_off(q >> 3, q & 7)) =
+          make_uint4(0u, 0u, 0u, 0u);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_s;
   bool ok = true;
 
-  auto load_stage = [&](int i) {  // K tile kt0 + i into stage i % TC_ST
-    unsigned char* st = tc_smem + (i % TC_ST) * TC_STAGE;
+  auto load_stage = [&](int i) {  // K tile kt0 + i into stage i % NST
+    unsigned char* st = tc_smem + (i % NST) * Cfg::STAGE;
     const int k0 = (kt0 + i) * TC_K;
-#pragma unroll
-    for (int p = 0; p < TC_NP; ++p)
-      for (int q = tid; q < TC_M * 8; q += 128) {
-        const int r = q >> 3, c = q & 7;
-        cp_async16(st + p * TC_TILE + canon_off(r, c), A + p * a_piece + (int64_t)r * lda + k0 + c * 8);
-      }
-    for (int q = tid; q < TC_N * 8; q += 128) {
+    for (int q = tid; q < TC_M * 8; q += 128) {
       const int r = q >> 3, c = q & 7;
-      unsigned char* dst = st + TC_NP * TC_TILE + canon_off(r, c);
-      if (n0 + r < nb) cp_async16(dst, B + (int64_t)(n0 + r) * ldb + k0 + c * 8);
+      unsigned char* dst = st + canon_off(r, c);
+      if (n0 + r < nw) cp_async16(dst, W + (int64_t)(n0 + r) * ldw + k0 + c * 8);
       else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    for (int q = tid; q < xr * 8; q += 128) {
+      const int r = q >> 3, c = q & 7;
+      cp_async16(st + TC_WTILE + canon_off(r, c), X + (int64_t)r * ldw + k0 + c * 8);
     }
   };
 
-  for (int i = 0; i < TC_ST - 1; ++i) {
+  // prefetch distance PD = NST - 2: the stage refilled in iteration i last
+  // held tile i - 2, whose MMAs were issued an iteration before the latest
+  // ones, so the refill rarely waits on the tensor core
+  constexpr int PD = NST - 2;
+  for (int i = 0; i < PD; ++i) {
     if (i < nk) load_stage(i);
     cp_async_commit();
   }
   for (int i = 0; i < nk; ++i) {
-    const int j = i + TC_ST - 1;
+    const int j = i + PD;
     if (j < nk) {
-      // stage j % TC_ST last held tile j - TC_ST: wait until its MMAs are done
-      if (j >= TC_ST && !mbar_wait(&bar_mma[j % TC_ST], (uint32_t)((j / TC_ST) - 1) & 1u)) ok = false;
+      // stage j % NST last held tile j - NST: wait until its MMAs are done
+      if (j >= NST && !mbar_wait(&bar_mma[j % NST], (uint32_t)((j / NST) - 1) & 1u)) ok = false;
       load_stage(j);
     }
     cp_async_commit();
-    cp_async_wait_group<TC_ST - 1>();
+    cp_async_wait_group<PD>();
     fence_proxy_async_smem();  // this thread's shared-memory writes, visible to the tensor core
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      const unsigned char* st = tc_smem + (i % TC_ST) * TC_STAGE;
-      const uint32_t sb = smem_u32(st + TC_NP * TC_TILE);
+      const unsigned char* st = tc_smem + (i % NST) * Cfg::STAGE;
+      const uint32_t sa = smem_u32(st), sb = smem_u32(st + TC_WTILE);
 #pragma unroll
-      for (int p = 0; p < TC_NP; ++p) {
-        const uint32_t sa = smem_u32(st + p * TC_TILE);
-#pragma unroll
-        for (int kk = 0; kk < TC_K / 16; ++kk)
-          tc_mma(tmem, smem_desc(sa + kk * 256), smem_desc(sb + kk * 256), (i | p | kk) != 0);
-      }
-      tc_commit(&bar_mma[i % TC_ST]);
+      for (int kk = 0; kk < TC_K / 16; ++kk)
+        tc_mma(tmem, smem_desc(sa + kk * 256), smem_desc(sb + kk * 256), tc_idesc(NT), (i | kk) != 0);
+      tc_commit(&bar_mma[i % NST]);
     }
   }
   if (tid == 0) tc_commit(&bar_done);  // arrives when every MMA issued above has completed
   if (nk > 0 && !mbar_wait(&bar_done, 0)) ok = false;
   tc_fence_after();
-  // epilogue: warp w owns accumulator rows (tensor-memory lanes) 32w .. 32w+31
-  const int row = warp * 32 + lane;
-  float* dst = P + ((int64_t)blockIdx.y * TC_M + row) * ldp + n0;
+  // epilogue: thread = weight row m (tensor-memory lane); column 3t + p holds
+  // piece p of token t, summed as (hi + mid) + lo
+  const int m = warp * 32 + lane;
+  float* dst = P + (int64_t)blockIdx.y * TC_TMAX * ldp + n0 + m;
+  float acc = 0.0f;
 #pragma unroll 1
-  for (int c0 = 0; c0 < TC_N; c0 += 32) {
-    uint32_t v[32];
-    tc_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+  for (int c0 = 0; c0 < xr; c0 += 16) {
+    uint32_t v[16];
+    tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
 #pragma unroll
-    for (int q = 0; q < 32; q += 4) {
-      float4 f = nk > 0 ? make_float4(__uint_as_float(v[q]), __uint_as_float(v[q + 1]), __uint_as_float(v[q + 2]),
-                                      __uint_as_float(v[q + 3]))
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<float4*>(dst + c0 + q) = f;
+    for (int q = 0; q < 16; ++q) {
+      const int col = c0 + q;
+      if (col >= xr) break;
+      const int p = col % TC_NP;
+      acc = p == 0 ? __uint_as_float(v[q]) : __fadd_rn(acc, __uint_as_float(v[q]));
+      if (p == TC_NP - 1) dst[(int64_t)(col / TC_NP) * ldp] = nk > 0 ? acc : 0.0f;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TC_N) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(Cfg::TMEM_COLS)
+                 : "memory");
   if (!ok && tid == 0) atomicOr(err, DERR_TIMEOUT);
 }
 
-// x[T][n] f32 -> three bf16 pieces [3][TC_M][ld] with x = hi + mid + lo
-// exactly (each piece holds the next 8 significant bits); rows >= T and
-// columns >= n are zero.
+// x[T][n] f32 -> three bf16 pieces, row 3t + p of [3 * TC_TMAX][ld] holding
+// piece p of token t, with x = hi + mid + lo exactly (each piece holds the
+// next 8 significant bits); columns >= n are zero.
 __global__ void split3_kernel(const float* __restrict__ x, int T, int n, int ldx, __nv_bfloat16* __restrict__ out,
                               int ld) {
   const int t = blockIdx.y;
-  const int64_t piece = (int64_t)TC_M * ld;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ld; i += gridDim.x * blockDim.x) {
     const float v = (t < T && i < n) ? x[(int64_t)t * ldx + i] : 0.0f;
     const __nv_bfloat16 hi = __float2bfloat16_rn(v);
@@ -188,109 +211,178 @@ __global__ void split3_kernel(const float* __restrict__ x, int T, int n, int ldx
     const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
     const float r2 = __fsub_rn(r1, __bfloat162float(mid));
     const __nv_bfloat16 lo = __float2bfloat16_rn(r2);
-    const int64_t o = (int64_t)t * ld + i;
+    const int64_t o = (int64_t)(TC_NP * t) * ld + i;
     out[o] = hi;
-    out[piece + o] = mid;
-    out[2 * piece + o] = lo;
+    out[o + ld] = mid;
+    out[o + 2 * (int64_t)ld] = lo;
   }
 }
 
 // y[t][j] = act(sum over splits of P[s][t][j] + bias[j]) for t < T, j < n;
-// act 0 = ReLU (f32::max against 0), 1 = sigmoid.
+// act 0 = ReLU (f32::max against 0), 1 = sigmoid.  With xs_next, the result
+// is also written as the next layer's three bf16 pieces (rows 3t .. 3t+2 of
+// [3 * TC_TMAX][ld_next], columns n .. ld_next-1 zero).
 __global__ void splitk_finish_kernel(const float* __restrict__ P, int splits, int ldp, const float* __restrict__ bias,
-                                     int T, int n, int act, float* __restrict__ y, int ldy) {
+                                     int T, int n, int act, float* __restrict__ y, int ldy,
+                                     __nv_bfloat16* __restrict__ xs_next, int ld_next) {
   const int t = blockIdx.y;
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    for (int q = 0; q < splits; ++q) s = __fadd_rn(s, P[((int64_t)q * TC_M + t) * ldp + j]);
-    const float v = __fadd_rn(s, bias[j]);
-    y[(int64_t)t * ldy + j] = act == 0 ? fmaxf(v, 0.0f) : __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+  const int lim = xs_next ? ld_next : n;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < lim; j += gridDim.x * blockDim.x) {
+    float v = 0.0f;
+    if (j < n) {
+      float s = 0.0f;
+      for (int q = 0; q < splits; ++q) s = __fadd_rn(s, P[((int64_t)q * TC_TMAX + t) * ldp + j]);
+      v = __fadd_rn(s, bias[j]);
+      v = act == 0 ? fmaxf(v, 0.0f) : __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+      y[(int64_t)t * ldy + j] = v;
+    }
+    if (xs_next) {
+      const int64_t o = (int64_t)(TC_NP * t) * ld_next + j;
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      const float r1 = __fsub_rn(v, __bfloat162float(hi));
+      const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+      xs_next[o] = hi;
+      xs_next[o + ld_next] = mid;
+      xs_next[o + 2 * (int64_t)ld_next] = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(mid)));
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
 // select_top_k (mlp_predictor.rs:126-132): the k largest scores of a row in
-// (score descending, index ascending) order -- the stable sort's order.
-// Scores are sigmoid outputs, non-negative, so their bit patterns order like
-// the values.  One block per token: a 4-pass 8-bit radix select finds the
-// k-th largest key, the keys above it and the first ties (lowest indices)
-// are gathered, and a bitonic sort of (~key, index) orders them.
+// (score descending, index ascending) order -- the stable sort's order.  One
+// block per token, the row staged in shared memory:
+//  1. min / max of the row;
+//  2. a histogram over TK_NB equal-width bins of [min, max]; the bin map
+//     (v - min) * scale, truncated, is monotonic in v, so every key of a
+//     higher bin is larger than every key of a lower one;
+//  3. a scan from the top bin finds bin b* where the count reaches k;
+//  4. keys of bins above b* are taken, and the keys of b* are ranked exactly
+//     among themselves (score desc, index asc) to take the rest;
+//  5. a bitonic sort of (~score bits, index) orders the k taken keys.
+// Scores are sigmoid outputs: non-negative and finite, so their bit
+// patterns order like their values.
 // ---------------------------------------------------------------------------
 constexpr int TK_NT = 1024;
+constexpr int TK_NB = 4096;
+constexpr int TK_MAXC = 2048;  // candidates of the threshold bin ranked in shared memory
 
 __global__ void __launch_bounds__(TK_NT) topk_kernel(const float* __restrict__ scores, int n, int lds, int k,
                                                      uint32_t* __restrict__ idx, int ldi, int pow2) {
   extern __shared__ __align__(1024) unsigned char tk_smem[];
   uint64_t* keys = reinterpret_cast<uint64_t*>(tk_smem);  // [pow2]
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t sel_prefix, sel_mask, need_s, n_gt, n_eq_taken;
-  const int t = blockIdx.x, tid = threadIdx.x;
-  const float* row = scores + (int64_t)t * lds;
-  if (tid == 0) {
-    sel_prefix = 0;
-    sel_mask = 0;
-    need_s = (uint32_t)k;
-  }
-  __syncthreads();
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = tid; b < 256; b += TK_NT) hist[b] = 0;
-    __syncthreads();
-    const uint32_t pre = sel_prefix, msk = sel_mask;
-    for (int i = tid; i < n; i += TK_NT) {
-      const uint32_t key = __float_as_uint(row[i]);
-      if ((key & msk) == pre) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-    }
-    __syncthreads();
-    if (tid == 0) {
-      uint32_t need = need_s, b = 255;
-      for (;; --b) {  // walk down from the largest digit
-        if (hist[b] >= need || b == 0) break;
-        need -= hist[b];
-      }
-      sel_prefix = pre | (b << shift);
-      sel_mask = msk | (255u << shift);
-      need_s = need;  // how many keys equal to the final threshold are still needed (after the last pass)
-    }
-    __syncthreads();
-  }
-  const uint32_t thr = sel_prefix;
-  if (tid == 0) {
-    n_gt = 0;
-    n_eq_taken = 0;
-  }
-  for (int i = tid; i < pow2; i += TK_NT) keys[i] = ~0ull;
-  __syncthreads();
-  // keys above the threshold, in any order; then ties in index order
+  float* row = reinterpret_cast<float*>(keys + pow2);     // [n]
+  __shared__ uint32_t hist[TK_NB];
+  __shared__ uint64_t cands[TK_MAXC];
+  __shared__ float red_mn[TK_NT / 32], red_mx[TK_NT / 32];
+  __shared__ uint32_t wsum[TK_NT / 32];
+  __shared__ int bstar_s;
+  __shared__ uint32_t above_s, n_taken, n_cand;
+  const int t = blockIdx.x, tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const float* grow = scores + (int64_t)t * lds;
+  float mn = INFINITY, mx = -INFINITY;
   for (int i = tid; i < n; i += TK_NT) {
-    const uint32_t key = __float_as_uint(row[i]);
-    if (key > thr) {
-      const uint32_t pos = atomicAdd(&n_gt, 1u);
-      keys[pos] = ((uint64_t)(~key) << 32) | (uint32_t)i;
+    const float v = grow[i];
+    row[i] = v;
+    mn = fminf(mn, v);
+    mx = fmaxf(mx, v);
+  }
+  for (int i = tid; i < TK_NB; i += TK_NT) hist[i] = 0;
+  for (int i = tid; i < pow2; i += TK_NT) keys[i] = ~0ull;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if (l == 0) {
+    red_mn[w] = mn;
+    red_mx[w] = mx;
+  }
+  if (tid == 0) {
+    n_taken = 0;
+    n_cand = 0;
+  }
+  __syncthreads();
+  mn = red_mn[0];
+  mx = red_mx[0];
+  for (int q = 1; q < TK_NT / 32; ++q) {
+    mn = fminf(mn, red_mn[q]);
+    mx = fmaxf(mx, red_mx[q]);
+  }
+  const float scale = mx > mn ? (float)(TK_NB - 1) / (mx - mn) : 0.0f;
+  auto bin_of = [&](float v) { return min(TK_NB - 1, (int)__fmul_rz(__fsub_rz(v, mn), scale)); };
+  for (int i = tid; i < n; i += TK_NT) atomicAdd(&hist[bin_of(row[i])], 1u);
+  __syncthreads();
+  // suffix counts: thread j owns bins TK_NB-1-4j .. TK_NB-4-4j (descending)
+  {
+    uint32_t c[4], tot = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      c[q] = hist[TK_NB - 1 - 4 * tid - q];
+      tot += c[q];
+    }
+    uint32_t incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (l >= o) incl += v;
+    }
+    if (l == 31) wsum[w] = incl;
+    __syncthreads();
+    uint32_t wbase = 0;
+    for (int q = 0; q < w; ++q) wbase += wsum[q];
+    const uint32_t before = wbase + incl - tot;  // keys in higher bins than this thread's
+    if (before < (uint32_t)k && before + tot >= (uint32_t)k) {
+      uint32_t run = before;
+      for (int q = 0; q < 4; ++q) {
+        if (run + c[q] >= (uint32_t)k) {
+          bstar_s = TK_NB - 1 - 4 * tid - q;
+          above_s = run;
+          break;
+        }
+        run += c[q];
+      }
     }
   }
   __syncthreads();
-  const uint32_t ties = need_s;  // number of threshold-equal keys to take, lowest indices first
-  for (int base = 0; base < n && n_eq_taken < ties; base += TK_NT) {
-    const int i = base + tid;
-    const bool eq = i < n && __float_as_uint(row[i]) == thr;
-    // rank among the equal keys of this chunk (block-wide prefix via warp ballots)
-    const uint32_t bal = __ballot_sync(0xffffffffu, eq);
-    __shared__ uint32_t wcnt[TK_NT / 32];
-    if ((tid & 31) == 0) wcnt[tid >> 5] = __popc(bal);
-    __syncthreads();
-    uint32_t before = 0;
-    for (int w = 0; w < (tid >> 5); ++w) before += wcnt[w];
-    before += __popc(bal & ((1u << (tid & 31)) - 1u));
-    const uint32_t taken = n_eq_taken;
-    if (eq && taken + before < ties) keys[n_gt + taken + before] = ((uint64_t)(~thr) << 32) | (uint32_t)i;
-    __syncthreads();
-    if (tid == 0) {
-      uint32_t tot = 0;
-      for (int w = 0; w < TK_NT / 32; ++w) tot += wcnt[w];
-      n_eq_taken = min(ties, taken + tot);
+  const int bstar = bstar_s;
+  const uint32_t above = above_s, need = (uint32_t)k - above;
+  // keys above b*: taken in any order; keys of b*: candidates, ranked
+  // exactly among themselves (score desc, index asc) for the remaining slots
+  for (int i = tid; i < n; i += TK_NT) {
+    const float v = row[i];
+    const int b = bin_of(v);
+    if (b < bstar) continue;
+    const uint64_t key = ((uint64_t)(~__float_as_uint(v)) << 32) | (uint32_t)i;
+    if (b > bstar) keys[atomicAdd(&n_taken, 1u)] = key;
+    else {
+      const uint32_t c = atomicAdd(&n_cand, 1u);
+      if (c < TK_MAXC) cands[c] = key;
     }
-    __syncthreads();
   }
+  __syncthreads();
+  const uint32_t nc = n_cand;
+  if (nc <= TK_MAXC) {
+    for (uint32_t ci = tid; ci < nc; ci += TK_NT) {
+      const uint64_t key = cands[ci];
+      uint32_t rank = 0;
+      for (uint32_t j = 0; j < nc; ++j) rank += cands[j] < key;
+      if (rank < need) keys[above + rank] = key;
+    }
+  } else {  // a bin holding very many equal or near-equal scores: rank against the whole row
+    for (int i = tid; i < n; i += TK_NT) {
+      const float v = row[i];
+      if (bin_of(v) != bstar) continue;
+      const uint64_t key = ((uint64_t)(~__float_as_uint(v)) << 32) | (uint32_t)i;
+      uint32_t rank = 0;
+      for (int j = 0; j < n; ++j) {
+        const float u = row[j];
+        if (bin_of(u) == bstar) rank += (((uint64_t)(~__float_as_uint(u)) << 32) | (uint32_t)j) < key;
+      }
+      if (rank < need) keys[above + rank] = key;
+    }
+  }
+  __syncthreads();
   // bitonic sort ascending of keys[0, pow2)
   for (int size = 2; size <= pow2; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
@@ -341,6 +433,7 @@ __global__ void __launch_bounds__(DV_WARPS * 32)
     const uint4* g4 = reinterpret_cast<const uint4*>(gate + (int64_t)row * ldw);
     const uint4* u4 = reinterpret_cast<const uint4*>(up + (int64_t)row * ldw);
     float g = 0.f, u = 0.f;
+#pragma unroll 4
     for (int c = l; c < ldw / 8; c += 32) {
       const uint4 gr = g4[c], ur = u4[c];
       const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gr);
@@ -363,7 +456,7 @@ __global__ void __launch_bounds__(DV_WARPS * 32)
 }
 
 constexpr int DV_DN_T = 256;  // output columns per block
-constexpr int DV_PF = 8;      // selected rows in flight per thread
+constexpr int DV_PF = 16;     // selected rows in flight per thread
 
 __global__ void __launch_bounds__(DV_DN_T)
     dv_down_kernel(const __nv_bfloat16* __restrict__ downT, int hid, int ldw, const uint32_t* __restrict__ sel, int k,
@@ -398,7 +491,14 @@ __global__ void dv_down_finish_kernel(const float* __restrict__ part, int splits
   const int t = blockIdx.y;
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < hid; j += gridDim.x * blockDim.x) {
     float s = 0.0f;
-    for (int q = 0; q < splits; ++q) s = __fadd_rn(s, part[((int64_t)t * splits + q) * ldw + j]);
+    for (int q0 = 0; q0 < splits; q0 += 8) {  // 8 loads in flight, added in split order
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = q0 + u < splits ? part[((int64_t)t * splits + q0 + u) * ldw + j] : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (q0 + u < splits) s = __fadd_rn(s, v[u]);
+    }
     out[(int64_t)t * hid + j] = bias ? __fadd_rn(s, bias[j]) : s;
   }
 }
@@ -415,53 +515,71 @@ int sm_count() {
 
 }  // namespace
 
-// K splits of the tcgen05 linear: enough CTAs to cover the SMs, at least two
-// K tiles per split.  *per = K tiles per split.
+// K splits of the tcgen05 linear: as many CTAs as fit in one wave (one CTA
+// per SM), at least two K tiles per split.  *per = K tiles per split.
 int tc_linear_splits(int n, int ldw, int* per) {
-  const int ntile = (int)ceil_div(n, TC_N);
+  const int ntile = (int)ceil_div(n, TC_M);
   const int ktiles = ldw / TC_K;
-  int splits = std::max(1, std::min(std::min(16, ktiles / 2), (int)ceil_div(sm_count(), ntile)));
+  int splits = std::max(1, std::min(std::min(32, ktiles / 2), sm_count() / ntile));
   const int p = (int)ceil_div(ktiles, splits);
   if (per) *per = p;
   return (int)ceil_div(ktiles, p);
 }
 size_t tc_linear_scratch_floats(int n, int ldw) {
-  return (size_t)tc_linear_splits(n, ldw, nullptr) * TC_M * ceil_div(n, TC_N) * TC_N;
+  return (size_t)tc_linear_splits(n, ldw, nullptr) * TC_TMAX * ceil_div(n, TC_M) * TC_M;
 }
 
-// y[T][n] = act(x[T][d] . W^T + b) through the tcgen05 GEMM; T <= 128.
-// W: [n][ldw] bf16 (ldw a multiple of 64, zero beyond d).  xs: split scratch
-// [3][128][ldw] bf16; P: split-K scratch [splits][128][round_up(n, 128)] f32.
-void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16* W, int n, int ldw,
-                      const float* bias, int act, float* y, int ldy, __nv_bfloat16* xs, float* P, int max_splits,
-                      int* err, cudaStream_t st) {
+template <int NT>
+static void tc_gemm_launch(dim3 grid, const __nv_bfloat16* W, int ldw, int nw, const __nv_bfloat16* xs, int T,
+                           int ktiles, int per, float* P, int ldp, int* err, cudaStream_t st) {
+  using Cfg = TcCfg<NT>;
+  constexpr int smem = Cfg::NST * Cfg::STAGE;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_ST * TC_STAGE);
+    cudaFuncSetAttribute(tc_gemm_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr = true;
   }
-  split3_kernel<<<dim3((unsigned)ceil_div(ldw, 256), TC_M), 256, 0, st>>>(x, T, d, ldx, xs, ldw);
-  count_launch();
-  const int ntile = (int)ceil_div(n, TC_N);
+  tc_gemm_kernel<NT><<<grid, 128, smem, st>>>(W, ldw, nw, xs, T, ktiles, per, P, ldp, err);
+}
+
+// y[T][n] = act(x[T][d] . W^T + b) through the tcgen05 GEMM; T <= TC_TMAX.
+// W: [n][ldw] bf16 (ldw a multiple of 64, zero beyond d).  xs: the split
+// activations [3][128][ldw] bf16 -- written here from x, or, when x is
+// null, already written by the previous layer's finish.  P: split-K scratch.
+// xs_next (nullable): where the finish writes y's pieces for the next layer.
+void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16* W, int n, int ldw,
+                      const float* bias, int act, float* y, int ldy, __nv_bfloat16* xs, float* P,
+                      __nv_bfloat16* xs_next, int ld_next, int* err, cudaStream_t st) {
+  if (x) {
+    split3_kernel<<<dim3((unsigned)ceil_div(ldw, 256), T), 256, 0, st>>>(x, T, d, ldx, xs, ldw);
+    count_launch();
+  }
+  const int ntile = (int)ceil_div(n, TC_M);
   const int ktiles = ldw / TC_K;
   int per = 0;
   const int splits = tc_linear_splits(n, ldw, &per);
-  (void)max_splits;
-  const int ldp = ntile * TC_N;
-  tc_gemm_kernel<<<dim3(ntile, splits), 128, TC_ST * TC_STAGE, st>>>(xs, (int64_t)TC_M * ldw, ldw, W, ldw, n, ktiles,
-                                                                     per, P, ldp, err);
+  const int ldp = ntile * TC_M;
+  const dim3 grid(ntile, splits);
+  const int xr = TC_NP * T;  // token-piece rows: the MMA's N, rounded up to 16
+  if (xr <= 16) tc_gemm_launch<16>(grid, W, ldw, n, xs, T, ktiles, per, P, ldp, err, st);
+  else if (xr <= 32) tc_gemm_launch<32>(grid, W, ldw, n, xs, T, ktiles, per, P, ldp, err, st);
+  else if (xr <= 64) tc_gemm_launch<64>(grid, W, ldw, n, xs, T, ktiles, per, P, ldp, err, st);
+  else if (xr <= 128) tc_gemm_launch<128>(grid, W, ldw, n, xs, T, ktiles, per, P, ldp, err, st);
+  else tc_gemm_launch<256>(grid, W, ldw, n, xs, T, ktiles, per, P, ldp, err, st);
   count_launch();
-  splitk_finish_kernel<<<dim3((unsigned)ceil_div(n, 256), T), 256, 0, st>>>(P, splits, ldp, bias, T, n, act, y, ldy);
+  const int lim = xs_next ? ld_next : n;
+  splitk_finish_kernel<<<dim3((unsigned)ceil_div(lim, 256), T), 256, 0, st>>>(P, splits, ldp, bias, T, n, act, y, ldy,
+                                                                            xs_next, ld_next);
   count_launch();
 }
 
 void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* idx, int ldi, cudaStream_t st) {
   int pow2 = 1;
   while (pow2 < k) pow2 <<= 1;
-  const size_t sm = (size_t)pow2 * 8;
+  const size_t sm = (size_t)pow2 * 8 + (size_t)n * 4;
   static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (!attr) {  // the kernel's static shared memory (~34 KB) counts against the 227 KB per block
+    cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 190 * 1024);
     attr = true;
   }
   topk_kernel<<<T, TK_NT, sm, st>>>(scores, n, lds, k, idx, ldi, pow2);

@@ -269,16 +269,18 @@ void launch_shard_or_masks(uint32_t* tmask, const uint32_t* all, int P, int nw, 
 
 // ---- Deja Vu sparse FFN (dejavu.cu) ----
 // Rows per tcgen05 linear call (tokens); K pitch granularity of its weights.
-constexpr int TC_LINEAR_MAX_T = 128;
+constexpr int TC_LINEAR_MAX_T = 85;
 constexpr int TC_LINEAR_KPAD = 64;
 int tc_linear_splits(int n, int ldw, int* per);
 size_t tc_linear_scratch_floats(int n, int ldw);
-// y[T][n] = act(x[T][d] . W^T + bias), act 0 = ReLU, 1 = sigmoid; T <= 128;
-// W [n][ldw] bf16 zero beyond d; xs scratch [3][128][ldw] bf16; P scratch of
-// tc_linear_scratch_floats(n, ldw) floats.
+// y[T][n] = act(x[T][d] . W^T + bias), act 0 = ReLU, 1 = sigmoid; T <= 85;
+// W [n][ldw] bf16 zero beyond d; xs scratch [3 * 85][ldw] bf16 holding the
+// split x (x == nullptr: already written by the previous layer); P scratch of
+// tc_linear_scratch_floats(n, ldw) floats; xs_next (nullable): y's pieces
+// for a following layer of pitch ld_next.
 void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16* W, int n, int ldw,
-                      const float* bias, int act, float* y, int ldy, __nv_bfloat16* xs, float* P, int max_splits,
-                      int* err, cudaStream_t st);
+                      const float* bias, int act, float* y, int ldy, __nv_bfloat16* xs, float* P,
+                      __nv_bfloat16* xs_next, int ld_next, int* err, cudaStream_t st);
 // idx[t][0, k) = the k largest of scores[t][0, n) in (score desc, index asc)
 // order; scores non-negative; k <= n.
 void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* idx, int ldi, cudaStream_t st);
