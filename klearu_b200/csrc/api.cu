@@ -2376,10 +2376,16 @@ struct kl_predictor_s {
 
 struct kl_sparse_mlp_s {
   kl_ctx_t ctx;
-  int hid = 0, inter = 0, ldw = 0;
-  DBuf gate, up, downT, bias, a, part;
+  int hid = 0, inter = 0, ldw = 0, ldd = 0;
+  DBuf gate, up, downT, down, bias, a, part;
+  // dense-masked path (n_tokens >= KL_DENSE_MIN_TOKENS): scratch
+  DBuf G, U, mask, xs, hs, P;
   bool has_bias = false;
 };
+// From this many tokens on, one pass over all MLP weights (dense tensor-core
+// GEMMs with the selection as a mask) moves fewer bytes than gathering the
+// selected rows once per token (about 10 % of the rows each).
+constexpr int KL_DENSE_MIN_TOKENS = 8;
 
 namespace {
 
@@ -2483,7 +2489,7 @@ extern "C" kl_status kl_predictor_select_topk(kl_predictor_t p, const float* x, 
   const int kk = std::min(k, p->out);
   if (n_tokens == 0 || kk == 0) return KL_OK;
   require(x && idx, "select_topk: x and idx are required");
-  int pow2 = 1;
+  int pow2 = 2048;
   while (pow2 < kk) pow2 <<= 1;
   support((size_t)pow2 * 8 + (size_t)p->out * 4 <= 190 * 1024,
           "select_topk: k and output_dim too large for one block's shared memory");
@@ -2510,11 +2516,22 @@ extern "C" kl_status kl_sparse_mlp_create(kl_ctx_t ctx, int hidden, int intermed
   m->ctx = ctx;
   m->hid = hidden;
   m->inter = intermediate;
-  m->ldw = (int)round_up(hidden, 8);
+  m->ldw = (int)round_up(hidden, TC_LINEAR_KPAD);
+  m->ldd = (int)round_up(intermediate, TC_LINEAR_KPAD);
   upload_bf16(ctx, m->gate, gate_host, intermediate, hidden, m->ldw, intermediate, false);
   upload_bf16(ctx, m->up, up_host, intermediate, hidden, m->ldw, intermediate, false);
-  // down [hidden][intermediate] stored transposed: a neuron's weights are one row
+  // down [hidden][intermediate] twice: transposed for the per-token gather (a
+  // neuron's weights are one row), as is for the dense GEMM
   upload_bf16(ctx, m->downT, down_host, hidden, intermediate, m->ldw, intermediate, true);
+  upload_bf16(ctx, m->down, down_host, hidden, intermediate, m->ldd, hidden, false);
+  const size_t tmax = TC_LINEAR_MAX_T;
+  m->G.alloc(tmax * intermediate * 4);
+  m->U.alloc(tmax * intermediate * 4);
+  m->mask.alloc(tmax * intermediate);
+  ck(cudaMemsetAsync(m->mask.p, 0, tmax * intermediate, ctx->stream), "memset");
+  m->xs.alloc(3 * tmax * m->ldw * 2);
+  m->hs.alloc(3 * tmax * m->ldd * 2);
+  m->P.alloc(std::max(tc_linear_scratch_floats(intermediate, m->ldw), tc_linear_scratch_floats(hidden, m->ldd)) * 4);
   m->has_bias = down_bias_host != nullptr;
   if (m->has_bias) upload_f32(ctx, m->bias, down_bias_host, hidden);
   ck(cudaStreamSynchronize(ctx->stream), "sync");
@@ -2547,7 +2564,19 @@ extern "C" kl_status kl_sparse_mlp_forward(kl_sparse_mlp_t m, const float* x, in
     return KL_OK;
   }
   require(sel != nullptr, "sparse_mlp_forward: sel is required");
-  // enough blocks for the down projection: (hidden / 256) x splits x tokens
+  if (n_tokens >= KL_DENSE_MIN_TOKENS) {
+    for (int t0 = 0; t0 < n_tokens; t0 += TC_LINEAR_MAX_T) {
+      const int tn = std::min(TC_LINEAR_MAX_T, n_tokens - t0);
+      launch_sparse_mlp_dense(m->gate.as<__nv_bfloat16>(), m->up.as<__nv_bfloat16>(), m->down.as<__nv_bfloat16>(),
+                              m->hid, m->ldw, m->inter, m->ldd, m->has_bias ? m->bias.as<float>() : nullptr,
+                              x + (int64_t)t0 * m->hid, tn, sel + (int64_t)t0 * k, k, m->G.as<float>(),
+                              m->U.as<float>(), m->mask.as<uint8_t>(), m->xs.as<__nv_bfloat16>(),
+                              m->hs.as<__nv_bfloat16>(), m->P.as<float>(), out + (int64_t)t0 * m->hid,
+                              ctx__->err.as<int>(), st);
+      ck_launch("sparse mlp (dense)");
+    }
+    return KL_OK;
+  }
   // K splits of the down projection: at most ~32 selected rows per thread,
   // and enough blocks ((hidden / 256) x splits x tokens) to fill the SMs
   const int cols = (int)ceil_div(m->hid, 256);

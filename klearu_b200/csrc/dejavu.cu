@@ -83,13 +83,15 @@ template <int NT>
 struct TcCfg {
   static constexpr int XTILE = NT * TC_K * 2;  // the token-piece rows
   static constexpr int STAGE = TC_WTILE + XTILE;
-  static constexpr int NST = (TC_SMEM / STAGE) < 8 ? (TC_SMEM / STAGE) : 8;
+  // narrow token tiles: two CTAs per SM, so that two MMA chains share the SM
+  static constexpr int CTAS = NT <= 32 ? 2 : 1;
+  static constexpr int NST = (TC_SMEM / CTAS / STAGE) < 8 ? (TC_SMEM / CTAS / STAGE) : 8;
   static_assert(NST >= 3, "the ring needs a prefetch distance of at least one stage");
   static constexpr int TMEM_COLS = NT < 32 ? 32 : NT;
 };
 
 template <int NT>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, TcCfg<NT>::CTAS)
     tc_gemm_kernel(const __nv_bfloat16* __restrict__ W, int ldw, int nw, const __nv_bfloat16* __restrict__ X, int T,
                    int ktiles, int kt_per_split, float* __restrict__ P, int ldp, int* err) {
   using Cfg = TcCfg<NT>;
@@ -219,7 +221,8 @@ __global__ void split3_kernel(const float* __restrict__ x, int T, int n, int ldx
 }
 
 // y[t][j] = act(sum over splits of P[s][t][j] + bias[j]) for t < T, j < n;
-// act 0 = ReLU (f32::max against 0), 1 = sigmoid.  With xs_next, the result
+// act 0 = ReLU (f32::max against 0), 1 = sigmoid, 2 = none; bias nullable.
+// With xs_next, the result
 // is also written as the next layer's three bf16 pieces (rows 3t .. 3t+2 of
 // [3 * TC_TMAX][ld_next], columns n .. ld_next-1 zero).
 __global__ void splitk_finish_kernel(const float* __restrict__ P, int splits, int ldp, const float* __restrict__ bias,
@@ -232,8 +235,9 @@ __global__ void splitk_finish_kernel(const float* __restrict__ P, int splits, in
     if (j < n) {
       float s = 0.0f;
       for (int q = 0; q < splits; ++q) s = __fadd_rn(s, P[((int64_t)q * TC_TMAX + t) * ldp + j]);
-      v = __fadd_rn(s, bias[j]);
-      v = act == 0 ? fmaxf(v, 0.0f) : __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+      v = bias ? __fadd_rn(s, bias[j]) : s;
+      if (act == 0) v = fmaxf(v, 0.0f);
+      else if (act == 1) v = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
       y[(int64_t)t * ldy + j] = v;
     }
     if (xs_next) {
@@ -384,20 +388,67 @@ __global__ void __launch_bounds__(TK_NT) topk_kernel(const float* __restrict__ s
   }
   __syncthreads();
   // bitonic sort ascending of keys[0, pow2)
-  for (int size = 2; size <= pow2; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < pow2; i += TK_NT) {
-        const int j = i ^ stride;
-        if (j > i) {
+  if (pow2 == 2 * TK_NT) {
+    // two keys per thread (elements 2*tid, 2*tid+1; warp w holds 64w ..
+    // 64w+63): strides below 64 in registers and shuffles, larger strides
+    // through shared memory
+    uint64_t v0 = keys[2 * tid], v1 = keys[2 * tid + 1];
+    for (int size = 2; size <= pow2; size <<= 1) {
+      int stride = size >> 1;
+      if (stride >= 64) {
+        keys[2 * tid] = v0;
+        keys[2 * tid + 1] = v1;
+        __syncthreads();
+        for (; stride >= 64; stride >>= 1) {
+          const int i = (tid / stride) * 2 * stride + (tid % stride), j = i + stride;
           const bool up = (i & size) == 0;
           const uint64_t a = keys[i], b = keys[j];
           if ((a > b) == up) {
             keys[i] = b;
             keys[j] = a;
           }
+          __syncthreads();
+        }
+        v0 = keys[2 * tid];
+        v1 = keys[2 * tid + 1];
+        __syncthreads();
+      }
+      for (; stride >= 2; stride >>= 1) {
+        const int lm = stride >> 1;  // partner lane offset
+        const uint64_t o0 = __shfl_xor_sync(0xffffffffu, v0, lm), o1 = __shfl_xor_sync(0xffffffffu, v1, lm);
+        const int e = 2 * tid;  // both keys share (e & stride) and (e & size)
+        const bool keep_min = ((e & stride) == 0) == ((e & size) == 0);
+        v0 = keep_min ? (v0 < o0 ? v0 : o0) : (v0 > o0 ? v0 : o0);
+        v1 = keep_min ? (v1 < o1 ? v1 : o1) : (v1 > o1 ? v1 : o1);
+      }
+      {  // stride 1: the thread's own pair
+        const bool up = ((2 * tid) & size) == 0;
+        if ((v0 > v1) == up) {
+          const uint64_t x = v0;
+          v0 = v1;
+          v1 = x;
         }
       }
-      __syncthreads();
+    }
+    keys[2 * tid] = v0;
+    keys[2 * tid + 1] = v1;
+    __syncthreads();
+  } else {
+    for (int size = 2; size <= pow2; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = tid; i < pow2; i += TK_NT) {
+          const int j = i ^ stride;
+          if (j > i) {
+            const bool up = (i & size) == 0;
+            const uint64_t a = keys[i], b = keys[j];
+            if ((a > b) == up) {
+              keys[i] = b;
+              keys[j] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
     }
   }
   for (int i = tid; i < k; i += TK_NT) idx[(int64_t)t * ldi + i] = (uint32_t)(keys[i] & 0xffffffffu);
@@ -515,18 +566,19 @@ int sm_count() {
 
 }  // namespace
 
-// K splits of the tcgen05 linear: as many CTAs as fit in one wave (one CTA
-// per SM), at least two K tiles per split.  *per = K tiles per split.
-int tc_linear_splits(int n, int ldw, int* per) {
+// K splits of the tcgen05 linear: as many CTAs as fit in one wave
+// (ctas_per_sm per SM), at least two K tiles per split.  *per = K tiles per
+// split.
+int tc_linear_splits(int n, int ldw, int* per, int ctas_per_sm) {
   const int ntile = (int)ceil_div(n, TC_M);
   const int ktiles = ldw / TC_K;
-  int splits = std::max(1, std::min(std::min(32, ktiles / 2), sm_count() / ntile));
+  int splits = std::max(1, std::min(std::min(32, ktiles / 2), sm_count() * ctas_per_sm / ntile));
   const int p = (int)ceil_div(ktiles, splits);
   if (per) *per = p;
   return (int)ceil_div(ktiles, p);
 }
 size_t tc_linear_scratch_floats(int n, int ldw) {
-  return (size_t)tc_linear_splits(n, ldw, nullptr) * TC_TMAX * ceil_div(n, TC_M) * TC_M;
+  return (size_t)tc_linear_splits(n, ldw, nullptr, 2) * TC_TMAX * ceil_div(n, TC_M) * TC_M;
 }
 
 template <int NT>
@@ -556,11 +608,11 @@ void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16
   }
   const int ntile = (int)ceil_div(n, TC_M);
   const int ktiles = ldw / TC_K;
+  const int xr = TC_NP * T;  // token-piece rows: the MMA's N, rounded up to 16
   int per = 0;
-  const int splits = tc_linear_splits(n, ldw, &per);
+  const int splits = tc_linear_splits(n, ldw, &per, xr <= 32 ? 2 : 1);
   const int ldp = ntile * TC_M;
   const dim3 grid(ntile, splits);
-  const int xr = TC_NP * T;  // token-piece rows: the MMA's N, rounded up to 16
   if (xr <= 16) tc_gemm_launch<16>(grid, W, ldw, n, xs, T, ktiles, per, P, ldp, err, st);
   else if (xr <= 32) tc_gemm_launch<32>(grid, W, ldw, n, xs, T, ktiles, per, P, ldp, err, st);
   else if (xr <= 64) tc_gemm_launch<64>(grid, W, ldw, n, xs, T, ktiles, per, P, ldp, err, st);
@@ -574,7 +626,7 @@ void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16
 }
 
 void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* idx, int ldi, cudaStream_t st) {
-  int pow2 = 1;
+  int pow2 = 2 * TK_NT;  // at least the register-sorted size
   while (pow2 < k) pow2 <<= 1;
   const size_t sm = (size_t)pow2 * 8 + (size_t)n * 4;
   static bool attr = false;
@@ -584,6 +636,60 @@ void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* id
   }
   topk_kernel<<<T, TK_NT, sm, st>>>(scores, n, lds, k, idx, ldi, pow2);
   count_launch();
+}
+
+namespace {
+// mask[t][i] = 1 for the selected neurons of token t (mask zeroed before)
+__global__ void dv_mask_kernel(const uint32_t* __restrict__ sel, int k, int inter, uint8_t* __restrict__ mask) {
+  const int t = blockIdx.y;
+  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < k; s += gridDim.x * blockDim.x) {
+    const uint32_t i = sel[(int64_t)t * k + s];
+    if (i < (uint32_t)inter) mask[(int64_t)t * inter + i] = 1;
+  }
+}
+// h[t][i] = mask ? silu(g) * u : 0, written as the down projection's three
+// bf16 pieces (rows 3t .. 3t+2 of [3 * TC_TMAX][ldh], columns >= inter zero);
+// the mask is cleared for the next call
+__global__ void dv_swiglu_mask_kernel(const float* __restrict__ G, const float* __restrict__ U, int inter,
+                                      uint8_t* __restrict__ mask, __nv_bfloat16* __restrict__ hs, int ldh) {
+  const int t = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ldh; i += gridDim.x * blockDim.x) {
+    float v = 0.0f;
+    if (i < inter && mask[(int64_t)t * inter + i]) {
+      const float g = G[(int64_t)t * inter + i], u = U[(int64_t)t * inter + i];
+      v = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+      mask[(int64_t)t * inter + i] = 0;
+    }
+    const int64_t o = (int64_t)(TC_NP * t) * ldh + i;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    const float r1 = __fsub_rn(v, __bfloat162float(hi));
+    const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+    hs[o] = hi;
+    hs[o + ldh] = mid;
+    hs[o + 2 * (int64_t)ldh] = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(mid)));
+  }
+}
+}  // namespace
+
+// The selection as a mask over dense tensor-core GEMMs: G = gate . x,
+// U = up . x over all neurons, h = silu(G) * U on the selected neurons and 0
+// elsewhere, out = down . h (+ bias).  The zero terms leave every sum
+// unchanged, so this equals the per-token gather; it reads each weight once
+// per call instead of once per token.  T <= TC_TMAX.
+void launch_sparse_mlp_dense(const __nv_bfloat16* gate, const __nv_bfloat16* up, const __nv_bfloat16* down,
+                             int hid, int ldg, int inter, int ldd, const float* bias, const float* x, int T,
+                             const uint32_t* sel, int k, float* G, float* U, uint8_t* mask, __nv_bfloat16* xs,
+                             __nv_bfloat16* hs, float* P, float* out, int* err, cudaStream_t st) {
+  // x's pieces once for gate and up
+  split3_kernel<<<dim3((unsigned)ceil_div(ldg, 256), T), 256, 0, st>>>(x, T, hid, hid, xs, ldg);
+  count_launch();
+  launch_tc_linear(nullptr, T, hid, hid, gate, inter, ldg, nullptr, 2, G, inter, xs, P, nullptr, 0, err, st);
+  launch_tc_linear(nullptr, T, hid, hid, up, inter, ldg, nullptr, 2, U, inter, xs, P, nullptr, 0, err, st);
+  dv_mask_kernel<<<dim3((unsigned)ceil_div(k, 256), T), 256, 0, st>>>(sel, k, inter, mask);
+  count_launch();
+  dv_swiglu_mask_kernel<<<dim3((unsigned)ceil_div(ldd, 256), T), 256, 0, st>>>(G, U, inter, mask, hs, ldd);
+  count_launch();
+  launch_tc_linear(nullptr, T, inter, inter, down, hid, ldd, bias, 2, out, hid, hs, P, nullptr, 0, err, st);
 }
 
 void launch_sparse_mlp(const __nv_bfloat16* gate, const __nv_bfloat16* up, const __nv_bfloat16* downT, int hid,

@@ -271,7 +271,7 @@ void launch_shard_or_masks(uint32_t* tmask, const uint32_t* all, int P, int nw, 
 // Rows per tcgen05 linear call (tokens); K pitch granularity of its weights.
 constexpr int TC_LINEAR_MAX_T = 85;
 constexpr int TC_LINEAR_KPAD = 64;
-int tc_linear_splits(int n, int ldw, int* per);
+int tc_linear_splits(int n, int ldw, int* per, int ctas_per_sm);
 size_t tc_linear_scratch_floats(int n, int ldw);
 // y[T][n] = act(x[T][d] . W^T + bias), act 0 = ReLU, 1 = sigmoid; T <= 85;
 // W [n][ldw] bf16 zero beyond d; xs scratch [3 * 85][ldw] bf16 holding the
@@ -290,5 +290,15 @@ void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* id
 void launch_sparse_mlp(const __nv_bfloat16* gate, const __nv_bfloat16* up, const __nv_bfloat16* downT, int hid,
                        int ldw, int inter, const float* bias, const float* x, int T, const uint32_t* sel, int k,
                        float* a, float* part, int splits, float* out, int* err, cudaStream_t st);
+
+// The same MLP as launch_sparse_mlp through dense tcgen05 GEMMs with the
+// selection as a mask (T <= TC_LINEAR_MAX_T): gate / up [inter][ldg], down
+// [hid][ldd] bf16 (ldg, ldd multiples of 64); scratch G, U [T][inter] f32,
+// mask [T][inter] bytes (zero between calls), xs [3*85][ldg], hs [3*85][ldd]
+// bf16, P of max(tc_linear_scratch_floats(inter, ldg), (hid, ldd)) floats.
+void launch_sparse_mlp_dense(const __nv_bfloat16* gate, const __nv_bfloat16* up, const __nv_bfloat16* down,
+                             int hid, int ldg, int inter, int ldd, const float* bias, const float* x, int T,
+                             const uint32_t* sel, int k, float* G, float* U, uint8_t* mask, __nv_bfloat16* xs,
+                             __nv_bfloat16* hs, float* P, float* out, int* err, cudaStream_t st);
 
 }  // namespace kl
