@@ -83,8 +83,9 @@ template <int NT>
 struct TcCfg {
   static constexpr int XTILE = NT * TC_K * 2;  // the token-piece rows
   static constexpr int STAGE = TC_WTILE + XTILE;
-  // narrow token tiles: two CTAs per SM, so that two MMA chains share the SM
-  static constexpr int CTAS = NT <= 32 ? 2 : 1;
+  // token tiles up to 64 wide: two CTAs per SM, so that two MMA chains and
+  // their load rings share the SM
+  static constexpr int CTAS = NT <= 64 ? 2 : 1;
   static constexpr int NST = (TC_SMEM / CTAS / STAGE) < 8 ? (TC_SMEM / CTAS / STAGE) : 8;
   static_assert(NST >= 3, "the ring needs a prefetch distance of at least one stage");
   static constexpr int TMEM_COLS = NT < 32 ? 32 : NT;
@@ -610,7 +611,7 @@ void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16
   const int ktiles = ldw / TC_K;
   const int xr = TC_NP * T;  // token-piece rows: the MMA's N, rounded up to 16
   int per = 0;
-  const int splits = tc_linear_splits(n, ldw, &per, xr <= 32 ? 2 : 1);
+  const int splits = tc_linear_splits(n, ldw, &per, xr <= 64 ? 2 : 1);
   const int ldp = ntile * TC_M;
   const dim3 grid(ntile, splits);
   if (xr <= 16) tc_gemm_launch<16>(grid, W, ldw, n, xs, T, ktiles, per, P, ldp, err, st);
