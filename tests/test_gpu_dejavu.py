@@ -88,11 +88,11 @@ def mlp_weights(rng, hid, inter, std=0.02):
     return gate, up, down
 
 
-# T < 8: per-token row gather; T >= 8: dense tensor-core GEMMs with the
+# T < 24: per-token row gather; T >= 24: dense tensor-core GEMMs with the
 # selection as a mask (90 tokens: two 85-token chunks)
 @pytest.mark.parametrize("hid,inter,k,T,bias", [(64, 128, 128, 1, False), (96, 200, 37, 3, True),
-                                                (4096, 11008, 1101, 2, False), (96, 200, 37, 8, True),
-                                                (4096, 11008, 1101, 16, False), (256, 600, 60, 90, True)])
+                                                (4096, 11008, 1101, 2, False), (96, 200, 37, 24, True),
+                                                (4096, 11008, 1101, 32, False), (256, 600, 60, 90, True)])
 def test_sparse_mlp_matches_oracle(gpu_ctx, hid, inter, k, T, bias):
     rng = np.random.default_rng(hid + k)
     gate, up, down = mlp_weights(rng, hid, inter, std=0.02 if hid >= 1000 else 0.1)
