@@ -1,43 +1,55 @@
-"""SLIDE train-step benchmark (BASELINE.json metric: SLIDE train samples/s on
-the 670K-way sparse layer, with % of HBM peak).
+"""SLIDE train-step benchmark: SLIDE train samples/s on the 670K-way sparse
+layer at 1/2/4/8 B200, with the dominant kernel's fraction of HBM peak.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c1|c0|c2]
 
 One step = one batched train step (hash, probe, active-row forward + loss +
-input gradient, segmented gradient reduction + lazy Adam on both layers, and
-the table rebuild when the RebuildScheduler fires) over one batch of B=256
-synthetic C1 examples.  Prints ONE JSON line on rank 0.
+input gradient, segmented gradient reduction + lazy Adam on both layers) over
+one batch of synthetic examples.  Prints ONE JSON line on rank 0.
+
+Workloads (``--config``): c1 (default) is the 670K-way extreme-classification
+net (135909 -> 128 -> 670091, B=256 per GPU, weak scaling); c0 the README MLP
+(784 -> 1024 -> 10 softmax, B=128); c2 the 3.1M-way net (hidden 256, SimHash
+K9 L50 reservoir) at a fixed global batch of 1024 (strong scaling).
 
 * ``value``: samples/s of the whole job with the batches already resident in
   HBM, timed with CUDA events (max over ranks).
 * ``e2e``: the same metric through the C-ABI host-batch train step
   (kl_net_train_step_host), each batch uploaded from pinned host memory inside
   the timed region and the loss read back every step.
-* ``roofline``: the dominant phase's algorithmic bytes / its event-timed
-  duration, against MEASURED_PEAKS.json's HBM copy bandwidth.
+* ``roofline``: the step's dominant kernel (the output layer's active-row
+  forward, rm_forward_kernel): its algorithmic bytes / its event-timed
+  duration, against the measured HBM copy bandwidth.  ``roofline_hbm`` does the
+  same for the HBM-streaming hidden-layer Adam (fm_adam_kernel).
+* ``rebuild``: one forced table rebuild of every layer, timed, and its cost
+  amortised over the reference's rebuild schedule (maintenance.rs:70-82).
+* ``parity``: an untimed check, before timing, of a small network of the same
+  kind (sharded like the timed one) against the CPU oracle.
 * ``cpu_baseline``: the CPU restatement of the reference path (HOGWILD, all
   host threads) on a bounded sample of the same workload.
 * ``--impl reference``: that CPU path alone, as the reference arm.
 
 Multi-GPU (torchrun, one rank per GPU): ONE network, neuron-sharded over the
-ranks (kl_net_create_sharded): each rank owns 1/N of the 670K output neurons
-(rows, Adam state, LSH tables with bucket capacity 128/N) and contributes its
-own B=256 examples to a global batch of N*256 (weak scaling).  The hidden layer
-is replicated and data parallel; NCCL all-gathers the batches, hidden
-activations and hidden gradients, and all-reduces / reduce-scatters the loss
-probabilities and the output layer's input gradient.
+ranks (kl_net_create_sharded): each rank owns 1/N of the output neurons (rows,
+Adam state, LSH tables with bucket capacity cap/N) and contributes its own
+examples to the global batch.  The hidden layer is replicated and data
+parallel; NCCL all-gathers the batches, hidden activations and hidden
+gradients, and all-reduces / reduce-scatters the loss probabilities and the
+output layer's input gradient.
 """
 
 from __future__ import annotations
 
 import argparse
+import ctypes as C
 import json
+import math
 import os
 import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 from pathlib import Path
 
@@ -55,21 +67,70 @@ def parse():
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--batch", type=int, default=256)
+    p.add_argument("--config", default="c1", choices=["c1", "c0", "c2"])
+    p.add_argument("--batch", type=int, default=0, help="examples per GPU (0: the config's)")
     p.add_argument("--pool", type=int, default=8, help="distinct resident batches cycled through")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-parity", action="store_true")
+    p.add_argument("--no-exact", action="store_true")
     return p.parse_args()
 
 
-def workload(cfg, B):
-    lo = cfg.network.layers
-    return {"workload": "C1 extreme classification (synthetic Amazon-670K shape)",
-            "input_dim": lo[0].input_dim, "hidden": lo[0].num_neurons, "output": lo[1].num_neurons,
-            "hidden_lsh": "SimHash K6 L50 TopK12 FIFO128", "output_lsh": "DWTA K8 L50 FIFO128 (union<=6400)",
-            "per_gpu_batch": B, "weights": "bf16 storage, fp32 Adam state",
-            "l2": "working set > L2 (1.03 GB of output weights + Adam state in total)"}
+class Workload:
+    """One benchmark configuration: network, batch shape and input stream."""
+
+    def __init__(self, name: str, world: int, batch: int):
+        from klearu_b200 import synthetic as S
+
+        self.name = name
+        if name == "c1":
+            self.cfg = S.config_c1()
+            self.B = batch or 256
+            self.scaling = "weak"
+            self.dtype = "bf16"
+        elif name == "c0":
+            self.cfg = S.config_c0()
+            self.B = batch or 128
+            self.scaling = "weak"
+            self.dtype = "f32"
+        else:
+            self.cfg = S.config_c2()
+            # strong scaling: a fixed global batch of 1024 split over the ranks
+            self.B = batch or max(1, 1024 // world)
+            self.scaling = "strong"
+            self.dtype = "bf16"
+        lo = self.cfg.network.layers
+        self.d_in, self.d_h, self.n_out = lo[0].input_dim, lo[0].num_neurons, lo[1].num_neurons
+        self.out_L, self.out_cap = lo[1].lsh.num_tables, lo[1].lsh.bucket_capacity
+
+    def generator(self, seed: int):
+        from klearu_b200 import synthetic as S
+
+        if self.name == "c0":
+            rng = np.random.default_rng(seed)
+            return lambda B: S.dense_batch(rng, B, 784, 10)
+        g = S.XcGenerator(self.d_in, self.n_out, seed=seed)
+        return g.batch
+
+    def describe(self, world: int) -> dict:
+        lo = self.cfg.network.layers
+        names = {0: "SimHash", 1: "WTA", 2: "DWTA", 3: "MinHash", 4: "SRP"}
+
+        def lsh(l):
+            return (f"{names.get(int(l.lsh.hash_function), '?')} K{l.lsh.num_hashes} L{l.lsh.num_tables} "
+                    f"{'FIFO' if int(l.lsh.bucket_type) == 0 else 'reservoir'}{l.lsh.bucket_capacity} "
+                    f"TopK{l.top_k}")
+        title = {"c1": "C1 extreme classification (synthetic Amazon-670K shape)",
+                 "c0": "C0 README MLP (784-1024-10 softmax, dense U[0,1) inputs)",
+                 "c2": "C2 3.1M-way extreme classification (hidden 256, SimHash K9 L50 reservoir)"}[self.name]
+        return {"workload": title, "input_dim": self.d_in, "hidden": self.d_h, "output": self.n_out,
+                "hidden_lsh": lsh(lo[0]), "output_lsh": lsh(lo[1]), "per_gpu_batch": self.B,
+                "global_batch": self.B * world,
+                "weights": "bf16 storage, fp32 Adam state" if self.dtype == "bf16" else "f32",
+                "l2": "inputs larger than L2: output weights + Adam state exceed 126 MB" if self.name != "c0"
+                else "whole network L2-resident (11 MB of f32 weights + Adam state)"}
 
 
 def measured_peaks():
@@ -118,27 +179,26 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_baseline(cfg, init, gen_seed, seconds, threads, batch=64):
+def cpu_baseline(wl: Workload, seconds, threads, batch=64):
     """The reference CPU path (oracle restatement: per-example train_step,
     dense to_dense input, f32, HOGWILD over `threads`) on a bounded sample."""
     import oracle
     from klearu_b200 import synthetic as S
 
     t0 = time.time()
-    net = oracle.Net(cfg, init, weight_dtype="f32", sparse_input=False)
+    net = oracle.Net(wl.cfg, S.make_init(wl.cfg, 42), weight_dtype="f32", sparse_input=False)
     build_s = time.time() - t0
-    gen = S.XcGenerator(cfg.network.layers[0].input_dim, cfg.network.layers[-1].num_neurons, seed=gen_seed)
-    done, t = 0, 0.0
-    nb = 0
+    gen = wl.generator(4321)
+    done, t, nb = 0, 0.0, 0
     while t < seconds or nb == 0:
-        hb = gen.batch(batch)
+        hb = gen(batch)
         t1 = time.perf_counter()
         net.train_hogwild(hb, 1e-3, threads)
         t += time.perf_counter() - t1
         done += hb.batch
         nb += 1
     return {"value": done / t, "unit": "samples/s", "cores": threads, "kind": "port",
-            "sample": f"{done} C1 examples in {nb} HOGWILD train_parallel calls of {batch} "
+            "sample": f"{done} {wl.name.upper()} examples in {nb} HOGWILD train_parallel calls of {batch} "
                       f"(f32, dense inputs as the reference), {t:.1f} s timed; network build {build_s:.1f} s"}
 
 
@@ -146,35 +206,103 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    import oracle
     from klearu_b200 import synthetic as S
 
-    cfg = S.config_c1()
-    init = S.make_init(cfg, 42)
+    wl = Workload(args.config, args.gpus, args.batch)
     threads = os.cpu_count() or 1
-    import oracle
-
-    net = oracle.Net(cfg, init, weight_dtype="f32", sparse_input=False)
-    gen = S.XcGenerator(135909, 670091, seed=1234)
+    net = oracle.Net(wl.cfg, S.make_init(wl.cfg, 42), weight_dtype="f32", sparse_input=False)
+    gen = wl.generator(1234)
     per_step = max(threads, 32)  # bounded sample per step
     for _ in range(args.warmup):
-        net.train_hogwild(gen.batch(per_step), 1e-3, threads)
+        net.train_hogwild(gen(per_step), 1e-3, threads)
     t = 0.0
     for _ in range(args.steps):
-        hb = gen.batch(per_step)
+        hb = gen(per_step)
         t0 = time.perf_counter()
         net.train_hogwild(hb, 1e-3, threads)
         t += time.perf_counter() - t0
     v = args.steps * per_step / t
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "samples/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload(cfg, per_step),
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {**wl.describe(1), "per_gpu_batch": per_step, "global_batch": per_step},
             "cpu_baseline": {"value": v, "unit": "samples/s", "cores": threads, "kind": "port",
                              "sample": f"{args.steps} steps of {per_step} examples (HOGWILD train_parallel, "
                                        f"f32, dense inputs), CPU restatement of klearu-core (Rust reference "
                                        f"not buildable here)"},
             "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def parity_check(rank: int, world: int, local: int) -> dict:
+    """Untimed checker run before timing: a small network of the timed kind
+    (neuron-sharded over the same ranks when world > 1) trained for two batched
+    steps and compared with the CPU oracle (the oracle's sharded mode with the
+    same number of shards).  Bar: losses within 1e-4 relative; every layer's
+    weights (one bf16 ulp), bias and Adam state within 1e-3 relative."""
+    import torch.distributed as dist
+
+    from klearu_b200 import synthetic as S
+    from klearu_b200.config import LshConfig
+    from klearu_b200.core import Network, default_context
+    from klearu_b200.dist import rank_slice, share_unique_id
+
+    cfg = S.config_xc(d_in=2000, hidden=64, n_out=5000, out_l=10, cap=32,
+                      hidden_lsh=LshConfig(num_tables=10, num_hashes=6), rebuild_base=2, rebuild_decay=0.1)
+    init = S.make_init(cfg, 42)
+    B = 24
+    shard = (share_unique_id(rank, world), rank, world) if world > 1 else None
+    net = Network(cfg, init, weight_dtype="bf16", max_batch=B, shard=shard, ctx=default_context(local))
+    gen = S.XcGenerator(2000, 5000, seed=3, mean_nnz=20)
+    batches = [gen.batch(B * world) for _ in range(3)]
+    losses = [net.train_step_host(rank_slice(hb, rank, world) if world > 1 else hb, 1e-3) for hb in batches]
+    base, n = (net.shard_info()[2:] if world > 1 else (0, 5000))
+    res = {"losses": losses, "hidden": net.get_layer(0), "out": net.get_layer(1), "base": base, "n": n}
+    del net
+    gathered = [None] * world
+    if world > 1:
+        dist.all_gather_object(gathered, res)
+    else:
+        gathered = [res]
+    if rank != 0:
+        return {}
+    import oracle
+
+    o = oracle.Net(cfg, init, weight_dtype="bf16", nshards=world)
+    ol = [o.train_step(hb, 1e-3, mode="batched") for hb in batches]
+    oh, oo = o.get_layer(0), o.get_layer(1)
+    bad = 0
+    for g in gathered:
+        bad += sum(abs(a - b) > 1e-4 * abs(b) + 1e-6 for a, b in zip(g["losses"], ol))
+        lo, hi = g["base"], g["base"] + g["n"]
+        for k in ("weights", "bias", "m", "v", "mb", "vb"):
+            for a, b in ((g["hidden"][k], oh[k]), (g["out"][k], oo[k][lo:hi])):
+                if k == "weights":
+                    tol = np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -7 + 1e-6
+                else:
+                    tol = 1e-3 * np.abs(b) + 1e-6
+                bad += int((np.abs(a - b) > tol).sum())
+    return {"ok": bad == 0, "mismatches": bad, "ranks": world, "steps": len(batches),
+            "check": "2000-64-5000 net (DWTA K8 L10 cap 32, bf16), 3 batched steps of 24 examples per rank, "
+                     f"vs the CPU oracle with {world} shard(s): losses, weights, bias, Adam state"}
+
+
+def rebuild_schedule_cost(ms_rebuild: float, ms_step: float, base: int = 100, decay: float = 0.1,
+                          horizon: int = 10000) -> dict:
+    """Rebuilds in the first `horizon` steps under RebuildScheduler
+    (maintenance.rs:70-82: next = step + max(1, floor(base * e^(decay*count)))),
+    and the per-step share of their cost."""
+    step, nxt, count = 0, base, 0
+    while True:
+        step = nxt
+        if step > horizon:
+            break
+        count += 1
+        nxt = step + max(1, math.floor(base * math.exp(decay * count)))
+    per_step = ms_rebuild * count / horizon
+    return {"rebuilds_in_first_steps": count, "horizon_steps": horizon, "ms_per_step_amortised": per_step,
+            "ms_per_step_with_rebuild": ms_step + per_step}
 
 
 def main():
@@ -195,25 +323,28 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    B = args.batch
-    cfg = S.config_c1()
-    init = S.make_init(cfg, 42)
+    lib = _lib.load()
+    wl = Workload(args.config, world, args.batch)
+    B = wl.B
+
+    parity = None if args.no_parity else parity_check(rank, world, local)
+
+    init = S.make_init(wl.cfg, 42) if wl.name != "c2" else None  # c2: the library's seeded init (3.1M rows)
     shard = None
     if world > 1:
         from klearu_b200.dist import share_unique_id
 
         shard = (share_unique_id(rank, world), rank, world)
-    net = Network(cfg, init, weight_dtype="bf16", max_batch=B, shard=shard, ctx=default_context(local))
+    net = Network(wl.cfg, init, weight_dtype=wl.dtype, max_batch=B, shard=shard, ctx=default_context(local))
     del init
-    gen = S.XcGenerator(135909, 670091, seed=1234 + rank)
-    pool_host = [gen.batch(B) for _ in range(args.pool)]
+    gen = wl.generator(1234 + rank)
+    pool_host = [gen(B) for _ in range(args.pool)]
     pool = [net.device_batch(hb) for hb in pool_host]
-    # size the per-batch buffers for every pooled batch (forward only, no update) so that no
-    # allocation happens inside the timed region
-    from klearu_b200 import _lib as _L
-    import ctypes as _C
-    for db in (sorted(pool, key=lambda db: -db.c.nnz)[:1] if world == 1 else []):  # sharded nets pre-size
-        _L.check(net.lib.kl_net_forward(net.h, _C.byref(db.c)), net.ctx.h)
+    if world == 1:
+        # size the per-batch buffers for every pooled batch (forward only, no update) so that no
+        # allocation happens inside the timed region; sharded nets are sized at creation
+        db = max(pool, key=lambda db: db.c.nnz)
+        _lib.check(net.lib.kl_net_forward(net.h, C.byref(db.c)), net.ctx.h)
     torch.cuda.synchronize()
 
     def barrier():
@@ -228,9 +359,6 @@ def main():
     torch.cuda.synchronize()
     for l in range(2):
         net.stats(l, reset=True)
-    lib = _lib.load()
-    import ctypes as C
-
     lc0 = C.c_uint64()
     lib.kl_launch_count(C.byref(lc0))
     uuid = None
@@ -256,6 +384,7 @@ def main():
     lc1 = C.c_uint64()
     lib.kl_launch_count(C.byref(lc1))
     stats = [net.stats(l) for l in range(2)]
+    steps_done = max(1, int(stats[1].steps))
     # Phase times come from a separate, untimed pass with the library's event profiler on (the
     # timed loop above replays the captured step graph, which carries no per-phase events).
     KP = min(args.steps, 20)
@@ -271,39 +400,78 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
+    ms_step = ms_max / args.steps
     value = world * B * args.steps / (ms_max / 1e3)
 
     # ---- roofline (per-step algorithmic bytes from the device counters)
-    K = args.steps
-    d_in, d_h, d_o = 135909, 128, 670091
-    A = stats[1].active_sum / K              # sum of output active set sizes per step
+    K = steps_done
+    d_in, d_h = wl.d_in, wl.d_h
+    A = stats[1].active_sum / K              # sum of output active-set sizes per step
     U_o = stats[1].touched_rows / K          # output rows updated per step
     U_h = stats[0].touched_rows / K          # hidden neurons updated per step
     nnz = stats[0].input_nnz / K
-    A_h = stats[0].active_sum / K
-    # The roofline kernel: layer 0's streaming Adam pass (fm_adam_kernel), the step's HBM-bound
-    # kernel: W (bf16), m, v (f32) of all 135909 feature rows x U_h touched neurons, read and
-    # written = 20 B per element.  Timed alone by the library's KL_PHASE_STREAM events.  The
-    # output-layer kernels take more time but read rows resident in L2 (issue-bound, see
-    # phase_ms_per_step and profiles/).
-    bytes_dom = 20.0 * d_in * U_h
-    ms_dom = prof[0]["stream"][0] * K / KP  # per-step time of the profiled pass, scaled to K steps
     peak, peak_kind = measured_peaks()
-    achieved = bytes_dom / (ms_dom / K / 1e3) / 1e9 if ms_dom > 0 else 0.0  # one launch per step
-    step_bytes_formula = (2 * d_h * A) * 2 + 20 * d_h * U_o + 16 * U_o + 4 * 50 * 128 * B + 2 * d_h * nnz + \
-        20 * d_in * U_h + nnz * 8
-    roofline = {"bound": "hbm", "kernel": "fm_adam_kernel (hidden-layer Adam over all 135909 feature rows)",
-                "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                # dram__bytes_read.sum + dram__bytes_write.sum of one launch, ncu --set full, C1
-                # (profiles/slide_step_c1_kernels_ncu.md): part of W/m/v is served from L2
-                "traffic": 295.8e6,
-                "bytes_per_launch": bytes_dom / 1.0, "ms_per_launch": ms_dom / K,
-                "step_bytes_formula": step_bytes_formula,
-                "step_frac_of_peak": step_bytes_formula / (ms_max / K / 1e3) / 1e9 / peak,
-                "phase_ms_per_step": {f"{l}.{p}": prof[i][p][0] / KP for i, l in enumerate(("hidden", "output"))
-                                      for p in _lib.PHASES},
-                "per_step": {"active_out": A, "touched_out": U_o, "touched_hidden": U_h, "nnz": nnz,
-                             "rebuilds": int(stats[1].rebuilds)}}
+    wbytes = 2 if wl.dtype == "bf16" else 4
+    phase = {f"{ln}.{p}": prof[i][p][0] / KP for i, ln in enumerate(("hidden", "output")) for p in _lib.PHASES}
+    # Dominant kernel: the output layer's fused active-row kernel (rm_forward_kernel: forward,
+    # loss gradient and input-gradient partials from one staged gather of each active row).
+    # Algorithmic bytes per launch: every active (example, row) pair's weight row once plus its id.
+    ms_fwd = phase["output.forward"]
+    bytes_fwd = wbytes * d_h * A + 4 * A
+    ach_fwd = bytes_fwd / (ms_fwd / 1e3) / 1e9 if ms_fwd > 0 else 0.0
+    roofline = {"bound": "hbm", "kernel": "rm_forward_kernel (output layer: active-row forward + loss gradient + "
+                                          "input-gradient partials, one launch per step)",
+                "limiter": "instruction issue; the active rows are mostly L2-resident on this workload, so the "
+                           "HBM fraction is an algorithmic-bytes rate, not DRAM traffic",
+                "achieved": ach_fwd, "peak": peak, "unit": "GB/s", "frac": ach_fwd / peak,
+                "peak_kind": f"{peak_kind} (HBM copy bandwidth)",
+                "traffic": None, "traffic_note": "DRAM bytes per launch come from ncu, not this run; see the "
+                                                 "kernel summaries under profiles/",
+                "bytes_per_launch": bytes_fwd, "ms_per_launch": ms_fwd,
+                "bytes_formula": f"{wbytes}*d_h*sum(A_s) + 4*sum(A_s), sum(A_s)={A:.0f} per step"}
+    # HBM-streaming kernel: layer 0's Adam over all feature rows x touched hidden neurons
+    # (W bf16, m, v f32, read and written = 20 B per element in bf16 storage).
+    ms_adam = prof[0]["stream"][0] / KP
+    bytes_adam = (2 * wbytes + 16) * d_in * U_h
+    ach_adam = bytes_adam / (ms_adam / 1e3) / 1e9 if ms_adam > 0 else 0.0
+    roofline_hbm = {"bound": "hbm", "kernel": "fm_adam_kernel (hidden-layer Adam over all feature rows of the "
+                                              "touched hidden neurons)",
+                    "achieved": ach_adam, "peak": peak, "unit": "GB/s", "frac": ach_adam / peak,
+                    "bytes_per_launch": bytes_adam, "ms_per_launch": ms_adam}
+    step_bytes = (2 * wbytes * d_h * A + (4 * wbytes + 16) * d_h * U_o + 16 * U_o + 4 * wl.out_L * wl.out_cap * B * world
+                  + wbytes * d_h * nnz + (2 * wbytes + 16) * d_in * U_h + 8 * nnz)
+    step_frac = {"formula_bytes_per_step": step_bytes,
+                 "frac_of_peak": step_bytes / (ms_step / 1e3) / 1e9 / peak,
+                 "note": "algorithmic bytes of every term of the step (forward and dX gathers counted "
+                         "separately) / step time / HBM peak; most output-row gathers are served from L2"}
+
+    # ---- a forced table rebuild of every layer, and its amortised cost
+    torch.cuda.synchronize()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(st)
+    net.rebuild()
+    r1.record(st)
+    torch.cuda.synchronize()
+    ms_rb = r0.elapsed_time(r1)
+    lo0 = wl.cfg.network.layers[0].lsh
+    rebuild = {"ms": ms_rb, **rebuild_schedule_cost(ms_rb, ms_step, lo0.rebuild_interval_base, lo0.rebuild_decay)}
+    value_with_rebuild = world * B / (rebuild["ms_per_step_with_rebuild"] / 1e3)
+
+    # ---- exact (per-example, the reference's own semantics) mode, a few steps
+    exact = None
+    if not args.no_exact and world == 1:
+        ex0, ex1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        nex = 2
+        net.train_step_device(pool[0], 1e-3, mode=_lib.MODE_EXACT_SEQUENTIAL)
+        torch.cuda.synchronize()
+        ex0.record(st)
+        for i in range(nex):
+            net.train_step_device(pool[(i + 1) % len(pool)], 1e-3, mode=_lib.MODE_EXACT_SEQUENTIAL)
+        ex1.record(st)
+        torch.cuda.synchronize()
+        exact = {"value": B * nex / (ex0.elapsed_time(ex1) / 1e3), "unit": "samples/s", "steps": nex,
+                 "mode": "KL_MODE_EXACT_SEQUENTIAL: one example at a time, weights updated after each "
+                         "(Network::train_step semantics)"}
 
     # ---- end to end through the C ABI with host buffers
     e2e = None
@@ -347,16 +515,27 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(cfg, S.make_init(cfg, 42), 4321, args.cpu_seconds, os.cpu_count() or 1)
+        if wl.name == "c2":
+            cpu = {"value": None, "unit": "samples/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": "not run: building the CPU network (3.1M rows hashed into 50 SimHash tables) takes "
+                             "longer than the bench's bound"}
+        else:
+            cpu = cpu_baseline(wl, args.cpu_seconds, os.cpu_count() or 1)
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {**workload(cfg, B), "global_batch": B * world,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+                "config": {**wl.describe(world),
                            "parallelism": f"output neurons sharded over {world} GPUs, hidden layer data parallel"
                            if world > 1 else "single"},
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "roofline": roofline, "roofline_hbm": roofline_hbm, "step_bytes": step_frac,
+                "phase_ms_per_step": phase,
+                "per_step": {"active_out": A, "touched_out": U_o, "touched_hidden": U_h, "nnz": nnz,
+                             "rebuilds_in_timed_steps": int(stats[1].rebuilds)},
+                "rebuild": rebuild, "value_with_rebuild": value_with_rebuild,
+                "exact_mode": exact, "parity": parity,
+                "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": int(lc1.value - lc0.value), "clocks": clk}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define KLEARU_GPU_ABI_VERSION 1
+#define KLEARU_GPU_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define KL_API __attribute__((visibility("default")))
@@ -104,6 +104,8 @@ typedef struct kl_ctx_s* kl_ctx_t;
 typedef struct kl_hash_s* kl_hash_t;
 typedef struct kl_index_s* kl_index_t;
 typedef struct kl_net_s* kl_net_t;
+typedef struct kl_dataset_s* kl_dataset_t;
+typedef struct kl_batch_iter_s* kl_batch_iter_t;
 
 /* ------------------------------------------------------------------------ */
 /* Context                                                                  */
@@ -119,6 +121,9 @@ KL_API kl_status kl_ctx_set_stream(kl_ctx_t ctx, void* stream);
 KL_API kl_status kl_ctx_sync(kl_ctx_t ctx);
 /* Synchronise and report (then clear) the device-side error word. */
 KL_API kl_status kl_ctx_check(kl_ctx_t ctx);
+/* Message of the context's last failed call.  With ctx NULL: the message of
+ * the last failed call made on this host thread (the dataset calls below take
+ * no context). */
 KL_API const char* kl_last_error(kl_ctx_t ctx);
 KL_API int kl_abi_version(void);
 
@@ -312,6 +317,11 @@ typedef struct {
   uint64_t seed;
   int32_t weight_dtype;          /* kl_dtype */
   int32_t max_batch;             /* capacity of per-step buffers (examples per call) */
+  /* Largest sample-major gradient matrix (bytes) the output-layer update may
+   * use (the dense-collision path); a layer whose matrix would be larger takes
+   * the segmented path.  0 = 2 GiB; < 0 = always the segmented path.  No
+   * reference counterpart (a memory/speed choice of this engine). */
+  int64_t dense_update_max_bytes;
 } kl_net_config;
 
 /* Explicit initial parameters of one layer (host memory).  weights/bias are
@@ -426,6 +436,9 @@ KL_API kl_status kl_net_profile_read(kl_net_t net, int layer, double* ms_host, u
                                      int reset);
 /* Kernels launched by this library in this process so far. */
 KL_API kl_status kl_launch_count(uint64_t* count_host);
+/* Device (cudaMalloc) and pinned host (cudaHostAlloc) allocations made by this
+ * library in this process so far.  No reference counterpart (diagnostic). */
+KL_API kl_status kl_alloc_count(uint64_t* count_host);
 
 /* ------------------------------------------------------------------------ */
 /* Neuron sharding of the output layer over NCCL (no reference counterpart: */
@@ -509,6 +522,53 @@ KL_API kl_status kl_sparse_mlp_destroy(kl_sparse_mlp_t m);
  * out [n_tokens][hidden]; all device. */
 KL_API kl_status kl_sparse_mlp_forward(kl_sparse_mlp_t m, const float* x, int n_tokens, const uint32_t* sel, int k,
                                        float* out);
+
+/* ------------------------------------------------------------------------ */
+/* Datasets: LibSVM / XML files and shuffled CSR batches (host memory).      */
+/* These calls take no context; on failure kl_last_error(NULL) returns the   */
+/* message (parse errors name the 1-based line, as the reference does).      */
+/* ------------------------------------------------------------------------ */
+/* LibSvmDataset::load (crates/klearu-core/src/data/libsvm.rs:31-36): parse a
+ * file of "l1,l2,... idx:val idx:val ..." lines on `threads` host threads
+ * (<= 0: all).  1-based indices are detected over the whole file (minimum
+ * index 1, no index 0) and shifted; indices >= feature_dim are clamped to
+ * feature_dim - 1; each row is sorted by index with duplicates summed
+ * (SparseVector::from_pairs, tensor/sparse.rs:36-57).  KL_EINVAL on a
+ * malformed line, with the reference's messages (libsvm.rs:127-185). */
+KL_API kl_status kl_libsvm_load(const char* path, int64_t feature_dim, int64_t num_labels, int threads,
+                                kl_dataset_t* out);
+/* LibSvmDataset::load_from_reader (libsvm.rs:39-111) over an in-memory text. */
+KL_API kl_status kl_libsvm_parse(const char* text_host, size_t len, int64_t feature_dim, int64_t num_labels,
+                                 int threads, kl_dataset_t* out);
+/* LibSvmDataset::from_examples (libsvm.rs:114-124): a dataset over CSR arrays
+ * (rows already sorted and unique), copied. */
+KL_API kl_status kl_dataset_from_csr(const int64_t* rowptr_host, const uint32_t* idx_host, const float* val_host,
+                                     const int64_t* label_ptr_host, const uint32_t* labels_host, int64_t n,
+                                     int64_t feature_dim, int64_t num_labels, kl_dataset_t* out);
+KL_API kl_status kl_dataset_destroy(kl_dataset_t ds);
+/* Dataset::len / feature_dim / num_labels (data/dataset.rs:19-35), plus the
+ * total feature and label counts. */
+KL_API kl_status kl_dataset_info(kl_dataset_t ds, int64_t* len_host, int64_t* feature_dim_host,
+                                 int64_t* num_labels_host, int64_t* nnz_host, int64_t* nlabels_host);
+/* Dataset::get (dataset.rs:29) for every example at once: the store's CSR
+ * arrays (rowptr / label_ptr [len+1]), valid while the dataset lives. */
+KL_API kl_status kl_dataset_csr(kl_dataset_t ds, const int64_t** rowptr, const uint32_t** idx, const float** val,
+                                const int64_t** label_ptr, const uint32_t** labels);
+/* BatchIterator::new (dataset.rs:48-56): the example order is the SplitMix64
+ * Fisher-Yates shuffle of the reference (dataset.rs:60-87) for `seed`.  With
+ * `prefetch` a worker thread assembles the next batch while the caller trains
+ * on the current one.  The dataset must outlive the iterator. */
+KL_API kl_status kl_batch_iter_create(kl_dataset_t ds, int batch_size, uint64_t seed, int prefetch,
+                                      kl_batch_iter_t* out);
+/* BatchIterator::reset (dataset.rs:58-68): reshuffle from the identity order. */
+KL_API kl_status kl_batch_iter_reset(kl_batch_iter_t it, uint64_t seed);
+/* Iterator::next (dataset.rs:94-111): the next batch_size examples in
+ * shuffled order (the last batch short) as a kl_batch of HOST arrays in
+ * page-locked memory, ready for kl_net_train_step_host; nnz / nlabels are
+ * filled.  The arrays stay valid until the next call on the iterator.  At the
+ * end of the epoch it returns KL_OK with batch_host->batch == 0. */
+KL_API kl_status kl_batch_iter_next(kl_batch_iter_t it, kl_batch* batch_host);
+KL_API kl_status kl_batch_iter_destroy(kl_batch_iter_t it);
 
 #ifdef __cplusplus
 }

@@ -49,7 +49,8 @@ class LayerConfigC(C.Structure):
 class NetConfigC(C.Structure):
     _fields_ = [("num_layers", C.c_int32), ("layers", C.POINTER(LayerConfigC)), ("optimizer", C.c_int32),
                 ("learning_rate", C.c_double), ("batch_size", C.c_int32), ("num_threads", C.c_int32),
-                ("seed", C.c_uint64), ("weight_dtype", C.c_int32), ("max_batch", C.c_int32)]
+                ("seed", C.c_uint64), ("weight_dtype", C.c_int32), ("max_batch", C.c_int32),
+                ("dense_update_max_bytes", C.c_int64)]
 
 
 class LayerInitC(C.Structure):
@@ -117,6 +118,7 @@ _PROTOS = {
     "kl_net_profile": (_S, [_H, C.c_int]),
     "kl_net_profile_read": (_S, [_H, C.c_int, _P, _P, C.c_int]),
     "kl_launch_count": (_S, [C.POINTER(C.c_uint64)]),
+    "kl_alloc_count": (_S, [C.POINTER(C.c_uint64)]),
     "kl_dist_unique_id_size": (C.c_int, []),
     "kl_dist_get_unique_id": (_S, [_P]),
     "kl_net_create_sharded": (_S, [_H, C.POINTER(NetConfigC), _P, _P, C.c_int, C.c_int, C.POINTER(_H)]),
@@ -135,6 +137,16 @@ _PROTOS = {
     "kl_adaptive_should_rebuild": (_S, [_H, _P, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)]),
     "kl_adaptive_notify_rebuild": (_S, [_H]),
     "kl_adaptive_state": (_S, [_H, _P, _P, _P]),
+    "kl_libsvm_load": (_S, [C.c_char_p, C.c_int64, C.c_int64, C.c_int, C.POINTER(_H)]),
+    "kl_libsvm_parse": (_S, [C.c_char_p, C.c_size_t, C.c_int64, C.c_int64, C.c_int, C.POINTER(_H)]),
+    "kl_dataset_from_csr": (_S, [_P, _P, _P, _P, _P, C.c_int64, C.c_int64, C.c_int64, C.POINTER(_H)]),
+    "kl_dataset_destroy": (_S, [_H]),
+    "kl_dataset_info": (_S, [_H, _P, _P, _P, _P, _P]),
+    "kl_dataset_csr": (_S, [_H, _P, _P, _P, _P, _P]),
+    "kl_batch_iter_create": (_S, [_H, C.c_int, C.c_uint64, C.c_int, C.POINTER(_H)]),
+    "kl_batch_iter_reset": (_S, [_H, C.c_uint64]),
+    "kl_batch_iter_next": (_S, [_H, C.POINTER(BatchC)]),
+    "kl_batch_iter_destroy": (_S, [_H]),
 }
 
 _lib = None

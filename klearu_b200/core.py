@@ -442,16 +442,20 @@ class Network:
     """
 
     def __init__(self, config: SlideConfig, init=None, weight_dtype: str = "f32", max_batch: int = 256,
-                 ctx: Context | None = None, shard: tuple[bytes, int, int] | None = None):
+                 ctx: Context | None = None, shard: tuple[bytes, int, int] | None = None,
+                 dense_update_max_bytes: int = 0):
         """``shard=(unique_id, rank, nranks)`` builds this rank's part of a
         neuron-sharded network (kl_net_create_sharded); ``unique_id`` comes from
-        klearu_b200.dist.share_unique_id."""
+        klearu_b200.dist.share_unique_id.  ``dense_update_max_bytes`` bounds the
+        output update's gradient matrix (0: 2 GiB; negative: always the
+        segmented update)."""
         self.ctx = ctx or default_context()
         self.lib = self.ctx.lib
         self.config = config
         self.max_batch = max_batch
         self.weight_dtype = _lib.DTYPE_BF16 if weight_dtype == "bf16" else _lib.DTYPE_F32
         cfg, keep_cfg = config.to_c(self.weight_dtype, max_batch)
+        cfg.dense_update_max_bytes = int(dense_update_max_bytes)
         keep = [keep_cfg]
         init_arr = None
         if init is not None:
@@ -549,6 +553,35 @@ class Network:
         check(self.lib.kl_net_train_step_host(self.h, C.byref(c), float(lr), mode, loss_out.data_ptr()),
               self.ctx.h, "kl_net_train_step_host")
         return None
+
+    def train_step_batch_host(self, b, lr: float, mode=_lib.MODE_BATCHED, loss_out=None) -> float | None:
+        """kl_net_train_step_host on a kl_batch of host arrays (for example one
+        drawn from data.BatchIterator); same waiting rules as train_step_host."""
+        if loss_out is None:
+            out = torch.zeros(1, dtype=torch.float32).pin_memory()
+            check(self.lib.kl_net_train_step_host(self.h, C.byref(b), float(lr), mode, out.data_ptr()),
+                  self.ctx.h, "kl_net_train_step_host")
+            self.ctx.sync()
+            return float(out[0])
+        check(self.lib.kl_net_train_step_host(self.h, C.byref(b), float(lr), mode, loss_out.data_ptr()),
+              self.ctx.h, "kl_net_train_step_host")
+        return None
+
+    def train_epoch(self, it, lr: float, mode=_lib.MODE_BATCHED) -> list[float]:
+        """One pass over a data.BatchIterator: each batch goes to
+        kl_net_train_step_host without waiting (the iterator's worker assembles
+        the next batch and the library uploads it while this one trains); the
+        per-batch losses are read after the last step."""
+        n = 0
+        outs = []
+        for b in it:
+            if n == len(outs):
+                outs.append(torch.zeros(1, dtype=torch.float32).pin_memory())
+            self.train_step_batch_host(b, lr, mode, loss_out=outs[n])
+            # the iterator reuses its buffers two draws later; the library copied them at the call
+            n += 1
+        self.ctx.sync()
+        return [float(o[0]) for o in outs[:n]]
 
     # -- inference --------------------------------------------------------
     def forward_batch(self, examples) -> list[list[LayerOutput]]:

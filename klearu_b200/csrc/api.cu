@@ -29,6 +29,8 @@ using namespace kl;
 namespace kl {
 static std::atomic<unsigned long long> g_launches{0};
 void count_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+// Process-wide count of device and pinned-host allocations made by this library.
+static std::atomic<unsigned long long> g_allocs{0};
 }  // namespace kl
 
 // ---------------------------------------------------------------------------
@@ -72,6 +74,7 @@ struct DBuf {
     bytes = 0;
     if (n == 0) n = 16;
     ck(cudaMalloc(&p, n), "cudaMalloc");
+    g_allocs.fetch_add(1, std::memory_order_relaxed);
     bytes = n;
   }
   template <class T>
@@ -473,8 +476,11 @@ DenseIn dense_rows(const void* rows, int dtype, int n, int ld) {
   return in;
 }
 
+thread_local std::string g_thread_error;
+
 kl_status finish(kl_ctx_t ctx, const KlError& e) {
   if (ctx) ctx->last_error = e.msg;
+  g_thread_error = e.msg;
   return e.st;
 }
 
@@ -563,8 +569,11 @@ extern "C" kl_status kl_ctx_sync(kl_ctx_t ctx) {
 }
 extern "C" kl_status kl_ctx_check(kl_ctx_t ctx) { return kl_ctx_sync(ctx); }
 extern "C" const char* kl_last_error(kl_ctx_t ctx) {
-  return ctx ? ctx->last_error.c_str() : "null context";
+  return ctx ? ctx->last_error.c_str() : g_thread_error.c_str();
 }
+namespace kl {
+void set_thread_error(const std::string& m) { g_thread_error = m; }
+}  // namespace kl
 
 // ===========================================================================
 // Hash
@@ -1422,19 +1431,25 @@ struct kl_net_s {
   // The replicated hidden layer then applies the same update on every rank.
   void train_sharded(const kl_batch& lb, double lr) {
     cudaStream_t st = ctx->stream;
-    const int P = nranks, B = lb.batch, PB = P * B;
-    if (lb.nnz > nnz_cap || lb.nlabels > lab_cap)
-      raise(KL_ECAPACITY, "sharded train_step: batch exceeds the exchange capacity (" +
-                              std::to_string(KL_SHARD_NNZ_PER_EXAMPLE_H) + " nnz and " +
-                              std::to_string(KL_SHARD_LABELS_PER_EXAMPLE_H) + " labels per example)");
+    // Every collective below is sized by the configured per-rank batch, never by this
+    // rank's data, so that no rank can leave the collective sequence on its own.  A
+    // batch that cannot be exchanged (another example count, or more nnz / labels than
+    // the fixed exchange capacity) is sent as an empty batch with a fault word: every
+    // rank then raises the fault at its next synchronising call and applies the step
+    // with a zero learning rate.
+    const int P = nranks, B = rank_batch, PB = P * B;
+    uint32_t fault = 0;
+    if (lb.batch != B) fault = DERR_BOUNDS;
+    else if (lb.nnz > nnz_cap || lb.nlabels > lab_cap) fault = DERR_CAPACITY;
     Layer& H = *layers[0];
     Layer& O = *layers[1];
     // (1) the global batch
-    launch_shard_pack(dsend.as<uint32_t>(), shl, lb, st);
+    launch_shard_pack(dsend.as<uint32_t>(), shl, lb, B, fault, st);
     ck_launch("shard pack");
     nccl_ck(ncclAllGather(dsend.p, drecv.p, (size_t)shl.words, ncclUint32, comm, st), "all-gather batches");
     launch_shard_unpack(drecv.as<uint32_t>(), shl, P, B, g_rowptr.as<int32_t>(), g_idx.as<uint32_t>(),
-                        g_val.as<float>(), g_lptr.as<int32_t>(), g_labels.as<uint32_t>(), ctx->err.as<int>(), st);
+                        g_val.as<float>(), g_lptr.as<int32_t>(), g_labels.as<uint32_t>(), ctx->err.as<int>(),
+                        dopt.as<OptStep>(), st);
     ck_launch("shard unpack");
     kl_batch gb{};
     gb.batch = PB;
@@ -1754,7 +1769,7 @@ void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_
     // dense-collision update scratch when its gradient matrix fits the budget
     const int64_t drows = std::min<int64_t>((int64_t)L.N, (int64_t)B * L.stride);
     const int64_t ldu = round_up(drows + 16, 32);  // update tiles read whole 32-slot groups below ldu
-    if (rm_dense_fits(ldu, std::max(B, 1))) {
+    if (rm_dense_fits(ldu, std::max(B, 1), net->cfg.dense_update_max_bytes)) {
       L.dldu = ldu;
       const size_t nwords = (size_t)ceil_div(L.N, 32);
       L.dbits.alloc(nwords * 4);
@@ -1905,9 +1920,29 @@ extern "C" kl_status kl_net_destroy(kl_net_t net) {
 // The body of Network::train_step (net.rs:81-119) on a validated device
 // batch; the mean loss ends in net->loss_acc (and `loss` when non-null).
 static void train_step_body(kl_net_t net, const kl_batch* b, double lr, int mode, float* loss) {
-  validate_batch(net, b);
   require(mode == KL_MODE_EXACT_SEQUENTIAL || mode == KL_MODE_BATCHED, "train_step: unknown mode");
   cudaStream_t st = net->ctx->stream;
+  if (net->nranks > 1) {
+    // A sharded step never returns before its collectives on a data-dependent
+    // condition (batch size, nnz, labels): train_sharded reports those faults on
+    // every rank together.  Only argument errors, which every rank makes alike
+    // when it calls with the same code, raise here.
+    require(b != nullptr, "batch is NULL");
+    support(mode == KL_MODE_BATCHED, "sharded net: only KL_MODE_BATCHED train steps");
+    net->upload_opt(lr);
+    net->train_sharded(*b, lr);
+    launch_loss_final(net->loss_acc.as<float>(), net->rank_batch * net->nranks, loss, net->loss_acc.as<float>(), st);
+    ck_launch("loss final");
+    for (auto& L : net->layers) {
+      L->examples += (uint64_t)b->batch;
+      L->steps += 1;
+    }
+    net->layers[0]->input_nnz += (uint64_t)b->nnz;
+    net->step += 1;
+    if (net->sched.should_rebuild(net->step)) net->rebuild_all();
+    return;
+  }
+  validate_batch(net, b);
   if (b->batch == 0) {  // net.rs:82-84
     ck(cudaMemsetAsync(net->loss_acc.p, 0, 4, st), "memset");
     if (loss) ck(cudaMemsetAsync(loss, 0, 4, st), "memset");
@@ -1915,12 +1950,7 @@ static void train_step_body(kl_net_t net, const kl_batch* b, double lr, int mode
   }
   int loss_div = b->batch;
   net->upload_opt(lr);
-  if (net->nranks > 1) {
-    support(mode == KL_MODE_BATCHED, "sharded net: only KL_MODE_BATCHED train steps");
-    require(b->batch <= net->rank_batch, "sharded train_step: batch exceeds max_batch");
-    net->train_sharded(*b, lr);
-    loss_div = b->batch * net->nranks;
-  } else if (mode == KL_MODE_BATCHED && net->graph_usable(*b)) {
+  if (mode == KL_MODE_BATCHED && net->graph_usable(*b)) {
     net->graph_step(*b, loss);
     loss_div = -1;  // the captured body wrote the loss
   } else {
@@ -1975,6 +2005,14 @@ extern "C" kl_status kl_net_train_step_host(kl_net_t net, const kl_batch* hb, do
   if (!net) return KL_EINVAL;
   KL_API_BEGIN(net->ctx)
   require(hb != nullptr, "batch is NULL");
+  if (net->nranks > 1 && (hb->batch < 0 || hb->batch > net->rank_batch)) {
+    // a sharded step reports a wrong batch size on every rank together (train_sharded)
+    kl_batch bad{};
+    bad.batch = hb->batch;
+    train_step_body(net, &bad, lr, mode, nullptr);
+    if (loss_host) ck(cudaMemcpyAsync(loss_host, net->loss_acc.p, 4, cudaMemcpyDeviceToHost, ctx__->stream), "loss copy");
+    return KL_OK;
+  }
   require(hb->batch >= 0 && hb->batch <= net->max_batch, "batch size outside [0, max_batch]");
   const int B = hb->batch;
   if (B > 0) require(hb->rowptr && hb->label_ptr, "batch rowptr / label_ptr required");
@@ -2006,6 +2044,7 @@ extern "C" kl_status kl_net_train_step_host(kl_net_t net, const kl_batch* hb, do
     h.cap = 0;
     const size_t cap = a16(total + total / 2);
     ck(cudaHostAlloc(&h.pinned, cap, cudaHostAllocDefault), "cudaHostAlloc");
+    g_allocs.fetch_add(1, std::memory_order_relaxed);
     h.dev.alloc(cap);
     h.cap = cap;
   }
@@ -2223,6 +2262,11 @@ extern "C" kl_status kl_net_profile_read(kl_net_t net, int layer, double* ms_hos
 extern "C" kl_status kl_launch_count(uint64_t* count_host) {
   if (!count_host) return KL_EINVAL;
   *count_host = g_launches.load();
+  return KL_OK;
+}
+extern "C" kl_status kl_alloc_count(uint64_t* count_host) {
+  if (!count_host) return KL_EINVAL;
+  *count_host = g_allocs.load(std::memory_order_relaxed);
   return KL_OK;
 }
 

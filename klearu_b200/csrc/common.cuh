@@ -5,10 +5,31 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "../../include/klearu_gpu.h"
 
 namespace kl {
+
+// Function attributes such as the dynamic shared memory limit apply to the
+// device that is current when they are set.  A launch site keeps one
+// OncePerDevice and runs its set-up through it: the set-up runs once on each
+// device the process launches on, under a lock shared by the host threads.
+struct OncePerDevice {
+  std::mutex mu;
+  unsigned long long done = 0;
+  template <class F>
+  void operator()(F&& f) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    std::lock_guard<std::mutex> g(mu);
+    if (!(done & bit)) {
+      f();
+      done |= bit;
+    }
+  }
+};
 
 // Device-side error word bits (never __trap: kernels record and return).
 enum : int {

@@ -587,11 +587,10 @@ static void tc_gemm_launch(dim3 grid, const __nv_bfloat16* W, int ldw, int nw, c
                            int ktiles, int per, float* P, int ldp, int* err, cudaStream_t st) {
   using Cfg = TcCfg<NT>;
   constexpr int smem = Cfg::NST * Cfg::STAGE;
-  static bool attr = false;
-  if (!attr) {
+  static OncePerDevice attr;
+  attr([&] {
     cudaFuncSetAttribute(tc_gemm_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  });
   tc_gemm_kernel<NT><<<grid, 128, smem, st>>>(W, ldw, nw, xs, T, ktiles, per, P, ldp, err);
 }
 
@@ -630,11 +629,10 @@ void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* id
   int pow2 = 2 * TK_NT;  // at least the register-sorted size
   while (pow2 < k) pow2 <<= 1;
   const size_t sm = (size_t)pow2 * 8 + (size_t)n * 4;
-  static bool attr = false;
-  if (!attr) {  // the kernel's static shared memory (~34 KB) counts against the 227 KB per block
+  static OncePerDevice attr;
+  attr([&] {  // the kernel's static shared memory (~34 KB) counts against the 227 KB per block
     cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 190 * 1024);
-    attr = true;
-  }
+  });
   topk_kernel<<<T, TK_NT, sm, st>>>(scores, n, lds, k, idx, ldi, pow2);
   count_launch();
 }

@@ -221,7 +221,7 @@ struct DenseScratch {
   float* LGd;          // [max batch][ldu], zero between steps
   int64_t ldu;         // >= rows, multiple of 32
 };
-bool rm_dense_fits(int64_t rows, int nb);
+bool rm_dense_fits(int64_t rows, int nb, int64_t max_bytes);
 // stat += ctr[0] (touched-row counter of the roofline statistics)
 void launch_count_touched(const uint32_t* ctr, unsigned long long* stat, cudaStream_t st);
 void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
@@ -260,9 +260,10 @@ struct ShardLayout {
   int rowptr = 0, lptr = 0, idx = 0, val = 0, labels = 0, words = 0;  // word offsets / block size
 };
 ShardLayout shard_layout(int max_batch, int nnz_cap, int lab_cap);
-void launch_shard_pack(uint32_t* send, const ShardLayout& Ly, const kl_batch& b, cudaStream_t st);
+void launch_shard_pack(uint32_t* send, const ShardLayout& Ly, const kl_batch& b, int B, uint32_t fault,
+                       cudaStream_t st);
 void launch_shard_unpack(const uint32_t* recv, const ShardLayout& Ly, int P, int B, int32_t* g_rowptr,
-                         uint32_t* g_idx, float* g_val, int32_t* g_lptr, uint32_t* g_labels, int* err,
+                         uint32_t* g_idx, float* g_val, int32_t* g_lptr, uint32_t* g_labels, int* err, OptStep* opt,
                          cudaStream_t st);
 void launch_shard_fallback(ActiveSet A, const int32_t* gcnt, int n_local, int nq, int* err, cudaStream_t st);
 void launch_shard_or_masks(uint32_t* tmask, const uint32_t* all, int P, int nw, cudaStream_t st);

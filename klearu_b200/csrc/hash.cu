@@ -409,12 +409,11 @@ void launch_hash_dense(const DevHash& h, const DenseIn& in, const HashOut& out, 
                        (reinterpret_cast<uintptr_t>(in.X) & 15) == 0;
       const size_t xbytes = fmb ? (size_t)2 * tdim * 64 : (size_t)tdim * PL_PITCH * 4;
       const size_t sm = (size_t)round_up((int64_t)xbytes, 16) + (size_t)TT * h.k * 32 * sizeof(float);
-      static bool attr = false;
-      if (!attr) {
+      static OncePerDevice attr;
+      attr([&] {
         cudaFuncSetAttribute(proj_list_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         cudaFuncSetAttribute(proj_list_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr = true;
-      }
+      });
       if (fmb) proj_list_kernel<true><<<grid, block, sm, st>>>(h, in, out, TT);
       else proj_list_kernel<false><<<grid, block, sm, st>>>(h, in, out, TT);
       count_launch();
@@ -429,11 +428,10 @@ void launch_hash_dense(const DevHash& h, const DenseIn& in, const HashOut& out, 
           const int bits = __builtin_popcount(out.nb_mask);
           nwin = std::min(h.k, (bits + h.bpw - 1) / h.bpw);
         }
-        static bool attr = false;
-        if (!attr) {
+        static OncePerDevice attr;
+        attr([&] {
           cudaFuncSetAttribute(wta_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-          attr = true;
-        }
+        });
         // few row tiles (a query batch): spread the tables over more blocks
         const int rt = (int)ceil_div(in.n, 32);
         const int tg = std::max(1, std::min(h.L / 8, 296 / std::max(rt, 1)));
@@ -461,11 +459,10 @@ void launch_hash_sparse(const DevHash& h, const SparseIn& in, const HashOut& out
     case KL_HASH_SRP: {
       int nt = (int)round_up(h.LK, 32);
       const size_t sm = ((size_t)round_up(h.LK, 4) + (size_t)PS_CH * h.lkpad / 4) * sizeof(float);
-      static bool attr = false;
-      if (!attr) {
+      static OncePerDevice attr;
+      attr([&] {
         cudaFuncSetAttribute(proj_sparse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr = true;
-      }
+      });
       proj_sparse_kernel<<<in.n, nt, sm, st>>>(h, in, out);
   count_launch();
       break;

@@ -676,12 +676,11 @@ void launch_probe(const ProbeArgs& a, cudaStream_t st) {
     }
   }
   const size_t sm = sizeof(ProbeSmem) + words * 4;
-  static bool attr = false;
-  if (!attr) {
+  static OncePerDevice attr;
+  attr([&] {
     cudaFuncSetAttribute(probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)(sizeof(ProbeSmem) + (size_t)PB_MAXWORDS * 4));
-    attr = true;
-  }
+  });
   probe_kernel<<<a.nq, PB_NT, sm, st>>>(b);
   count_launch();
 }

@@ -1263,12 +1263,11 @@ void launch_fm_forward(const void* W, int wdtype, int ldw, int d, const float* b
   const size_t rowb = (size_t)ldw * (wdtype == KL_DTYPE_BF16 ? 2 : 4);
   const int ch = (int)std::max<size_t>(8, std::min<size_t>(64, (size_t)(48 * 1024) / rowb));
   const size_t sm = (size_t)round_up((int64_t)ch * 8, 16) + (size_t)ch * rowb;
-  static bool attr = false;
-  if (!attr) {
+  static OncePerDevice attr;
+  attr([&] {
     cudaFuncSetAttribute(fm_forward_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(fm_forward_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
+  });
   if (wdtype == KL_DTYPE_BF16)
     fm_forward_kernel<__nv_bfloat16><<<in.n, 128, sm, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err, ch);
   else
@@ -1282,12 +1281,11 @@ static void rm_launch(const RmArgs& a, int nq, cudaStream_t st) {
   constexpr int EPT = TILEB / (int)sizeof(W);
   const size_t sm = (size_t)round_up((int64_t)a.ldx * 4, 16) + (size_t)RM_NWB * 32 * PITCH +
                     (size_t)RM_NWB * EPT * 4;
-  static bool attr = false;
-  if (!attr) {
+  static OncePerDevice attr;
+  attr([&] {
     cudaFuncSetAttribute(rm_forward_kernel<W, MODE, TILEB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          200 * 1024);
-    attr = true;
-  }
+  });
   dim3 grid(a.nchunk, nq);
   rm_forward_kernel<W, MODE, TILEB><<<grid, RM_RPB, sm, st>>>(a);
   count_launch();
@@ -1360,8 +1358,10 @@ void launch_count_touched(const uint32_t* ctr, unsigned long long* stat, cudaStr
   count_launch();
 }
 
-bool rm_dense_fits(int64_t rows, int nb) {
-  return rows * (int64_t)nb * 4 <= ((int64_t)2 << 30);
+bool rm_dense_fits(int64_t rows, int nb, int64_t max_bytes) {
+  if (max_bytes < 0) return false;
+  if (max_bytes == 0) max_bytes = (int64_t)2 << 30;
+  return rows * (int64_t)nb * 4 <= max_bytes;
 }
 
 void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
@@ -1436,27 +1436,26 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
   count_launch();
   const int nwords = (int)ceil_div(nq, 32);
   const size_t sm = (size_t)nwords * 4 * 65;
-  static bool attr = false;
-  if (!attr) {
+  static OncePerDevice attr;
+  attr([&] {
     cudaFuncSetAttribute(fm_grad_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
+  });
   const int lthreads = std::min(1024, 32 * (int)ceil_div(N, 32));
   fm_grad_long_kernel<<<upd_grid(), lthreads, sm, st>>>(N, lgd, ldl, S, nwords, G, ldl);
   count_launch();
   const int vpr = ldl / 4;  // vectors per feature row (ldw == ldl == pitch of N)
   const int rpw = vpr <= 32 ? 32 / vpr : 1;
   const int nk = vpr <= 32 ? 1 : (int)ceil_div(vpr, 32);
-  static int agrid = 0;
   const size_t smem = (size_t)(FA_NT / 32) * FA_D * FA_STG;
-  if (!agrid) {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    agrid = sms * 4;  // resident blocks per SM under the kernel's launch bounds
+  static OncePerDevice attr_adam;
+  attr_adam([&] {
     cudaFuncSetAttribute(fm_adam_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(fm_adam_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  }
+  });
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int agrid = sms * 4;  // resident blocks per SM under the kernel's launch bounds
   (void)err;
   if (around_adam) around_adam(hook_arg, 0);
   if (wdtype == KL_DTYPE_BF16)

@@ -11,19 +11,34 @@
 namespace kl {
 namespace {
 
-// Header of a packed batch: B, nnz, nlabels (word 3 unused).
-__global__ void shard_header_kernel(uint32_t* send, int B, int nnz, int nlab) {
-  send[0] = (uint32_t)B;
-  send[1] = (uint32_t)nnz;
-  send[2] = (uint32_t)nlab;
-  send[3] = 0u;
+// Header of a packed batch: B, nnz, nlabels and a fault word.  A rank whose
+// batch cannot be exchanged (wrong example count, or more nnz / labels than
+// the fixed exchange capacity) sends an empty batch of B examples with the
+// fault word set (a DERR_* bit) instead of leaving the collective sequence,
+// so every rank stays in step and every rank sees the fault.
+__global__ void shard_header_kernel(uint32_t* send, int B, int nnz, int nlab, uint32_t fault, int32_t* rowptr_empty,
+                                    int32_t* lptr_empty) {
+  if (threadIdx.x == 0) {
+    send[0] = (uint32_t)B;
+    send[1] = (uint32_t)nnz;
+    send[2] = (uint32_t)nlab;
+    send[3] = fault;
+  }
+  if (fault)
+    for (int s = threadIdx.x; s <= B; s += blockDim.x) {
+      rowptr_empty[s] = 0;
+      lptr_empty[s] = 0;
+    }
 }
 
 // Block r rebuilds rank r's part of the global batch from the gathered
 // buffers: CSR rows and label rows are appended in rank order with their
 // offsets rebased onto the global arrays.
+// A fault word from any rank is raised on every rank, and the step's learning
+// rate is set to 0 so that no weight moves (Adam moments still advance).
 __global__ void shard_unpack_kernel(const uint32_t* recv, ShardLayout Ly, int P, int B, int32_t* g_rowptr,
-                                    uint32_t* g_idx, float* g_val, int32_t* g_lptr, uint32_t* g_labels, int* err) {
+                                    uint32_t* g_idx, float* g_val, int32_t* g_lptr, uint32_t* g_labels, int* err,
+                                    OptStep* opt) {
   const int r = blockIdx.x;
   __shared__ uint32_t pre_nnz, pre_lab;
   if (threadIdx.x == 0) {
@@ -34,8 +49,15 @@ __global__ void shard_unpack_kernel(const uint32_t* recv, ShardLayout Ly, int P,
     }
     pre_nnz = a;
     pre_lab = b;
-    for (int q = 0; q < P; ++q)
-      if ((int)recv[(size_t)q * Ly.words] != B) atomicOr(err, DERR_BOUNDS);  // every rank must pass B examples
+    uint32_t fault = 0;
+    for (int q = 0; q < P; ++q) {
+      if ((int)recv[(size_t)q * Ly.words] != B) fault |= DERR_BOUNDS;  // every rank must pass B examples
+      fault |= recv[(size_t)q * Ly.words + 3];
+    }
+    if (fault) {
+      atomicOr(err, (int)fault);
+      if (r == 0) opt->lr = 0.0f;
+    }
   }
   __syncthreads();
   const uint32_t* blk = recv + (size_t)r * Ly.words;
@@ -91,11 +113,15 @@ ShardLayout shard_layout(int max_batch, int nnz_cap, int lab_cap) {
   return L;
 }
 
-void launch_shard_pack(uint32_t* send, const ShardLayout& Ly, const kl_batch& b, cudaStream_t st) {
-  shard_header_kernel<<<1, 1, 0, st>>>(send, b.batch, b.nnz, b.nlabels);
+void launch_shard_pack(uint32_t* send, const ShardLayout& Ly, const kl_batch& b, int B, uint32_t fault,
+                       cudaStream_t st) {
+  int32_t* rp = reinterpret_cast<int32_t*>(send + Ly.rowptr);
+  int32_t* lp = reinterpret_cast<int32_t*>(send + Ly.lptr);
+  shard_header_kernel<<<1, 256, 0, st>>>(send, B, fault ? 0 : b.nnz, fault ? 0 : b.nlabels, fault, rp, lp);
   count_launch();
-  cudaMemcpyAsync(send + Ly.rowptr, b.rowptr, (size_t)(b.batch + 1) * 4, cudaMemcpyDeviceToDevice, st);
-  cudaMemcpyAsync(send + Ly.lptr, b.label_ptr, (size_t)(b.batch + 1) * 4, cudaMemcpyDeviceToDevice, st);
+  if (fault) return;
+  cudaMemcpyAsync(rp, b.rowptr, (size_t)(B + 1) * 4, cudaMemcpyDeviceToDevice, st);
+  cudaMemcpyAsync(lp, b.label_ptr, (size_t)(B + 1) * 4, cudaMemcpyDeviceToDevice, st);
   if (b.nnz > 0) {
     cudaMemcpyAsync(send + Ly.idx, b.idx, (size_t)b.nnz * 4, cudaMemcpyDeviceToDevice, st);
     cudaMemcpyAsync(send + Ly.val, b.val, (size_t)b.nnz * 4, cudaMemcpyDeviceToDevice, st);
@@ -104,9 +130,9 @@ void launch_shard_pack(uint32_t* send, const ShardLayout& Ly, const kl_batch& b,
 }
 
 void launch_shard_unpack(const uint32_t* recv, const ShardLayout& Ly, int P, int B, int32_t* g_rowptr,
-                         uint32_t* g_idx, float* g_val, int32_t* g_lptr, uint32_t* g_labels, int* err,
+                         uint32_t* g_idx, float* g_val, int32_t* g_lptr, uint32_t* g_labels, int* err, OptStep* opt,
                          cudaStream_t st) {
-  shard_unpack_kernel<<<P, 512, 0, st>>>(recv, Ly, P, B, g_rowptr, g_idx, g_val, g_lptr, g_labels, err);
+  shard_unpack_kernel<<<P, 512, 0, st>>>(recv, Ly, P, B, g_rowptr, g_idx, g_val, g_lptr, g_labels, err, opt);
   count_launch();
 }
 

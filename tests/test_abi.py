@@ -33,13 +33,13 @@ def test_binding_covers_header():
 
 def test_abi_version_and_null_handles():
     lib = _lib.load()
-    assert lib.kl_abi_version() == 1
+    assert lib.kl_abi_version() == 2
     assert lib.kl_ctx_destroy(None) == _lib.KL_EINVAL
     assert lib.kl_hash_destroy(None) == _lib.KL_EINVAL
     assert lib.kl_index_destroy(None) == _lib.KL_EINVAL
     assert lib.kl_net_destroy(None) == _lib.KL_EINVAL
     assert lib.kl_net_train_step(None, None, 0.1, 0, None, None) == _lib.KL_EINVAL
-    assert lib.kl_last_error(None) == b"null context"
+    assert isinstance(lib.kl_last_error(None), bytes)  # this thread's last error (context-free calls)
 
 
 def test_library_is_sm100a_only():

@@ -115,3 +115,78 @@ def test_sharded_two_gpus_match_oracle(dtype):
         p.join(120)
         assert p.exitcode == 0
     assert not msgs, "\n".join(msgs)
+
+
+def _fault_worker(rank, world, port, out):
+    """Rank 1 passes a batch the exchange cannot carry (more nnz than its fixed
+    capacity, then one example short).  Every rank must return the fault from
+    the same step, none may block, and no weight may move in that step."""
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from klearu_b200 import _lib
+        from klearu_b200 import synthetic as S
+        from klearu_b200.core import Context, Network
+        from klearu_b200.data import HostBatch
+        from klearu_b200.dist import rank_slice, share_unique_id
+
+        cfg = _cfg()
+        init = S.make_init(cfg, 42)
+        uid = share_unique_id(rank, world)
+        B = 24
+        net = Network(cfg, init, weight_dtype="f32", max_batch=B, ctx=Context(rank), shard=(uid, rank, world))
+        gen = S.XcGenerator(2000, 5000, seed=3, mean_nnz=20)
+        good = rank_slice(gen.batch(B * world), rank, world)
+        rng = np.random.default_rng(rank)
+        nz = 600  # > the exchange's 512 nnz per example
+        heavy = HostBatch(np.arange(B + 1, dtype=np.int32) * nz,
+                          np.concatenate([np.sort(rng.choice(2000, nz, replace=False)) for _ in range(B)]).astype(np.uint32),
+                          np.full(B * nz, 0.05, np.float32), np.arange(B + 1, dtype=np.int32),
+                          np.zeros(B, np.uint32))
+        short = rank_slice(gen.batch(B * world), rank, world)
+        short = HostBatch(short.rowptr[:B], short.idx[:short.rowptr[B - 1]], short.val[:short.rowptr[B - 1]],
+                          short.label_ptr[:B], short.labels[:short.label_ptr[B - 1]])
+        res = []
+        net.train_step_host(good, 1e-3)
+        for bad, want in ((heavy, 7), (short, 6)):  # KL_ECAPACITY, KL_EBOUNDS
+            w0 = net.get_layer(1)["weights"]
+            code = 0
+            try:
+                net.train_step_host(bad if rank == 1 else good, 1e-3)
+            except _lib.KlError as e:
+                code = e.status
+            moved = not np.array_equal(w0, net.get_layer(1)["weights"])
+            res.append((code, want, moved))
+        net.train_step_host(good, 1e-3)  # the network keeps working afterwards
+        res.append((0, 0, False))
+        out.put((rank, res))
+    except Exception:
+        import traceback
+
+        out.put((rank, traceback.format_exc()))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_fault_is_raised_on_every_rank():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_fault_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=240) for _ in range(2))
+    for p in ps:
+        p.join(120)
+    for r in range(2):
+        assert not isinstance(got[r], str), got[r]
+        for code, want, moved in got[r]:
+            assert code == want, (r, got[r])
+            assert not moved, (r, got[r])

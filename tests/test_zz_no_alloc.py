@@ -92,10 +92,18 @@ def test_noalloc_query_allocates_no_device_memory(gpu_ctx):
                                                        cap, None), ix.ctx.h)
         ix.ctx.sync()
 
+    def allocs():
+        n = C.c_uint64()
+        _lib.check(ix.lib.kl_alloc_count(C.byref(n)))
+        return n.value
+
     call()  # first call on the device: symbol address lookup and lazy kernel loading
+    a0 = allocs()
     free0 = torch.cuda.mem_get_info(gpu_ctx.device)[0]
     call()
     call()
+    # the library's own allocation counter is exact; free device memory is a coarser second check
+    assert allocs() == a0
     assert torch.cuda.mem_get_info(gpu_ctx.device)[0] == free0
     # self-queries find their own id in every table
     o = offs.cpu().numpy()
