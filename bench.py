@@ -161,11 +161,16 @@ class ClockSampler:
             self.proc = subprocess.Popen(cmd, stdout=self.file, stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.proc = None
+            return
+        # the timed region starts only once the sampler is writing (at most ~2 s)
+        t0 = time.time()
+        while time.time() - t0 < 2.0 and os.path.getsize(self.file.name) == 0:
+            time.sleep(0.05)
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        time.sleep(0.45)  # at least two samples after the timed region
         self.proc.terminate()
         self.proc.wait()
         self.file.flush()
@@ -425,8 +430,8 @@ def main():
                            "HBM fraction is an algorithmic-bytes rate, not DRAM traffic",
                 "achieved": ach_fwd, "peak": peak, "unit": "GB/s", "frac": ach_fwd / peak,
                 "peak_kind": f"{peak_kind} (HBM copy bandwidth)",
-                "traffic": None, "traffic_note": "DRAM bytes per launch come from ncu, not this run; see the "
-                                                 "kernel summaries under profiles/",
+                "traffic": None, "traffic_note": "DRAM bytes per launch come from an ncu capture of the "
+                                                 "same kernel, not from this run",
                 "bytes_per_launch": bytes_fwd, "ms_per_launch": ms_fwd,
                 "bytes_formula": f"{wbytes}*d_h*sum(A_s) + 4*sum(A_s), sum(A_s)={A:.0f} per step"}
     # HBM-streaming kernel: layer 0's Adam over all feature rows x touched hidden neurons
@@ -444,34 +449,6 @@ def main():
                  "frac_of_peak": step_bytes / (ms_step / 1e3) / 1e9 / peak,
                  "note": "algorithmic bytes of every term of the step (forward and dX gathers counted "
                          "separately) / step time / HBM peak; most output-row gathers are served from L2"}
-
-    # ---- a forced table rebuild of every layer, and its amortised cost
-    torch.cuda.synchronize()
-    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    r0.record(st)
-    net.rebuild()
-    r1.record(st)
-    torch.cuda.synchronize()
-    ms_rb = r0.elapsed_time(r1)
-    lo0 = wl.cfg.network.layers[0].lsh
-    rebuild = {"ms": ms_rb, **rebuild_schedule_cost(ms_rb, ms_step, lo0.rebuild_interval_base, lo0.rebuild_decay)}
-    value_with_rebuild = world * B / (rebuild["ms_per_step_with_rebuild"] / 1e3)
-
-    # ---- exact (per-example, the reference's own semantics) mode, a few steps
-    exact = None
-    if not args.no_exact and world == 1:
-        ex0, ex1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        nex = 2
-        net.train_step_device(pool[0], 1e-3, mode=_lib.MODE_EXACT_SEQUENTIAL)
-        torch.cuda.synchronize()
-        ex0.record(st)
-        for i in range(nex):
-            net.train_step_device(pool[(i + 1) % len(pool)], 1e-3, mode=_lib.MODE_EXACT_SEQUENTIAL)
-        ex1.record(st)
-        torch.cuda.synchronize()
-        exact = {"value": B * nex / (ex0.elapsed_time(ex1) / 1e3), "unit": "samples/s", "steps": nex,
-                 "mode": "KL_MODE_EXACT_SEQUENTIAL: one example at a time, weights updated after each "
-                         "(Network::train_step semantics)"}
 
     # ---- end to end through the C ABI with host buffers
     e2e = None
@@ -512,6 +489,34 @@ def main():
         e2e = {"value": world * B * args.steps / (float(t2.item()) / 1e3), "unit": "samples/s",
                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4,
                "api": "kl_net_train_step_host (C ABI): per-step upload of the pinned host CSR batch and loss readback"}
+
+    # ---- (after the timed legs, which they would perturb) a forced table rebuild of every layer, and its amortised cost
+    torch.cuda.synchronize()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(st)
+    net.rebuild()
+    r1.record(st)
+    torch.cuda.synchronize()
+    ms_rb = r0.elapsed_time(r1)
+    lo0 = wl.cfg.network.layers[0].lsh
+    rebuild = {"ms": ms_rb, **rebuild_schedule_cost(ms_rb, ms_step, lo0.rebuild_interval_base, lo0.rebuild_decay)}
+    value_with_rebuild = world * B / (rebuild["ms_per_step_with_rebuild"] / 1e3)
+
+    # ---- exact (per-example, the reference's own semantics) mode, a few steps
+    exact = None
+    if not args.no_exact and world == 1:
+        ex0, ex1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        nex = 2
+        net.train_step_device(pool[0], 1e-3, mode=_lib.MODE_EXACT_SEQUENTIAL)
+        torch.cuda.synchronize()
+        ex0.record(st)
+        for i in range(nex):
+            net.train_step_device(pool[(i + 1) % len(pool)], 1e-3, mode=_lib.MODE_EXACT_SEQUENTIAL)
+        ex1.record(st)
+        torch.cuda.synchronize()
+        exact = {"value": B * nex / (ex0.elapsed_time(ex1) / 1e3), "unit": "samples/s", "steps": nex,
+                 "mode": "KL_MODE_EXACT_SEQUENTIAL: one example at a time, weights updated after each "
+                         "(Network::train_step semantics)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -165,6 +165,24 @@ KL_API kl_status kl_hash_destroy(kl_hash_t h);
 /* HashFamily::k / input_dim / num_tables (hash/mod.rs:32-38). */
 KL_API kl_status kl_hash_info(kl_hash_t h, int* kind_host, int* input_dim_host, int* k_host,
                        int* num_tables_host);
+/* Arithmetic of the SimHash / SRP projection of dense rows (no reference
+ * counterpart; the reference has one scalar path, simhash.rs:75-126).
+ *  KL_PROJ_AUTO (0, default): batches of >= 4096 bf16 rows (table rebuilds)
+ *    on the tensor cores (exact bf16 products, f32 accumulation in the tensor
+ *    core's order), everything else on the sequential path;
+ *  KL_PROJ_SEQUENTIAL (1): always the reference's sequential f32 sums, so
+ *    every code equals the reference's bit for bit;
+ *  KL_PROJ_TENSOR (2): the tensor cores for every bf16 row batch.
+ * On the tensor cores a projection within a few f32 ulps of zero (|p| far
+ * below 1e-6 for unit-scale rows) may take the other sign; min_abs_proj
+ * outputs identify such rows. */
+#define KL_PROJ_AUTO 0
+#define KL_PROJ_SEQUENTIAL 1
+#define KL_PROJ_TENSOR 2
+KL_API kl_status kl_hash_set_projection(kl_hash_t h, int mode);
+/* The same setting on an index's hash family (for a network layer's index,
+ * from kl_net_layer_index). */
+KL_API kl_status kl_index_set_projection(kl_index_t ix, int mode);
 /* Batched HashFamily::hash_dense (hash/mod.rs:26): codes[i*L + t] =
  * hash_dense(X[i*ldx ..], t) for all rows i < n and tables t < L.  For
  * SIMHASH/SRP, `min_abs_proj` (nullable, [n][L]) receives min over the K bits
@@ -172,6 +190,10 @@ KL_API kl_status kl_hash_info(kl_hash_t h, int* kind_host, int* input_dim_host, 
  * summation-order sensitive. */
 KL_API kl_status kl_hash_dense_batch(kl_hash_t h, const float* X, int n, int ldx, uint64_t* codes,
                               float* min_abs_proj);
+/* kl_hash_dense_batch over rows of either storage type: rows [n][ld] of
+ * `dtype` (KL_DTYPE_F32 / KL_DTYPE_BF16), as the index rebuild hashes them. */
+KL_API kl_status kl_hash_dense_batch_rows(kl_hash_t h, const void* rows, int n, int ld, int dtype, uint64_t* codes,
+                                          float* min_abs_proj);
 /* Batched HashFamily::hash_sparse (hash/mod.rs:29) over a CSR batch with
  * sorted, unique column indices per row. */
 KL_API kl_status kl_hash_sparse_batch(kl_hash_t h, const int32_t* rowptr, const uint32_t* idx,

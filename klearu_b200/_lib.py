@@ -26,6 +26,7 @@ OPT_SGD, OPT_ADAM = range(2)
 DTYPE_F32, DTYPE_BF16 = range(2)
 QUERY_COUNTS, QUERY_UNION = range(2)
 MODE_EXACT_SEQUENTIAL, MODE_BATCHED = range(2)
+PROJ_AUTO, PROJ_SEQUENTIAL, PROJ_TENSOR = 0, 1, 2
 PHASES = ["hash", "probe", "forward", "backward", "update", "rebuild", "stream"]
 
 
@@ -84,6 +85,9 @@ _PROTOS = {
                                    C.POINTER(_H)]),
     "kl_hash_destroy": (_S, [_H]),
     "kl_hash_info": (_S, [_H, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "kl_hash_set_projection": (_S, [_H, C.c_int]),
+    "kl_hash_dense_batch_rows": (_S, [_H, _P, C.c_int, C.c_int, C.c_int, _P, _P]),
+    "kl_index_set_projection": (_S, [_H, C.c_int]),
     "kl_hash_dense_batch": (_S, [_H, _P, C.c_int, C.c_int, _P, _P]),
     "kl_hash_sparse_batch": (_S, [_H, _P, _P, _P, C.c_int, _P, _P]),
     "kl_index_create": (_S, [_H, _H, C.c_int, C.c_int, C.POINTER(_H)]),

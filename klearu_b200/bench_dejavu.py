@@ -1,4 +1,4 @@
-"""Deja Vu sparse FFN microbenchmark on one B200.
+"""Deja Vu sparse FFN microbenchmark (the C3 workload: LLaMA-7B-shaped MLP) on one B200.
 
     python -m klearu_b200.bench_dejavu [--tokens 1,16,64] [--layers 32] [--distinct 2] [--reps 5]
 

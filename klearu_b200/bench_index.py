@@ -1,4 +1,4 @@
-"""LSH index microbenchmark on one B200.
+"""LSH index microbenchmark (the C4 workload: 1M-row index) on one B200.
 
     python -m klearu_b200.bench_index [--rows 1000000] [--queries 4096] [--reps 5] [--cpu-rows 20000]
 
@@ -82,12 +82,26 @@ def main() -> None:
             for q in qs:
                 ocfg.query(q)
             c2 = time.perf_counter()
+            rb_seq = None
+            if kind == HF.SimHash:
+                # the same rebuild with the reference's sequential projection sums
+                ix.set_projection(_lib.PROJ_SEQUENTIAL)
+                ts = []
+                for _ in range(2):
+                    e0.record()
+                    ix.rebuild_rows(rows)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    ts.append(e0.elapsed_time(e1))
+                rb_seq = float(np.median(ts))
+                ix.set_projection(_lib.PROJ_AUTO)
             rb_ms = float(np.median(t_rb))
             q_ms = float(np.median(t_q))
             print(json.dumps({
                 "workload": "C4 LSH index microbench (synthetic)", "hash": f"{HF(kind).name} K{K} L{L}",
                 "bucket": BucketType(bucket).name, "rows": args.rows, "dim": args.dim, "queries": nq,
                 "rebuild_ms": rb_ms, "rebuild_rows_per_s": args.rows / (rb_ms / 1e3),
+                "rebuild_ms_sequential_projection": rb_seq,
                 "query_union_ms": q_ms, "queries_per_s": nq / (q_ms / 1e3), "mean_union": union,
                 "near_duplicate_self_hit": near_hit,
                 "cpu_oracle": {"rows": len(sub), "rebuild_rows_per_s": len(sub) / (c1 - c0),

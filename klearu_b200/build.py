@@ -22,7 +22,7 @@ PKG = ROOT / "klearu_b200"
 CSRC = PKG / "csrc"
 BUILD = ROOT / "_build" / "gpu"
 LIB = PKG / "libklearu_gpu.so"
-SOURCES = ["hash.cu", "index.cu", "layer.cu", "shard.cu", "dejavu.cu", "data.cu", "api.cu"]
+SOURCES = ["hash.cu", "hash_tc.cu", "index.cu", "layer.cu", "shard.cu", "dejavu.cu", "data.cu", "api.cu"]
 
 def _nccl_dirs() -> tuple[str, str]:
     """NCCL headers and library: the copy PyTorch itself loads (nvidia-nccl

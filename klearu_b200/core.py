@@ -133,6 +133,22 @@ class HashFamily:
               self.ctx.h, "kl_hash_dense_batch")
         return (codes, mn) if with_min_abs else codes
 
+    def hash_rows(self, rows: torch.Tensor, with_min_abs: bool = False):
+        """kl_hash_dense_batch_rows: rows kept in their storage type (bf16 or f32)."""
+        rows = torch.as_tensor(rows).to(f"cuda:{self.ctx.device}")
+        dt = _lib.DTYPE_BF16 if rows.dtype == torch.bfloat16 else _lib.DTYPE_F32
+        rows = (rows if dt == _lib.DTYPE_BF16 else rows.float()).contiguous()
+        n = rows.shape[0]
+        codes = torch.empty((n, self._L), dtype=torch.int64, device=rows.device)
+        mn = torch.empty((n, self._L), dtype=torch.float32, device=rows.device) if with_min_abs else None
+        check(self.lib.kl_hash_dense_batch_rows(self.h, _ptr(rows), n, rows.shape[1] if n else self._d, dt,
+                                                _ptr(codes), _ptr(mn)), self.ctx.h, "kl_hash_dense_batch_rows")
+        return (codes, mn) if with_min_abs else codes
+
+    def set_projection(self, mode: int) -> None:
+        """_lib.PROJ_AUTO / PROJ_SEQUENTIAL / PROJ_TENSOR (kl_hash_set_projection)."""
+        check(self.lib.kl_hash_set_projection(self.h, int(mode)), self.ctx.h, "kl_hash_set_projection")
+
     def hash_sparse_batch(self, rowptr, idx, val, with_min_abs: bool = False):
         dev = f"cuda:{self.ctx.device}"
         rowptr = torch.as_tensor(rowptr, dtype=torch.int32).to(dev)
@@ -264,6 +280,9 @@ class LshIndex:
         rows = (rows if dt == _lib.DTYPE_BF16 else rows.float()).contiguous()
         check(self.lib.kl_index_rebuild(self.h, None, _ptr(rows), rows.shape[0], rows.shape[1], dt),
               self.ctx.h, "kl_index_rebuild")
+
+    def set_projection(self, mode: int) -> None:
+        check(self.lib.kl_index_set_projection(self.h, int(mode)), self.ctx.h, "kl_index_set_projection")
 
     def clear(self) -> None:  # index.rs:313-315
         check(self.lib.kl_index_clear(self.h), self.ctx.h, "kl_index_clear")

@@ -181,7 +181,8 @@ struct kl_ctx_s {
 struct HashImpl {
   kl_ctx_t ctx;
   DevHash dh;
-  DBuf planes, planesT, windows, fallback, perms, plist, poff;
+  DBuf planes, planesT, windows, fallback, perms, plist, poff, tcplanes;
+  std::unique_ptr<TcPlanes> tc;
 };
 struct kl_hash_s {
   std::shared_ptr<HashImpl> h;
@@ -325,6 +326,28 @@ std::shared_ptr<HashImpl> make_hash(kl_ctx_t ctx, int kind, int d, int k, int L,
       H->planesT.alloc(dT.size());
       ck(cudaMemcpyAsync(H->planes.p, dense.data(), dense.size(), cudaMemcpyHostToDevice, st), "upload");
       ck(cudaMemcpyAsync(H->planesT.p, dT.data(), dT.size(), cudaMemcpyHostToDevice, st), "upload");
+      // exact bf16 copy of the planes for the tensor-core projection, grouped by table
+      auto tc = std::make_unique<TcPlanes>();
+      if (tc_plane_layout(d, k, L, tc.get())) {
+        std::vector<uint16_t> pb((size_t)tc->H * tc->Nh * tc->dpad, 0);
+        for (int t = 0; t < L; ++t) {
+          const int grp = t / tc->tph, lt = t % tc->tph;
+          for (int b = 0; b < k; ++b) {
+            const size_t row = (size_t)grp * tc->Nh + (size_t)lt * k + b;
+            for (int i = 0; i < d; ++i) {
+              const int8_t v = dense[(size_t)(t * k + b) * h.dpad + i];
+              pb[row * tc->dpad + i] = v == 0 ? 0 : (v > 0 ? 0x3F80 : 0xBF80);  // bf16 +1 / -1
+            }
+          }
+        }
+        H->tcplanes.alloc(pb.size() * 2);
+        ck(cudaMemcpyAsync(H->tcplanes.p, pb.data(), pb.size() * 2, cudaMemcpyHostToDevice, st), "upload");
+        tc->planes = H->tcplanes.p;
+        tc->err = ctx->err.as<int>();
+        tc->ready = tc_plane_map(tc.get());
+        H->tc = std::move(tc);
+        h.tc = H->tc.get();
+      }
       ck(cudaStreamSynchronize(st), "sync");
       h.planes = H->planes.as<int8_t>();
       h.planesT = H->planesT.as<int8_t>();
@@ -616,6 +639,17 @@ extern "C" kl_status kl_hash_info(kl_hash_t h, int* kind, int* d, int* k, int* L
   if (L) *L = h->h->dh.L;
   return KL_OK;
 }
+static kl_status set_projection(HashImpl* H, int mode) {
+  if (mode < KL_PROJ_AUTO || mode > KL_PROJ_TENSOR) return KL_EINVAL;
+  if (H->tc) H->tc->mode = mode;
+  else if (mode == KL_PROJ_TENSOR && (H->dh.kind == KL_HASH_SIMHASH || H->dh.kind == KL_HASH_SRP))
+    return KL_EUNSUPPORTED;  // the planes do not fit the tensor-core kernel's shared memory
+  return KL_OK;
+}
+extern "C" kl_status kl_hash_set_projection(kl_hash_t h, int mode) {
+  if (!h) return KL_EINVAL;
+  return set_projection(h->h.get(), mode);
+}
 extern "C" kl_status kl_hash_dense_batch(kl_hash_t h, const float* X, int n, int ldx, uint64_t* codes,
                                          float* min_abs_proj) {
   if (!h) return KL_EINVAL;
@@ -626,6 +660,18 @@ extern "C" kl_status kl_hash_dense_batch(kl_hash_t h, const float* X, int n, int
   o.min_abs = min_abs_proj;
   launch_hash_dense(h->h->dh, dense_rows(X, KL_DTYPE_F32, n, ldx), o, ctx__->stream);
   ck_launch("hash_dense_batch");
+  KL_API_END
+}
+extern "C" kl_status kl_hash_dense_batch_rows(kl_hash_t h, const void* rows, int n, int ld, int dtype,
+                                              uint64_t* codes, float* min_abs_proj) {
+  if (!h) return KL_EINVAL;
+  KL_API_BEGIN(h->h->ctx)
+  require(n >= 0 && (n == 0 || (rows && codes && ld >= h->h->dh.d)), "hash_dense_batch_rows: bad arguments");
+  HashOut o;
+  o.codes = codes;
+  o.min_abs = min_abs_proj;
+  launch_hash_dense(h->h->dh, dense_rows(rows, dtype, n, ld), o, ctx__->stream);
+  ck_launch("hash_dense_batch_rows");
   KL_API_END
 }
 extern "C" kl_status kl_hash_sparse_batch(kl_hash_t h, const int32_t* rowptr, const uint32_t* idx,
@@ -657,6 +703,10 @@ extern "C" kl_status kl_index_destroy(kl_index_t ix) {
   if (!ix) return KL_EINVAL;
   delete ix;
   return KL_OK;
+}
+extern "C" kl_status kl_index_set_projection(kl_index_t ix, int mode) {
+  if (!ix) return KL_EINVAL;
+  return set_projection(ix->ix->hash.get(), mode);
 }
 extern "C" kl_status kl_index_info(kl_index_t ix, int* L, int* nb, int* cap, int* type) {
   if (!ix) return KL_EINVAL;
@@ -807,16 +857,17 @@ struct kl_adaptive_s {
 };
 
 namespace {
-// rows[i] = f32 copy of row idx[i] (zeros for indices >= n)
-__global__ void adaptive_gather_kernel(const void* X, int dtype, int64_t ld, int n, const uint32_t* idx, int S,
-                                       int d, float* out) {
+// rows[i] = f32 copy of row idx[i] (zeros for indices >= n); element (r, c)
+// of the source at r * ld_row + c * ld_elem (row- or feature-major weights)
+__global__ void adaptive_gather_kernel(const void* X, int dtype, int64_t ld_row, int64_t ld_elem, int n,
+                                       const uint32_t* idx, int S, int d, float* out) {
   const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (g >= (int64_t)S * d) return;
   const int i = (int)(g / d), c = (int)(g % d);
   const uint32_t r = idx[i];
   float v = 0.f;
   if (r < (uint32_t)n) {
-    const int64_t o = (int64_t)r * ld + c;
+    const int64_t o = (int64_t)r * ld_row + (int64_t)c * ld_elem;
     v = dtype == KL_DTYPE_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(X)[o])
                                : static_cast<const float*>(X)[o];
   }
@@ -832,11 +883,20 @@ __global__ void adaptive_compare_kernel(const uint64_t* cur, const uint64_t* bas
   if (any) atomicAdd(changed, 1);
 }
 
-void adaptive_hash(kl_adaptive_s* a, const void* rows, int n, int ld, int dtype, DBuf& codes) {
+// The rows a scheduler watches: n rows of d elements, element (r, c) at
+// X[r * ld_row + c * ld_elem].
+struct RowsView {
+  const void* X;
+  int dtype;
+  int64_t ld_row, ld_elem;
+  int n;
+};
+
+void adaptive_hash(kl_adaptive_s* a, const RowsView& rv, DBuf& codes) {
   cudaStream_t st = a->ctx->stream;
   const DevHash& h = a->hash->dh;
   adaptive_gather_kernel<<<(unsigned)ceil_div((int64_t)a->S * h.d, 256), 256, 0, st>>>(
-      rows, dtype, ld, n, a->idx.as<uint32_t>(), a->S, h.d, a->rows.as<float>());
+      rv.X, rv.dtype, rv.ld_row, rv.ld_elem, rv.n, a->idx.as<uint32_t>(), a->S, h.d, a->rows.as<float>());
   count_launch();
   ck_launch("adaptive gather");
   DenseIn in;
@@ -849,6 +909,78 @@ void adaptive_hash(kl_adaptive_s* a, const void* rows, int n, int ld, int dtype,
   o.codes = codes.as<uint64_t>();
   launch_hash_dense(h, in, o, st);
   ck_launch("adaptive hash");
+}
+
+// AdaptiveScheduler::record_baseline (scheduler.rs:89-125).
+void adaptive_record(kl_adaptive_s* a, const std::shared_ptr<HashImpl>& hash, const RowsView& rv,
+                     const uint32_t* sampled_host, int n_sampled, uint64_t seed) {
+  const int n = rv.n;
+  std::vector<uint32_t> idx;
+  if (sampled_host) {
+    require(n_sampled >= 0, "adaptive: n_sampled must be >= 0");
+    idx.assign(sampled_host, sampled_host + n_sampled);
+  } else {
+    // scheduler.rs:104-110: ceil(n * fraction) clamped to [1, n] indices of a
+    // seeded shuffle, sorted (this library's SplitMix64 stream, not StdRng)
+    const size_t S = std::min<size_t>((size_t)n, std::max<size_t>(1, (size_t)std::ceil((float)n * a->sample_fraction)));
+    std::vector<uint32_t> perm((size_t)n);
+    for (int i = 0; i < n; ++i) perm[(size_t)i] = (uint32_t)i;
+    SplitMix rng{seed};
+    for (size_t i = (size_t)n - 1; n > 0 && i > 0; --i) std::swap(perm[i], perm[(size_t)(rng.next() % (uint64_t)(i + 1))]);
+    idx.assign(perm.begin(), perm.begin() + S);
+  }
+  std::sort(idx.begin(), idx.end());
+  a->hash = hash;
+  a->S = (int)idx.size();
+  const int L = a->hash->dh.L;
+  a->steps_since_rebuild = 0;
+  a->steps_since_check = 0;
+  a->drift_ema = 0.f;
+  if (idx.empty()) return;  // no neurons: nothing to watch (scheduler.rs tests: empty_neurons)
+  a->idx.alloc(idx.size() * 4);
+  a->base.alloc(idx.size() * L * 8);
+  a->cur.alloc(idx.size() * L * 8);
+  a->rows.alloc(idx.size() * (size_t)a->hash->dh.d * 4);
+  cudaStream_t st = a->ctx->stream;
+  ck(cudaMemcpyAsync(a->idx.p, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice, st), "upload");
+  adaptive_hash(a, rv, a->base);
+  ck(cudaStreamSynchronize(st), "sync");
+}
+
+// AdaptiveScheduler::should_rebuild (scheduler.rs:130-160) with
+// estimate_drift (scheduler.rs:163-195) on the GPU.  A drift check reads the
+// changed count back, so it waits for the work queued before it.
+bool adaptive_check(kl_adaptive_s* a, const RowsView& rv) {
+  a->steps_since_rebuild += 1;
+  a->steps_since_check += 1;
+  if (a->steps_since_rebuild >= a->max_interval) {  // forced (scheduler.rs:141-145)
+    a->steps_since_rebuild = 0;
+    a->steps_since_check = 0;
+    return true;
+  }
+  if (a->steps_since_check < a->min_interval) return false;
+  float drift = 0.f;
+  if (a->hash && a->S > 0) {
+    cudaStream_t st = a->ctx->stream;
+    adaptive_hash(a, rv, a->cur);
+    ck(cudaMemsetAsync(a->changed.p, 0, 4, st), "memset");
+    adaptive_compare_kernel<<<(unsigned)ceil_div(a->S, 256), 256, 0, st>>>(
+        a->cur.as<uint64_t>(), a->base.as<uint64_t>(), a->idx.as<uint32_t>(), a->S, a->hash->dh.L, rv.n,
+        a->changed.as<int>());
+    count_launch();
+    ck_launch("adaptive compare");
+    int changed = 0;
+    ck(cudaMemcpyAsync(&changed, a->changed.p, 4, cudaMemcpyDeviceToHost, st), "copy");
+    ck(cudaStreamSynchronize(st), "sync");
+    drift = (float)changed / (float)a->S;
+  }
+  a->drift_ema = a->ema_alpha * drift + (1.0f - a->ema_alpha) * a->drift_ema;
+  a->steps_since_check = 0;
+  if (a->drift_ema >= a->drift_threshold) {
+    a->steps_since_rebuild = 0;
+    return true;
+  }
+  return false;
 }
 }  // namespace
 
@@ -886,39 +1018,7 @@ extern "C" kl_status kl_adaptive_record_baseline(kl_adaptive_t a, kl_hash_t h, c
   KL_API_BEGIN(a->ctx)
   require(n >= 0 && (n == 0 || (rows && ld >= h->h->dh.d)), "adaptive: bad rows");
   require(dtype == KL_DTYPE_F32 || dtype == KL_DTYPE_BF16, "adaptive: dtype must be F32 or BF16");
-  std::vector<uint32_t> idx;
-  if (sampled_host) {
-    require(n_sampled >= 0, "adaptive: n_sampled must be >= 0");
-    idx.assign(sampled_host, sampled_host + n_sampled);
-  } else {
-    // scheduler.rs:104-110: ceil(n * fraction) clamped to [1, n] indices of a
-    // seeded shuffle, sorted (this library's SplitMix64 stream, not StdRng)
-    const size_t S = std::min<size_t>((size_t)n, std::max<size_t>(1, (size_t)std::ceil((float)n * a->sample_fraction)));
-    std::vector<uint32_t> perm((size_t)n);
-    for (int i = 0; i < n; ++i) perm[(size_t)i] = (uint32_t)i;
-    SplitMix rng{seed};
-    for (size_t i = (size_t)n - 1; i > 0; --i) std::swap(perm[i], perm[(size_t)(rng.next() % (uint64_t)(i + 1))]);
-    idx.assign(perm.begin(), perm.begin() + S);
-  }
-  std::sort(idx.begin(), idx.end());
-  a->hash = h->h;
-  a->S = (int)idx.size();
-  const int L = a->hash->dh.L;
-  a->steps_since_rebuild = 0;
-  a->steps_since_check = 0;
-  a->drift_ema = 0.f;
-  if (idx.empty()) return KL_OK;  // no neurons: nothing to watch (scheduler.rs tests: empty_neurons)
-  a->idx.alloc(idx.size() * 4);
-  a->base.alloc(idx.size() * L * 8);
-  a->cur.alloc(idx.size() * L * 8);
-  a->rows.alloc(idx.size() * (size_t)a->hash->dh.d * 4);
-  cudaStream_t st = ctx__->stream;
-  ck(cudaMemcpyAsync(a->idx.p, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice, st), "upload");
-  adaptive_hash(a, rows, n, ld, dtype, a->base);
-  ck(cudaStreamSynchronize(st), "sync");
-  a->steps_since_rebuild = 0;
-  a->steps_since_check = 0;
-  a->drift_ema = 0.f;
+  adaptive_record(a, h->h, RowsView{rows, dtype, ld, 1, n}, sampled_host, n_sampled, seed);
   KL_API_END
 }
 extern "C" kl_status kl_adaptive_should_rebuild(kl_adaptive_t a, const void* rows, int n, int ld, int dtype,
@@ -926,38 +1026,12 @@ extern "C" kl_status kl_adaptive_should_rebuild(kl_adaptive_t a, const void* row
   if (!a || !rebuild_host) return KL_EINVAL;
   KL_API_BEGIN(a->ctx)
   *rebuild_host = 0;
-  a->steps_since_rebuild += 1;
-  a->steps_since_check += 1;
-  if (a->steps_since_rebuild >= a->max_interval) {  // forced (scheduler.rs:141-145)
-    a->steps_since_rebuild = 0;
-    a->steps_since_check = 0;
-    *rebuild_host = 1;
-    return KL_OK;
-  }
-  if (a->steps_since_check < a->min_interval) return KL_OK;
-  float drift = 0.f;
-  if (a->hash && a->S > 0) {  // estimate_drift (scheduler.rs:163-195)
+  if (a->hash && a->S > 0 && a->steps_since_rebuild + 1 < a->max_interval &&
+      a->steps_since_check + 1 >= a->min_interval) {
     require(rows && ld >= a->hash->dh.d, "adaptive: bad rows");
     require(dtype == KL_DTYPE_F32 || dtype == KL_DTYPE_BF16, "adaptive: dtype must be F32 or BF16");
-    cudaStream_t st = ctx__->stream;
-    adaptive_hash(a, rows, n, ld, dtype, a->cur);
-    ck(cudaMemsetAsync(a->changed.p, 0, 4, st), "memset");
-    adaptive_compare_kernel<<<(unsigned)ceil_div(a->S, 256), 256, 0, st>>>(
-        a->cur.as<uint64_t>(), a->base.as<uint64_t>(), a->idx.as<uint32_t>(), a->S, a->hash->dh.L, n,
-        a->changed.as<int>());
-    count_launch();
-    ck_launch("adaptive compare");
-    int changed = 0;
-    ck(cudaMemcpyAsync(&changed, a->changed.p, 4, cudaMemcpyDeviceToHost, st), "copy");
-    ck(cudaStreamSynchronize(st), "sync");
-    drift = (float)changed / (float)a->S;
   }
-  a->drift_ema = a->ema_alpha * drift + (1.0f - a->ema_alpha) * a->drift_ema;
-  a->steps_since_check = 0;
-  if (a->drift_ema >= a->drift_threshold) {
-    a->steps_since_rebuild = 0;
-    *rebuild_host = 1;
-  }
+  *rebuild_host = adaptive_check(a, RowsView{rows, dtype, ld, 1, n}) ? 1 : 0;
   KL_API_END
 }
 extern "C" kl_status kl_adaptive_notify_rebuild(kl_adaptive_t a) {

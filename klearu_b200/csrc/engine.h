@@ -4,6 +4,8 @@
 
 #include <cstdint>
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace kl {
@@ -14,6 +16,7 @@ void count_launch(unsigned n = 1);
 // ---------------------------------------------------------------------------
 // Hash families on the device.
 // ---------------------------------------------------------------------------
+struct TcPlanes;
 struct DevHash {
   int kind = 0, d = 0, k = 0, L = 0, w = 0, bpw = 0, bin_size = 0;
   int LK = 0;           // L*K projections (SIMHASH / SRP)
@@ -31,7 +34,22 @@ struct DevHash {
   uint16_t* plist = nullptr;
   uint32_t* poff = nullptr;     // [LK][nt+1]
   int nt = 0;                   // ceil(d / PL_T)
+  const TcPlanes* tc = nullptr; // host-side: the tensor-core projection's planes (SIMHASH / SRP), or null
 };
+
+// Planes of the tensor-core SimHash / SRP projection (hash_tc.cu): exact bf16
+// copies of the ternary planes, [H * Nh][dpad] with table group g in rows
+// [g * Nh, g * Nh + tph * k), and their TMA descriptor.
+struct TcPlanes {
+  int H = 0, tph = 0, Nh = 0, kc = 0, dpad = 0, nst = 0;
+  int mode = KL_PROJ_AUTO;
+  bool ready = false;
+  const void* planes = nullptr;  // device bf16 [H * Nh][dpad]
+  int* err = nullptr;            // device error word
+  alignas(64) CUtensorMap map;
+};
+bool tc_plane_layout(int d, int k, int L, TcPlanes* tp);
+bool tc_plane_map(TcPlanes* tp);
 constexpr int PL_T = 640;       // dimensions per staged tile (< 2^15)
 
 // Dense input: element (i, j) of row i at X[i*ld_row + j*ld_elem], as f32 or bf16.
@@ -59,6 +77,9 @@ struct HashOut {
 };
 
 void launch_hash_dense(const DevHash& h, const DenseIn& in, const HashOut& out, cudaStream_t st);
+// The tensor-core SimHash / SRP projection of bf16 rows; false (nothing launched)
+// when the input or the hash does not qualify.
+bool launch_proj_tc(const DevHash& h, const DenseIn& in, const HashOut& out, int* err, cudaStream_t st);
 void launch_hash_sparse(const DevHash& h, const SparseIn& in, const HashOut& out, cudaStream_t st);
 
 // ---------------------------------------------------------------------------

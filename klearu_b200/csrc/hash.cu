@@ -401,6 +401,11 @@ void launch_hash_dense(const DevHash& h, const DenseIn& in, const HashOut& out, 
   switch (h.kind) {
     case KL_HASH_SIMHASH:
     case KL_HASH_SRP: {
+      // bf16 row batches (table rebuilds) go to the tensor cores unless the
+      // caller asked for the reference's sequential sums
+      if (h.tc && h.tc->mode != KL_PROJ_SEQUENTIAL && (h.tc->mode == KL_PROJ_TENSOR || in.n >= 4096) &&
+          launch_proj_tc(h, in, out, h.tc->err, st))
+        break;
       const int TT = std::min(h.L, std::max(1, 12 / h.k));
       dim3 grid((unsigned)ceil_div(in.n, 32), (unsigned)ceil_div(h.L, TT));
       dim3 block(32 * TT * h.k);
