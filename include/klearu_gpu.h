@@ -266,6 +266,22 @@ KL_API kl_status kl_index_query_sparse_batch(kl_index_t ix, const int32_t* rowpt
 /* Copy the bucket arrays out (checkpointing / parity): ids [L][2^K][cap] in
  * bucket order (Bucket::contents, bucket/mod.rs:11-31), lens [L][2^K],
  * insertion counts [L][2^K] (ReservoirBucket::total_insertions; nullable). */
+/* BOLT SparseInferenceEngine::infer / infer_linear
+ * (crates/klearu-bolt/src/sparse_inference.rs:32-106) for n inputs X [n][ldx]
+ * (device f32): the index's candidates ordered by table count descending
+ * (ties by id ascending, where the reference's follow HashMap order), the
+ * first effective_k = (int)((float)base_top_k * sparsity_multiplier) kept,
+ * and for each kept id < num_neurons the activation
+ * sum_j X[j] * weights[id][j] (sequential f32, the reference's order)
+ * + bias[id] (bias nullable = 0), clamped at 0 when `relu` (infer) or not
+ * (infer_linear).  weights: [num_neurons][ld] of `dtype`, device.  Output per
+ * input i: out_ids / out_act [i*stride .. i*stride + out_n[i]) in that order;
+ * more than `stride` results are truncated and reported as KL_ECAPACITY by
+ * the next synchronising call. */
+KL_API kl_status kl_bolt_infer_batch(kl_index_t ix, const void* weights, int dtype, int ld, const float* bias,
+                                     int num_neurons, const float* X, int n, int ldx, float sparsity_multiplier,
+                                     int base_top_k, int relu, uint32_t* out_ids, float* out_act, int32_t* out_n,
+                                     int stride);
 KL_API kl_status kl_index_export(kl_index_t ix, uint32_t* ids, uint32_t* lens, uint64_t* counts);
 /* Inverse of kl_index_export. */
 KL_API kl_status kl_index_import(kl_index_t ix, const uint32_t* ids, const uint32_t* lens,
@@ -409,6 +425,12 @@ KL_API kl_status kl_net_predict_topk(kl_net_t net, const kl_batch* batch_host, i
 /* Read / write one layer's parameters as reference-layout f32 rows (host
  * memory): weights [N][d], bias [N], optimizer state m/v [N][d] and mb/vb [N]
  * (Adam m_w, v_w, m_b, v_b; SGD momentum in m/mb).  Any pointer may be NULL. */
+/* kl_bolt_infer_batch over layer `layer` (>= 1) of a network: its LSH index,
+ * weights and bias; X [n][ldx] is the layer's input (the previous layer's
+ * activations), device f32. */
+KL_API kl_status kl_net_bolt_infer(kl_net_t net, int layer, const float* X, int n, int ldx,
+                                   float sparsity_multiplier, int base_top_k, int relu, uint32_t* out_ids,
+                                   float* out_act, int32_t* out_n, int stride);
 KL_API kl_status kl_net_get_layer(kl_net_t net, int layer, float* weights_host, float* bias_host,
                            float* m_host, float* v_host, float* mb_host, float* vb_host);
 KL_API kl_status kl_net_set_layer(kl_net_t net, int layer, const float* weights_host,
@@ -423,6 +445,45 @@ KL_API kl_status kl_net_get_step(kl_net_t net, uint64_t* step_host, uint64_t* ne
                           uint64_t* rebuild_count_host);
 KL_API kl_status kl_net_set_step(kl_net_t net, uint64_t step, uint64_t next_rebuild,
                           uint64_t rebuild_count);
+
+/* Rebuild policy of a network's LSH tables (no reference counterpart as a
+ * network setting: the reference's Network always uses RebuildScheduler,
+ * net.rs:109-116, and klearu-mongoose's AdaptiveScheduler is a standalone
+ * component, crates/klearu-mongoose/src/scheduler.rs:44-213).
+ *  KL_REBUILD_SCHEDULE (default): RebuildScheduler, every layer at once.
+ *  KL_REBUILD_ADAPTIVE: one AdaptiveScheduler per layer with the given
+ *    intervals, sample fraction and drift threshold; a layer is rebuilt when
+ *    the EMA of the fraction of its sampled neurons whose hash codes changed
+ *    reaches the threshold (or at max_interval), and its baseline is then
+ *    re-recorded from a sample drawn with `seed`.  Setting the policy records
+ *    the first baselines.  A drift check (every min_interval steps) reads a
+ *    count back from the device, so it waits for the step to finish. */
+#define KL_REBUILD_SCHEDULE 0
+#define KL_REBUILD_ADAPTIVE 1
+typedef struct {
+  int32_t kind;
+  uint64_t min_interval;
+  uint64_t max_interval;
+  float sample_fraction;
+  float drift_threshold;
+  uint64_t seed;
+} kl_rebuild_policy;
+KL_API kl_status kl_net_set_rebuild_policy(kl_net_t net, const kl_rebuild_policy* policy_host);
+/* A layer's rebuild state: its AdaptiveScheduler's drift EMA and steps since
+ * its last rebuild (0 under KL_REBUILD_SCHEDULE), and its rebuild count. */
+KL_API kl_status kl_net_rebuild_state(kl_net_t net, int layer, float* drift_ema_host,
+                                      uint64_t* steps_since_rebuild_host, uint64_t* rebuilds_host);
+
+/* Checkpoint (no reference counterpart: the reference has no resume).  One
+ * file holds everything a train step reads or writes: every layer's weights
+ * (storage type), bias, Adam moments, LSH tables (ids, lengths, reservoir
+ * counts), the step, the RebuildScheduler and the AdaptiveScheduler states.
+ * kl_net_load restores into a network created with the same configuration
+ * (and, for a sharded network, the same rank and rank count: each rank saves
+ * and loads its own file); KL_EINVAL on a mismatch or a corrupt file
+ * (FNV-1a checksum).  Both synchronise the context stream. */
+KL_API kl_status kl_net_save(kl_net_t net, const char* path);
+KL_API kl_status kl_net_load(kl_net_t net, const char* path);
 
 /* Per-step work counters accumulated on the device since the last reset
  * (used for the HBM roofline): sum of active set sizes, distinct rows touched

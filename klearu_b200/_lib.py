@@ -63,6 +63,14 @@ class BatchC(C.Structure):
                 ("label_ptr", C.c_void_p), ("labels", C.c_void_p), ("nnz", C.c_int32), ("nlabels", C.c_int32)]
 
 
+class RebuildPolicyC(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("min_interval", C.c_uint64), ("max_interval", C.c_uint64),
+                ("sample_fraction", C.c_float), ("drift_threshold", C.c_float), ("seed", C.c_uint64)]
+
+
+REBUILD_SCHEDULE, REBUILD_ADAPTIVE = 0, 1
+
+
 class LayerStatsC(C.Structure):
     _fields_ = [("active_sum", C.c_uint64), ("touched_rows", C.c_uint64), ("input_nnz", C.c_uint64),
                 ("examples", C.c_uint64), ("steps", C.c_uint64), ("rebuilds", C.c_uint64)]
@@ -102,6 +110,9 @@ _PROTOS = {
     "kl_index_query_batch": (_S, [_H, _P, C.c_int, C.c_int, C.c_int, _P, _P, _P, C.c_int32, _P]),
     "kl_index_query_batch_noalloc": (_S, [_H, _P, C.c_int, C.c_int, C.c_int, _P, _P, _P, C.c_int32, _P]),
     "kl_index_query_sparse_batch": (_S, [_H, _P, _P, _P, C.c_int, C.c_int, _P, _P, _P, C.c_int32, _P]),
+    "kl_bolt_infer_batch": (_S, [_H, _P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_int, C.c_int, C.c_float, C.c_int,
+                                 C.c_int, _P, _P, _P, C.c_int]),
+    "kl_net_bolt_infer": (_S, [_H, C.c_int, _P, C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, _P, _P, _P, C.c_int]),
     "kl_index_export": (_S, [_H, _P, _P, _P]),
     "kl_index_import": (_S, [_H, _P, _P, _P]),
     "kl_net_create": (_S, [_H, C.POINTER(NetConfigC), _P, C.POINTER(_H)]),
@@ -118,6 +129,10 @@ _PROTOS = {
     "kl_net_layer_index": (_S, [_H, C.c_int, C.POINTER(_H)]),
     "kl_net_get_step": (_S, [_H, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "kl_net_set_step": (_S, [_H, C.c_uint64, C.c_uint64, C.c_uint64]),
+    "kl_net_set_rebuild_policy": (_S, [_H, C.POINTER(RebuildPolicyC)]),
+    "kl_net_rebuild_state": (_S, [_H, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    "kl_net_save": (_S, [_H, C.c_char_p]),
+    "kl_net_load": (_S, [_H, C.c_char_p]),
     "kl_net_stats": (_S, [_H, C.c_int, C.POINTER(LayerStatsC), C.c_int]),
     "kl_net_profile": (_S, [_H, C.c_int]),
     "kl_net_profile_read": (_S, [_H, C.c_int, _P, _P, C.c_int]),

@@ -701,6 +701,29 @@ class Network:
     def rebuild(self) -> None:
         check(self.lib.kl_net_rebuild(self.h), self.ctx.h, "kl_net_rebuild")
 
+    def set_rebuild_policy(self, adaptive: bool, min_interval: int = 10, max_interval: int = 1000,
+                           sample_fraction: float = 0.05, drift_threshold: float = 0.1, seed: int = 0) -> None:
+        """The reference's RebuildScheduler (adaptive=False) or one mongoose
+        AdaptiveScheduler per layer (crates/klearu-mongoose/src/scheduler.rs)."""
+        p = _lib.RebuildPolicyC(_lib.REBUILD_ADAPTIVE if adaptive else _lib.REBUILD_SCHEDULE, int(min_interval),
+                                int(max_interval), float(sample_fraction), float(drift_threshold), int(seed))
+        check(self.lib.kl_net_set_rebuild_policy(self.h, C.byref(p)), self.ctx.h, "kl_net_set_rebuild_policy")
+
+    def rebuild_state(self, layer: int) -> tuple[float, int, int]:
+        """(drift EMA, steps since the layer's last rebuild, its rebuild count)."""
+        e, s, r = C.c_float(), C.c_uint64(), C.c_uint64()
+        check(self.lib.kl_net_rebuild_state(self.h, layer, C.byref(e), C.byref(s), C.byref(r)), self.ctx.h,
+              "kl_net_rebuild_state")
+        return e.value, s.value, r.value
+
+    def save(self, path) -> None:
+        """Checkpoint every train-step state array (kl_net_save)."""
+        check(self.lib.kl_net_save(self.h, str(path).encode()), self.ctx.h, "kl_net_save")
+
+    def load(self, path) -> None:
+        """Restore a checkpoint written by save() from a network of the same configuration."""
+        check(self.lib.kl_net_load(self.h, str(path).encode()), self.ctx.h, "kl_net_load")
+
     def profile(self, enable: bool) -> None:
         check(self.lib.kl_net_profile(self.h, int(enable)), self.ctx.h, "kl_net_profile")
 

@@ -227,8 +227,9 @@ struct IndexImpl {
     ck_launch("clear");
   }
   // Query: padded results into qids/qcnt/qn, then CSR compaction.
-  void query(int n, int mode, uint32_t* out_ids, uint32_t* out_counts, int32_t* out_offsets,
-             int32_t capacity, int32_t* overflow) {
+  // Probe into per-query padded (id, count) lists sorted by id: qids / qcnt
+  // [n][L*cap], sizes in qn.  Returns the stride.
+  int probe_padded(int n) {
     const int stride = T.L * T.cap;
     qids.alloc((size_t)std::max(n, 1) * stride * 4);
     qcnt.alloc((size_t)std::max(n, 1) * stride * 4);
@@ -247,6 +248,11 @@ struct IndexImpl {
     a.err = ctx->err.as<int>();
     launch_probe(a, ctx->stream);
     ck_launch("probe");
+    return stride;
+  }
+  void query(int n, int mode, uint32_t* out_ids, uint32_t* out_counts, int32_t* out_offsets,
+             int32_t capacity, int32_t* overflow) {
+    const int stride = probe_padded(n);
     if (overflow) ck(cudaMemsetAsync(overflow, 0, 4, ctx->stream), "memset");
     launch_scan(qn.as<int32_t>(), out_offsets, n, nullptr, ctx->stream);
     ck_launch("scan");
@@ -795,6 +801,57 @@ extern "C" kl_status kl_index_query_batch(kl_index_t ix, const float* X, int n, 
   I.query(n, mode, out_ids, out_counts, out_offsets, capacity, overflow);
   KL_API_END
 }
+// SparseInferenceEngine::infer / infer_linear for a batch of inputs.
+static void bolt_body(IndexImpl& I, const void* W, int dtype, int64_t ldw, const float* bias, int N, const float* X,
+                      int n, int ldx, float mult, int base_top_k, int relu, uint32_t* out_ids, float* out_act,
+                      int32_t* out_n, int stride) {
+  require(dtype == KL_DTYPE_F32 || dtype == KL_DTYPE_BF16, "bolt: dtype must be KL_DTYPE_F32 or KL_DTYPE_BF16");
+  require(n >= 0 && N >= 0 && base_top_k >= 0 && stride >= 0, "bolt: negative size");
+  require(n == 0 || (X && W && out_ids && out_act && out_n && ldx >= I.hash->dh.d && ldw >= I.hash->dh.d),
+          "bolt: bad arguments");
+  support(I.T.L * I.T.cap <= probe_max_items(), "bolt: num_tables * bucket_capacity exceeds the probe's limit");
+  support(bolt_smem_bytes(I.hash->dh.d, I.T.L * I.T.cap) <= 200 * 1024, "bolt: input_dim too large");
+  if (n == 0) return;
+  // effective_k = (base_top_k as f32 * sparsity_multiplier) as usize (sparse_inference.rs:40)
+  const float ek = (float)base_top_k * mult;
+  const int k = !(ek > 0.0f) ? 0 : (ek >= 2147483647.0f ? 2147483647 : (int)ek);
+  I.hash_dense_to_bkt(dense_rows(X, KL_DTYPE_F32, n, ldx));
+  BoltArgs a;
+  a.cand_stride = I.probe_padded(n);
+  a.cand_ids = I.qids.as<uint32_t>();
+  a.cand_cnt = I.qcnt.as<uint32_t>();
+  a.cand_n = I.qn.as<int32_t>();
+  a.nq = n;
+  a.L = I.T.L;
+  a.k = k;
+  a.N = N;
+  a.d = I.hash->dh.d;
+  a.X = X;
+  a.ldx = ldx;
+  a.W = W;
+  a.wdtype = dtype;
+  a.ldw = ldw;
+  a.bias = bias;
+  a.relu = relu;
+  a.out_ids = out_ids;
+  a.out_act = out_act;
+  a.out_n = out_n;
+  a.out_stride = stride;
+  a.err = I.ctx->err.as<int>();
+  launch_bolt(a, I.ctx->stream);
+  ck_launch("bolt");
+}
+extern "C" kl_status kl_bolt_infer_batch(kl_index_t ix, const void* weights, int dtype, int ld, const float* bias,
+                                         int num_neurons, const float* X, int n, int ldx, float sparsity_multiplier,
+                                         int base_top_k, int relu, uint32_t* out_ids, float* out_act,
+                                         int32_t* out_n, int stride) {
+  if (!ix) return KL_EINVAL;
+  IndexImpl& I = *ix->ix;
+  KL_API_BEGIN(I.ctx)
+  bolt_body(I, weights, dtype, ld, bias, num_neurons, X, n, ldx, sparsity_multiplier, base_top_k, relu, out_ids,
+            out_act, out_n, stride);
+  KL_API_END
+}
 extern "C" kl_status kl_index_query_sparse_batch(kl_index_t ix, const int32_t* rowptr, const uint32_t* idx,
                                                  const float* val, int n, int mode, uint32_t* out_ids,
                                                  uint32_t* out_counts, int32_t* out_offsets, int32_t capacity,
@@ -1262,6 +1319,32 @@ struct kl_net_s {
   }
   void rebuild_all() {
     for (auto& L : layers) rebuild_layer(*L);
+  }
+
+  // Rebuild policy.  KL_REBUILD_SCHEDULE: the reference's RebuildScheduler
+  // (net.rs:109-116), all layers together.  KL_REBUILD_ADAPTIVE: one mongoose
+  // AdaptiveScheduler per layer (scheduler.rs:44-213), each layer rebuilt when
+  // its own sampled hash codes drift, then a new baseline is recorded.
+  kl_rebuild_policy policy{};
+  std::vector<std::unique_ptr<kl_adaptive_s>> adapt;
+  RowsView rows_of(const Layer& L) const {
+    return L.fm ? RowsView{L.W.p, wdtype, 1, L.ldw, L.N} : RowsView{L.W.p, wdtype, L.ldw, 1, L.N};
+  }
+  uint64_t adaptive_seed(int l) const {
+    return policy.seed + (uint64_t)l * 1000003ULL + layers[(size_t)l]->rebuilds * 7919ULL;
+  }
+  void after_step() {
+    if (policy.kind != KL_REBUILD_ADAPTIVE) {
+      if (sched.should_rebuild(step)) rebuild_all();
+      return;
+    }
+    for (size_t l = 0; l < layers.size(); ++l) {
+      Layer& L = *layers[l];
+      if (adaptive_check(adapt[l].get(), rows_of(L))) {
+        rebuild_layer(L);
+        adaptive_record(adapt[l].get(), L.index->hash, rows_of(L), nullptr, 0, adaptive_seed((int)l));
+      }
+    }
   }
 
   // Optimizer constants of the current step, copied to the device before
@@ -2013,7 +2096,7 @@ static void train_step_body(kl_net_t net, const kl_batch* b, double lr, int mode
     }
     net->layers[0]->input_nnz += (uint64_t)b->nnz;
     net->step += 1;
-    if (net->sched.should_rebuild(net->step)) net->rebuild_all();
+    net->after_step();
     return;
   }
   validate_batch(net, b);
@@ -2054,7 +2137,7 @@ static void train_step_body(kl_net_t net, const kl_batch* b, double lr, int mode
   net->layers[0]->input_nnz += (uint64_t)b->nnz;
   // net.rs:109-116
   net->step += 1;
-  if (net->sched.should_rebuild(net->step)) net->rebuild_all();
+  net->after_step();
 }
 
 extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double lr, int mode, float* loss,
@@ -2205,6 +2288,19 @@ extern "C" kl_status kl_net_predict_topk(kl_net_t net, const kl_batch* b, int k,
   KL_API_END
 }
 
+extern "C" kl_status kl_net_bolt_infer(kl_net_t net, int layer, const float* X, int n, int ldx,
+                                       float sparsity_multiplier, int base_top_k, int relu, uint32_t* out_ids,
+                                       float* out_act, int32_t* out_n, int stride) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  require(layer >= 0 && layer < (int)net->layers.size(), "bolt: layer out of range");
+  Layer& L = *net->layers[(size_t)layer];
+  support(!L.fm, "bolt: layer 0 (sparse input, feature-major weights) is not supported; use layers >= 1");
+  bolt_body(*L.index, L.W.p, net->wdtype, L.ldw, L.b.as<float>(), L.N, X, n, ldx, sparsity_multiplier, base_top_k,
+            relu, out_ids, out_act, out_n, stride);
+  KL_API_END
+}
+
 extern "C" kl_status kl_net_get_layer(kl_net_t net, int layer, float* w, float* bias, float* m, float* v,
                                       float* mb, float* vb) {
   if (!net) return KL_EINVAL;
@@ -2286,6 +2382,239 @@ extern "C" kl_status kl_net_set_step(kl_net_t net, uint64_t step, uint64_t next_
   net->sched.count = count;
   net->sched.cur = step;
   return KL_OK;
+}
+
+extern "C" kl_status kl_net_set_rebuild_policy(kl_net_t net, const kl_rebuild_policy* p) {
+  if (!net || !p) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  require(p->kind == KL_REBUILD_SCHEDULE || p->kind == KL_REBUILD_ADAPTIVE, "rebuild policy: unknown kind");
+  net->adapt.clear();
+  net->policy = *p;
+  if (p->kind == KL_REBUILD_ADAPTIVE) {
+    require(p->min_interval <= p->max_interval, "adaptive: min_interval must be <= max_interval (scheduler.rs:61-64)");
+    require(p->sample_fraction >= 0.f && p->sample_fraction <= 1.f, "adaptive: sample_fraction must be in [0, 1]");
+    require(p->drift_threshold >= 0.f && p->drift_threshold <= 1.f, "adaptive: drift_threshold must be in [0, 1]");
+    for (size_t l = 0; l < net->layers.size(); ++l) {
+      auto a = std::make_unique<kl_adaptive_s>();
+      a->ctx = net->ctx;
+      a->min_interval = (size_t)p->min_interval;
+      a->max_interval = (size_t)p->max_interval;
+      a->sample_fraction = p->sample_fraction;
+      a->drift_threshold = p->drift_threshold;
+      a->changed.alloc(4);
+      Layer& L = *net->layers[l];
+      adaptive_record(a.get(), L.index->hash, net->rows_of(L), nullptr, 0, net->adaptive_seed((int)l));
+      net->adapt.push_back(std::move(a));
+    }
+  }
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_rebuild_state(kl_net_t net, int layer, float* drift_ema, uint64_t* since,
+                                          uint64_t* rebuilds) {
+  if (!net || layer < 0 || layer >= (int)net->layers.size()) return KL_EINVAL;
+  const bool ad = net->policy.kind == KL_REBUILD_ADAPTIVE && (size_t)layer < net->adapt.size();
+  if (drift_ema) *drift_ema = ad ? net->adapt[(size_t)layer]->drift_ema : 0.f;
+  if (since) *since = ad ? (uint64_t)net->adapt[(size_t)layer]->steps_since_rebuild : 0;
+  if (rebuilds) *rebuilds = net->layers[(size_t)layer]->rebuilds;
+  return KL_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Checkpoint file: "KLB2CKPT" magic, format version, the configuration it was
+// written from, then every state array as raw little-endian bytes in the
+// device layout, and an FNV-1a 64-bit checksum of all preceding bytes.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr char kCkptMagic[8] = {'K', 'L', 'B', '2', 'C', 'K', 'P', 'T'};
+constexpr uint32_t kCkptVersion = 1;
+
+struct CkptFile {
+  FILE* f = nullptr;
+  uint64_t h = 1469598103934665603ULL;
+  bool writing = false;
+  ~CkptFile() {
+    if (f) std::fclose(f);
+  }
+  void mix(const void* p, size_t n) {
+    const unsigned char* c = static_cast<const unsigned char*>(p);
+    for (size_t i = 0; i < n; ++i) h = (h ^ c[i]) * 1099511628211ULL;
+  }
+  void put(const void* p, size_t n) {
+    mix(p, n);
+    if (n && std::fwrite(p, 1, n, f) != n) raise(KL_EINVAL, "checkpoint: write failed");
+  }
+  void get(void* p, size_t n) {
+    if (n && std::fread(p, 1, n, f) != n) raise(KL_EINVAL, "checkpoint: file truncated");
+    mix(p, n);
+  }
+  template <class T>
+  void put_v(T v) {
+    put(&v, sizeof(v));
+  }
+  template <class T>
+  T get_v() {
+    T v;
+    get(&v, sizeof(v));
+    return v;
+  }
+  // a device array, staged through a bounded host buffer
+  void dev(void* d, size_t n, cudaStream_t st) {
+    std::vector<unsigned char> buf(std::min<size_t>(n, (size_t)64 << 20));
+    for (size_t o = 0; o < n; o += buf.size()) {
+      const size_t c = std::min(buf.size(), n - o);
+      if (writing) {
+        ck(cudaMemcpyAsync(buf.data(), static_cast<unsigned char*>(d) + o, c, cudaMemcpyDeviceToHost, st), "copy");
+        ck(cudaStreamSynchronize(st), "sync");
+        put(buf.data(), c);
+      } else {
+        get(buf.data(), c);
+        ck(cudaMemcpyAsync(static_cast<unsigned char*>(d) + o, buf.data(), c, cudaMemcpyHostToDevice, st), "copy");
+        ck(cudaStreamSynchronize(st), "sync");
+      }
+    }
+  }
+  template <class T>
+  void field(T& v, const char* what, bool must_match) {
+    if (writing) {
+      put_v(v);
+    } else {
+      const T r = get_v<T>();
+      if (must_match && r != v) raise(KL_EINVAL, std::string("checkpoint: ") + what + " differs from this network's");
+      v = r;
+    }
+  }
+};
+
+void ckpt_body(kl_net_s* net, CkptFile& F) {
+  cudaStream_t st = net->ctx->stream;
+  ck(cudaStreamSynchronize(st), "sync");
+  int32_t nl = (int32_t)net->layers.size(), wd = net->wdtype, rank = net->rank, nranks = net->nranks;
+  F.field(nl, "layer count", true);
+  F.field(wd, "weight dtype", true);
+  F.field(rank, "rank", true);
+  F.field(nranks, "rank count", true);
+  F.field(net->step, "step", false);
+  F.field(net->sched.next, "next rebuild", false);
+  F.field(net->sched.count, "rebuild count", false);
+  const size_t wsz = net->wdtype == KL_DTYPE_BF16 ? 2 : 4;
+  for (auto& Lp : net->layers) {
+    Layer& L = *Lp;
+    IndexImpl& I = *L.index;
+    int32_t d = L.d, N = L.N, ldw = L.ldw, fm = L.fm, tl = I.T.L, nb = I.T.nb, cap = I.T.cap, bt = I.T.type;
+    uint32_t base = L.id_base;
+    F.field(d, "input_dim", true);
+    F.field(N, "num_neurons", true);
+    F.field(ldw, "weight pitch", true);
+    F.field(fm, "weight layout", true);
+    F.field(tl, "num_tables", true);
+    F.field(nb, "bucket count", true);
+    F.field(cap, "bucket capacity", true);
+    F.field(bt, "bucket type", true);
+    F.field(base, "neuron slice", true);
+    F.field(L.rebuilds, "layer rebuilds", false);
+    const size_t rows = L.fm ? (size_t)L.d : (size_t)L.N;
+    F.dev(L.W.p, rows * L.ldw * wsz, st);
+    F.dev(L.m.p, rows * L.ldw * 4, st);
+    F.dev(L.v.p, rows * L.ldw * 4, st);
+    F.dev(L.b.p, (size_t)L.N * 4, st);
+    F.dev(L.mb.p, (size_t)L.N * 4, st);
+    F.dev(L.vb.p, (size_t)L.N * 4, st);
+    const size_t LB = (size_t)I.T.L * I.T.nb;
+    F.dev(I.T.ids, LB * I.T.cap * 4, st);
+    F.dev(I.T.len, LB * 4, st);
+    F.dev(I.T.cnt, LB * 8, st);
+  }
+  // rebuild policy and the adaptive schedulers' state
+  int32_t kind = net->policy.kind;
+  F.field(kind, "rebuild policy", false);
+  if (!F.writing) {
+    net->policy.kind = kind;
+    net->adapt.clear();
+  }
+  F.field(net->policy.min_interval, "", false);
+  F.field(net->policy.max_interval, "", false);
+  F.field(net->policy.sample_fraction, "", false);
+  F.field(net->policy.drift_threshold, "", false);
+  F.field(net->policy.seed, "", false);
+  if (kind == KL_REBUILD_ADAPTIVE) {
+    for (size_t l = 0; l < net->layers.size(); ++l) {
+      if (!F.writing) {
+        auto a = std::make_unique<kl_adaptive_s>();
+        a->ctx = net->ctx;
+        a->min_interval = (size_t)net->policy.min_interval;
+        a->max_interval = (size_t)net->policy.max_interval;
+        a->sample_fraction = net->policy.sample_fraction;
+        a->drift_threshold = net->policy.drift_threshold;
+        a->changed.alloc(4);
+        a->hash = net->layers[l]->index->hash;
+        net->adapt.push_back(std::move(a));
+      }
+      kl_adaptive_s& a = *net->adapt[l];
+      uint64_t since = a.steps_since_rebuild, check = a.steps_since_check;
+      int32_t S = a.S;
+      F.field(a.drift_ema, "", false);
+      F.field(since, "", false);
+      F.field(check, "", false);
+      F.field(S, "", false);
+      a.steps_since_rebuild = (size_t)since;
+      a.steps_since_check = (size_t)check;
+      if (!F.writing) {
+        require(S >= 0 && S <= net->layers[l]->N, "checkpoint: bad adaptive sample size");
+        a.S = S;
+        const int L = a.hash->dh.L;
+        a.idx.alloc((size_t)S * 4);
+        a.base.alloc((size_t)S * L * 8);
+        a.cur.alloc((size_t)S * L * 8);
+        a.rows.alloc((size_t)S * a.hash->dh.d * 4);
+      }
+      if (S > 0) {
+        F.dev(a.idx.p, (size_t)S * 4, st);
+        F.dev(a.base.p, (size_t)S * a.hash->dh.L * 8, st);
+      }
+    }
+  }
+}
+}  // namespace
+
+extern "C" kl_status kl_net_save(kl_net_t net, const char* path) {
+  if (!net || !path) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  const std::string tmp = std::string(path) + ".tmp";
+  {
+    CkptFile F;
+    F.writing = true;
+    F.f = std::fopen(tmp.c_str(), "wb");
+    require(F.f != nullptr, std::string("checkpoint: cannot create ") + tmp);
+    F.put(kCkptMagic, 8);
+    F.put_v(kCkptVersion);
+    ckpt_body(net, F);
+    const uint64_t sum = F.h;
+    if (std::fwrite(&sum, 1, 8, F.f) != 8 || std::fflush(F.f) != 0) raise(KL_EINVAL, "checkpoint: write failed");
+  }
+  require(std::rename(tmp.c_str(), path) == 0, std::string("checkpoint: cannot rename to ") + path);
+  KL_API_END
+}
+
+extern "C" kl_status kl_net_load(kl_net_t net, const char* path) {
+  if (!net || !path) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  CkptFile F;
+  F.f = std::fopen(path, "rb");
+  require(F.f != nullptr, std::string("checkpoint: cannot open ") + path);
+  char magic[8];
+  F.get(magic, 8);
+  require(std::memcmp(magic, kCkptMagic, 8) == 0, "checkpoint: not a klearu_b200 network checkpoint");
+  require(F.get_v<uint32_t>() == kCkptVersion, "checkpoint: unsupported format version");
+  // read into the network, then verify the checksum; a corrupt file leaves the
+  // network in an undefined state, as the error says
+  ckpt_body(net, F);
+  const uint64_t want = F.h;
+  uint64_t sum = 0;
+  require(std::fread(&sum, 1, 8, F.f) == 8, "checkpoint: file truncated");
+  require(sum == want, "checkpoint: checksum mismatch (corrupt file); the network's state is undefined");
+  net->sched.cur = net->step;
+  KL_API_END
 }
 
 extern "C" kl_status kl_net_stats(kl_net_t net, int layer, kl_layer_stats* out, int reset) {

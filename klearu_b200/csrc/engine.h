@@ -136,6 +136,30 @@ struct ProbeArgs {
   bool fallback = true;  // empty selection -> every neuron (layer.rs:82-84); off on a shard
   int mode = 0;       // set by launch_probe: 0 radix sort, 1 small-N count array, 2 bitmap (all selected)
 };
+// BOLT sparse inference over per-query candidate lists (ids sorted by id
+// with their table counts, as the probe's COUNTS output).
+struct BoltArgs {
+  const uint32_t* cand_ids = nullptr;
+  const uint32_t* cand_cnt = nullptr;
+  const int32_t* cand_n = nullptr;
+  int cand_stride = 0;
+  int nq = 0, L = 0, k = 0, N = 0, d = 0;
+  const float* X = nullptr;
+  int64_t ldx = 0;
+  const void* W = nullptr;
+  int wdtype = 0;
+  int64_t ldw = 0;
+  const float* bias = nullptr;
+  int relu = 1;
+  uint32_t* out_ids = nullptr;
+  float* out_act = nullptr;
+  int32_t* out_n = nullptr;
+  int out_stride = 0;
+  int* err = nullptr;
+  int maxm = 0, count_bits = 0;  // set by launch_bolt
+};
+void launch_bolt(const BoltArgs& a, cudaStream_t st);
+size_t bolt_smem_bytes(int d, int cand_stride);
 int probe_max_items();  // largest L*cap the probe kernel holds in shared memory
 void launch_probe(const ProbeArgs& a, cudaStream_t st);
 

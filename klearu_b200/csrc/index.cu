@@ -654,6 +654,100 @@ void launch_tables_remove_hashed(const DevTables& T, const uint32_t* ids, const 
   count_launch();
 }
 
+// ---------------------------------------------------------------------------
+// BOLT sparse inference (crates/klearu-bolt/src/sparse_inference.rs:32-106):
+// per input, the index's candidates with their table counts (sorted by id),
+// ordered by count descending (ties by id ascending: a stable sort of the
+// id-sorted list; the reference's ties follow HashMap order), the first
+// effective_k kept, and for each kept neuron id < N the activation
+// sum_j x[j] * W[id][j] (sequential f32, the reference's order) + bias[id],
+// ReLU'd when `relu`.  One 512-thread block per input: the (count, position)
+// keys go through one or two stable radix passes on the count digits; the dot
+// products run one thread per kept neuron over x staged in shared memory.
+// ---------------------------------------------------------------------------
+template <class W>
+__global__ void __launch_bounds__(PB_NT) bolt_kernel(BoltArgs a) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  ProbeSmem& S = *reinterpret_cast<ProbeSmem*>(dyn);
+  float* xs = reinterpret_cast<float*>(dyn + sizeof(ProbeSmem));
+  uint32_t* A = reinterpret_cast<uint32_t*>(xs + round_up(a.d, 4));
+  uint32_t* Bf = A + a.maxm;
+  const int q = blockIdx.x;
+  const int M = min(a.cand_n[q], a.maxm);
+  const uint32_t* ids = a.cand_ids + (int64_t)q * a.cand_stride;
+  const uint32_t* cnt = a.cand_cnt + (int64_t)q * a.cand_stride;
+  for (int j = threadIdx.x; j < a.d; j += PB_NT) xs[j] = a.X[(int64_t)q * a.ldx + j];
+  // key: (L - count) above the 14-bit position, so an LSD sort of the count
+  // digits orders by count descending and keeps id order among equal counts
+  for (int i = threadIdx.x; i < M; i += PB_NT) {
+    const uint32_t c = min(cnt[i], (uint32_t)a.L);
+    A[i] = ((uint32_t)(a.L - c) << 14) | (uint32_t)i;
+  }
+  __syncthreads();
+  uint32_t* cur = A;
+  uint32_t* oth = Bf;
+  for (int shift = 14; shift < 14 + a.count_bits; shift += 8) {
+    probe_radix_pass(cur, oth, M, shift, S.hist, S.tmp);
+    uint32_t* t = cur;
+    cur = oth;
+    oth = t;
+  }
+  const int K = min(M, a.k);
+  // kept neurons with weights (id < N), compacted in order (neurons without
+  // weights are skipped after the truncation, as `weights.find` does)
+  const int IPT = (int)ceil_div(K, PB_NT);
+  int mine = 0;
+  for (int j = 0; j < IPT; ++j) {
+    const int r = threadIdx.x * IPT + j;
+    if (r < K && ids[cur[r] & 0x3FFFu] < (uint32_t)a.N) ++mine;
+  }
+  int total;
+  int pos = block_excl_scan<PB_NT>(mine, S.tmp, &total);
+  uint32_t* out_ids = a.out_ids + (int64_t)q * a.out_stride;
+  float* out_act = a.out_act + (int64_t)q * a.out_stride;
+  const W* Wp = static_cast<const W*>(a.W);
+  for (int j = 0; j < IPT; ++j) {
+    const int r = threadIdx.x * IPT + j;
+    if (r >= K) break;
+    const uint32_t id = ids[cur[r] & 0x3FFFu];
+    if (id >= (uint32_t)a.N) continue;
+    if (pos < a.out_stride) {
+      const W* row = Wp + (int64_t)id * a.ldw;
+      float acc = 0.0f;
+      for (int e = 0; e < a.d; ++e) acc = __fadd_rn(acc, __fmul_rn(xs[e], to_f(row[e])));
+      float v = __fadd_rn(acc, a.bias ? a.bias[id] : 0.0f);
+      if (a.relu) v = fmaxf(v, 0.0f);
+      out_ids[pos] = id;
+      out_act[pos] = v;
+    }
+    ++pos;
+  }
+  if (threadIdx.x == 0) {
+    a.out_n[q] = min(total, a.out_stride);
+    if (total > a.out_stride) atomicOr(a.err, DERR_CAPACITY);
+  }
+}
+
+void launch_bolt(const BoltArgs& a0, cudaStream_t st) {
+  if (a0.nq <= 0) return;
+  BoltArgs a = a0;
+  a.maxm = (int)round_up(std::max(a.cand_stride, 1), 32);
+  a.count_bits = 1;
+  while ((1 << a.count_bits) <= a.L) ++a.count_bits;
+  const size_t sm = sizeof(ProbeSmem) + (size_t)round_up(a.d, 4) * 4 + (size_t)2 * a.maxm * 4;
+  static OncePerDevice attr;
+  attr([&] {
+    cudaFuncSetAttribute(bolt_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(bolt_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  if (a.wdtype == KL_DTYPE_BF16) bolt_kernel<__nv_bfloat16><<<a.nq, PB_NT, sm, st>>>(a);
+  else bolt_kernel<float><<<a.nq, PB_NT, sm, st>>>(a);
+  count_launch();
+}
+size_t bolt_smem_bytes(int d, int cand_stride) {
+  return sizeof(ProbeSmem) + (size_t)round_up(d, 4) * 4 + (size_t)2 * round_up(std::max(cand_stride, 1), 32) * 4;
+}
+
 int probe_max_items() { return PB_MAXM; }
 
 void launch_probe(const ProbeArgs& a, cudaStream_t st) {
