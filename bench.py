@@ -263,7 +263,8 @@ def parity_check(rank: int, world: int, local: int) -> dict:
     batches = [gen.batch(B * world) for _ in range(3)]
     losses = [net.train_step_host(rank_slice(hb, rank, world) if world > 1 else hb, 1e-3) for hb in batches]
     base, n = (net.shard_info()[2:] if world > 1 else (0, 5000))
-    res = {"losses": losses, "hidden": net.get_layer(0), "out": net.get_layer(1), "base": base, "n": n}
+    res = {"losses": losses, "hidden": net.get_layer(0), "out": net.get_layer(1), "base": base, "n": n,
+           "feat": net.owned_features()}
     del net
     gathered = [None] * world
     if world > 1:
@@ -281,8 +282,12 @@ def parity_check(rank: int, world: int, local: int) -> dict:
     for g in gathered:
         bad += sum(abs(a - b) > 1e-4 * abs(b) + 1e-6 for a, b in zip(g["losses"], ol))
         lo, hi = g["base"], g["base"] + g["n"]
+        f0, nf = g["feat"]
         for k in ("weights", "bias", "m", "v", "mb", "vb"):
-            for a, b in ((g["hidden"][k], oh[k]), (g["out"][k], oo[k][lo:hi])):
+            ha, hb = g["hidden"][k], oh[k]
+            if k in ("m", "v"):  # a rank updates the Adam moments of its own feature rows
+                ha, hb = ha[:, f0:f0 + nf], hb[:, f0:f0 + nf]
+            for a, b in ((ha, hb), (g["out"][k], oo[k][lo:hi])):
                 if k == "weights":
                     tol = np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -7 + 1e-6
                 else:

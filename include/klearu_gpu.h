@@ -540,15 +540,23 @@ KL_API kl_status kl_dist_get_unique_id(void* id_host);
  *    state and LSH tables, whose buckets hold bucket_capacity / nranks ids so
  *    that an example's candidates over all shards stay num_tables *
  *    bucket_capacity, as in the unsharded network.
- *  - The sparse-input hidden layer is replicated and data parallel: in
- *    kl_net_train_step each rank passes its own `max_batch`-bounded batch
- *    (every rank the same number of examples); the step trains on the global
- *    batch of all ranks' examples in rank order (KL_MODE_BATCHED only).
- *  - Collectives per step (NCCL, on the context stream): all-gather of the
- *    batches and of the hidden activations, all-reduce of per-example
- *    selection counts, all-reduce of the label probabilities with a
- *    reduce-scatter of the output layer's input gradient, all-gather of the
- *    hidden local gradients and touched masks.
+ *  - The sparse-input hidden layer is data parallel: in kl_net_train_step
+ *    each rank passes exactly `max_batch` examples; the step trains on the
+ *    global batch of all ranks' examples in rank order (KL_MODE_BATCHED only).
+ *    Its weights and bias are replicated; its Adam moments are split by
+ *    feature: rank r updates feature rows [r*R, (r+1)*R), R = ceil(d/nranks)
+ *    (kl_net_owned_features), and the updated rows are all-gathered.
+ *  - Collectives per step (NCCL): all-gather of the batches and of the hidden
+ *    activations, all-reduce of per-example selection counts, all-reduce of
+ *    the label probabilities with a reduce-scatter of the output layer's
+ *    input gradient, all-gather of the hidden local gradients and touched
+ *    masks, and all-gather of the updated hidden weight rows (on a second
+ *    stream, overlapping the output layer's update).
+ *  - A rank's batch that cannot be exchanged (another example count, or more
+ *    than 512 nnz / 32 labels per example on average) does not make that rank
+ *    leave the collective sequence: it is sent empty with a fault flag, every
+ *    rank applies the step with a zero learning rate and reports KL_EBOUNDS
+ *    (example count) or KL_ECAPACITY at its next synchronising call.
  *  - Supported shapes: two layers, non-softmax output, output sampling that
  *    selects every candidate (Vanilla, or TopK with top_k >= num_tables *
  *    bucket_capacity).  Per example at most 512 input nnz and 32 labels.
@@ -565,6 +573,11 @@ KL_API kl_status kl_net_create_sharded(kl_ctx_t ctx, const kl_net_config* cfg_ho
  * unsharded network). */
 KL_API kl_status kl_net_shard_info(kl_net_t net, int* rank_host, int* nranks_host, uint32_t* id_base_host,
                             int* num_local_host);
+/* The hidden layer's feature rows [first, first + count) whose Adam moments
+ * this rank updates (every feature of an unsharded network).  In
+ * kl_net_get_layer(0)'s [neuron][feature] layout these are columns; the
+ * moments of the other columns are another rank's. */
+KL_API kl_status kl_net_owned_features(kl_net_t net, uint32_t* first_host, uint32_t* count_host);
 
 /* ---------------------------------------------------------------------------
  * Deja Vu sparse FFN.

@@ -142,6 +142,7 @@ _PROTOS = {
     "kl_dist_get_unique_id": (_S, [_P]),
     "kl_net_create_sharded": (_S, [_H, C.POINTER(NetConfigC), _P, _P, C.c_int, C.c_int, C.POINTER(_H)]),
     "kl_net_shard_info": (_S, [_H, _P, _P, _P, _P]),
+    "kl_net_owned_features": (_S, [_H, _P, _P]),
     "kl_adaptive_create": (_S, [_H, C.c_uint64, C.c_uint64, C.c_float, C.c_float, C.POINTER(_H)]),
     "kl_predictor_create": (_S, [_H, C.c_int, C.c_int, C.c_int, _P, _P, _P, _P, C.POINTER(_H)]),
     "kl_predictor_destroy": (_S, [_H]),

@@ -513,6 +513,12 @@ class Network:
     def _dev(self) -> str:
         return f"cuda:{self.ctx.device}"
 
+    def owned_features(self) -> tuple[int, int]:
+        """(first, count): the hidden layer's feature rows whose Adam moments this rank updates."""
+        f, n = C.c_uint32(), C.c_uint32()
+        check(self.lib.kl_net_owned_features(self.h, C.byref(f), C.byref(n)))
+        return f.value, n.value
+
     def shard_info(self) -> tuple[int, int, int, int]:
         """(rank, nranks, global id of the first local output neuron, local output neurons)."""
         r, n, nl = C.c_int(), C.c_int(), C.c_int()

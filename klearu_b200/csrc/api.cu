@@ -1139,6 +1139,7 @@ struct Layer {
   int nchunk = 0;
   int id_bits = 0;
   uint32_t id_base = 0;  // global id of row 0 (the rank's slice of a sharded output layer)
+  int f0 = 0, nf = 0;    // feature rows whose optimizer state this rank updates (layer 0; all rows unsharded)
   DBuf W, b, m, v, mb, vb;
   std::shared_ptr<IndexImpl> index;
   // per-step buffers
@@ -1201,6 +1202,9 @@ struct kl_net_s {
   HostSlot hslots[2];
   int hnext = 0;
   cudaStream_t copy_stream = nullptr;
+  // sharded step: the hidden-weight all-gather's stream and its ordering events
+  cudaStream_t comm_stream = nullptr;
+  cudaEvent_t ev_hidden = nullptr, ev_gather = nullptr;
   // neuron sharding of the output layer (kl_net_create_sharded)
   int rank = 0, nranks = 1;
   ncclComm_t comm = nullptr;
@@ -1272,6 +1276,9 @@ struct kl_net_s {
       if (h.used) cudaEventDestroy(h.used);
     }
     if (copy_stream) cudaStreamDestroy(copy_stream);
+    if (comm_stream) cudaStreamSynchronize(comm_stream), cudaStreamDestroy(comm_stream);
+    if (ev_hidden) cudaEventDestroy(ev_hidden);
+    if (ev_gather) cudaEventDestroy(ev_gather);
     if (gexec) cudaGraphExecDestroy(gexec);
     if (cap_stream) cudaStreamDestroy(cap_stream);
     if (comm) ncclCommDestroy(comm);
@@ -1540,11 +1547,13 @@ struct kl_net_s {
   // Optimizer updates of every layer for examples [s0, s0+nq) of the batch.
   void update_layers(const kl_batch& b, int s0, int nq, double lr) {
     (void)lr;  // the step's optimizer constants are in dopt (upload_opt)
+    for (int l = (int)layers.size() - 1; l >= 0; --l) update_layer(l, b, s0, nq);
+  }
+  void update_layer(int l, const kl_batch& b, int s0, int nq) {
     cudaStream_t st = ctx->stream;
-    const int nL = (int)layers.size();
     const OptStep* o = dopt.as<OptStep>();
     SparseIn in{b.rowptr + s0, b.idx, b.val, nq};
-    for (int l = nL - 1; l >= 0; --l) {
+    {
       Phase ph(this, l, KL_PHASE_UPDATE);
       Layer& L = *layers[l];
       unsigned long long* stat = L.stats.as<unsigned long long>() + 1;
@@ -1552,7 +1561,7 @@ struct kl_net_s {
       SegScratch S{L.hist.as<uint32_t>(), L.cur.as<uint32_t>(), L.touched.as<uint32_t>(), L.ctr.as<uint32_t>(),
                    L.ent_s.as<uint32_t>(), L.ent_v.as<float>(), L.fslot.as<uint32_t>(), L.flong.as<uint32_t>()};
       if (L.fm) {
-        launch_fm_update(L.W.p, wdtype, L.ldw, L.d, L.N, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
+        launch_fm_update(L.W.p, wdtype, L.ldw, L.d, L.f0, L.nf, L.N, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
                          L.mb.as<float>(), L.vb.as<float>(), in, L.lgd.as<float>(), L.ldN, L.tmask.as<uint32_t>(),
                          S, L.gfeat.as<float>(), o, stat, ctx->err.as<int>(), st, &kl_net_s::stream_hook, this);
         ck_launch("fm update");
@@ -1666,7 +1675,24 @@ struct kl_net_s {
       launch_shard_or_masks(H.tmask.as<uint32_t>(), tmask_all.as<uint32_t>(), P, nw, st);
       ck_launch("or masks");
     }
-    update_layers(gb, 0, PB, lr);
+    // (6) The hidden layer's update first, over this rank's feature rows only;
+    // then an in-place all-gather of the updated rows on the comm stream, which
+    // overlaps the output layer's update on the context stream.  The next
+    // step's kernels wait for it.
+    update_layer(0, gb, 0, PB);
+    {
+      const int R = (int)ceil_div(H.d, P);
+      ck(cudaEventRecord(ev_hidden, st), "event");
+      ck(cudaStreamWaitEvent(comm_stream, ev_hidden, 0), "stream wait");
+      const size_t esz = wdtype == KL_DTYPE_BF16 ? 2 : 4;
+      char* w = static_cast<char*>(H.W.p);
+      nccl_ck(ncclAllGather(w + (size_t)rank * R * H.ldw * esz, w, (size_t)R * H.ldw,
+                            wdtype == KL_DTYPE_BF16 ? ncclBfloat16 : ncclFloat32, comm, comm_stream),
+              "all-gather hidden weights");
+      ck(cudaEventRecord(ev_gather, comm_stream), "event");
+    }
+    update_layer(1, gb, 0, PB);
+    ck(cudaStreamWaitEvent(st, ev_gather, 0), "stream wait");
   }
 
   // ---- CUDA graph of the batched single-GPU train step ------------------
@@ -1854,13 +1880,24 @@ void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_
   const size_t wsz = net->wdtype == KL_DTYPE_BF16 ? 2 : 4;
   const size_t nrows_store = L.fm ? (size_t)L.d : (size_t)L.N;
   const size_t welems = nrows_store * L.ldw;
-  L.W.alloc(welems * wsz);
+  // A sharded network's hidden layer updates feature rows in P equal slices of
+  // R = ceil(d / P) rows and all-gathers them in place: W holds P * R rows.
+  L.f0 = 0;
+  L.nf = L.d;
+  size_t wrows = nrows_store;
+  if (L.fm && net->nranks > 1) {
+    const int R = (int)ceil_div(L.d, net->nranks);
+    L.f0 = std::min(L.d, net->rank * R);
+    L.nf = std::min(L.d, L.f0 + R) - L.f0;
+    wrows = (size_t)R * net->nranks;
+  }
+  L.W.alloc(wrows * L.ldw * wsz);
+  ck(cudaMemsetAsync(L.W.p, 0, wrows * L.ldw * wsz, st), "memset");
   L.m.alloc(welems * 4);
   L.v.alloc(welems * 4);
   L.b.alloc((size_t)L.N * 4);
   L.mb.alloc((size_t)L.N * 4);
   L.vb.alloc((size_t)L.N * 4);
-  ck(cudaMemsetAsync(L.W.p, 0, welems * wsz, st), "memset");
   ck(cudaMemsetAsync(L.m.p, 0, welems * 4, st), "memset");
   ck(cudaMemsetAsync(L.v.p, 0, welems * 4, st), "memset");
   ck(cudaMemsetAsync(L.mb.p, 0, (size_t)L.N * 4, st), "memset");
@@ -2045,6 +2082,9 @@ kl_net_s* create_net(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init
     cap_b.nnz = P * net->nnz_cap;
     cap_b.nlabels = P * net->lab_cap;
     net->ensure_batch_buffers(cap_b);
+    ck(cudaStreamCreateWithFlags(&net->comm_stream, cudaStreamNonBlocking), "comm stream");
+    ck(cudaEventCreateWithFlags(&net->ev_hidden, cudaEventDisableTiming), "event");
+    ck(cudaEventCreateWithFlags(&net->ev_gather, cudaEventDisableTiming), "event");
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof(id));
     nccl_ck(ncclCommInitRank(&net->comm, nranks, id, rank), "ncclCommInitRank");
@@ -2486,6 +2526,28 @@ struct CkptFile {
   }
 };
 
+// FNV-1a over a hash family's kind, sizes and parameter arrays.
+uint64_t hash_fingerprint(const DevHash& h, cudaStream_t st) {
+  uint64_t f = 1469598103934665603ULL;
+  auto mix = [&](const void* p, size_t n) {
+    const unsigned char* c = static_cast<const unsigned char*>(p);
+    for (size_t i = 0; i < n; ++i) f = (f ^ c[i]) * 1099511628211ULL;
+  };
+  const int hdr[6] = {h.kind, h.d, h.k, h.L, h.w, h.dpad};
+  mix(hdr, sizeof(hdr));
+  auto dev = [&](const void* p, size_t n) {
+    if (!p || !n) return;
+    std::vector<unsigned char> b(n);
+    ck(cudaMemcpyAsync(b.data(), p, n, cudaMemcpyDeviceToHost, st), "copy");
+    ck(cudaStreamSynchronize(st), "sync");
+    mix(b.data(), n);
+  };
+  dev(h.planes, (size_t)h.LK * h.dpad);
+  dev(h.windows, (size_t)h.L * h.k * h.w * 4);
+  dev(h.perms, (size_t)h.L * h.d * 4);
+  return f;
+}
+
 void ckpt_body(kl_net_s* net, CkptFile& F) {
   cudaStream_t st = net->ctx->stream;
   ck(cudaStreamSynchronize(st), "sync");
@@ -2512,6 +2574,10 @@ void ckpt_body(kl_net_s* net, CkptFile& F) {
     F.field(cap, "bucket capacity", true);
     F.field(bt, "bucket type", true);
     F.field(base, "neuron slice", true);
+    // the hash family is part of the network's construction, not of its state:
+    // a checkpoint restores only into a network built with the same parameters
+    uint64_t hfp = hash_fingerprint(I.hash->dh, st);
+    F.field(hfp, "LSH hash parameters (planes / windows / permutations)", true);
     F.field(L.rebuilds, "layer rebuilds", false);
     const size_t rows = L.fm ? (size_t)L.d : (size_t)L.N;
     F.dev(L.W.p, rows * L.ldw * wsz, st);
@@ -2691,6 +2757,12 @@ extern "C" kl_status kl_net_create_sharded(kl_ctx_t ctx, const kl_net_config* cf
   *out = nullptr;
   *out = create_net(ctx, cfg, init, unique_id, rank, nranks);
   KL_API_END
+}
+extern "C" kl_status kl_net_owned_features(kl_net_t net, uint32_t* first, uint32_t* count) {
+  if (!net) return KL_EINVAL;
+  if (first) *first = (uint32_t)net->layers[0]->f0;
+  if (count) *count = (uint32_t)net->layers[0]->nf;
+  return KL_OK;
 }
 extern "C" kl_status kl_net_shard_info(kl_net_t net, int* rank_host, int* nranks_host, uint32_t* id_base_host,
                                        int* num_local_host) {

@@ -278,7 +278,9 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
 // rows of the touched features, [min(d, nnz)][ldl] f32 scratch.  around_adam
 // (nullable) is called with 0 before and 1 after the streaming Adam launch.
 // S.slot must hold round_up(d, 4) + 4 entries (stages copy it in 16-byte units).
-void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
+// Update of feature rows [f0, f0 + nf) of the feature-major layer (all d rows:
+// f0 = 0, nf = d); the bias of every neuron is updated in every call.
+void launch_fm_update(const void* W, int wdtype, int ldw, int d, int f0, int nf, int N, float* bias, float* m,
                       float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
                       const uint32_t* touched_mask, SegScratch S, float* G, const OptStep* o,
                       unsigned long long* stat_touched, int* err, cudaStream_t st,

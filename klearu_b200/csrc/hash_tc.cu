@@ -44,7 +44,7 @@ constexpr int TP_M = 128;          // rows per tile (MMA M)
 constexpr int TP_KC = 64;          // K elements per TMA box / stage: 128-byte rows
 constexpr int TP_ASTAGE = TP_M * TP_KC * 2;
 constexpr int TP_NT = 192;         // 6 warps
-constexpr int TP_SMEM_MAX = 225 * 1024;
+constexpr int TP_SMEM_MAX = 218 * 1024;  // + ~4.5 KB static, under the 227 KB per block
 
 __device__ __forceinline__ void tp_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tp_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
@@ -71,14 +71,20 @@ __device__ __forceinline__ void tp_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void tp_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+// 16 consecutive accumulator columns of this thread's lane; tp_ld_wait()
+// before the registers are read.
+__device__ __forceinline__ void tp_ld16_async(uint32_t taddr, uint32_t* v) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
       "%15}, [%16];\n"
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
         "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tp_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void tp_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  tp_ld16_async(taddr, v);
+  tp_ld_wait();
 }
 // 2-D tiled TMA load (no multicast): box at element coordinates (x, y).
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -106,10 +112,15 @@ struct TpArgs {
 };
 
 // Shared memory: [B: kc chunks of Nh x 128 B][A ring: nst x 16 KB], 1024-aligned.
+// MINABS: the per-table min |projection| is wanted (a column-by-column
+// epilogue); otherwise the epilogue packs the sign bits of 64 columns at a
+// time and cuts the tables' codes out of the packed words.
+template <bool MINABS>
 __global__ void __launch_bounds__(TP_NT, 1)
     proj_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap pmap, TpArgs a) {
   extern __shared__ unsigned char tp_dyn[];
   __shared__ uint64_t full[16], empty[16], bfull, acc_full[2], acc_empty[2];
+  __shared__ uint32_t ebits[4][9][32];  // per epilogue warp: packed sign bits [word][lane] (+1 spare word)
   __shared__ uint32_t tmem_s;
   __shared__ int fail;
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tp_dyn) + 1023) & ~uintptr_t(1023));
@@ -216,6 +227,45 @@ __global__ void __launch_bounds__(TP_NT, 1)
       tp_fence_after();
       const int row = t * TP_M + quad * 32 + lane;
       const uint32_t base = tmem + ((uint32_t)(quad * 32) << 16) + buf * (uint32_t)a.Nh;
+      if (!MINABS) {
+        // sign bits: 64 columns per round (4 loads, one wait), 2 words each
+        uint32_t (*eb)[32] = ebits[quad];
+#pragma unroll
+        for (int g64 = 0; g64 < 4; ++g64) {
+          if (g64 * 64 < ncols) {
+            uint32_t v[64];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) tp_ld16_async(base + (uint32_t)(g64 * 64 + u * 16), v + u * 16);
+            tp_ld_wait();
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int qq = 0; qq < 32; ++qq) {
+              lo |= (__uint_as_float(v[qq]) >= 0.0f ? 1u : 0u) << qq;
+              hi |= (__uint_as_float(v[32 + qq]) >= 0.0f ? 1u : 0u) << qq;
+            }
+            eb[2 * g64][lane] = lo;
+            eb[2 * g64 + 1][lane] = hi;
+          }
+        }
+        eb[8][lane] = 0u;
+        tp_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);  // the accumulator is free again
+        if (row < a.n) {
+          const int ntab = ncols / kbits;
+          const uint32_t kmask = kbits >= 32 ? 0xffffffffu : (1u << kbits) - 1u;
+          for (int lt = 0; lt < ntab; ++lt) {
+            const int p0 = lt * kbits, w0 = p0 >> 5, off = p0 & 31;
+            const uint64_t win = (uint64_t)eb[w0][lane] | ((uint64_t)eb[w0 + 1][lane] << 32);
+            const uint64_t code = (uint64_t)((uint32_t)(win >> off) & kmask);
+            const int tab = g * a.tph + lt;
+            if (a.out.codes) a.out.codes[(int64_t)row * a.L + tab] = code;
+            if (a.out.bkt) a.out.bkt[(int64_t)tab * a.out.bkt_ld + row] = (uint16_t)(code & a.out.nb_mask);
+          }
+        }
+        __syncwarp();  // eb is rewritten by the next tile
+        continue;
+      }
       int tab = g * a.tph, bit = 0;
       uint64_t code = 0;
       float mn = INFINITY;
@@ -323,7 +373,10 @@ bool launch_proj_tc(const DevHash& h, const DenseIn& in, const HashOut& out, int
   CUtensorMap xmap;
   if (!make_map(&xmap, in.X, in.n, h.d, in.ld_row, TP_KC, TP_M)) return false;
   static OncePerDevice attr;
-  attr([&] { cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM_MAX); });
+  attr([&] {
+    cudaFuncSetAttribute(proj_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM_MAX);
+    cudaFuncSetAttribute(proj_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM_MAX);
+  });
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -345,7 +398,8 @@ bool launch_proj_tc(const DevHash& h, const DenseIn& in, const HashOut& out, int
   a.out = out;
   a.err = err;
   const size_t smem = 1024 + (size_t)tp->kc * tp->Nh * 128 + (size_t)tp->nst * TP_ASTAGE;
-  proj_tc_kernel<<<grid, TP_NT, smem, st>>>(xmap, tp->map, a);
+  if (out.min_abs) proj_tc_kernel<true><<<grid, TP_NT, smem, st>>>(xmap, tp->map, a);
+  else proj_tc_kernel<false><<<grid, TP_NT, smem, st>>>(xmap, tp->map, a);
   count_launch();
   return true;
 }

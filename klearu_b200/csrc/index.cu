@@ -243,6 +243,67 @@ __device__ void probe_radix_pass(const uint32_t* in, uint32_t* out, int M, int s
   __syncthreads();
 }
 
+// Mode 2 (every candidate selected, no counts) as its own kernel with a
+// block size chosen from the bitmap's size: the union sorted by id is the set
+// bits of a presence bitmap over the N neuron ids.  A shard's small bitmap
+// (N/P ids) gets 128-thread blocks, so that more queries run per SM.
+template <int NT>
+__global__ void __launch_bounds__(NT) probe_bitmap_kernel(ProbeArgs a) {
+  extern __shared__ __align__(16) uint32_t bm[];
+  __shared__ int tmp[40];
+  constexpr int NW = NT / 32;
+  const int q = blockIdx.x;
+  const DevTables& T = a.T;
+  const int w_ = threadIdx.x >> 5, l_ = threadIdx.x & 31;
+  const int nwd = (a.N + 31) >> 5;
+  for (int i = threadIdx.x; i < nwd; i += NT) bm[i] = 0;
+  __syncthreads();
+  for (int t = w_; t < T.L; t += NW) {
+    const int b = a.bkt[(int64_t)t * a.bkt_ld + q];
+    const int n = (int)min(T.len[(int64_t)t * T.nb + b], (uint32_t)T.cap);
+    const uint32_t* src = T.ids + ((int64_t)t * T.nb + b) * T.cap;
+    for (int j0 = 0; j0 < n; j0 += 128) {  // 4 loads in flight per lane
+      uint32_t id[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) id[u] = j0 + u * 32 + l_ < n ? src[j0 + u * 32 + l_] : 0xffffffffu;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (id[u] < (uint32_t)a.N) atomicOr(&bm[id[u] >> 5], 1u << (id[u] & 31));
+    }
+  }
+  __syncthreads();
+  const int wpt = (nwd + NT - 1) / NT;  // contiguous words per thread
+  const int w0 = threadIdx.x * wpt, w1 = min(nwd, w0 + wpt);
+  int c = 0;
+  for (int i = w0; i < w1; ++i) c += __popc(bm[i]);
+  int nsel;
+  int pos = block_excl_scan<NT>(c, tmp, &nsel);
+  uint32_t* out_ids = a.out_ids + (int64_t)q * a.out_stride;
+  int nout;
+  if (nsel == 0 && a.fallback) {
+    // fallback: every neuron (layer.rs:82-84)
+    nout = min(a.N, a.out_stride);
+    if (a.N > a.out_stride && threadIdx.x == 0) atomicOr(a.err, DERR_CAPACITY);
+    for (int j = threadIdx.x; j < nout; j += NT) out_ids[j] = (uint32_t)j;
+  } else {
+    for (int i = w0; i < w1; ++i) {
+      uint32_t bits = bm[i];
+      while (bits) {
+        const int j = __ffs(bits) - 1;
+        bits &= bits - 1;
+        if (pos < a.out_stride) out_ids[pos] = (uint32_t)(i * 32 + j);
+        ++pos;
+      }
+    }
+    nout = min(nsel, a.out_stride);
+    if (nsel > a.out_stride && threadIdx.x == 0) atomicOr(a.err, DERR_CAPACITY);
+  }
+  if (threadIdx.x == 0) {
+    a.out_n[q] = nout;
+    if (a.stat_active) atomicAdd(a.stat_active, (unsigned long long)nout);
+  }
+}
+
 __global__ void __launch_bounds__(PB_NT) probe_kernel(ProbeArgs a) {
   extern __shared__ __align__(16) unsigned char dyn[];
   ProbeSmem& S = *reinterpret_cast<ProbeSmem*>(dyn);
@@ -276,61 +337,7 @@ __global__ void __launch_bounds__(PB_NT) probe_kernel(ProbeArgs a) {
   }
   const int M = tot;
   const int w_ = threadIdx.x >> 5, l_ = threadIdx.x & 31;
-  if (a.mode == 2) {
-    // Every candidate is selected and no counts are wanted (Vanilla, or TopK
-    // with top_k >= L*cap >= |union|): the union sorted by id is the set bits
-    // of a presence bitmap over the N neuron ids.  Ids >= N are dropped
-    // (retain, layer.rs:87); the network's own tables never hold them.
-    uint32_t* bm = A;
-    const int nwd = (a.N + 31) >> 5;
-    for (int i = threadIdx.x; i < nwd; i += PB_NT) bm[i] = 0;
-    __syncthreads();
-    for (int t = w_; t < T.L; t += PB_NW) {
-      const int b = S.bsel[t];
-      const uint32_t* src = T.ids + ((int64_t)t * T.nb + b) * T.cap;
-      const int n = S.lens_off[t + 1] - S.lens_off[t];
-      for (int j0 = 0; j0 < n; j0 += 128) {  // 4 loads in flight per lane
-        uint32_t id[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) id[u] = j0 + u * 32 + l_ < n ? src[j0 + u * 32 + l_] : 0xffffffffu;
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (id[u] < (uint32_t)a.N) atomicOr(&bm[id[u] >> 5], 1u << (id[u] & 31));
-      }
-    }
-    __syncthreads();
-    const int wpt = (nwd + PB_NT - 1) / PB_NT;  // contiguous words per thread
-    const int w0 = threadIdx.x * wpt, w1 = min(nwd, w0 + wpt);
-    int c = 0;
-    for (int i = w0; i < w1; ++i) c += __popc(bm[i]);
-    int nsel;
-    int pos = block_excl_scan<PB_NT>(c, S.tmp, &nsel);
-    uint32_t* out_ids = a.out_ids + (int64_t)q * a.out_stride;
-    int nout;
-    if (nsel == 0 && a.fallback) {
-      // fallback: every neuron (layer.rs:82-84)
-      nout = min(a.N, a.out_stride);
-      if (a.N > a.out_stride && threadIdx.x == 0) atomicOr(a.err, DERR_CAPACITY);
-      for (int j = threadIdx.x; j < nout; j += PB_NT) out_ids[j] = (uint32_t)j;
-    } else {
-      for (int i = w0; i < w1; ++i) {
-        uint32_t bits = bm[i];
-        while (bits) {
-          const int j = __ffs(bits) - 1;
-          bits &= bits - 1;
-          if (pos < a.out_stride) out_ids[pos] = (uint32_t)(i * 32 + j);
-          ++pos;
-        }
-      }
-      nout = min(nsel, a.out_stride);
-      if (nsel > a.out_stride && threadIdx.x == 0) atomicOr(a.err, DERR_CAPACITY);
-    }
-    if (threadIdx.x == 0) {
-      a.out_n[q] = nout;
-      if (a.stat_active) atomicAdd(a.stat_active, (unsigned long long)nout);
-    }
-    return;
-  }
+  // mode 2 (every candidate selected) runs in probe_bitmap_kernel
   uint32_t* uid;
   uint32_t* ucnt;
   int U;
@@ -768,6 +775,19 @@ void launch_probe(const ProbeArgs& a, cudaStream_t st) {
       b.maxm = (int)round_up(a.N, 32);
       words = 4 * (size_t)b.maxm;
     }
+  }
+  if (b.mode == 2) {
+    const int nwd = (a.N + 31) / 32;
+    const size_t bsm = (size_t)nwd * 4;
+    static OncePerDevice battr;
+    battr([&] {
+      cudaFuncSetAttribute(probe_bitmap_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, PB_MAXWORDS * 4);
+      cudaFuncSetAttribute(probe_bitmap_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, PB_MAXWORDS * 4);
+    });
+    if (nwd >= 8192) probe_bitmap_kernel<512><<<a.nq, 512, bsm, st>>>(b);
+    else probe_bitmap_kernel<128><<<a.nq, 128, bsm, st>>>(b);
+    count_launch();
+    return;
   }
   const size_t sm = sizeof(ProbeSmem) + words * 4;
   static OncePerDevice attr;

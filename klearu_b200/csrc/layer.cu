@@ -456,7 +456,9 @@ __global__ void rm_touch_kernel(ActiveSet A, uint32_t* hist, uint32_t* touched, 
   const int pos = warp_append(valid && old == 0, &ctr[0]);
   if (pos >= 0) touched[pos] = id;
 }
-__global__ void fm_touch_kernel(SparseIn in, uint32_t* hist, uint32_t* touched, uint32_t* ctr, int d) {
+// Feature rows [f0, f0 + nf) only (a rank's slice of a sharded hidden update).
+__global__ void fm_touch_kernel(SparseIn in, uint32_t* hist, uint32_t* touched, uint32_t* ctr, uint32_t f0,
+                                uint32_t nf) {
   const int s = blockIdx.x;
   const int beg = in.rowptr[s], end = in.rowptr[s + 1];
   for (int base = beg; base < end; base += blockDim.x) {
@@ -465,7 +467,7 @@ __global__ void fm_touch_kernel(SparseIn in, uint32_t* hist, uint32_t* touched, 
     uint32_t f = 0, old = 1;
     if (valid) {
       f = in.idx[e];
-      valid = f < (uint32_t)d;
+      valid = f - f0 < nf;
       if (valid) old = atomicAdd(&hist[f], 1u);
     }
     const int pos = warp_append(valid && old == 0, &ctr[0]);
@@ -496,11 +498,12 @@ __global__ void rm_scatter_kernel(ActiveSet A, uint32_t* cur, uint32_t* ent_s, f
   ent_s[pos] = (uint32_t)s;
   ent_v[pos] = A.lg[o];
 }
-__global__ void fm_scatter_kernel(SparseIn in, uint32_t* cur, uint32_t* ent_s, float* ent_v, int d) {
+__global__ void fm_scatter_kernel(SparseIn in, uint32_t* cur, uint32_t* ent_s, float* ent_v, uint32_t f0,
+                                  uint32_t nf) {
   const int s = blockIdx.x;
   for (int e = in.rowptr[s] + threadIdx.x; e < in.rowptr[s + 1]; e += blockDim.x) {
     const uint32_t f = in.idx[e];
-    if (f >= (uint32_t)d) continue;
+    if (f - f0 >= nf) continue;
     const uint32_t pos = atomicAdd(&cur[f], 1u);
     ent_s[pos] = (uint32_t)s;
     ent_v[pos] = in.val[e];
@@ -687,8 +690,9 @@ __global__ void rm_dense_scatter_kernel(ActiveSet A, const uint32_t* slot_of, fl
     if (id[u] != 0xffffffffu) LGd[(int64_t)s * ldu + sl[u]] = lg[u];
 }
 
-constexpr int RDU_RPW = 4;               // slots per warp
-constexpr int RDU_ROWS = 8 * RDU_RPW;    // slots per block (8 warps)
+// Slots per warp RPW (a template parameter: 4, or 2 / 1 when a long sample
+// loop meets few touched rows -- a shard over a large global batch -- so that
+// more blocks share the work); 8 * RPW slots per block (8 warps).
 constexpr int RDU_COLS = 32;             // columns per block (one per lane)
 constexpr int RDU_S = 32;                // samples per staged chunk
 constexpr int RDU_ST = 4;                // cp.async pipeline stages
@@ -701,26 +705,40 @@ constexpr int RDU_ST = 4;                // cp.async pipeline stages
 // not active) leaves a sum unchanged and the result equals the sum over the
 // active samples in ascending order (finite activations assumed).  The
 // gradient matrix is left as read; rm_lg_zero_kernel restores its zeros.
-template <class W, bool BIAS>
-__device__ __forceinline__ void rdu_sum_chunk(const float (*xs)[RDU_COLS], const float (*ls)[RDU_ROWS], int ns,
+template <class W, bool BIAS, int RPW>
+__device__ __forceinline__ void rdu_sum_chunk(const float (*xs)[RDU_COLS], const float (*ls)[8 * RPW], int ns,
                                               int w, int l, float* g, float* gb) {
   for (int j = 0; j < ns; ++j) {
     const float xv = xs[j][l];
-    const float4 l4 = *reinterpret_cast<const float4*>(&ls[j][w * RDU_RPW]);
-    const float lv[RDU_RPW] = {l4.x, l4.y, l4.z, l4.w};
+    float lv[RPW];
+    if (RPW == 4) {
+      const float4 l4 = *reinterpret_cast<const float4*>(&ls[j][w * RPW]);
+      lv[0] = l4.x;
+      lv[RPW > 1 ? 1 : 0] = l4.y;
+      lv[RPW > 2 ? 2 : 0] = l4.z;
+      lv[RPW > 3 ? 3 : 0] = l4.w;
+    } else if (RPW == 2) {
+      const float2 l2 = *reinterpret_cast<const float2*>(&ls[j][w * RPW]);
+      lv[0] = l2.x;
+      lv[RPW > 1 ? 1 : 0] = l2.y;
+    } else {
+      lv[0] = ls[j][w];
+    }
 #pragma unroll
-    for (int i = 0; i < RDU_RPW; ++i) {
+    for (int i = 0; i < RPW; ++i) {
       g[i] = __fadd_rn(g[i], __fmul_rn(lv[i], xv));
       if (BIAS) gb[i] = __fadd_rn(gb[i], lv[i]);
     }
   }
 }
 
-template <class W>
+template <class W, int RPW>
 __global__ void __launch_bounds__(256)
     rm_dense_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
                            const float* X, int ldx, uint32_t* bits, const uint32_t* touched, const uint32_t* ctr,
                            float* LGd, int64_t ldu, int nq, const OptStep* op) {
+  constexpr int RDU_RPW = RPW;
+  constexpr int RDU_ROWS = 8 * RPW;
   const OptStep o = *op;
   __shared__ __align__(16) float xs[RDU_ST][RDU_S][RDU_COLS];
   __shared__ __align__(16) float ls[RDU_ST][RDU_S][RDU_ROWS];
@@ -742,9 +760,13 @@ __global__ void __launch_bounds__(256)
         cp_async16(dx, X + (int64_t)(s0 + r) * ldx + cb * RDU_COLS + c4);
       else
         *reinterpret_cast<float4*>(dx) = make_float4(0.f, 0.f, 0.f, 0.f);
-      float* dl = &ls[bf][r][c4];
-      if (s0 + r < nq) cp_async16(dl, LGd + (int64_t)(s0 + r) * ldu + k0 + c4);
-      else *reinterpret_cast<float4*>(dl) = make_float4(0.f, 0.f, 0.f, 0.f);
+      // RDU_S samples x RDU_ROWS slots of LGd: 8 * RDU_ROWS float4s
+      if (t < 8 * RDU_ROWS) {
+        const int lr = t / (RDU_ROWS / 4), lc4 = (t % (RDU_ROWS / 4)) * 4;
+        float* dl = &ls[bf][lr][lc4];
+        if (s0 + lr < nq) cp_async16(dl, LGd + (int64_t)(s0 + lr) * ldu + k0 + lc4);
+        else *reinterpret_cast<float4*>(dl) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     };
     // optimizer state of this lane's elements, loaded now and used after the sum
     float wv[RDU_RPW], mv[RDU_RPW], vv[RDU_RPW];
@@ -760,7 +782,9 @@ __global__ void __launch_bounds__(256)
         vv[i] = o.opt == KL_OPT_ADAM ? v[roff[i]] : 0.f;
       }
     }
-    float g[RDU_RPW] = {0.f, 0.f, 0.f, 0.f}, gb[RDU_RPW] = {0.f, 0.f, 0.f, 0.f};
+    float g[RDU_RPW], gb[RDU_RPW];
+#pragma unroll
+    for (int i = 0; i < RDU_RPW; ++i) g[i] = gb[i] = 0.f;
     __syncthreads();  // previous users of the buffers are done
 #pragma unroll
     for (int p = 0; p < RDU_ST - 1; ++p) {
@@ -774,8 +798,8 @@ __global__ void __launch_bounds__(256)
       cp_async_wait_group<RDU_ST - 1>();
       __syncthreads();
       const int ns = min(RDU_S, nq - ch * RDU_S);
-      if (cb == 0) rdu_sum_chunk<W, true>(xs[bf], ls[bf], ns, w, l, g, gb);
-      else rdu_sum_chunk<W, false>(xs[bf], ls[bf], ns, w, l, g, gb);
+      if (cb == 0) rdu_sum_chunk<W, true, RPW>(xs[bf], ls[bf], ns, w, l, g, gb);
+      else rdu_sum_chunk<W, false, RPW>(xs[bf], ls[bf], ns, w, l, g, gb);
       __syncthreads();  // buffer bf is restaged RDU_ST - 1 chunks later
     }
     cp_async_wait_group<0>();
@@ -791,7 +815,10 @@ __global__ void __launch_bounds__(256)
       const int k = k0 + w * RDU_RPW + l;
       if (k < n) {
         const uint32_t row = touched[k];
-        const float gbl = l == 0 ? gb[0] : l == 1 ? gb[1] : l == 2 ? gb[2] : gb[3];
+        float gbl = gb[0];
+#pragma unroll
+        for (int i = 1; i < RDU_RPW; ++i)
+          if (l == i) gbl = gb[i];
         bias_update(bias, mb, vb, row, gbl, o);
         atomicAnd(bits + (row >> 5), ~(1u << (row & 31)));  // ready for the next step's mark
       }
@@ -1377,13 +1404,23 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
   count_launch();
   const int64_t maxn = std::min<int64_t>((int64_t)N, (int64_t)nq * A.stride);
   const int ncb = (int)ceil_div(d, RDU_COLS);
-  const int grid = (int)std::min<int64_t>((int64_t)upd_grid() * 2, ceil_div(maxn, RDU_ROWS) * ncb);
-  if (wdtype == KL_DTYPE_BF16)
-    rm_dense_update_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X,
-                                                                ldx, D.bits, D.touched, D.ctr, D.LGd, D.ldu, nq, o);
-  else
-    rm_dense_update_kernel<float><<<grid, 256, 0, st>>>(const_cast<void*>(W), ldw, d, bias, m, v, mb, vb, X, ldx,
-                                                        D.bits, D.touched, D.ctr, D.LGd, D.ldu, nq, o);
+  // long sample loops (large batches) get fewer rows per block, so more blocks
+  const int rpw = nq >= 1024 ? 1 : nq >= 512 ? 2 : 4;
+  const int grid = (int)std::min<int64_t>((int64_t)upd_grid() * 2, ceil_div(maxn, 8 * rpw) * ncb);
+  void* Wv = const_cast<void*>(W);
+#define KL_RDU(WT, R)                                                                                     \
+  rm_dense_update_kernel<WT, R><<<grid, 256, 0, st>>>(Wv, ldw, d, bias, m, v, mb, vb, X, ldx, D.bits, D.touched, \
+                                                      D.ctr, D.LGd, D.ldu, nq, o)
+  if (wdtype == KL_DTYPE_BF16) {
+    if (rpw == 1) KL_RDU(__nv_bfloat16, 1);
+    else if (rpw == 2) KL_RDU(__nv_bfloat16, 2);
+    else KL_RDU(__nv_bfloat16, 4);
+  } else {
+    if (rpw == 1) KL_RDU(float, 1);
+    else if (rpw == 2) KL_RDU(float, 2);
+    else KL_RDU(float, 4);
+  }
+#undef KL_RDU
   count_launch();
   rm_lg_zero_kernel<<<nq, 256, 0, st>>>(D.LGd, D.ldu, D.ctr, nq);
   count_launch();
@@ -1418,20 +1455,21 @@ void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, fl
   }
 }
 
-void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* bias, float* m,
+void launch_fm_update(const void* W, int wdtype, int ldw, int d, int f0, int nf, int N, float* bias, float* m,
                       float* v, float* mb, float* vb, SparseIn in, const float* lgd, int ldl,
                       const uint32_t* touched_mask, SegScratch S, float* G, const OptStep* o,
                       unsigned long long* stat_touched, int* err, cudaStream_t st,
                       void (*around_adam)(void*, int), void* hook_arg) {
   const int nq = in.n;
   if (nq <= 0) return;
-  fm_touch_kernel<<<nq, 256, 0, st>>>(in, S.hist, S.touched, S.ctr, d);
+  (void)d;
+  fm_touch_kernel<<<nq, 256, 0, st>>>(in, S.hist, S.touched, S.ctr, (uint32_t)f0, (uint32_t)nf);
   count_launch();
-  seg_alloc_kernel<<<(unsigned)ceil_div(d, 256), 256, 0, st>>>(S.hist, S.touched, S.cur, S.ctr, d);
+  seg_alloc_kernel<<<(unsigned)ceil_div(std::max(nf, 1), 256), 256, 0, st>>>(S.hist, S.touched, S.cur, S.ctr, nf);
   count_launch();
-  fm_scatter_kernel<<<nq, 256, 0, st>>>(in, S.cur, S.ent_s, S.ent_v, d);
+  fm_scatter_kernel<<<nq, 256, 0, st>>>(in, S.cur, S.ent_s, S.ent_v, (uint32_t)f0, (uint32_t)nf);
   count_launch();
-  const int ggrid = (int)std::min<int64_t>((int64_t)upd_grid() * 2, ceil_div(d, FM_GW));
+  const int ggrid = (int)std::min<int64_t>((int64_t)upd_grid() * 2, ceil_div(std::max(nf, 1), FM_GW));
   fm_grad_short_kernel<<<ggrid, FM_GW * 32, 0, st>>>(N, lgd, ldl, S, G, ldl);
   count_launch();
   const int nwords = (int)ceil_div(nq, 32);
@@ -1458,16 +1496,20 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int N, float* b
   const int agrid = sms * 4;  // resident blocks per SM under the kernel's launch bounds
   (void)err;
   if (around_adam) around_adam(hook_arg, 0);
+  // the slice's rows: row pointers, optimizer state and per-feature slots offset by f0
+  const int64_t ro = (int64_t)f0 * ldw;
   if (wdtype == KL_DTYPE_BF16)
-    fm_adam_kernel<__nv_bfloat16><<<agrid, FA_NT, smem, st>>>(const_cast<void*>(W), ldw, d, vpr, rpw, nk, N, m, v,
-                                                              touched_mask, S.hist, S.slot, G, ldl, o);
+    fm_adam_kernel<__nv_bfloat16><<<agrid, FA_NT, smem, st>>>(
+        const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(W)) + ro, ldw, nf, vpr, rpw, nk, N, m + ro,
+        v + ro, touched_mask, S.hist + f0, S.slot + f0, G, ldl, o);
   else
-    fm_adam_kernel<float><<<agrid, FA_NT, smem, st>>>(const_cast<void*>(W), ldw, d, vpr, rpw, nk, N, m, v,
-                                                      touched_mask, S.hist, S.slot, G, ldl, o);
+    fm_adam_kernel<float><<<agrid, FA_NT, smem, st>>>(const_cast<float*>(static_cast<const float*>(W)) + ro, ldw, nf,
+                                                      vpr, rpw, nk, N, m + ro, v + ro, touched_mask, S.hist + f0,
+                                                      S.slot + f0, G, ldl, o);
   count_launch();
   if (around_adam) around_adam(hook_arg, 1);
   if (nk > 1) {
-    fm_hist_clear_kernel<<<(unsigned)ceil_div(d, 256), 256, 0, st>>>(S);
+    fm_hist_clear_kernel<<<(unsigned)ceil_div(std::max(nf, 1), 256), 256, 0, st>>>(S);
     count_launch();
   }
   fm_bias_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask, o,

@@ -60,7 +60,10 @@ def test_checkpoint_round_trip_continues_identically(gpu_ctx, tmp_path, dtype):
         a.train_step_host(hb, 1e-3)
     path = tmp_path / "net.ckpt"
     a.save(path)
-    b = Network(cfg, S.make_init(cfg, 7), weight_dtype=dtype, max_batch=32)  # other weights: all overwritten
+    other = S.make_init(cfg, 7)
+    for l in range(2):  # other weights and biases (all overwritten), the same hash parameters
+        other[l] = {**init[l], "weights": other[l]["weights"], "bias": other[l]["bias"] + 0.5}
+    b = Network(cfg, other, weight_dtype=dtype, max_batch=32)
     b.load(path)
     _same(_state(a), _state(b))
     la = [a.train_step_host(hb, 1e-3) for hb in bs[4:]]
@@ -85,6 +88,9 @@ def test_checkpoint_refuses_corrupt_and_mismatched_files(gpu_ctx, tmp_path):
     c = Network(other, S.make_init(other, 1), max_batch=32)
     with pytest.raises(_lib.KlError, match="differs"):
         c.load(path)
+    h = Network(cfg, S.make_init(cfg, 9), max_batch=32)  # the same shapes, other hash planes / windows
+    with pytest.raises(_lib.KlError, match="hash parameters"):
+        h.load(path)
     (tmp_path / "junk.ckpt").write_bytes(b"not a checkpoint at all")
     with pytest.raises(_lib.KlError, match="not a klearu_b200"):
         a.load(tmp_path / "junk.ckpt")
