@@ -619,6 +619,26 @@ KL_API kl_status kl_sparse_mlp_destroy(kl_sparse_mlp_t m);
 KL_API kl_status kl_sparse_mlp_forward(kl_sparse_mlp_t m, const float* x, int n_tokens, const uint32_t* sel, int k,
                                        float* out);
 
+/* The MLP half of SparseModel::forward_decode_sparse
+ * (crates/klearu-llm/src/sparse/mod.rs:112-141) over n_layers layers: for
+ * each layer l, norm = RMSNorm_l(hidden) (model/rms_norm.rs: x / sqrt(mean(x^2)
+ * + eps) * w, or * (1 + w) with one_plus_weight), idx = predictors[l]'s
+ * select_top_k(norm, k) with k = ceil(intermediate * neuron_sparsity)
+ * (mod.rs:121-125), hidden += sparse_mlp_l(norm, idx).  Attention, embedding,
+ * the final norm and the LM head are outside this engine: `hidden` is the
+ * residual stream the caller's attention writes.  The predictor and MLP
+ * handles are borrowed (they must outlive the stack and share its context);
+ * norm_weights_host is [n_layers][hidden] f32. */
+typedef struct kl_ffn_stack_s* kl_ffn_stack_t;
+KL_API kl_status kl_ffn_stack_create(kl_ctx_t ctx, int n_layers, const kl_predictor_t* predictors_host,
+                                     const kl_sparse_mlp_t* mlps_host, const float* norm_weights_host, float eps,
+                                     int one_plus_weight, kl_ffn_stack_t* out);
+KL_API kl_status kl_ffn_stack_destroy(kl_ffn_stack_t s);
+/* hidden [n_tokens][hidden] (device f32), updated in place.  The second call
+ * with the same (hidden pointer, n_tokens, k) captures the per-layer launches
+ * in a CUDA graph, later calls replay it. */
+KL_API kl_status kl_ffn_stack_decode(kl_ffn_stack_t s, float* hidden, int n_tokens, float neuron_sparsity);
+
 /* ------------------------------------------------------------------------ */
 /* Datasets: LibSVM / XML files and shuffled CSR batches (host memory).      */
 /* These calls take no context; on failure kl_last_error(NULL) returns the   */

@@ -157,6 +157,9 @@ _PROTOS = {
     "kl_adaptive_should_rebuild": (_S, [_H, _P, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)]),
     "kl_adaptive_notify_rebuild": (_S, [_H]),
     "kl_adaptive_state": (_S, [_H, _P, _P, _P]),
+    "kl_ffn_stack_create": (_S, [_H, C.c_int, _P, _P, _P, C.c_float, C.c_int, C.POINTER(_H)]),
+    "kl_ffn_stack_destroy": (_S, [_H]),
+    "kl_ffn_stack_decode": (_S, [_H, _P, C.c_int, C.c_float]),
     "kl_libsvm_load": (_S, [C.c_char_p, C.c_int64, C.c_int64, C.c_int, C.POINTER(_H)]),
     "kl_libsvm_parse": (_S, [C.c_char_p, C.c_size_t, C.c_int64, C.c_int64, C.c_int, C.POINTER(_H)]),
     "kl_dataset_from_csr": (_S, [_P, _P, _P, _P, _P, C.c_int64, C.c_int64, C.c_int64, C.POINTER(_H)]),

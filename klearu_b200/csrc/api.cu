@@ -2945,6 +2945,20 @@ void predictor_scores(kl_predictor_t p, const float* x, int T, float* scores, cu
   }
 }
 
+void topk_check(kl_predictor_t p, int kk) {
+  int pow2 = 2048;
+  while (pow2 < kk) pow2 <<= 1;
+  support((size_t)pow2 * 8 + (size_t)p->out * 4 <= 190 * 1024,
+          "select_topk: k and output_dim too large for one block's shared memory");
+}
+// select_top_k for T tokens into idx [T][kk]; sc [T][out] receives the scores.
+void predictor_topk_body(kl_predictor_t p, const float* x, int T, int kk, uint32_t* idx, float* sc, cudaStream_t st) {
+  topk_check(p, kk);
+  predictor_scores(p, x, T, sc, st);
+  launch_topk(sc, T, p->out, p->out, kk, idx, kk, st);
+  ck_launch("topk");
+}
+
 }  // namespace
 
 extern "C" kl_status kl_predictor_create(kl_ctx_t ctx, int input_dim, int hidden_dim, int output_dim,
@@ -3009,19 +3023,12 @@ extern "C" kl_status kl_predictor_select_topk(kl_predictor_t p, const float* x, 
   const int kk = std::min(k, p->out);
   if (n_tokens == 0 || kk == 0) return KL_OK;
   require(x && idx, "select_topk: x and idx are required");
-  int pow2 = 2048;
-  while (pow2 < kk) pow2 <<= 1;
-  support((size_t)pow2 * 8 + (size_t)p->out * 4 <= 190 * 1024,
-          "select_topk: k and output_dim too large for one block's shared memory");
-  cudaStream_t st = ctx__->stream;
   float* sc = scores;
   if (!sc) {
     p->sc.alloc((size_t)n_tokens * p->out * 4);
     sc = p->sc.as<float>();
   }
-  predictor_scores(p, x, n_tokens, sc, st);
-  launch_topk(sc, n_tokens, p->out, p->out, kk, idx, kk, st);
-  ck_launch("topk");
+  predictor_topk_body(p, x, n_tokens, kk, idx, sc, ctx__->stream);
   KL_API_END
 }
 
@@ -3067,6 +3074,35 @@ extern "C" kl_status kl_sparse_mlp_destroy(kl_sparse_mlp_t m) {
   KL_API_END
 }
 
+// sparse_mlp::forward_sparse for T tokens on stream st (k >= 1).
+static void sparse_mlp_body(kl_sparse_mlp_t m, const float* x, int n_tokens, const uint32_t* sel, int k, float* out,
+                            cudaStream_t st) {
+  int* err = m->ctx->err.as<int>();
+  if (n_tokens >= KL_DENSE_MIN_TOKENS) {
+    for (int t0 = 0; t0 < n_tokens; t0 += TC_LINEAR_MAX_T) {
+      const int tn = std::min(TC_LINEAR_MAX_T, n_tokens - t0);
+      launch_sparse_mlp_dense(m->gate.as<__nv_bfloat16>(), m->up.as<__nv_bfloat16>(), m->down.as<__nv_bfloat16>(),
+                              m->hid, m->ldw, m->inter, m->ldd, m->has_bias ? m->bias.as<float>() : nullptr,
+                              x + (int64_t)t0 * m->hid, tn, sel + (int64_t)t0 * k, k, m->G.as<float>(),
+                              m->U.as<float>(), m->mask.as<uint8_t>(), m->xs.as<__nv_bfloat16>(),
+                              m->hs.as<__nv_bfloat16>(), m->P.as<float>(), out + (int64_t)t0 * m->hid, err, st);
+      ck_launch("sparse mlp (dense)");
+    }
+    return;
+  }
+  // K splits of the down projection: at most ~32 selected rows per thread,
+  // and enough blocks ((hidden / 256) x splits x tokens) to fill the SMs
+  const int cols = (int)ceil_div(m->hid, 256);
+  const int splits = std::max(1, std::min(k, std::max((int)ceil_div(k, 32),
+                                                      (int)ceil_div(592, (int64_t)cols * n_tokens))));
+  m->a.alloc((size_t)n_tokens * k * 4);
+  m->part.alloc((size_t)n_tokens * splits * m->ldw * 4);
+  launch_sparse_mlp(m->gate.as<__nv_bfloat16>(), m->up.as<__nv_bfloat16>(), m->downT.as<__nv_bfloat16>(), m->hid,
+                    m->ldw, m->inter, m->has_bias ? m->bias.as<float>() : nullptr, x, n_tokens, sel, k,
+                    m->a.as<float>(), m->part.as<float>(), splits, out, err, st);
+  ck_launch("sparse mlp");
+}
+
 extern "C" kl_status kl_sparse_mlp_forward(kl_sparse_mlp_t m, const float* x, int n_tokens, const uint32_t* sel, int k,
                                            float* out) {
   if (!m) return KL_EINVAL;
@@ -3084,29 +3120,144 @@ extern "C" kl_status kl_sparse_mlp_forward(kl_sparse_mlp_t m, const float* x, in
     return KL_OK;
   }
   require(sel != nullptr, "sparse_mlp_forward: sel is required");
-  if (n_tokens >= KL_DENSE_MIN_TOKENS) {
-    for (int t0 = 0; t0 < n_tokens; t0 += TC_LINEAR_MAX_T) {
-      const int tn = std::min(TC_LINEAR_MAX_T, n_tokens - t0);
-      launch_sparse_mlp_dense(m->gate.as<__nv_bfloat16>(), m->up.as<__nv_bfloat16>(), m->down.as<__nv_bfloat16>(),
-                              m->hid, m->ldw, m->inter, m->ldd, m->has_bias ? m->bias.as<float>() : nullptr,
-                              x + (int64_t)t0 * m->hid, tn, sel + (int64_t)t0 * k, k, m->G.as<float>(),
-                              m->U.as<float>(), m->mask.as<uint8_t>(), m->xs.as<__nv_bfloat16>(),
-                              m->hs.as<__nv_bfloat16>(), m->P.as<float>(), out + (int64_t)t0 * m->hid,
-                              ctx__->err.as<int>(), st);
-      ck_launch("sparse mlp (dense)");
+  sparse_mlp_body(m, x, n_tokens, sel, k, out, st);
+  KL_API_END
+}
+
+// ===========================================================================
+// Deja Vu FFN stack: the MLP half of SparseModel::forward_decode_sparse
+// (crates/klearu-llm/src/sparse/mod.rs:112-141) over every layer, as one
+// call.  Per layer: RMSNorm (mlp_norm), select_top_k of the layer's predictor,
+// the sparse SwiGLU MLP, residual add.  The launches of one (tokens, k) shape
+// are captured once in a CUDA graph and replayed.
+// ===========================================================================
+struct kl_ffn_stack_s {
+  kl_ctx_t ctx;
+  int nl = 0, hid = 0, inter = 0;
+  float eps = 1e-5f;
+  int one_plus = 0;
+  std::vector<kl_predictor_t> pred;
+  std::vector<kl_sparse_mlp_t> mlp;
+  DBuf normw, norm, out, idx, sc;
+  int cap_T = 0, cap_k = 0;
+  cudaGraphExec_t gexec = nullptr;
+  cudaStream_t cap_stream = nullptr;
+  int g_T = -1, g_k = -1;
+  float* g_hidden = nullptr;
+  bool g_warm = false;
+  ~kl_ffn_stack_s() {
+    if (gexec) cudaGraphExecDestroy(gexec);
+    if (cap_stream) cudaStreamDestroy(cap_stream);
+  }
+  void body(float* hidden, int T, int k, cudaStream_t st) {
+    for (int l = 0; l < nl; ++l) {
+      launch_rmsnorm(hidden, T, hid, normw.as<float>() + (size_t)l * hid, eps, one_plus, norm.as<float>(), st);
+      ck_launch("rmsnorm");
+      predictor_topk_body(pred[(size_t)l], norm.as<float>(), T, k, idx.as<uint32_t>(), sc.as<float>(), st);
+      sparse_mlp_body(mlp[(size_t)l], norm.as<float>(), T, idx.as<uint32_t>(), k, out.as<float>(), st);
+      launch_residual_add(hidden, out.as<float>(), (int64_t)T * hid, st);
+      ck_launch("residual add");
     }
+  }
+};
+
+extern "C" kl_status kl_ffn_stack_create(kl_ctx_t ctx, int n_layers, const kl_predictor_t* predictors_host,
+                                         const kl_sparse_mlp_t* mlps_host, const float* norm_weights_host, float eps,
+                                         int one_plus_weight, kl_ffn_stack_t* out) {
+  if (!ctx || !out) return KL_EINVAL;
+  KL_API_BEGIN(ctx)
+  require(n_layers >= 1 && predictors_host && mlps_host && norm_weights_host, "ffn stack: bad arguments");
+  auto s = std::make_unique<kl_ffn_stack_s>();
+  s->ctx = ctx;
+  s->nl = n_layers;
+  s->eps = eps;
+  s->one_plus = one_plus_weight ? 1 : 0;
+  for (int l = 0; l < n_layers; ++l) {
+    kl_predictor_t p = predictors_host[l];
+    kl_sparse_mlp_t m = mlps_host[l];
+    require(p && m, "ffn stack: every layer needs a predictor and an MLP");
+    require(p->ctx == ctx && m->ctx == ctx, "ffn stack: the predictors and MLPs must share the stack's context");
+    if (l == 0) {
+      s->hid = m->hid;
+      s->inter = m->inter;
+    }
+    require(m->hid == s->hid && m->inter == s->inter && p->in == s->hid && p->out == s->inter,
+            "ffn stack: every layer must have the same hidden / intermediate sizes, predictor input = hidden, "
+            "predictor output = intermediate");
+    s->pred.push_back(p);
+    s->mlp.push_back(m);
+  }
+  upload_f32(ctx, s->normw, norm_weights_host, (int64_t)n_layers * s->hid);
+  ck(cudaStreamSynchronize(ctx->stream), "sync");
+  *out = s.release();
+  KL_API_END
+}
+
+extern "C" kl_status kl_ffn_stack_destroy(kl_ffn_stack_t s) {
+  if (!s) return KL_EINVAL;
+  KL_API_BEGIN(s->ctx)
+  ck(cudaStreamSynchronize(s->ctx->stream), "sync");
+  delete s;
+  KL_API_END
+}
+
+extern "C" kl_status kl_ffn_stack_decode(kl_ffn_stack_t s, float* hidden, int n_tokens, float neuron_sparsity) {
+  if (!s) return KL_EINVAL;
+  KL_API_BEGIN(s->ctx)
+  require(n_tokens >= 0 && hidden, "ffn stack decode: bad arguments");
+  require(neuron_sparsity >= 0.f && neuron_sparsity <= 1.f, "ffn stack decode: neuron_sparsity must be in [0, 1]");
+  if (n_tokens == 0) return KL_OK;
+  // num_neurons_to_keep = ceil(intermediate * neuron_sparsity) (mod.rs:121-122)
+  const int k = std::min(s->inter, (int)std::ceil((float)s->inter * neuron_sparsity));
+  support(k >= 1, "ffn stack decode: a sparsity that keeps no neuron is not supported");
+  topk_check(s->pred[0], k);
+  cudaStream_t st = ctx__->stream;
+  if (n_tokens > s->cap_T || k > s->cap_k) {
+    s->cap_T = std::max(n_tokens, s->cap_T);
+    s->cap_k = std::max(k, s->cap_k);
+    s->norm.alloc((size_t)s->cap_T * s->hid * 4);
+    s->out.alloc((size_t)s->cap_T * s->hid * 4);
+    s->idx.alloc((size_t)s->cap_T * s->cap_k * 4);
+    s->sc.alloc((size_t)s->cap_T * s->inter * 4);
+    if (s->gexec) cudaGraphExecDestroy(s->gexec);
+    s->gexec = nullptr;
+    s->g_warm = false;
+  }
+  if (!s->g_warm || s->g_T != n_tokens || s->g_k != k || s->g_hidden != hidden) {
+    // a new shape: run eagerly (this also sizes every scratch buffer), capture next time
+    if (s->gexec) cudaGraphExecDestroy(s->gexec);
+    s->gexec = nullptr;
+    s->body(hidden, n_tokens, k, st);
+    s->g_warm = true;
+    s->g_T = n_tokens;
+    s->g_k = k;
+    s->g_hidden = hidden;
     return KL_OK;
   }
-  // K splits of the down projection: at most ~32 selected rows per thread,
-  // and enough blocks ((hidden / 256) x splits x tokens) to fill the SMs
-  const int cols = (int)ceil_div(m->hid, 256);
-  const int splits = std::max(1, std::min(k, std::max((int)ceil_div(k, 32),
-                                                      (int)ceil_div(592, (int64_t)cols * n_tokens))));
-  m->a.alloc((size_t)n_tokens * k * 4);
-  m->part.alloc((size_t)n_tokens * splits * m->ldw * 4);
-  launch_sparse_mlp(m->gate.as<__nv_bfloat16>(), m->up.as<__nv_bfloat16>(), m->downT.as<__nv_bfloat16>(), m->hid,
-                    m->ldw, m->inter, m->has_bias ? m->bias.as<float>() : nullptr, x, n_tokens, sel, k,
-                    m->a.as<float>(), m->part.as<float>(), splits, out, ctx__->err.as<int>(), st);
-  ck_launch("sparse mlp");
+  if (!s->gexec) {
+    if (!s->cap_stream) ck(cudaStreamCreateWithFlags(&s->cap_stream, cudaStreamNonBlocking), "capture stream");
+    cudaGraph_t g = nullptr;
+    bool ok = cudaStreamBeginCapture(s->cap_stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+    const unsigned long long n0 = g_launches.load();
+    if (ok) {
+      try {
+        s->body(hidden, n_tokens, k, s->cap_stream);
+      } catch (...) {
+        ok = false;
+      }
+      ok = cudaStreamEndCapture(s->cap_stream, &g) == cudaSuccess && ok && g;
+    }
+    if (ok) ok = cudaGraphInstantiate(&s->gexec, g, 0) == cudaSuccess;
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    g_launches.fetch_sub(g_launches.load() - n0);
+    if (!ok) {
+      s->gexec = nullptr;
+      s->body(hidden, n_tokens, k, st);
+      return KL_OK;
+    }
+  }
+  ck(cudaGraphLaunch(s->gexec, st), "graph launch");
+  count_launch((unsigned)(4 * s->nl));
   KL_API_END
 }

@@ -555,6 +555,36 @@ __global__ void dv_down_finish_kernel(const float* __restrict__ part, int splits
   }
 }
 
+// RMSNorm (klearu-llm model/rms_norm.rs): y = x * (1 / sqrt(mean(x^2) + eps))
+// * w (or * (1 + w)), one block per token.  The sum of squares is a block
+// reduction (the reference sums sequentially: equal within f32 rounding).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, int ld, int n, const float* w, float eps,
+                                                      int one_plus, float* y) {
+  __shared__ float red[8];
+  const int t = blockIdx.x;
+  const float* xr = x + (int64_t)t * ld;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += 256) ss = fmaf(xr[i], xr[i], ss);
+  ss = warp_sum_f(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    v = warp_sum_f(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv = 1.0f / sqrtf(red[0] / (float)n + eps);
+  for (int i = threadIdx.x; i < n; i += 256) {
+    const float wi = one_plus ? 1.0f + w[i] : w[i];
+    y[(int64_t)t * ld + i] = xr[i] * inv * wi;
+  }
+}
+__global__ void residual_add_kernel(float* h, const float* d, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) h[i] += d[i];
+}
+
 int sm_count() {
   static int n = 0;
   if (!n) {
@@ -702,6 +732,18 @@ void launch_sparse_mlp(const __nv_bfloat16* gate, const __nv_bfloat16* up, const
                                                                                        inter, a, splits, part);
   count_launch();
   dv_down_finish_kernel<<<dim3((unsigned)ceil_div(hid, 256), T), 256, 0, st>>>(part, splits, hid, ldw, bias, out);
+  count_launch();
+}
+
+void launch_rmsnorm(const float* x, int T, int n, const float* w, float eps, int one_plus, float* y,
+                    cudaStream_t st) {
+  if (T <= 0) return;
+  rmsnorm_kernel<<<T, 256, 0, st>>>(x, n, n, w, eps, one_plus, y);
+  count_launch();
+}
+void launch_residual_add(float* h, const float* d, int64_t n, cudaStream_t st) {
+  if (n <= 0) return;
+  residual_add_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(h, d, n);
   count_launch();
 }
 

@@ -349,4 +349,9 @@ void launch_sparse_mlp_dense(const __nv_bfloat16* gate, const __nv_bfloat16* up,
                              const uint32_t* sel, int k, float* G, float* U, uint8_t* mask, __nv_bfloat16* xs,
                              __nv_bfloat16* hs, float* P, float* out, int* err, cudaStream_t st);
 
+// Deja Vu FFN stack helpers (dejavu.cu): RMSNorm of T rows of n and h += d.
+void launch_rmsnorm(const float* x, int T, int n, const float* w, float eps, int one_plus, float* y,
+                    cudaStream_t st);
+void launch_residual_add(float* h, const float* d, int64_t n, cudaStream_t st);
+
 }  // namespace kl

@@ -111,3 +111,38 @@ class SparseMlp:
         check(self.lib.kl_sparse_mlp_forward(self.h, xt.data_ptr(), xt.shape[0], sel.data_ptr(), sel.shape[1],
                                              out.data_ptr()), self.ctx.h, "kl_sparse_mlp_forward")
         return out[0] if one else out
+
+
+class FfnStack:
+    """The MLP half of klearu-llm's ``SparseModel::forward_decode_sparse``
+    (sparse/mod.rs:112-141) over every layer: per layer RMSNorm, the layer's
+    predictor top-k, the sparse SwiGLU MLP and the residual add, in one
+    kl_ffn_stack_decode call (replayed as a CUDA graph for a repeated shape).
+    ``predictors`` / ``mlps`` are lists of SparsityPredictor / SparseMlp on the
+    same context; ``norm_weights`` is [layers][hidden]."""
+
+    def __init__(self, predictors, mlps, norm_weights, eps: float = 1e-5, one_plus_weight: bool = False,
+                 ctx: Context | None = None):
+        self.ctx = ctx or default_context()
+        self.lib = self.ctx.lib
+        self._keep = (list(predictors), list(mlps))
+        n = len(predictors)
+        ph = (C.c_void_p * n)(*[p.h.value if hasattr(p.h, "value") else p.h for p in predictors])
+        mh = (C.c_void_p * n)(*[m.h.value if hasattr(m.h, "value") else m.h for m in mlps])
+        nw = _host_f32(norm_weights)
+        self.hidden_size = nw.shape[1]
+        h = C.c_void_p()
+        check(self.lib.kl_ffn_stack_create(self.ctx.h, n, ph, mh, nw.ctypes.data, float(eps), int(one_plus_weight),
+                                           C.byref(h)), self.ctx.h, "kl_ffn_stack_create")
+        self.h = h
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.lib.kl_ffn_stack_destroy(self.h)
+
+    def decode(self, hidden: torch.Tensor, neuron_sparsity: float) -> torch.Tensor:
+        """Updates ``hidden`` [tokens][hidden] (a CUDA f32 tensor) in place and returns it."""
+        assert hidden.is_cuda and hidden.dtype == torch.float32 and hidden.is_contiguous()
+        check(self.lib.kl_ffn_stack_decode(self.h, hidden.data_ptr(), hidden.shape[0], float(neuron_sparsity)),
+              self.ctx.h, "kl_ffn_stack_decode")
+        return hidden

@@ -116,3 +116,52 @@ def test_sparse_mlp_no_selection_is_bias(gpu_ctx):
     assert (out == b).all()
     out0 = SparseMlp(gate, up, down, None, ctx=gpu_ctx).forward_sparse(x, np.zeros((2, 0), np.int32)).cpu().numpy()
     assert (out0 == 0).all()
+
+
+def _rmsnorm(x, w, eps):  # klearu-llm model/rms_norm.rs, f32
+    ss = np.float32(0.0)
+    for v in x:
+        ss = np.float32(ss + np.float32(v * v))
+    inv = np.float32(1.0) / np.sqrt(np.float32(ss / np.float32(len(x)) + np.float32(eps)))
+    return (x * inv * w).astype(np.float32)
+
+
+@pytest.mark.parametrize("T", [1, 3, 30])
+def test_ffn_stack_decode_matches_oracle_chain(gpu_ctx, T):
+    # The predictors' biases are spread far apart, so that every layer's
+    # top-k is the same on the GPU and in the restatement; the chain of
+    # RMSNorm -> top-k -> sparse MLP -> residual is then compared within the
+    # MLP tolerance, and graph replays equal the eager result bit for bit.
+    from klearu_b200.dejavu import FfnStack
+
+    hid, phid, inter, nl, sp = 128, 48, 320, 3, 0.1
+    rng = np.random.default_rng(T)
+    preds, mlps, raw, norms = [], [], [], []
+    for _ in range(nl):
+        w1, b1, w2, b2 = predictor_weights(rng, hid, phid, inter, std=0.01)
+        b2 = np.linspace(6.0, -6.0, inter).astype(np.float32)[rng.permutation(inter)]
+        gate, up, down = mlp_weights(rng, hid, inter, std=0.1)
+        preds.append(SparsityPredictor(w1, b1, w2, b2, ctx=gpu_ctx))
+        mlps.append(SparseMlp(gate, up, down, None, ctx=gpu_ctx))
+        raw.append((w1, b1, w2, b2, gate, up, down))
+        norms.append((1.0 + 0.1 * rng.standard_normal(hid)).astype(np.float32))
+    stack = FfnStack(preds, mlps, np.stack(norms), eps=1e-5, ctx=gpu_ctx)
+    x0 = rng.standard_normal((T, hid)).astype(np.float32)
+    k = int(np.ceil(inter * np.float32(sp)))
+    ref = x0.copy()
+    for l, (w1, b1, w2, b2, gate, up, down) in enumerate(raw):
+        for t in range(T):
+            nrm = _rmsnorm(ref[t], norms[l], 1e-5)
+            sc = oracle.pred_predict(bf16(w1), b1, bf16(w2), b2, nrm[None, :])[0]
+            sel = oracle.pred_topk(sc, k)
+            ref[t] = ref[t] + oracle.sparse_mlp(bf16(gate), bf16(up), bf16(down), None, nrm, sel)
+    outs = []
+    h = torch.empty((T, hid), dtype=torch.float32, device=f"cuda:{gpu_ctx.device}")
+    for _ in range(3):  # eager, captured, replayed (same buffer and shape)
+        h.copy_(torch.from_numpy(x0))
+        stack.decode(h, sp)
+        gpu_ctx.sync()
+        outs.append(h.cpu().numpy())
+    scale = np.abs(ref).max()
+    assert np.abs(outs[0] - ref).max() <= 1e-3 * scale
+    assert (outs[0] == outs[1]).all() and (outs[1] == outs[2]).all()
