@@ -541,6 +541,7 @@ void check_device_errors(kl_ctx_t ctx) {
     if (e & DERR_BOUNDS) raise(KL_EBOUNDS, "device kernel saw an out-of-range id or index");
     if (e & DERR_CAPACITY) raise(KL_ECAPACITY, "an output exceeded its capacity and was truncated");
     if (e & DERR_TIMEOUT) raise(KL_ETIMEOUT, "a bounded device wait gave up");
+    if (e & DERR_TMA) raise(KL_ECUDA, "a TMA tensor map could not be encoded (misaligned buffer or pitch)");
   }
 }
 }  // namespace

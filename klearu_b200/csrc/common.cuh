@@ -36,6 +36,7 @@ enum : int {
   DERR_BOUNDS = 1,    // id / index outside its array
   DERR_CAPACITY = 2,  // an output did not fit its buffer (truncated)
   DERR_TIMEOUT = 4,   // a bounded wait gave up
+  DERR_TMA = 8,       // a TMA tensor map could not be encoded (nothing was launched)
 };
 
 constexpr int WARP = 32;

@@ -15,6 +15,7 @@
 #include <algorithm>
 
 #include "engine.h"
+#include "tcgen05.cuh"
 
 namespace kl {
 namespace {
@@ -26,59 +27,19 @@ constexpr int TC_TMAX = 85;                // tokens per call: 3 piece rows each
 constexpr int TC_WTILE = TC_M * TC_K * 2;  // bytes of one 128 x 64 bf16 weight tile
 constexpr int TC_SMEM = 200 * 1024;        // shared-memory budget of the stage ring
 
-// Canonical K-major layout without swizzle: 8-row x 16-byte core matrices,
-// stored contiguously (128 B); the next 16 bytes of K are the next core
-// matrix (leading byte offset 128 B); the next 8 rows start 8 core matrices
-// later (stride byte offset 1024 B).
-__device__ __forceinline__ uint32_t canon_off(int r, int c16) { return (r >> 3) * 1024 + c16 * 128 + (r & 7) * 16; }
-
-// Shared-memory matrix descriptor: start address, leading and stride byte
-// offsets (all >> 4), descriptor version 1, no swizzle.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         (1ull << 46);
-}
-// Instruction descriptor: f32 accumulator, bf16 A and B, both K-major,
-// M = TC_M, N = n (a multiple of 16 up to 256).
-__host__ __device__ constexpr uint32_t tc_idesc(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-
-__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];\n"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-}
-
 // P[split][t][n0 + m] (f32 partial sums, t < T) = sum over the split's K tiles
 // of W[n0 + m] . x[t]: the weights are the MMA's A operand (M = 128 rows per
 // tile), the token pieces its B operand: row 3t + p of X is piece p of token
 // t, so one MMA per 16-wide K step covers every piece of every token, and the
 // epilogue adds a token's three accumulator columns (hi + mid + lo).
-// A: [nw][ldw] bf16, rows >= nw read as zero.  X: [3 * TC_TMAX][ldw] bf16;
-// rows 3T .. NT-1 are zeroed in every stage once and never loaded.  NST stages of
-// (weight tile + token pieces) stream through shared memory (cp.async); the
-// MMAs of a stage release it through tcgen05.commit on its mbarrier.  One CTA
-// per (128-row tile, K split); 128 threads; warp 0 owns the tensor memory,
-// thread 0 issues the MMAs; the epilogue reads row m = lane of warp m / 32.
+// Both operands arrive by TMA (128-byte swizzle, no multicast): thread 0
+// (warp 0) keeps NST stages of (128 x 64 weight tile + NT x 64 token tile)
+// in flight, thread 32 (warp 1) issues the MMAs of a stage once its bytes
+// have landed and releases the stage through tcgen05.commit.  Weight rows
+// >= nw and token rows beyond the piece buffer read as zero; token-piece
+// rows 3T .. NT-1 hold other data, whose accumulator columns the epilogue
+// never reads.  One CTA per (128-row tile, K split); warp 1 owns the tensor
+// memory; the epilogue reads row m = lane of warp m / 32.
 template <int NT>
 struct TcCfg {
   static constexpr int XTILE = NT * TC_K * 2;  // the token-piece rows
@@ -86,119 +47,106 @@ struct TcCfg {
   // token tiles up to 64 wide: two CTAs per SM, so that two MMA chains and
   // their load rings share the SM
   static constexpr int CTAS = NT <= 64 ? 2 : 1;
-  static constexpr int NST = (TC_SMEM / CTAS / STAGE) < 8 ? (TC_SMEM / CTAS / STAGE) : 8;
-  static_assert(NST >= 3, "the ring needs a prefetch distance of at least one stage");
+  static constexpr int NST = ((TC_SMEM / CTAS - 1024) / STAGE) < 8 ? ((TC_SMEM / CTAS - 1024) / STAGE) : 8;
+  static_assert(NST >= 2, "the ring needs two stages");
   static constexpr int TMEM_COLS = NT < 32 ? 32 : NT;
+  static constexpr int SMEM = 1024 + NST * STAGE;
 };
 
 template <int NT>
 __global__ void __launch_bounds__(128, TcCfg<NT>::CTAS)
-    tc_gemm_kernel(const __nv_bfloat16* __restrict__ W, int ldw, int nw, const __nv_bfloat16* __restrict__ X, int T,
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, int T,
                    int ktiles, int kt_per_split, float* __restrict__ P, int ldp, int* err) {
   using Cfg = TcCfg<NT>;
   constexpr int NST = Cfg::NST;
-  extern __shared__ __align__(1024) unsigned char tc_smem[];
-  __shared__ uint64_t bar_mma[NST];
-  __shared__ uint64_t bar_done;
+  extern __shared__ unsigned char tc_dyn[];
+  __shared__ uint64_t full[NST], empty[NST], done;
   __shared__ uint32_t tmem_s;
+  __shared__ int fail;
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_dyn) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * TC_M;
   const int kt0 = blockIdx.y * kt_per_split;
   const int nk = max(0, min(ktiles, kt0 + kt_per_split) - kt0);
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(&tmem_s)),
-                 "r"(Cfg::TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
-  }
   if (tid == 0) {
-    for (int s = 0; s < NST; ++s) mbar_init(&bar_mma[s], 1);
-    mbar_init(&bar_done, 1);
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    fail = 0;
     fence_mbar_init();
   }
-  const int xr = TC_NP * T;  // token-piece rows
-  // rows xr .. NT-1 of the token tile are zero in every stage
-  for (int s = 0; s < NST; ++s)
-    for (int q = xr * 8 + tid; q < NT * 8; q += 128)
-      *reinterpret_cast<uint4*>(tc_smem + s * Cfg::STAGE + TC_WTILE + canon_off(q >> 3, q & 7)) =
-          make_uint4(0u, 0u, 0u, 0u);
-  tc_fence_before();
+  if (warp == 1) tc5_alloc(&tmem_s, Cfg::TMEM_COLS);
+  tc5_fence_before();
   __syncthreads();
-  tc_fence_after();
+  tc5_fence_after();
   const uint32_t tmem = tmem_s;
-  bool ok = true;
-
-  auto load_stage = [&](int i) {  // K tile kt0 + i into stage i % NST
-    unsigned char* st = tc_smem + (i % NST) * Cfg::STAGE;
-    const int k0 = (kt0 + i) * TC_K;
-    for (int q = tid; q < TC_M * 8; q += 128) {
-      const int r = q >> 3, c = q & 7;
-      unsigned char* dst = st + canon_off(r, c);
-      if (n0 + r < nw) cp_async16(dst, W + (int64_t)(n0 + r) * ldw + k0 + c * 8);
-      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+  if (tid == 0) {
+    // producer
+    int i = 0;
+    for (; i < nk; ++i) {
+      const int s = i % NST;
+      const uint32_t round = (uint32_t)(i / NST);
+      if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u)) {
+        atomicExch(&fail, 1);
+        break;
+      }
+      unsigned char* st = sm + s * Cfg::STAGE;
+      mbar_arrive_expect_tx(&full[s], (uint32_t)Cfg::STAGE);
+      const int k0 = (kt0 + i) * TC_K;
+      tma_load_2d(st, &wmap, k0, n0, &full[s]);
+      tma_load_2d(st + TC_WTILE, &xmap, k0, 0, &full[s]);
     }
-    for (int q = tid; q < xr * 8; q += 128) {
-      const int r = q >> 3, c = q & 7;
-      cp_async16(st + TC_WTILE + canon_off(r, c), X + (int64_t)r * ldw + k0 + c * 8);
-    }
-  };
-
-  // prefetch distance PD = NST - 2: the stage refilled in iteration i last
-  // held tile i - 2, whose MMAs were issued an iteration before the latest
-  // ones, so the refill rarely waits on the tensor core
-  constexpr int PD = NST - 2;
-  for (int i = 0; i < PD; ++i) {
-    if (i < nk) load_stage(i);
-    cp_async_commit();
-  }
-  for (int i = 0; i < nk; ++i) {
-    const int j = i + PD;
-    if (j < nk) {
-      // stage j % NST last held tile j - NST: wait until its MMAs are done
-      if (j >= NST && !mbar_wait(&bar_mma[j % NST], (uint32_t)((j / NST) - 1) & 1u)) ok = false;
-      load_stage(j);
-    }
-    cp_async_commit();
-    cp_async_wait_group<PD>();
-    fence_proxy_async_smem();  // this thread's shared-memory writes, visible to the tensor core
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const unsigned char* st = tc_smem + (i % NST) * Cfg::STAGE;
-      const uint32_t sa = smem_u32(st), sb = smem_u32(st + TC_WTILE);
+    // no copy may outlive the CTA: wait (bounded) for the last round of every stage
+    for (int r = i > NST ? i - NST : 0; r < i; ++r) mbar_wait(&full[r % NST], (uint32_t)(r / NST) & 1u);
+  } else if (tid == 32) {
+    // MMA issuer
+    const uint32_t sa0 = smem_u32(sm);
+    bool ok = true;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % NST;
+      if (!mbar_wait(&full[s], (uint32_t)(i / NST) & 1u)) {
+        ok = false;
+        break;
+      }
+      tc5_fence_after();
+      const uint32_t sa = sa0 + s * Cfg::STAGE, sb = sa + TC_WTILE;
 #pragma unroll
       for (int kk = 0; kk < TC_K / 16; ++kk)
-        tc_mma(tmem, smem_desc(sa + kk * 256), smem_desc(sb + kk * 256), tc_idesc(NT), (i | kk) != 0);
-      tc_commit(&bar_mma[i % NST]);
+        tc5_mma(tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), f16_idesc(TC_M, NT), (i | kk) != 0);
+      tc5_commit(&empty[s]);
     }
+    tc5_commit(&done);  // arrives when every MMA issued above has completed
+    if (!ok) atomicExch(&fail, 1);
   }
-  if (tid == 0) tc_commit(&bar_done);  // arrives when every MMA issued above has completed
-  if (nk > 0 && !mbar_wait(&bar_done, 0)) ok = false;
-  tc_fence_after();
+  __syncwarp();
+  bool ok = nk == 0 || mbar_wait(&done, 0);
+  tc5_fence_after();
   // epilogue: thread = weight row m (tensor-memory lane); column 3t + p holds
   // piece p of token t, summed as (hi + mid) + lo
   const int m = warp * 32 + lane;
+  const int xr = TC_NP * T;
   float* dst = P + (int64_t)blockIdx.y * TC_TMAX * ldp + n0 + m;
   float acc = 0.0f;
 #pragma unroll 1
   for (int c0 = 0; c0 < xr; c0 += 16) {
     uint32_t v[16];
-    tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+    tc5_ld16_async(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+    tc5_ld_wait();
 #pragma unroll
     for (int q = 0; q < 16; ++q) {
       const int col = c0 + q;
       if (col >= xr) break;
       const int p = col % TC_NP;
       acc = p == 0 ? __uint_as_float(v[q]) : __fadd_rn(acc, __uint_as_float(v[q]));
-      if (p == TC_NP - 1) dst[(int64_t)(col / TC_NP) * ldp] = nk > 0 ? acc : 0.0f;
+      if (p == TC_NP - 1) dst[(int64_t)(col / TC_NP) * ldp] = nk > 0 && ok ? acc : 0.0f;
     }
   }
-  tc_fence_before();
+  tc5_fence_before();
   __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(Cfg::TMEM_COLS)
-                 : "memory");
-  if (!ok && tid == 0) atomicOr(err, DERR_TIMEOUT);
+  if (warp == 1) tc5_dealloc(tmem, Cfg::TMEM_COLS);
+  if (tid == 0 && (!ok || fail)) atomicOr(err, DERR_TIMEOUT);
 }
 
 // x[T][n] f32 -> three bf16 pieces, row 3t + p of [3 * TC_TMAX][ld] holding
@@ -616,12 +564,17 @@ template <int NT>
 static void tc_gemm_launch(dim3 grid, const __nv_bfloat16* W, int ldw, int nw, const __nv_bfloat16* xs, int T,
                            int ktiles, int per, float* P, int ldp, int* err, cudaStream_t st) {
   using Cfg = TcCfg<NT>;
-  constexpr int smem = Cfg::NST * Cfg::STAGE;
   static OncePerDevice attr;
   attr([&] {
-    cudaFuncSetAttribute(tc_gemm_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(tc_gemm_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
   });
-  tc_gemm_kernel<NT><<<grid, 128, smem, st>>>(W, ldw, nw, xs, T, ktiles, per, P, ldp, err);
+  CUtensorMap wmap, xmap;
+  if (!tma_map_bf16(&wmap, W, nw, ldw, ldw, TC_K, TC_M) ||
+      !tma_map_bf16(&xmap, xs, TC_NP * TC_TMAX, ldw, ldw, TC_K, NT)) {
+    flag_error(err, DERR_TMA, st);
+    return;
+  }
+  tc_gemm_kernel<NT><<<grid, 128, Cfg::SMEM, st>>>(wmap, xmap, T, ktiles, per, P, ldp, err);
 }
 
 // y[T][n] = act(x[T][d] . W^T + b) through the tcgen05 GEMM; T <= TC_TMAX.

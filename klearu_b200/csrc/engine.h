@@ -12,6 +12,8 @@ namespace kl {
 
 // Process-wide count of kernels launched by this library (defined in api.cu).
 void count_launch(unsigned n = 1);
+// err |= bits, in stream order (a host-side failure reported like a kernel's).
+void flag_error(int* err, int bits, cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // Hash families on the device.

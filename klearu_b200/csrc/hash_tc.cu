@@ -36,6 +36,7 @@
 #include <mutex>
 
 #include "engine.h"
+#include "tcgen05.cuh"
 
 namespace kl {
 namespace {
@@ -46,56 +47,10 @@ constexpr int TP_ASTAGE = TP_M * TP_KC * 2;
 constexpr int TP_NT = 192;         // 6 warps
 constexpr int TP_SMEM_MAX = 218 * 1024;  // + ~4.5 KB static, under the 227 KB per block
 
-__device__ __forceinline__ void tp_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void tp_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-
-// UMMA shared-memory descriptor, K-major, 128-byte swizzle: 8-row groups of
-// 1024 bytes (stride byte offset), descriptor version 1, layout type 2.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
-         (2ull << 61);
-}
-// kind::f16 instruction descriptor: f32 accumulator, bf16 A and B, both
-// K-major, M = 128, N = n.
-__device__ __forceinline__ uint32_t tp_idesc(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TP_M >> 4) << 24);
-}
-__device__ __forceinline__ void tp_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-      "l"(da), "l"(db), "r"(idesc), "r"(acc)
-      : "memory");
-}
-__device__ __forceinline__ void tp_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
-               : "memory");
-}
-// 16 consecutive accumulator columns of this thread's lane; tp_ld_wait()
-// before the registers are read.
-__device__ __forceinline__ void tp_ld16_async(uint32_t taddr, uint32_t* v) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];\n"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tp_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+__host__ __device__ constexpr uint32_t tp_idesc(int n) { return f16_idesc(TP_M, n); }
 __device__ __forceinline__ void tp_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-  tp_ld16_async(taddr, v);
-  tp_ld_wait();
-}
-// 2-D tiled TMA load (no multicast): box at element coordinates (x, y).
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+  tc5_ld16_async(taddr, v);
+  tc5_ld_wait();
 }
 
 struct TpArgs {
@@ -151,9 +106,9 @@ __global__ void __launch_bounds__(TP_NT, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
   }
-  tp_fence_before();
+  tc5_fence_before();
   __syncthreads();
-  tp_fence_after();
+  tc5_fence_after();
   const uint32_t tmem = tmem_s;
 
   if (warp == 0) {
@@ -192,7 +147,7 @@ __global__ void __launch_bounds__(TP_NT, 1)
           ok = false;
           break;
         }
-        tp_fence_after();
+        tc5_fence_after();
         const uint32_t d = tmem + buf * (uint32_t)a.Nh;
         for (int c = 0; c < a.kc; ++c, ++q) {
           const int s = (int)(q % a.nst);
@@ -200,15 +155,15 @@ __global__ void __launch_bounds__(TP_NT, 1)
             ok = false;
             break;
           }
-          tp_fence_after();
+          tc5_fence_after();
 #pragma unroll
           for (int kk = 0; kk < TP_KC / 16; ++kk)
-            tp_mma(d, sw128_desc(sa0 + s * TP_ASTAGE + kk * 32), sw128_desc(sb0 + c * a.Nh * 128 + kk * 32), idesc,
+            tc5_mma(d, sw128_desc(sa0 + s * TP_ASTAGE + kk * 32), sw128_desc(sb0 + c * a.Nh * 128 + kk * 32), idesc,
                    (c | kk) != 0);
-          tp_commit(&empty[s]);
+          tc5_commit(&empty[s]);
         }
         if (!ok) break;
-        tp_commit(&acc_full[buf]);
+        tc5_commit(&acc_full[buf]);
       }
       if (!ok) atomicExch(&fail, 1);
     }
@@ -224,7 +179,7 @@ __global__ void __launch_bounds__(TP_NT, 1)
         atomicExch(&fail, 1);
         break;
       }
-      tp_fence_after();
+      tc5_fence_after();
       const int row = t * TP_M + quad * 32 + lane;
       const uint32_t base = tmem + ((uint32_t)(quad * 32) << 16) + buf * (uint32_t)a.Nh;
       if (!MINABS) {
@@ -235,8 +190,8 @@ __global__ void __launch_bounds__(TP_NT, 1)
           if (g64 * 64 < ncols) {
             uint32_t v[64];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) tp_ld16_async(base + (uint32_t)(g64 * 64 + u * 16), v + u * 16);
-            tp_ld_wait();
+            for (int u = 0; u < 4; ++u) tc5_ld16_async(base + (uint32_t)(g64 * 64 + u * 16), v + u * 16);
+            tc5_ld_wait();
             uint32_t lo = 0, hi = 0;
 #pragma unroll
             for (int qq = 0; qq < 32; ++qq) {
@@ -248,7 +203,7 @@ __global__ void __launch_bounds__(TP_NT, 1)
           }
         }
         eb[8][lane] = 0u;
-        tp_fence_before();
+        tc5_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);  // the accumulator is free again
         if (row < a.n) {
@@ -293,12 +248,12 @@ __global__ void __launch_bounds__(TP_NT, 1)
           }
         }
       }
-      tp_fence_before();
+      tc5_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
-  tp_fence_before();
+  tc5_fence_before();
   __syncthreads();
   if (fail && threadIdx.x == 0) atomicOr(a.err, DERR_TIMEOUT);
   if (warp == 1)
@@ -306,7 +261,9 @@ __global__ void __launch_bounds__(TP_NT, 1)
                  : "memory");
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+}  // namespace
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -319,8 +276,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// bf16 matrix [rows][cols] with a row pitch of `ld` elements; box = box_cols x box_rows.
-bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows) {
+bool tma_map_bf16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -332,7 +288,6 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int6
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-}  // namespace
 
 // Host-side plane layout of the tensor-core projection: H groups of `tph`
 // tables; group g's rows [g*Nh, g*Nh + tph*k) hold its tables' planes in
@@ -359,7 +314,7 @@ bool tc_plane_layout(int d, int k, int L, TcPlanes* tp) {
 }
 
 bool tc_plane_map(TcPlanes* tp) {
-  return make_map(&tp->map, tp->planes, (int64_t)tp->H * tp->Nh, tp->dpad, tp->dpad, TP_KC, tp->Nh);
+  return tma_map_bf16(&tp->map, tp->planes, (int64_t)tp->H * tp->Nh, tp->dpad, tp->dpad, TP_KC, tp->Nh);
 }
 
 // Launches the tensor-core projection when the input allows it (bf16 rows,
@@ -371,7 +326,7 @@ bool launch_proj_tc(const DevHash& h, const DenseIn& in, const HashOut& out, int
       (reinterpret_cast<uintptr_t>(in.X) & 15) != 0 || in.ld_row < h.d || in.n <= 0)
     return false;
   CUtensorMap xmap;
-  if (!make_map(&xmap, in.X, in.n, h.d, in.ld_row, TP_KC, TP_M)) return false;
+  if (!tma_map_bf16(&xmap, in.X, in.n, h.d, in.ld_row, TP_KC, TP_M)) return false;
   static OncePerDevice attr;
   attr([&] {
     cudaFuncSetAttribute(proj_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM_MAX);

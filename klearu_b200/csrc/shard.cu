@@ -147,4 +147,12 @@ void launch_shard_or_masks(uint32_t* tmask, const uint32_t* all, int P, int nw, 
   count_launch();
 }
 
+namespace {
+__global__ void flag_error_kernel(int* err, int bits) { atomicOr(err, bits); }
+}  // namespace
+void flag_error(int* err, int bits, cudaStream_t st) {
+  flag_error_kernel<<<1, 1, 0, st>>>(err, bits);
+  count_launch();
+}
+
 }  // namespace kl
