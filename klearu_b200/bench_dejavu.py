@@ -6,7 +6,9 @@ LLaMA-7B-shaped MLP: hidden 4096, SwiGLU intermediate 11008, bf16 N(0, 0.02)
 weights; a rank-1000 predictor (4096 -> 1000 ReLU -> 11008 sigmoid) keeps the
 top ceil(0.1 * 11008) = 1101 neurons per token; Gaussian token activations.
 One decode step = 32 layers, each: kl_predictor_select_topk, then
-kl_sparse_mlp_forward on the selected neurons.  `--distinct` layers of
+kl_sparse_mlp_forward on the selected neurons; the same step is also timed
+through kl_ffn_stack_decode (adds RMSNorm and the residual add per layer, one
+CUDA graph).  `--distinct` layers of
 weights are cycled (2 x 0.6 GB of bf16 > L2), so every layer reads its
 weights from HBM.  Timed with CUDA events after a warm-up.  The CPU oracle
 runs one layer for one token as a reference.  Prints one JSON line per token
@@ -26,7 +28,7 @@ import torch
 
 from ._lib import check
 from .core import default_context
-from .dejavu import SparseMlp, SparsityPredictor
+from .dejavu import FfnStack, SparseMlp, SparsityPredictor
 
 HID, INTER, RANK = 4096, 11008, 1000
 
@@ -102,12 +104,33 @@ def main() -> None:
                 torch.cuda.synchronize()
                 ts.append(e0.elapsed_time(e1) / args.layers * 1e3)  # us per layer
             res[name] = float(np.median(ts))
+        # the whole decode step's FFN half as one call (kl_ffn_stack_decode: RMSNorm, select, sparse
+        # MLP and residual add per layer, replayed as a CUDA graph)
+        stack = FfnStack([layers[l % args.distinct][0] for l in range(args.layers)],
+                         [layers[l % args.distinct][1] for l in range(args.layers)],
+                         np.ones((args.layers, HID), np.float32), ctx=ctx)
+        hs = torch.randn(T, HID, device=dev, generator=g).contiguous()
+        for _ in range(3):
+            stack.decode(hs, 0.1)
+        ctx.sync()
+        ts = []
+        for _ in range(args.reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            stack.decode(hs, 0.1)
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        res["stack_step_ms"] = float(np.median(ts))
+        del stack
         mlp_bytes = T * k * HID * 2 * 3  # gate, up and down rows gathered per token (bf16)
         step_us = res["layer"] * args.layers
         line = {"bench": "dejavu_sparse_ffn", "config": "C3 LLaMA-7B MLP, predictor rank 1000, keep 1101 of 11008",
                 "tokens": T, "layers": args.layers, "us_per_layer": res["layer"],
                 "predictor_select_us": res["predictor_select"], "sparse_mlp_us": res["sparse_mlp"],
                 "decode_step_ms": step_us / 1e3, "tokens_per_s": T / (step_us / 1e6),
+                "ffn_stack_step_ms": res["stack_step_ms"],
+                "ffn_stack_tokens_per_s": T / (res["stack_step_ms"] / 1e3),
                 "predictor_GBs": pred_bytes / (res["predictor_select"] * 1e-6) / 1e9,
                 "predictor_TFLOPs_useful": 2 * T * (HID * RANK + RANK * INTER) / (res["predictor_select"] * 1e-6) / 1e12,
                 "sparse_mlp_GBs": mlp_bytes / (res["sparse_mlp"] * 1e-6) / 1e9,

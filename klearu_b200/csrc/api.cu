@@ -1278,6 +1278,9 @@ struct kl_net_s {
     }
     if (copy_stream) cudaStreamDestroy(copy_stream);
     if (comm_stream) cudaStreamSynchronize(comm_stream), cudaStreamDestroy(comm_stream);
+    if (side_stream) cudaStreamSynchronize(side_stream), cudaStreamDestroy(side_stream);
+    if (ev_fork) cudaEventDestroy(ev_fork);
+    if (ev_join) cudaEventDestroy(ev_join);
     if (ev_hidden) cudaEventDestroy(ev_hidden);
     if (ev_gather) cudaEventDestroy(ev_gather);
     if (gexec) cudaGraphExecDestroy(gexec);
@@ -1546,12 +1549,35 @@ struct kl_net_s {
   }
 
   // Optimizer updates of every layer for examples [s0, s0+nq) of the batch.
+  // The sparse-input layer's update (an HBM stream over all its feature rows)
+  // and the other layers' updates (latency-bound gathers of L2-resident rows)
+  // touch disjoint state, so without the phase profiler the first runs on a
+  // side stream, forked from and joined back into the context stream (in a
+  // captured step graph: two parallel branches).
+  cudaStream_t side_stream = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   void update_layers(const kl_batch& b, int s0, int nq, double lr) {
     (void)lr;  // the step's optimizer constants are in dopt (upload_opt)
-    for (int l = (int)layers.size() - 1; l >= 0; --l) update_layer(l, b, s0, nq);
-  }
-  void update_layer(int l, const kl_batch& b, int s0, int nq) {
+    const int nL = (int)layers.size();
+    if (prof || nL < 2) {
+      for (int l = nL - 1; l >= 0; --l) update_layer(l, b, s0, nq);
+      return;
+    }
+    if (!side_stream) {
+      ck(cudaStreamCreateWithFlags(&side_stream, cudaStreamNonBlocking), "side stream");
+      ck(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming), "event");
+      ck(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming), "event");
+    }
     cudaStream_t st = ctx->stream;
+    ck(cudaEventRecord(ev_fork, st), "event");
+    ck(cudaStreamWaitEvent(side_stream, ev_fork, 0), "stream wait");
+    update_layer(0, b, s0, nq, side_stream);
+    ck(cudaEventRecord(ev_join, side_stream), "event");
+    for (int l = nL - 1; l >= 1; --l) update_layer(l, b, s0, nq);
+    ck(cudaStreamWaitEvent(st, ev_join, 0), "stream wait");
+  }
+  void update_layer(int l, const kl_batch& b, int s0, int nq, cudaStream_t on = nullptr) {
+    cudaStream_t st = on ? on : ctx->stream;
     const OptStep* o = dopt.as<OptStep>();
     SparseIn in{b.rowptr + s0, b.idx, b.val, nq};
     {
