@@ -483,8 +483,10 @@ def main():
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(st)
+        th0 = time.perf_counter()
         for i in range(args.steps):
             e2e_step(i)
+        th1 = time.perf_counter()  # host time to issue the steps (the calls return before the GPU finishes)
         f1.record(st)
         torch.cuda.synchronize()
         barrier()
@@ -493,6 +495,7 @@ def main():
             dist.all_reduce(t2, op=dist.ReduceOp.MAX)
         e2e = {"value": world * B * args.steps / (float(t2.item()) / 1e3), "unit": "samples/s",
                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4,
+               "host_issue_ms_per_step": (th1 - th0) * 1e3 / args.steps,
                "api": "kl_net_train_step_host (C ABI): per-step upload of the pinned host CSR batch and loss readback"}
 
     # ---- (after the timed legs, which they would perturb) a forced table rebuild of every layer, and its amortised cost

@@ -110,7 +110,7 @@ def test_adaptive_policy_forced_and_threshold_rebuilds(gpu_ctx, orc):
     # threshold 0: every drift check (every min_interval steps) rebuilds
     m = Network(cfg, init, max_batch=32)
     m.set_rebuild_policy(True, min_interval=3, max_interval=1000, sample_fraction=0.5, drift_threshold=0.0, seed=5)
-    for hb in _batches(7, seed=12):
+    for hb in _batches(6, seed=12):  # checks at steps 3 and 6: the last step rebuilds
         m.train_step_host(hb, 1e-2)
     assert [m.rebuild_state(l)[2] for l in range(2)] == [2, 2]
     # the rebuilt output tables are a rebuild of the current weights
