@@ -781,10 +781,13 @@ void launch_probe(const ProbeArgs& a, cudaStream_t st) {
     const size_t bsm = (size_t)nwd * 4;
     static OncePerDevice battr;
     battr([&] {
+      cudaFuncSetAttribute(probe_bitmap_kernel<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize, PB_MAXWORDS * 4);
       cudaFuncSetAttribute(probe_bitmap_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, PB_MAXWORDS * 4);
       cudaFuncSetAttribute(probe_bitmap_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, PB_MAXWORDS * 4);
     });
-    if (nwd >= 8192) probe_bitmap_kernel<512><<<a.nq, 512, bsm, st>>>(b);
+    // threads per query grow with the bitmap (words cleared and scanned per thread)
+    if (nwd >= 16384) probe_bitmap_kernel<1024><<<a.nq, 1024, bsm, st>>>(b);
+    else if (nwd >= 8192) probe_bitmap_kernel<512><<<a.nq, 512, bsm, st>>>(b);
     else probe_bitmap_kernel<128><<<a.nq, 128, bsm, st>>>(b);
     count_launch();
     return;
