@@ -655,6 +655,12 @@ __device__ __forceinline__ void bias_update(float* bias, float* mb, float* vb, u
 
 constexpr int UPD_WARPS = 8;
 
+// One warp per touched row.  The row's (sample, coefficient) pairs are
+// marked in a per-warp sample bitmask, compacted into an ascending sample
+// list, and the gradient is summed over that list in order, eight samples'
+// X vectors loaded ahead of their sums (the loads are independent, the sums
+// stay sequential: bit-exact).
+constexpr int UPD_PF = 8;
 template <class W>
 __global__ void __launch_bounds__(UPD_WARPS * 32)
     rm_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
@@ -665,6 +671,7 @@ __global__ void __launch_bounds__(UPD_WARPS * 32)
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   uint32_t* mask = reinterpret_cast<uint32_t*>(dyn) + w * nwords;
   float* coef = reinterpret_cast<float*>(dyn + (size_t)UPD_WARPS * nwords * 4) + (size_t)w * nwords * 32;
+  uint16_t* list = reinterpret_cast<uint16_t*>(dyn + (size_t)UPD_WARPS * nwords * 4 * 33) + (size_t)w * nwords * 32;
   for (int i = l; i < nwords; i += 32) mask[i] = 0;
   __syncwarp();
   const int n = (int)S.ctr[0];
@@ -674,24 +681,47 @@ __global__ void __launch_bounds__(UPD_WARPS * 32)
     const uint32_t len = S.hist[row];
     const uint32_t start = S.cur[row] - len;
     seg_to_mask(S.ent_s, S.ent_v, start, len, coef, mask);
+    // ascending sample list (and the mask cleared for the next row)
+    int cnt = 0;
+    for (int w0 = 0; w0 < nwords; w0 += 32) {
+      const uint32_t mw = w0 + l < nwords ? mask[w0 + l] : 0u;
+      const int c = __popc(mw);
+      const int inc = warp_incl_scan(c);
+      int pos = cnt + inc - c;
+      uint32_t bb = mw;
+      while (bb) {
+        const int bit = __ffs(bb) - 1;
+        bb &= bb - 1;
+        list[pos++] = (uint16_t)((w0 + l) * 32 + bit);
+      }
+      cnt += __shfl_sync(FULL, inc, 31);
+      if (w0 + l < nwords) mask[w0 + l] = 0;
+    }
+    __syncwarp();
     float gb = 0.0f;
     for (int g0 = 0; g0 < d; g0 += 128) {
       const int c = g0 + l * 4;
       float g[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int wi = 0; wi < nwords; ++wi) {
-        uint32_t mw = mask[wi];
-        while (mw) {
-          const int b = __ffs(mw) - 1;
-          mw &= mw - 1;
-          const int s = wi * 32 + b;
-          const float cf = coef[s];
-          if (g0 == 0) gb = __fadd_rn(gb, cf);
-          if (c < d) {
-            const float4 xv = *reinterpret_cast<const float4*>(X + (int64_t)s * ldx + c);
-            g[0] = __fadd_rn(g[0], __fmul_rn(cf, xv.x));
-            g[1] = __fadd_rn(g[1], __fmul_rn(cf, xv.y));
-            g[2] = __fadd_rn(g[2], __fmul_rn(cf, xv.z));
-            g[3] = __fadd_rn(g[3], __fmul_rn(cf, xv.w));
+      for (int i0 = 0; i0 < cnt; i0 += UPD_PF) {
+        float4 xv[UPD_PF];
+        float cf[UPD_PF];
+#pragma unroll
+        for (int u = 0; u < UPD_PF; ++u) {
+          if (i0 + u < cnt) {
+            const uint32_t sidx = list[i0 + u];
+            cf[u] = coef[sidx];
+            xv[u] = c < d ? *reinterpret_cast<const float4*>(X + (int64_t)sidx * ldx + c)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < UPD_PF; ++u) {
+          if (i0 + u < cnt) {
+            if (g0 == 0) gb = __fadd_rn(gb, cf[u]);
+            g[0] = __fadd_rn(g[0], __fmul_rn(cf[u], xv[u].x));
+            g[1] = __fadd_rn(g[1], __fmul_rn(cf[u], xv[u].y));
+            g[2] = __fadd_rn(g[2], __fmul_rn(cf[u], xv[u].z));
+            g[3] = __fadd_rn(g[3], __fmul_rn(cf[u], xv[u].w));
           }
         }
       }
@@ -704,7 +734,6 @@ __global__ void __launch_bounds__(UPD_WARPS * 32)
       bias_update(bias, mb, vb, row, gb, o);
       S.hist[row] = 0;
     }
-    for (int i = l; i < nwords; i += 32) mask[i] = 0;
     __syncwarp();
   }
 }
@@ -1521,7 +1550,8 @@ void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, fl
   rm_scatter_kernel<<<g2, 256, 0, st>>>(A, S.cur, S.ent_s, S.ent_v);
   count_launch();
   const int nwords = (int)ceil_div(nq, 32);
-  const size_t sm = (size_t)UPD_WARPS * nwords * 4 * 33;
+  // per warp: mask, coefficients and the 16-bit sample list (<= 200 KB at 4096 samples)
+  const size_t sm = (size_t)UPD_WARPS * nwords * (4 * 33 + 2 * 32);
   const int grid = (int)std::min<int64_t>(upd_grid(), ceil_div(maxn, UPD_WARPS));
   if (wdtype == KL_DTYPE_BF16) {
     cudaFuncSetAttribute(rm_update_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
