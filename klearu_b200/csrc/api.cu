@@ -1364,7 +1364,8 @@ struct kl_net_s {
   OptStep opt_host{};
   void upload_opt(double lr) {
     opt_host = opt_step(lr);
-    ck(cudaMemcpyAsync(dopt.p, &opt_host, sizeof(OptStep), cudaMemcpyHostToDevice, ctx->stream), "upload optimizer step");
+    launch_set_opt(dopt.as<OptStep>(), opt_host, ctx->stream);
+    ck_launch("optimizer step");
   }
   OptStep opt_step(double lr) const {
     OptStep o;

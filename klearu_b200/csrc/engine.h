@@ -356,4 +356,6 @@ void launch_rmsnorm(const float* x, int T, int n, const float* w, float eps, int
                     cudaStream_t st);
 void launch_residual_add(float* h, const float* d, int64_t n, cudaStream_t st);
 
+void launch_set_opt(OptStep* dst, const OptStep& v, cudaStream_t st);
+
 }  // namespace kl

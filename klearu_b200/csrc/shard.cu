@@ -149,7 +149,14 @@ void launch_shard_or_masks(uint32_t* tmask, const uint32_t* all, int P, int nw, 
 
 namespace {
 __global__ void flag_error_kernel(int* err, int bits) { atomicOr(err, bits); }
+__global__ void set_opt_kernel(OptStep* dst, OptStep v) { *dst = v; }
 }  // namespace
+// The step's optimizer constants travel as a kernel argument: a copy from
+// pageable host memory could make the host wait for the stream.
+void launch_set_opt(OptStep* dst, const OptStep& v, cudaStream_t st) {
+  set_opt_kernel<<<1, 1, 0, st>>>(dst, v);
+  count_launch();
+}
 void flag_error(int* err, int bits, cudaStream_t st) {
   flag_error_kernel<<<1, 1, 0, st>>>(err, bits);
   count_launch();
