@@ -194,81 +194,6 @@ __device__ __forceinline__ void rm_load_tile(unsigned char* mt, const unsigned c
   __syncwarp();
 }
 
-// dX partial of one warp's staged tile: out[c] = sum over the 32 rows r of
-// lg_r * W_r[c], c < EPT, as the product [pieces x rows] . [rows x columns]
-// on the tensor cores.  A (16 x 16 per K step): rows 0..2 are the hi / mid /
-// lo bf16 pieces of lg (lg = hi + mid + lo exactly), rows 3..15 zero; B: the
-// staged bf16 rows, loaded K-by-N with ldmatrix.trans; f32 accumulation.
-// Every product is exact; only the summation order differs from a
-// sequential sum.  Rows >= nw of the tile are zeroed first (stale shared
-// memory could hold non-finite bit patterns).
-template <int EPT, int PITCH>
-__device__ __forceinline__ void rm_dx_mma(unsigned char* mt, int nw, float lgv, float* out) {
-  const int l = threadIdx.x & 31;
-  if (nw < 32) {
-    constexpr int V = EPT * 2 / 16;  // 16-byte vectors per row
-    for (int q = l; q < (32 - nw) * V; q += 32)
-      *reinterpret_cast<uint4*>(mt + (nw + q / V) * PITCH + (q % V) * 16) = make_uint4(0u, 0u, 0u, 0u);
-    __syncwarp();
-  }
-  const int g = l >> 2, c2 = (l & 3) * 2;
-  auto piece = [&](float v) -> float {  // piece g (0, 1, 2) of v, 0 for g >= 3
-    const float hi = __bfloat162float(__float2bfloat16_rn(v));
-    const float r1 = __fsub_rn(v, hi);
-    const float mid = __bfloat162float(__float2bfloat16_rn(r1));
-    const float lo = __fsub_rn(r1, mid);
-    return g == 0 ? hi : g == 1 ? mid : g == 2 ? lo : 0.0f;
-  };
-  auto pack = [](float a, float b) -> uint32_t {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // a -> low half
-    return *reinterpret_cast<const uint32_t*>(&h);
-  };
-  uint32_t afr[2][2];
-#pragma unroll
-  for (int ks = 0; ks < 2; ++ks) {
-    const int k0 = ks * 16 + c2;
-    const float g0 = __shfl_sync(FULL, lgv, k0), g1 = __shfl_sync(FULL, lgv, k0 + 1);
-    const float g8 = __shfl_sync(FULL, lgv, k0 + 8), g9 = __shfl_sync(FULL, lgv, k0 + 9);
-    afr[ks][0] = pack(piece(g0), piece(g1));
-    afr[ks][1] = pack(piece(g8), piece(g9));
-  }
-  // ldmatrix.x4.trans: lane l addresses row (l & 15) of the K step and the
-  // 8-column block (l >> 4) of the current pair of N tiles
-  const uint32_t base = smem_u32(mt) + (uint32_t)((l & 15) * PITCH + (l >> 4) * 16);
-#pragma unroll 4
-  for (int n0 = 0; n0 < EPT; n0 += 16) {
-    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-      uint32_t b0, b1, b2, b3;
-      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
-                   : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3)
-                   : "r"(base + (uint32_t)(ks * 16 * PITCH + n0 * 2)));
-      asm volatile(
-          "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-          "{%0, %1, %2, %3};\n"
-          : "+f"(d0[0]), "+f"(d0[1]), "+f"(d0[2]), "+f"(d0[3])
-          : "r"(afr[ks][0]), "r"(0u), "r"(afr[ks][1]), "r"(0u), "r"(b0), "r"(b1));
-      asm volatile(
-          "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-          "{%0, %1, %2, %3};\n"
-          : "+f"(d1[0]), "+f"(d1[1]), "+f"(d1[2]), "+f"(d1[3])
-          : "r"(afr[ks][0]), "r"(0u), "r"(afr[ks][1]), "r"(0u), "r"(b2), "r"(b3));
-    }
-    // rows 0, 1, 2 (lanes 0-3, 4-7, 8-11) hold the pieces' sums: (hi + mid) + lo
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      float v0 = j ? d1[0] : d0[0], v1 = j ? d1[1] : d0[1];
-      const float m0 = __shfl_down_sync(FULL, v0, 4), m1 = __shfl_down_sync(FULL, v1, 4);
-      const float o0 = __shfl_down_sync(FULL, v0, 8), o1 = __shfl_down_sync(FULL, v1, 8);
-      if (l < 4) {
-        out[n0 + j * 8 + c2] = __fadd_rn(__fadd_rn(v0, m0), o0);
-        out[n0 + j * 8 + c2 + 1] = __fadd_rn(__fadd_rn(v1, m1), o1);
-      }
-    }
-  }
-}
-
 template <class W, int MODE, int TILEB>
 __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
   constexpr int EPT = TILEB / (int)sizeof(W);
@@ -357,11 +282,6 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
   // input gradient of this block's rows (old weights, layer.rs:206-209)
   for (int tI = 0; tI < ntiles; ++tI) {
     if (MODE == RM_DX || ntiles > 1) rm_load_tile<W, TILEB>(mt, Wb, rowbytes, tI, myid, nw);
-    if constexpr (sizeof(W) == 2) {
-      // bf16 rows: the warp's dX partial over its 32 staged rows on the tensor
-      // cores (mma.sync m16n8k16), lg split into three exact bf16 pieces
-      rm_dx_mma<EPT, PITCH>(mt, nw, lgv, wpart + w * EPT);
-    } else {
     float part[CPL];
 #pragma unroll
     for (int c = 0; c < CPL; ++c) part[c] = 0.0f;
@@ -383,7 +303,6 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
     }
 #pragma unroll
     for (int c = 0; c < CPL; ++c) wpart[w * EPT + l * CPL + c] = part[c];
-    }
     __syncthreads();
     for (int col = threadIdx.x; col < EPT; col += RM_RPB) {
       const int kg = tI * EPT + col;
