@@ -15,12 +15,13 @@
 //    always serves group b % H, so it loads its planes once;
 //  * accumulator: f32 in tensor memory, two buffers so that the epilogue of
 //    one tile overlaps the MMAs of the next;
-//  * epilogue (4 warps, one row per thread): tcgen05.ld of the row's
+//  * epilogue (8 warps: one row per thread, the two warps of a TMEM lane
+//    quadrant on half the tables each): tcgen05.ld of the row's
 //    projections, sign-pack into each table's K-bit code, bucket index and
 //    min |projection| written straight to the hash outputs.
 //
 // Warp roles: warp 0 issues the TMA loads, warp 1 owns tensor memory and
-// issues the MMAs (one thread), warps 2..5 run the epilogue.  Every wait is
+// issues the MMAs (one thread), warps 2..9 run the epilogue.  Every wait is
 // bounded; a wait that gives up records DERR_TIMEOUT and the kernel winds
 // down without leaving copies in flight.
 //
@@ -44,8 +45,8 @@ namespace {
 constexpr int TP_M = 128;          // rows per tile (MMA M)
 constexpr int TP_KC = 64;          // K elements per TMA box / stage: 128-byte rows
 constexpr int TP_ASTAGE = TP_M * TP_KC * 2;
-constexpr int TP_NT = 192;         // 6 warps
-constexpr int TP_SMEM_MAX = 218 * 1024;  // + ~4.5 KB static, under the 227 KB per block
+constexpr int TP_NT = 320;         // 10 warps: TMA, MMA, 8 epilogue warps
+constexpr int TP_SMEM_MAX = 213 * 1024;  // + ~9.5 KB static, under the 227 KB per block
 
 __host__ __device__ constexpr uint32_t tp_idesc(int n) { return f16_idesc(TP_M, n); }
 __device__ __forceinline__ void tp_ld16(uint32_t taddr, uint32_t (&v)[16]) {
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(TP_NT, 1)
     proj_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap pmap, TpArgs a) {
   extern __shared__ unsigned char tp_dyn[];
   __shared__ uint64_t full[16], empty[16], bfull, acc_full[2], acc_empty[2];
-  __shared__ uint32_t ebits[4][9][32];  // per epilogue warp: packed sign bits [word][lane] (+1 spare word)
+  __shared__ uint32_t ebits[8][9][32];  // per epilogue warp: packed sign bits [word][lane] (+1 spare word)
   __shared__ uint32_t tmem_s;
   __shared__ int fail;
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tp_dyn) + 1023) & ~uintptr_t(1023));
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(TP_NT, 1)
     mbar_init(&bfull, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 8);
     }
     fail = 0;
     fence_mbar_init();
@@ -168,10 +169,13 @@ __global__ void __launch_bounds__(TP_NT, 1)
       if (!ok) atomicExch(&fail, 1);
     }
   } else {
-    // epilogue: warp w reads tensor-memory lanes 32 * (w % 4) .. + 31
-    const int quad = warp & 3;
+    // epilogue: warp w reads tensor-memory lanes 32 * (w % 4) .. + 31; the two
+    // warps of a lane quadrant split the group's tables in halves
+    const int quad = warp & 3, half = (warp - 2) >> 2;
     const int kbits = a.k;
-    const int ncols = min(a.tph, a.L - g * a.tph) * kbits;  // valid projection columns of this group
+    const int ntab_g = min(a.tph, a.L - g * a.tph);     // tables of this group
+    const int lt_lo = half ? ntab_g / 2 : 0, lt_hi = half ? ntab_g : ntab_g / 2;
+    const int c_lo = lt_lo * kbits, c_hi = lt_hi * kbits;  // this warp's projection columns
     uint32_t j = 0;
     for (int t = t0; t < tiles; t += tstride, ++j) {
       const uint32_t buf = j & 1u, use = j >> 1;
@@ -184,10 +188,10 @@ __global__ void __launch_bounds__(TP_NT, 1)
       const uint32_t base = tmem + ((uint32_t)(quad * 32) << 16) + buf * (uint32_t)a.Nh;
       if (!MINABS) {
         // sign bits: 64 columns per round (4 loads, one wait), 2 words each
-        uint32_t (*eb)[32] = ebits[quad];
+        uint32_t (*eb)[32] = ebits[warp - 2];
 #pragma unroll
         for (int g64 = 0; g64 < 4; ++g64) {
-          if (g64 * 64 < ncols) {
+          if (g64 * 64 < c_hi && g64 * 64 + 64 > c_lo) {
             uint32_t v[64];
 #pragma unroll
             for (int u = 0; u < 4; ++u) tc5_ld16_async(base + (uint32_t)(g64 * 64 + u * 16), v + u * 16);
@@ -207,9 +211,8 @@ __global__ void __launch_bounds__(TP_NT, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);  // the accumulator is free again
         if (row < a.n) {
-          const int ntab = ncols / kbits;
           const uint32_t kmask = kbits >= 32 ? 0xffffffffu : (1u << kbits) - 1u;
-          for (int lt = 0; lt < ntab; ++lt) {
+          for (int lt = lt_lo; lt < lt_hi; ++lt) {
             const int p0 = lt * kbits, w0 = p0 >> 5, off = p0 & 31;
             const uint64_t win = (uint64_t)eb[w0][lane] | ((uint64_t)eb[w0 + 1][lane] << 32);
             const uint64_t code = (uint64_t)((uint32_t)(win >> off) & kmask);
@@ -221,15 +224,15 @@ __global__ void __launch_bounds__(TP_NT, 1)
         __syncwarp();  // eb is rewritten by the next tile
         continue;
       }
-      int tab = g * a.tph, bit = 0;
+      int tab = g * a.tph + lt_lo, bit = 0;
       uint64_t code = 0;
       float mn = INFINITY;
-      for (int c0 = 0; c0 < ncols; c0 += 16) {
+      for (int cb = c_lo & ~15; cb < c_hi; cb += 16) {
         uint32_t v[16];
-        tp_ld16(base + (uint32_t)c0, v);
+        tp_ld16(base + (uint32_t)cb, v);
 #pragma unroll
         for (int qq = 0; qq < 16; ++qq) {
-          if (c0 + qq < ncols) {
+          if (cb + qq >= c_lo && cb + qq < c_hi) {
             const float p = __uint_as_float(v[qq]);
             if (p >= 0.0f) code |= 1ull << bit;
             mn = fminf(mn, fabsf(p));
