@@ -50,18 +50,25 @@ __global__ void ins_count_kernel(DevTables T, const uint16_t* bkt, int64_t bkt_l
 // ---- insert pass 2: exclusive scan over chunks per (table, bucket), then the
 // per-bucket plan: FIFO keeps `base` old ids (shifted to the front) and drops
 // the first `skip` new ones; reservoir seeds the packed slot array.
+// One warp per (table, bucket): the scan over the chunks runs 32 chunks at a
+// time (a warp scan per round), so a rebuild of millions of rows (thousands
+// of chunks) does not walk them one dependent load after another.
 __global__ void ins_plan_kernel(DevTables T, uint32_t* chunk_cnt, int nchunks, uint32_t* total,
                                 uint32_t* basev, uint32_t* skipv, unsigned long long* temp) {
-  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (g >= (int64_t)T.L * T.nb) return;
   const int t = (int)(g / T.nb), b = (int)(g % T.nb);
   uint32_t run = 0;
-  for (int c = 0; c < nchunks; ++c) {
+  for (int c0 = 0; c0 < nchunks; c0 += 32) {
+    const int c = c0 + lane;
     uint32_t* p = chunk_cnt + ((int64_t)t * nchunks + c) * T.nb + b;
-    uint32_t v = *p;
-    *p = run;
-    run += v;
+    const uint32_t v = c < nchunks ? *p : 0u;
+    const uint32_t inc = (uint32_t)warp_incl_scan((int)v);
+    if (c < nchunks) *p = run + inc - v;
+    run += __shfl_sync(FULL, inc, 31);
   }
+  if (lane != 0) return;
   total[g] = run;
   const uint32_t nnew = run;
   const uint32_t len0 = min(T.len[g], (uint32_t)T.cap);
@@ -632,7 +639,7 @@ void launch_tables_insert(const DevTables& T, const uint32_t* ids, const uint16_
   const size_t sm = (size_t)T.nb * 4;
   ins_count_kernel<<<g, 32, sm, st>>>(T, bkt, bkt_ld, n, s.chunk_cnt, nchunks);
   count_launch();
-  ins_plan_kernel<<<(unsigned)ceil_div(LB, 256), 256, 0, st>>>(T, s.chunk_cnt, nchunks, s.total,
+  ins_plan_kernel<<<(unsigned)ceil_div(LB * 32, 256), 256, 0, st>>>(T, s.chunk_cnt, nchunks, s.total,
                                                                s.base, s.skip, s.temp);
   count_launch();
   ins_place_kernel<<<g, 32, sm, st>>>(T, ids, bkt, bkt_ld, n, s.chunk_cnt, nchunks, s.base,
