@@ -886,7 +886,7 @@ __global__ void rm_lg_zero_kernel(float* LGd, int64_t ldu, const uint32_t* ctr, 
 //     the rest use g = 0.  slot[f] and hist[f] are zeroed for the next step
 //     (by fm_hist_clear_kernel when a row spans several items).
 // ---------------------------------------------------------------------------
-constexpr int FM_PF = 16;
+constexpr int FM_PF = 32;
 constexpr int FM_NT = 256;
 
 constexpr int FM_SHORT = 32;  // segments up to this length are ranked inside one warp
@@ -1007,18 +1007,15 @@ __global__ void __launch_bounds__(1024)
       float g = 0.f;
       if (c < N) {
         for (int i0 = 0; i0 < base; i0 += FM_PF) {
-          float lv[FM_PF], cf[FM_PF];
-#pragma unroll
-          for (int u = 0; u < FM_PF; ++u) {
-            if (i0 + u < base) {
-              const uint32_t s = list[i0 + u];
-              cf[u] = coef[s];
-              lv[u] = lgd[(int64_t)s * ldl + c];
-            }
-          }
+          // FM_PF global loads in flight; the coefficients are read from
+          // shared memory as they are used
+          float lv[FM_PF];
 #pragma unroll
           for (int u = 0; u < FM_PF; ++u)
-            if (i0 + u < base) g = __fadd_rn(g, __fmul_rn(cf[u], lv[u]));
+            if (i0 + u < base) lv[u] = lgd[(int64_t)list[i0 + u] * ldl + c];
+#pragma unroll
+          for (int u = 0; u < FM_PF; ++u)
+            if (i0 + u < base) g = __fadd_rn(g, __fmul_rn(coef[list[i0 + u]], lv[u]));
         }
       }
       G[(int64_t)k * ldg + c] = g;
