@@ -85,7 +85,8 @@ __device__ __forceinline__ void opt_apply(float& w, float& m, float& v, float g,
 template <class W>
 __global__ void __launch_bounds__(128) fm_forward_kernel(const void* Wm, int ldw, int d,
                                                          const float* bias, int act, SparseIn in,
-                                                         ActiveSet A, float* h, int ldh, int* err, int ch) {
+                                                         ActiveSet A, float* h, int ldh, int* err, int ch,
+                                                         int gather) {
   // chunks of `ch` nonzeros: their whole feature rows (ldw weights each, one
   // contiguous line per nonzero) are staged in shared memory with coalesced,
   // independent 16-byte loads; then each active neuron's thread sums its
@@ -94,9 +95,12 @@ __global__ void __launch_bounds__(128) fm_forward_kernel(const void* Wm, int ldw
   extern __shared__ __align__(16) unsigned char dyn[];
   uint32_t* sidx = reinterpret_cast<uint32_t*>(dyn);
   float* sval = reinterpret_cast<float*>(sidx + ch);
-  W* wt = reinterpret_cast<W*>(dyn + round_up((int64_t)ch * 8, 16));  // [ch][ldw]
+  W* wt = reinterpret_cast<W*>(dyn + round_up((int64_t)max(ch, 64) * 8, 16));  // [ch][ldw]
   const int s = blockIdx.x;
   const int na = min(A.cnt[s], NT * MAXJ);
+  // gather mode (see below) when this example's active neurons are few
+  const bool use_gather = gather && (int64_t)na * 8 <= (int64_t)ldw;
+  if (use_gather) ch = 64;
   const uint32_t* ids = A.ids + (int64_t)s * A.stride;
   float acc[MAXJ];
   uint32_t myid[MAXJ];
@@ -120,6 +124,33 @@ __global__ void __launch_bounds__(128) fm_forward_kernel(const void* Wm, int ldw
       sval[e] = in.val[c0 + e];
     }
     __syncthreads();
+    if (use_gather) {
+      // Wide rows with few active neurons (a dense input: every row is a
+      // nonzero): each thread loads only its neurons' weights of the chunk's
+      // rows, 16 independent loads ahead of the ordered sum.
+#pragma unroll
+      for (int j = 0; j < MAXJ; ++j) {
+        const int a = threadIdx.x + j * NT;
+        if (a < na) {
+          float x = acc[j];
+          const W* col = static_cast<const W*>(Wm) + myid[j];
+          for (int e0 = 0; e0 < m; e0 += 16) {
+            float wv[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              const uint32_t r = e0 + u < m ? sidx[e0 + u] : 0xffffffffu;
+              wv[u] = r != 0xffffffffu ? to_f(col[(int64_t)r * ldw]) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+              if (e0 + u < m && sidx[e0 + u] != 0xffffffffu) x = __fadd_rn(x, __fmul_rn(wv[u], sval[e0 + u]));
+          }
+          acc[j] = x;
+        }
+      }
+      __syncthreads();
+      continue;
+    }
     for (int q0 = threadIdx.x; q0 < m * vpr; q0 += 4 * NT) {
       uint4 v[4];
 #pragma unroll
@@ -1314,17 +1345,21 @@ void launch_fm_forward(const void* W, int wdtype, int ldw, int d, const float* b
                        SparseIn in, ActiveSet A, float* h, int ldh, int* err, cudaStream_t st) {
   if (in.n <= 0) return;
   const size_t rowb = (size_t)ldw * (wdtype == KL_DTYPE_BF16 ? 2 : 4);
+  // Wide rows of which only a small part is active (the README MLP's dense
+  // 784-dim input against 1024 neurons, ~10 % active) gather the active
+  // columns instead of staging whole rows.
+  const int gather = rowb > 1024 ? 1 : 0;  // decided per example from its active count
   const int ch = (int)std::max<size_t>(8, std::min<size_t>(64, (size_t)(48 * 1024) / rowb));
-  const size_t sm = (size_t)round_up((int64_t)ch * 8, 16) + (size_t)ch * rowb;
+  const size_t sm = (size_t)round_up((int64_t)std::max(ch, 64) * 8, 16) + (size_t)ch * rowb;
   static OncePerDevice attr;
   attr([&] {
     cudaFuncSetAttribute(fm_forward_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(fm_forward_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   });
   if (wdtype == KL_DTYPE_BF16)
-    fm_forward_kernel<__nv_bfloat16><<<in.n, 128, sm, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err, ch);
+    fm_forward_kernel<__nv_bfloat16><<<in.n, 128, sm, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err, ch, gather);
   else
-    fm_forward_kernel<float><<<in.n, 128, sm, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err, ch);
+    fm_forward_kernel<float><<<in.n, 128, sm, st>>>(W, ldw, d, bias, act, in, A, h, ldh, err, ch, gather);
   count_launch();
 }
 

@@ -319,3 +319,20 @@ def test_host_batch_train_step_matches_device_batches(gpu_ctx):
         for k in x:
             assert (x[k] == y[k]).all(), (l, k)
     assert b.train_step_host(HostBatch.from_examples([]), 1e-3) == 0.0
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_c0_readme_mlp_shape(gpu_ctx, dtype):
+    # the README MLP at full width (784 -> 1024 ReLU -> 10 softmax): wide hidden
+    # rows with ~10 % active neurons take the active-column gather forward
+    cfg = S.config_c0()
+    g, o = pair(cfg, dtype, max_batch=32)
+    rng = np.random.default_rng(8)
+    hb = S.dense_batch(rng, 6, 784, 10)
+    forward_sets_match(g, o, hb, exact_values=True)
+    for _ in range(2):
+        hb = S.dense_batch(rng, 32, 784, 10)
+        lg = g.train_step(_examples(hb), 1e-3, mode="batched")
+        lo = o.train_step(hb, 1e-3, mode="batched")
+        assert abs(lg - lo) <= 1e-4 * abs(lo) + 1e-6
+    assert_layers_close(g, o, 2, dtype)
