@@ -466,16 +466,19 @@ def main():
             hosts.append((hb, arrs))
         loss_h = torch.zeros(1).pin_memory()
         bi = sum(int(a.numel()) * 4 for a in hosts[0][1].values())
+        # the kl_batch descriptors of the host arrays (what a caller hands over)
+        descs = [_lib.BatchC(hb.batch, arrs["rowptr"].data_ptr(), arrs["idx"].data_ptr(), arrs["val"].data_ptr(),
+                             arrs["label_ptr"].data_ptr(), arrs["labels"].data_ptr(), int(hb.rowptr[-1]),
+                             int(hb.label_ptr[-1])) for hb, arrs in hosts]
+        train_host = lib.kl_net_train_step_host
+        lp = loss_h.data_ptr()
 
         def e2e_step(i):
             # the public host-batch call: it packs the pinned CSR arrays,
             # uploads them on its copy stream and enqueues the loss readback
-            hb, arrs = hosts[i % len(hosts)]
-            c = _lib.BatchC(hb.batch, arrs["rowptr"].data_ptr(), arrs["idx"].data_ptr(), arrs["val"].data_ptr(),
-                            arrs["label_ptr"].data_ptr(), arrs["labels"].data_ptr(), int(hb.rowptr[-1]),
-                            int(hb.label_ptr[-1]))
-            _lib.check(lib.kl_net_train_step_host(net.h, C.byref(c), 1e-3, _lib.MODE_BATCHED, loss_h.data_ptr()),
-                       net.ctx.h)
+            st_ = train_host(net.h, C.byref(descs[i % len(descs)]), 1e-3, _lib.MODE_BATCHED, lp)
+            if st_:
+                _lib.check(st_, net.ctx.h)
 
         for i in range(3):
             e2e_step(i)
