@@ -94,8 +94,9 @@ __global__ void __launch_bounds__(128) fm_forward_kernel(const void* Wm, int ldw
   constexpr int NT = 128, MAXJ = 8;
   extern __shared__ __align__(16) unsigned char dyn[];
   uint32_t* sidx = reinterpret_cast<uint32_t*>(dyn);
-  float* sval = reinterpret_cast<float*>(sidx + ch);
-  W* wt = reinterpret_cast<W*>(dyn + round_up((int64_t)max(ch, 64) * 8, 16));  // [ch][ldw]
+  const int chx = max(ch, 64);  // capacity of sidx / sval (64 in gather mode)
+  float* sval = reinterpret_cast<float*>(sidx + chx);
+  W* wt = reinterpret_cast<W*>(dyn + round_up((int64_t)chx * 8, 16));  // [ch][ldw]
   const int s = blockIdx.x;
   const int na = min(A.cnt[s], NT * MAXJ);
   // gather mode (see below) when this example's active neurons are few
