@@ -485,6 +485,7 @@ def main():
         torch.cuda.synchronize()
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        rb0 = int(net.stats(1).rebuilds)
         f0.record(st)
         th0 = time.perf_counter()
         for i in range(args.steps):
@@ -499,6 +500,7 @@ def main():
         e2e = {"value": world * B * args.steps / (float(t2.item()) / 1e3), "unit": "samples/s",
                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4,
                "host_issue_ms_per_step": (th1 - th0) * 1e3 / args.steps,
+               "table_rebuilds_in_window": int(net.stats(1).rebuilds) - rb0,
                "api": "kl_net_train_step_host (C ABI): per-step upload of the pinned host CSR batch and loss readback"}
 
     # ---- (after the timed legs, which they would perturb) a forced table rebuild of every layer, and its amortised cost
