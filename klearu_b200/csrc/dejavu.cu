@@ -302,16 +302,16 @@ __global__ void __launch_bounds__(TK_NT) topk_kernel(const float* __restrict__ s
   const uint32_t above = above_s, need = (uint32_t)k - above;
   // keys above b*: taken in any order; keys of b*: candidates, ranked
   // exactly among themselves (score desc, index asc) for the remaining slots
-  for (int i = tid; i < n; i += TK_NT) {
-    const float v = row[i];
-    const int b = bin_of(v);
-    if (b < bstar) continue;
+  // warp-aggregated appends: one shared-memory atomic per warp and list
+  for (int i0 = 0; i0 < n; i0 += TK_NT) {
+    const int i = i0 + tid;
+    const float v = i < n ? row[i] : 0.0f;
+    const int b = i < n ? bin_of(v) : -1;
     const uint64_t key = ((uint64_t)(~__float_as_uint(v)) << 32) | (uint32_t)i;
-    if (b > bstar) keys[atomicAdd(&n_taken, 1u)] = key;
-    else {
-      const uint32_t c = atomicAdd(&n_cand, 1u);
-      if (c < TK_MAXC) cands[c] = key;
-    }
+    const int pt = warp_append(b > bstar, &n_taken);
+    if (pt >= 0) keys[pt] = key;
+    const int pc = warp_append(b == bstar, &n_cand);
+    if (pc >= 0 && pc < TK_MAXC) cands[pc] = key;
   }
   __syncthreads();
   const uint32_t nc = n_cand;
