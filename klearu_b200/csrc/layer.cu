@@ -1381,8 +1381,9 @@ static void rm_launch(const RmArgs& a, int nq, cudaStream_t st) {
 }
 template <class W, int MODE>
 static void rm_launch_t(const RmArgs& a, int nq, cudaStream_t st) {
-  if ((int64_t)a.ldw * (int64_t)sizeof(W) <= 256) rm_launch<W, MODE, 256>(a, nq, st);
-  else rm_launch<W, MODE, 512>(a, nq, st);
+  // 256-byte column tiles for every width: wider rows take several tiles, and
+  // the smaller staging buffers keep three blocks (24 warps) per SM
+  rm_launch<W, MODE, 256>(a, nq, st);
 }
 void launch_rm_forward(const RmArgs& a, int nq, int mode, cudaStream_t st) {
   if (nq <= 0) return;
