@@ -128,22 +128,22 @@ __global__ void __launch_bounds__(128) fm_forward_kernel(const void* Wm, int ldw
     if (use_gather) {
       // Wide rows with few active neurons (a dense input: every row is a
       // nonzero): each thread loads only its neurons' weights of the chunk's
-      // rows, 16 independent loads ahead of the ordered sum.
+      // rows, 32 independent loads ahead of the ordered sum.
 #pragma unroll
       for (int j = 0; j < MAXJ; ++j) {
         const int a = threadIdx.x + j * NT;
         if (a < na) {
           float x = acc[j];
           const W* col = static_cast<const W*>(Wm) + myid[j];
-          for (int e0 = 0; e0 < m; e0 += 16) {
-            float wv[16];
+          for (int e0 = 0; e0 < m; e0 += 32) {
+            float wv[32];
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
+            for (int u = 0; u < 32; ++u) {
               const uint32_t r = e0 + u < m ? sidx[e0 + u] : 0xffffffffu;
               wv[u] = r != 0xffffffffu ? to_f(col[(int64_t)r * ldw]) : 0.0f;
             }
 #pragma unroll
-            for (int u = 0; u < 16; ++u)
+            for (int u = 0; u < 32; ++u)
               if (e0 + u < m && sidx[e0 + u] != 0xffffffffu) x = __fadd_rn(x, __fmul_rn(wv[u], sval[e0 + u]));
           }
           acc[j] = x;
