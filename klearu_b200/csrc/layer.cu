@@ -766,8 +766,8 @@ constexpr int RDU_ST = 4;                // cp.async pipeline stages
 // not active) leaves a sum unchanged and the result equals the sum over the
 // active samples in ascending order (finite activations assumed).  The
 // gradient matrix is left as read; rm_lg_zero_kernel restores its zeros.
-template <class W, bool BIAS, int RPW>
-__device__ __forceinline__ void rdu_sum_chunk(const float (*xs)[RDU_COLS], const float (*ls)[8 * RPW], int ns,
+template <class W, bool BIAS, int RPW, int ROWS>
+__device__ __forceinline__ void rdu_sum_chunk(const float (*xs)[RDU_COLS], const float (*ls)[ROWS], int ns,
                                               int w, int l, float* g, float* gb) {
   for (int j = 0; j < ns; ++j) {
     const float xv = xs[j][l];
@@ -793,13 +793,14 @@ __device__ __forceinline__ void rdu_sum_chunk(const float (*xs)[RDU_COLS], const
   }
 }
 
-template <class W, int RPW>
-__global__ void __launch_bounds__(256)
+template <class W, int RPW, int NWB>
+__global__ void __launch_bounds__(NWB * 32)
     rm_dense_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
                            const float* X, int ldx, uint32_t* bits, const uint32_t* touched, const uint32_t* ctr,
                            float* LGd, int64_t ldu, int nq, const OptStep* op) {
   constexpr int RDU_RPW = RPW;
-  constexpr int RDU_ROWS = 8 * RPW;
+  constexpr int RDU_ROWS = NWB * RPW;  // slots per block
+  constexpr int NT = NWB * 32;
   const OptStep o = *op;
   __shared__ __align__(16) float xs[RDU_ST][RDU_S][RDU_COLS];
   __shared__ __align__(16) float ls[RDU_ST][RDU_S][RDU_ROWS];
@@ -812,18 +813,19 @@ __global__ void __launch_bounds__(256)
     const int k0 = (item / ncb) * RDU_ROWS, cb = item % ncb;
     const int c = cb * RDU_COLS + l;
     const bool cin = c < d;
-    auto stage = [&](int ch) {  // 32 samples x 32 columns of X and x 32 slots of LGd: one float4 each per thread
+    auto stage = [&](int ch) {  // 32 samples x 32 columns of X and 32 samples x RDU_ROWS slots of LGd
       const int bf = ch % RDU_ST;
       const int s0 = ch * RDU_S;
-      const int r = t >> 3, c4 = (t & 7) * 4;
-      float* dx = &xs[bf][r][c4];
-      if (s0 + r < nq && cb * RDU_COLS + c4 < d)
-        cp_async16(dx, X + (int64_t)(s0 + r) * ldx + cb * RDU_COLS + c4);
-      else
-        *reinterpret_cast<float4*>(dx) = make_float4(0.f, 0.f, 0.f, 0.f);
-      // RDU_S samples x RDU_ROWS slots of LGd: 8 * RDU_ROWS float4s
-      if (t < 8 * RDU_ROWS) {
-        const int lr = t / (RDU_ROWS / 4), lc4 = (t % (RDU_ROWS / 4)) * 4;
+      for (int q = t; q < RDU_S * RDU_COLS / 4; q += NT) {
+        const int r = q >> 3, c4 = (q & 7) * 4;
+        float* dx = &xs[bf][r][c4];
+        if (s0 + r < nq && cb * RDU_COLS + c4 < d)
+          cp_async16(dx, X + (int64_t)(s0 + r) * ldx + cb * RDU_COLS + c4);
+        else
+          *reinterpret_cast<float4*>(dx) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      for (int q = t; q < RDU_S * RDU_ROWS / 4; q += NT) {
+        const int lr = q / (RDU_ROWS / 4), lc4 = (q % (RDU_ROWS / 4)) * 4;
         float* dl = &ls[bf][lr][lc4];
         if (s0 + lr < nq) cp_async16(dl, LGd + (int64_t)(s0 + lr) * ldu + k0 + lc4);
         else *reinterpret_cast<float4*>(dl) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -859,8 +861,8 @@ __global__ void __launch_bounds__(256)
       cp_async_wait_group<RDU_ST - 1>();
       __syncthreads();
       const int ns = min(RDU_S, nq - ch * RDU_S);
-      if (cb == 0) rdu_sum_chunk<W, true, RPW>(xs[bf], ls[bf], ns, w, l, g, gb);
-      else rdu_sum_chunk<W, false, RPW>(xs[bf], ls[bf], ns, w, l, g, gb);
+      if (cb == 0) rdu_sum_chunk<W, true, RPW, RDU_ROWS>(xs[bf], ls[bf], ns, w, l, g, gb);
+      else rdu_sum_chunk<W, false, RPW, RDU_ROWS>(xs[bf], ls[bf], ns, w, l, g, gb);
       __syncthreads();  // buffer bf is restaged RDU_ST - 1 chunks later
     }
     cp_async_wait_group<0>();
@@ -1467,21 +1469,21 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
   count_launch();
   const int64_t maxn = std::min<int64_t>((int64_t)N, (int64_t)nq * A.stride);
   const int ncb = (int)ceil_div(d, RDU_COLS);
-  // long sample loops (large batches) get fewer rows per block, so more blocks
-  const int rpw = nq >= 1024 ? 1 : nq >= 512 ? 2 : 4;
-  const int grid = (int)std::min<int64_t>((int64_t)upd_grid() * 2, ceil_div(maxn, 8 * rpw) * ncb);
+  // Long sample loops (large batches) meet few touched rows per shard: blocks
+  // of 2 warps x 4 rows (8 rows each) give 4x the blocks of 8 x 4 while each
+  // thread keeps 4 rows per staged sample.
+  const int nwb = nq >= 512 ? 2 : 8;
+  const int grid = (int)std::min<int64_t>((int64_t)upd_grid() * 8 / nwb, ceil_div(maxn, 4 * nwb) * ncb);
   void* Wv = const_cast<void*>(W);
-#define KL_RDU(WT, R)                                                                                     \
-  rm_dense_update_kernel<WT, R><<<grid, 256, 0, st>>>(Wv, ldw, d, bias, m, v, mb, vb, X, ldx, D.bits, D.touched, \
-                                                      D.ctr, D.LGd, D.ldu, nq, o)
+#define KL_RDU(WT, NW)                                                                                      \
+  rm_dense_update_kernel<WT, 4, NW><<<grid, NW * 32, 0, st>>>(Wv, ldw, d, bias, m, v, mb, vb, X, ldx, D.bits,   \
+                                                              D.touched, D.ctr, D.LGd, D.ldu, nq, o)
   if (wdtype == KL_DTYPE_BF16) {
-    if (rpw == 1) KL_RDU(__nv_bfloat16, 1);
-    else if (rpw == 2) KL_RDU(__nv_bfloat16, 2);
-    else KL_RDU(__nv_bfloat16, 4);
+    if (nwb == 2) KL_RDU(__nv_bfloat16, 2);
+    else KL_RDU(__nv_bfloat16, 8);
   } else {
-    if (rpw == 1) KL_RDU(float, 1);
-    else if (rpw == 2) KL_RDU(float, 2);
-    else KL_RDU(float, 4);
+    if (nwb == 2) KL_RDU(float, 2);
+    else KL_RDU(float, 8);
   }
 #undef KL_RDU
   count_launch();

@@ -336,3 +336,19 @@ def test_c0_readme_mlp_shape(gpu_ctx, dtype):
         lo = o.train_step(hb, 1e-3, mode="batched")
         assert abs(lg - lo) <= 1e-4 * abs(lo) + 1e-6
     assert_layers_close(g, o, 2, dtype)
+
+
+def test_large_batch_dense_update(gpu_ctx):
+    # a batch of >= 512 examples takes the dense update's 2-warp blocks (the
+    # shape a shard meets over an 8-rank global batch); first Adam moments
+    # equal the oracle's bit for bit (identity output: exact local gradients)
+    cfg = xc_small()
+    cfg.network.layers[1].activation = ActivationType.Identity
+    g, o = pair(cfg, "f32", max_batch=640)
+    hb = xc_batches(1, 640, seed=31)[0]
+    g.train_step(_examples(hb), 1e-3, mode="batched")
+    o.train_step(hb, 1e-3, mode="batched")
+    gl, ol = g.get_layer(1), o.get_layer(1)
+    for k in ("m", "mb"):
+        assert int((gl[k] != ol[k]).sum()) == 0, k
+    assert_layers_close(g, o, 2)
