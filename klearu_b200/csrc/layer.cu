@@ -920,7 +920,6 @@ __global__ void rm_lg_zero_kernel(float* LGd, int64_t ldu, const uint32_t* ctr, 
 //     the rest use g = 0.  slot[f] and hist[f] are zeroed for the next step
 //     (by fm_hist_clear_kernel when a row spans several items).
 // ---------------------------------------------------------------------------
-constexpr int FM_PF = 32;
 constexpr int FM_NT = 256;
 
 constexpr int FM_SHORT = 32;  // segments up to this length are ranked inside one warp
@@ -993,7 +992,7 @@ __global__ void __launch_bounds__(FM_GW * 32)
 }
 
 __global__ void __launch_bounds__(1024)
-    fm_grad_long_kernel(int N, const float* lgd, int ldl, SegScratch S, int nwords, float* G, int ldg) {
+    fm_grad_long_kernel(int N, const float* lgd, int ldl, SegScratch S, int nwords, float* G, int ldg, int chr) {
   // one block per queued feature (segment longer than FM_SHORT): the block
   // marks the samples in a bitmask, warp 0 compacts the set bits into an
   // ascending list, then warp w sums neuron 32w + lane over it
@@ -1002,6 +1001,7 @@ __global__ void __launch_bounds__(1024)
   uint32_t* mask = reinterpret_cast<uint32_t*>(dyn);   // [nwords]
   float* coef = reinterpret_cast<float*>(mask + nwords);  // [32*nwords]
   uint32_t* list = mask + nwords + 32 * nwords;          // [32*nwords]
+  float* rows = reinterpret_cast<float*>(dyn + round_up((int64_t)nwords * 4 * 65, 16));  // [2][chr][ldl]
   __shared__ int base_s;
   for (int i = threadIdx.x; i < nwords; i += blockDim.x) mask[i] = 0;
   __syncthreads();
@@ -1037,23 +1037,36 @@ __global__ void __launch_bounds__(1024)
     }
     __syncthreads();
     const int base = base_s;
-    for (int c = threadIdx.x; c < ldg; c += blockDim.x) {
-      float g = 0.f;
-      if (c < N) {
-        for (int i0 = 0; i0 < base; i0 += FM_PF) {
-          // FM_PF global loads in flight; the coefficients are read from
-          // shared memory as they are used
-          float lv[FM_PF];
-#pragma unroll
-          for (int u = 0; u < FM_PF; ++u)
-            if (i0 + u < base) lv[u] = lgd[(int64_t)list[i0 + u] * ldl + c];
-#pragma unroll
-          for (int u = 0; u < FM_PF; ++u)
-            if (i0 + u < base) g = __fadd_rn(g, __fmul_rn(coef[list[i0 + u]], lv[u]));
-        }
+    // The listed samples' gradient rows come through shared memory in chunks
+    // of `chr` rows, double-buffered with cp.async by the whole block
+    // (coalesced 16-byte copies, one L2 round trip per chunk); thread c then
+    // sums column c over the chunk in list order (bit-exact).
+    const int c = threadIdx.x;  // one column per thread (blockDim >= ldg)
+    float g = 0.f;
+    const int vpr = ldl / 4;
+    auto stage = [&](int i0, int b) {
+      const int cn = min(chr, base - i0);
+      float* dst = rows + (size_t)b * chr * ldl;
+      for (int q = threadIdx.x; q < cn * vpr; q += blockDim.x) {
+        const int r = q / vpr, c4 = (q - r * vpr) * 4;
+        cp_async16(dst + r * ldl + c4, lgd + (int64_t)list[i0 + r] * ldl + c4);
       }
-      G[(int64_t)k * ldg + c] = g;
+      cp_async_commit();
+    };
+    if (base > 0) stage(0, 0);
+    for (int i0 = 0, b = 0; i0 < base; i0 += chr, b ^= 1) {
+      if (i0 + chr < base) stage(i0 + chr, b ^ 1);
+      else cp_async_commit();  // keeps one group per iteration
+      cp_async_wait_group<1>();
+      __syncthreads();
+      if (c < N) {
+        const float* src = rows + (size_t)b * chr * ldl + c;
+        const int cn = min(chr, base - i0);
+        for (int r = 0; r < cn; ++r) g = __fadd_rn(g, __fmul_rn(coef[list[i0 + r]], src[r * ldl]));
+      }
+      __syncthreads();  // buffer b is restaged two chunks later
     }
+    if (c < ldg) G[(int64_t)k * ldg + c] = g;
     __syncthreads();  // list / coef reused by the next feature
   }
 }
@@ -1191,6 +1204,47 @@ __global__ void fm_hist_clear_kernel(SegScratch S) {
   if (k < (int)S.ctr[0]) {
     S.hist[S.touched[k]] = 0;
     S.slot[S.touched[k]] = 0;
+  }
+}
+
+// Bias gradient over a long batch: one block, thread j = neuron j; the
+// samples' gradient rows stream through shared memory in chunks of `chr`
+// rows, double-buffered with cp.async (coalesced 16-byte copies), and each
+// thread adds its column in ascending sample order (bit-exact).
+__global__ void __launch_bounds__(1024) fm_bias_stream_kernel(float* bias, float* mb, float* vb, const float* lgd,
+                                                             int ldl, int nq, int N, const uint32_t* tmask,
+                                                             const OptStep* op, unsigned long long* stat_touched,
+                                                             int chr) {
+  extern __shared__ __align__(16) float brows[];  // [2][chr][ldl]
+  const OptStep o = *op;
+  const int j = threadIdx.x;
+  const int vpr = ldl / 4;
+  auto stage = [&](int s0, int b) {
+    const int cn = min(chr, nq - s0);
+    float* dst = brows + (size_t)b * chr * ldl;
+    for (int q = threadIdx.x; q < cn * vpr; q += blockDim.x) {
+      const int r = q / vpr, c4 = (q - r * vpr) * 4;
+      cp_async16(dst + r * ldl + c4, lgd + (int64_t)(s0 + r) * ldl + c4);
+    }
+    cp_async_commit();
+  };
+  float gb = 0.0f;
+  stage(0, 0);
+  for (int s0 = 0, b = 0; s0 < nq; s0 += chr, b ^= 1) {
+    if (s0 + chr < nq) stage(s0 + chr, b ^ 1);
+    else cp_async_commit();
+    cp_async_wait_group<1>();
+    __syncthreads();
+    if (j < N) {
+      const float* src = brows + (size_t)b * chr * ldl + j;
+      const int cn = min(chr, nq - s0);
+      for (int r = 0; r < cn; ++r) gb = __fadd_rn(gb, src[r * ldl]);
+    }
+    __syncthreads();
+  }
+  if (j < N && ((tmask[j >> 5] >> (j & 31)) & 1u)) {
+    if (stat_touched) atomicAdd(stat_touched, 1ull);
+    bias_update(bias, mb, vb, (uint32_t)j, gb, o);
   }
 }
 
@@ -1539,13 +1593,15 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int f0, int nf,
   fm_grad_short_kernel<<<ggrid, FM_GW * 32, 0, st>>>(N, lgd, ldl, S, G, ldl);
   count_launch();
   const int nwords = (int)ceil_div(nq, 32);
-  const size_t sm = (size_t)nwords * 4 * 65;
+  // staged gradient rows: two chunks of `chr` rows, at most 64 KB
+  const int chr = std::max(4, std::min(64, (int)((32 * 1024) / ((size_t)ldl * 4))));
+  const size_t sm = (size_t)round_up((int64_t)nwords * 4 * 65, 16) + (size_t)2 * chr * ldl * 4;
   static OncePerDevice attr;
   attr([&] {
     cudaFuncSetAttribute(fm_grad_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   });
   const int lthreads = std::min(1024, 32 * (int)ceil_div(N, 32));
-  fm_grad_long_kernel<<<upd_grid(), lthreads, sm, st>>>(N, lgd, ldl, S, nwords, G, ldl);
+  fm_grad_long_kernel<<<upd_grid(), lthreads, sm, st>>>(N, lgd, ldl, S, nwords, G, ldl, chr);
   count_launch();
   const int vpr = ldl / 4;  // vectors per feature row (ldw == ldl == pitch of N)
   const int rpw = vpr <= 32 ? 32 / vpr : 1;
@@ -1578,8 +1634,19 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int f0, int nf,
     fm_hist_clear_kernel<<<(unsigned)ceil_div(std::max(nf, 1), 256), 256, 0, st>>>(S);
     count_launch();
   }
-  fm_bias_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask, o,
-                                                           stat_touched);
+  if (nq >= 512) {
+    // long batches: one block streams the gradient rows through shared memory
+    const int chr = std::max(8, std::min(256, (int)((96 * 1024) / ((size_t)ldl * 4))));
+    static OncePerDevice battr;
+    battr([&] {
+      cudaFuncSetAttribute(fm_bias_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    fm_bias_stream_kernel<<<1, 32 * (int)ceil_div(N, 32), (size_t)2 * chr * ldl * 4, st>>>(
+        bias, mb, vb, lgd, ldl, nq, N, touched_mask, o, stat_touched, chr);
+  } else {
+    fm_bias_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask, o,
+                                                             stat_touched);
+  }
   count_launch();
 }
 
