@@ -264,13 +264,7 @@ __global__ void __launch_bounds__(TK_NT) topk_kernel(const float* __restrict__ s
   }
   const float scale = mx > mn ? (float)(TK_NB - 1) / (mx - mn) : 0.0f;
   auto bin_of = [&](float v) { return min(TK_NB - 1, (int)__fmul_rz(__fsub_rz(v, mn), scale)); };
-  // scores crowd into a few bins: lanes with the same bin add once per warp
-  for (int i0 = 0; i0 < n; i0 += TK_NT) {
-    const int i = i0 + tid;
-    const int b = i < n ? bin_of(row[i]) : -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, b);
-    if (b >= 0 && l == __ffs(peers) - 1) atomicAdd(&hist[b], (uint32_t)__popc(peers));
-  }
+  for (int i = tid; i < n; i += TK_NT) atomicAdd(&hist[bin_of(row[i])], 1u);
   __syncthreads();
   // suffix counts: thread j owns bins TK_NB-1-4j .. TK_NB-4-4j (descending)
   {
