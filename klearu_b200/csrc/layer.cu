@@ -1207,42 +1207,42 @@ __global__ void fm_hist_clear_kernel(SegScratch S) {
   }
 }
 
-// Bias gradient over a long batch: one block, thread j = neuron j; the
-// samples' gradient rows stream through shared memory in chunks of `chr`
-// rows, double-buffered with cp.async (coalesced 16-byte copies), and each
-// thread adds its column in ascending sample order (bit-exact).
-__global__ void __launch_bounds__(1024) fm_bias_stream_kernel(float* bias, float* mb, float* vb, const float* lgd,
-                                                             int ldl, int nq, int N, const uint32_t* tmask,
-                                                             const OptStep* op, unsigned long long* stat_touched,
-                                                             int chr) {
-  extern __shared__ __align__(16) float brows[];  // [2][chr][ldl]
+// Bias gradient over a long batch: block b owns neurons [32b, 32b + 32).
+// Its 4 warps stage the samples' 32-column row segments through shared
+// memory in chunks of 128 rows, double-buffered with cp.async; warp 0 then
+// adds lane j's column in ascending sample order (bit-exact).
+constexpr int FB_CH = 128;
+__global__ void __launch_bounds__(128) fm_bias_stream_kernel(float* bias, float* mb, float* vb, const float* lgd,
+                                                            int ldl, int nq, int N, const uint32_t* tmask,
+                                                            const OptStep* op, unsigned long long* stat_touched) {
+  __shared__ __align__(16) float brows[2][FB_CH][32];
   const OptStep o = *op;
-  const int j = threadIdx.x;
-  const int vpr = ldl / 4;
+  const int j0 = blockIdx.x * 32;
+  const int ncol = min(32, ldl - j0);  // columns of this block inside the row pitch (a multiple of 8)
+  const int v4 = ncol / 4;
   auto stage = [&](int s0, int b) {
-    const int cn = min(chr, nq - s0);
-    float* dst = brows + (size_t)b * chr * ldl;
-    for (int q = threadIdx.x; q < cn * vpr; q += blockDim.x) {
-      const int r = q / vpr, c4 = (q - r * vpr) * 4;
-      cp_async16(dst + r * ldl + c4, lgd + (int64_t)(s0 + r) * ldl + c4);
+    const int cn = min(FB_CH, nq - s0);
+    for (int q = threadIdx.x; q < cn * v4; q += 128) {
+      const int r = q / v4, c4 = (q - r * v4) * 4;
+      cp_async16(&brows[b][r][c4], lgd + (int64_t)(s0 + r) * ldl + j0 + c4);
     }
     cp_async_commit();
   };
   float gb = 0.0f;
   stage(0, 0);
-  for (int s0 = 0, b = 0; s0 < nq; s0 += chr, b ^= 1) {
-    if (s0 + chr < nq) stage(s0 + chr, b ^ 1);
+  for (int s0 = 0, b = 0; s0 < nq; s0 += FB_CH, b ^= 1) {
+    if (s0 + FB_CH < nq) stage(s0 + FB_CH, b ^ 1);
     else cp_async_commit();
     cp_async_wait_group<1>();
     __syncthreads();
-    if (j < N) {
-      const float* src = brows + (size_t)b * chr * ldl + j;
-      const int cn = min(chr, nq - s0);
-      for (int r = 0; r < cn; ++r) gb = __fadd_rn(gb, src[r * ldl]);
+    if (threadIdx.x < 32) {
+      const int cn = min(FB_CH, nq - s0);
+      for (int r = 0; r < cn; ++r) gb = __fadd_rn(gb, brows[b][r][threadIdx.x]);
     }
     __syncthreads();
   }
-  if (j < N && ((tmask[j >> 5] >> (j & 31)) & 1u)) {
+  const int j = j0 + (int)threadIdx.x;
+  if (threadIdx.x < 32 && j < N && ((tmask[j >> 5] >> (j & 31)) & 1u)) {
     if (stat_touched) atomicAdd(stat_touched, 1ull);
     bias_update(bias, mb, vb, (uint32_t)j, gb, o);
   }
@@ -1635,14 +1635,9 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int f0, int nf,
     count_launch();
   }
   if (nq >= 512) {
-    // long batches: one block streams the gradient rows through shared memory
-    const int chr = std::max(8, std::min(256, (int)((96 * 1024) / ((size_t)ldl * 4))));
-    static OncePerDevice battr;
-    battr([&] {
-      cudaFuncSetAttribute(fm_bias_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    });
-    fm_bias_stream_kernel<<<1, 32 * (int)ceil_div(N, 32), (size_t)2 * chr * ldl * 4, st>>>(
-        bias, mb, vb, lgd, ldl, nq, N, touched_mask, o, stat_touched, chr);
+    // long batches: 32 neurons per block, gradient rows streamed through shared memory
+    fm_bias_stream_kernel<<<(unsigned)ceil_div(N, 32), 128, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask, o,
+                                                                      stat_touched);
   } else {
     fm_bias_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask, o,
                                                              stat_touched);
