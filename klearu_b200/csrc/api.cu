@@ -1145,8 +1145,8 @@ struct Layer {
   std::shared_ptr<IndexImpl> index;
   // per-step buffers
   DBuf bkt, ids, cnt, pre, post, lg, h, dx_in, dxpart, lgd, tmask, gfeat;
-  DBuf dbits, dtouched, dslot, dlg;  // dense-collision update scratch (row-major layers)
-  int64_t dldu = 0;
+  DBuf dmark, dtouched, dslot, dlg;  // dense-collision update scratch (row-major layers)
+  int64_t dldb = 0;  // sample pitch of the dense update's gradient matrix (0: segmented path)
   DBuf hist, cur, touched, ctr, ent_s, ent_v, fslot, flong;
   size_t ent_cap = 0;
   DBuf stats;  // u64 [3]: active_sum, touched_rows, input_nnz
@@ -1595,9 +1595,9 @@ struct kl_net_s {
         ck_launch("fm update");
       } else {
         const Layer& P = *layers[l - 1];
-        if (L.dldu > 0) {
-          DenseScratch D{L.dbits.as<uint32_t>(), L.dtouched.as<uint32_t>(), L.dslot.as<uint32_t>(),
-                         L.ctr.as<uint32_t>(), L.dlg.as<float>(), L.dldu};
+        if (L.dldb > 0) {
+          DenseScratch D{L.dmark.as<uint32_t>(), L.dtouched.as<uint32_t>(), L.dslot.as<uint32_t>(),
+                         L.ctr.as<uint32_t>(), L.dlg.as<float>(), L.dldb};
           launch_rm_update_dense(L.W.p, wdtype, L.ldw, L.d, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
                                  L.mb.as<float>(), L.vb.as<float>(), P.h.as<float>(), P.ldN, L.act(), nq, L.N, D,
                                  o, stat, st);
@@ -1990,16 +1990,17 @@ void build_layer(kl_net_s* net, int l, const kl_layer_config& c, const kl_layer_
   if (!L.fm) {
     // dense-collision update scratch when its gradient matrix fits the budget
     const int64_t drows = std::min<int64_t>((int64_t)L.N, (int64_t)B * L.stride);
-    const int64_t ldu = round_up(drows + 16, 32);  // update tiles read whole 32-slot groups below ldu
-    if (rm_dense_fits(ldu, std::max(B, 1), net->cfg.dense_update_max_bytes)) {
-      L.dldu = ldu;
-      const size_t nwords = (size_t)ceil_div(L.N, 32);
-      L.dbits.alloc(nwords * 4);
-      ck(cudaMemsetAsync(L.dbits.p, 0, nwords * 4, st), "memset");
+    // slot-major [slots][ldb] gradient matrix
+    const int64_t dslots = round_up(drows, 32);
+    const int64_t ldb = round_up(std::max(B, 1), 32);
+    if (rm_dense_fits(dslots, (int)ldb, net->cfg.dense_update_max_bytes)) {
+      L.dldb = ldb;
+      L.dmark.alloc((size_t)L.N * 4);
+      ck(cudaMemsetAsync(L.dmark.p, 0, (size_t)L.N * 4, st), "memset");
       L.dtouched.alloc((size_t)drows * 4);
       L.dslot.alloc((size_t)L.N * 4);
-      L.dlg.alloc((size_t)ldu * B * 4);
-      ck(cudaMemsetAsync(L.dlg.p, 0, (size_t)ldu * B * 4, st), "memset");
+      L.dlg.alloc((size_t)dslots * ldb * 4);
+      ck(cudaMemsetAsync(L.dlg.p, 0, (size_t)dslots * ldb * 4, st), "memset");
     }
     L.ent_s.alloc((size_t)B * L.stride * 4);
     L.ent_v.alloc((size_t)B * L.stride * 4);

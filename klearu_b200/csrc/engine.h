@@ -257,16 +257,17 @@ void launch_rm_update(const void* W, int wdtype, int ldw, int d, float* bias, fl
                       float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
                       SegScratch S, const OptStep* o, unsigned long long* stat_touched,
                       cudaStream_t st);
-// Dense-collision path of the row-major update: touched rows by a bitmap
-// (first setter appends), local gradients scattered sample-major into LGd
-// [max batch][ldu] (all zero between steps), tiled bit-exact reduction.
+// Dense-collision path of the row-major update: touched rows by mark words
+// (first setter appends), local gradients scattered slot-major into LGd
+// [round_up(rows, 32)][ldb] (all zero between steps), tiled bit-exact
+// reduction.
 struct DenseScratch {
-  uint32_t* bits;      // [ceil(N / 32)] bitmap, zero between steps
+  uint32_t* mark;      // [N] one word per row, zero between steps
   uint32_t* touched;   // [rows]
   uint32_t* slot_of;   // [N]
   uint32_t* ctr;       // [1] touched count (zeroed by the caller per step)
-  float* LGd;          // [max batch][ldu], zero between steps
-  int64_t ldu;         // >= rows, multiple of 32
+  float* LGd;          // [round_up(rows, 32)][ldb], zero between steps
+  int64_t ldb;         // sample pitch: >= max batch, multiple of 32
 };
 bool rm_dense_fits(int64_t rows, int nb, int64_t max_bytes);
 // stat += ctr[0] (touched-row counter of the roofline statistics)

@@ -694,17 +694,22 @@ __global__ void __launch_bounds__(UPD_WARPS * 32)
 // gradient matrix fits its memory budget.  In batched SLIDE steps many
 // samples share active rows (C1: ~6 K distinct rows behind 1.5 M (sample,
 // row) pairs), so instead of per-row segments built with contended atomics:
-//  (1) rm_mark_kernel: a bitmap over rows; a lane whose row bit is already
-//      set only reads it, the lane that sets it first appends the row to the
+//  (1) rm_mark_kernel: a mark word per row; a lane whose row is already
+//      marked only reads it, the lane that marks it first appends the row to the
 //      touched list (slot = position) and records slot_of[row];
-//  (2) rm_dense_scatter_kernel: LGd[s][slot] = local gradient of the row in
-//      sample s (sample-major, LGd is all zero between steps);
-//  (3) rm_dense_update_kernel: a block owns RDU_ROWS consecutive slots (2 per
-//      warp, 4 columns per lane).  Chunks of RDU_S samples of X and LGd are
-//      double-buffered into shared memory with cp.async; each lane sums
-//      g = sum_s lg_s * x_s in ascending s with the non-fused f32 operations
-//      of the batched oracle (bit-exact), zeroes the consumed LGd tile,
-//      applies the optimizer to its rows and biases, and clears their bits.
+//  (2) rm_dense_scatter_kernel: LGd[slot][s] = local gradient of the row in
+//      sample s, slot-major with a pitch of ldb >= max batch samples (the
+//      step uses the first n rows; LGd is all zero between steps);
+//  (3) rm_dense_update_kernel: a block owns RDU_ROWS consecutive slots (4 per
+//      warp) of one 32-column block (a column per lane).  Chunks of RDU_S
+//      samples of X and LGd are staged into shared memory by a 4-stage
+//      cp.async pipeline; each lane sums g = sum_s lg_s * x_s in ascending s
+//      with the non-fused f32 operations of the batched oracle (bit-exact),
+//      applies the optimizer to its rows and biases, and clears their marks;
+//  (4) rm_lg_zero_kernel zeroes the n x ldb block the step used.
+// The slot-major layout keeps a step's gradients in one contiguous block: a
+// sample-major [sample][slot] layout measured ~1.8x slower in the update and
+// zeroing kernels at 2048-example batches.
 // ---------------------------------------------------------------------------
 // rm_dense_scatter_kernel gives each thread RM_PK pairs of one sample (stride
 // blockDim), with the loads of all of them issued before any is used.
@@ -713,16 +718,17 @@ constexpr int RM_PK = 8;
 // One pair per thread: blocks run in waves, and the plain read lets pairs of
 // later waves skip the atomic on rows an earlier wave already set (batching
 // pairs per thread puts them all in one wave and every pair then contends).
-__global__ void rm_mark_kernel(ActiveSet A, uint32_t* bits, uint32_t* touched, uint32_t* slot_of,
+// One mark word per row: a few hundred samples of a large batch meet the same
+// rows at once, and words shared by 32 rows would serialise their atomics.
+__global__ void rm_mark_kernel(ActiveSet A, uint32_t* mark, uint32_t* touched, uint32_t* slot_of,
                                uint32_t* ctr) {
   const int s = blockIdx.y;
   const int a = blockIdx.x * blockDim.x + threadIdx.x;
   if (a >= A.cnt[s]) return;
   const uint32_t id = A.ids[(int64_t)s * A.stride + a];
-  const uint32_t b = 1u << (id & 31);
-  uint32_t* wp = bits + (id >> 5);
+  uint32_t* wp = mark + id;
   bool first = false;
-  if (!(*reinterpret_cast<volatile uint32_t*>(wp) & b)) first = !(atomicOr(wp, b) & b);
+  if (!*reinterpret_cast<volatile uint32_t*>(wp)) first = atomicExch(wp, 1u) == 0u;
   const int pos = warp_append(first, ctr);
   if (pos >= 0) {
     touched[pos] = id;
@@ -730,7 +736,7 @@ __global__ void rm_mark_kernel(ActiveSet A, uint32_t* bits, uint32_t* touched, u
   }
 }
 
-__global__ void rm_dense_scatter_kernel(ActiveSet A, const uint32_t* slot_of, float* LGd, int64_t ldu) {
+__global__ void rm_dense_scatter_kernel(ActiveSet A, const uint32_t* slot_of, float* LGd, int64_t ldb) {
   const int s = blockIdx.y;
   const int n = A.cnt[s];
   const int a0 = blockIdx.x * blockDim.x * RM_PK + threadIdx.x;
@@ -748,7 +754,7 @@ __global__ void rm_dense_scatter_kernel(ActiveSet A, const uint32_t* slot_of, fl
   for (int u = 0; u < RM_PK; ++u) sl[u] = id[u] != 0xffffffffu ? slot_of[id[u]] : 0u;
 #pragma unroll
   for (int u = 0; u < RM_PK; ++u)
-    if (id[u] != 0xffffffffu) LGd[(int64_t)s * ldu + sl[u]] = lg[u];
+    if (id[u] != 0xffffffffu) LGd[(int64_t)sl[u] * ldb + s] = lg[u];
 }
 
 // Slots per warp RPW (a template parameter: 4, or 2 / 1 when a long sample
@@ -756,54 +762,72 @@ __global__ void rm_dense_scatter_kernel(ActiveSet A, const uint32_t* slot_of, fl
 // more blocks share the work); 8 * RPW slots per block (8 warps).
 constexpr int RDU_COLS = 32;             // columns per block (one per lane)
 constexpr int RDU_S = 32;                // samples per staged chunk
-constexpr int RDU_ST = 4;                // cp.async pipeline stages
 
 // Block = (32 slots, 32 columns): warp w owns slots 4w .. 4w+3, lane l column
 // cb*32 + l.  Column blocks multiply the parallelism when few rows meet many
-// samples (a shard's union over a large global batch).  Every sample's term
-// is added, zero or not: the sums start at +0 and a round-to-nearest sum is
-// -0 only when both operands are, so a +-0 term (a sample where the row is
-// not active) leaves a sum unchanged and the result equals the sum over the
-// active samples in ascending order (finite activations assumed).  The
+// samples (a shard's union over a large global batch).  The sums start at
+// +0 and a round-to-nearest sum is -0 only when both operands are, so a +-0
+// term (a sample where the row is not active) leaves a sum unchanged: the sum
+// over any superset of the active samples, in ascending order, equals the
+// sum over the active samples (finite activations assumed).  The
 // gradient matrix is left as read; rm_lg_zero_kernel restores its zeros.
-template <class W, bool BIAS, int RPW, int ROWS>
-__device__ __forceinline__ void rdu_sum_chunk(const float (*xs)[RDU_COLS], const float (*ls)[ROWS], int ns,
+// Samples are taken in groups of RDU_G whose shared-memory operands are all
+// loaded before the group's arithmetic: the only loop-carried dependency is
+// then the running sum itself.  ls is the staged gradient tile, slot-major
+// ([slot][sample]); every lane of a warp reads the same ls words (broadcast).
+constexpr int RDU_G = 8;
+template <class W, bool BIAS, int RPW>
+__device__ __forceinline__ void rdu_sum_chunk(const float (*xs)[RDU_COLS], const float (*ls)[RDU_S], int ns,
                                               int w, int l, float* g, float* gb) {
-  for (int j = 0; j < ns; ++j) {
-    const float xv = xs[j][l];
-    float lv[RPW];
-    if (RPW == 4) {
-      const float4 l4 = *reinterpret_cast<const float4*>(&ls[j][w * RPW]);
-      lv[0] = l4.x;
-      lv[RPW > 1 ? 1 : 0] = l4.y;
-      lv[RPW > 2 ? 2 : 0] = l4.z;
-      lv[RPW > 3 ? 3 : 0] = l4.w;
-    } else if (RPW == 2) {
-      const float2 l2 = *reinterpret_cast<const float2*>(&ls[j][w * RPW]);
-      lv[0] = l2.x;
-      lv[RPW > 1 ? 1 : 0] = l2.y;
-    } else {
-      lv[0] = ls[j][w];
-    }
+  int j = 0;
+  for (; j + RDU_G <= ns; j += RDU_G) {
+    float xv[RDU_G], lv[RPW][RDU_G];
+#pragma unroll
+    for (int u = 0; u < RDU_G; ++u) xv[u] = xs[j + u][l];
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
-      g[i] = __fadd_rn(g[i], __fmul_rn(lv[i], xv));
-      if (BIAS) gb[i] = __fadd_rn(gb[i], lv[i]);
+#pragma unroll
+      for (int u = 0; u < RDU_G; u += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(&ls[w * RPW + i][j + u]);
+        lv[i][u] = q.x;
+        lv[i][u + 1] = q.y;
+        lv[i][u + 2] = q.z;
+        lv[i][u + 3] = q.w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < RDU_G; ++u) {
+#pragma unroll
+      for (int i = 0; i < RPW; ++i) {
+        g[i] = __fadd_rn(g[i], __fmul_rn(lv[i][u], xv[u]));
+        if (BIAS) gb[i] = __fadd_rn(gb[i], lv[i][u]);
+      }
+    }
+  }
+  for (; j < ns; ++j) {
+    const float xv = xs[j][l];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      const float lv = ls[w * RPW + i][j];
+      g[i] = __fadd_rn(g[i], __fmul_rn(lv, xv));
+      if (BIAS) gb[i] = __fadd_rn(gb[i], lv);
     }
   }
 }
 
-template <class W, int RPW, int NWB>
+template <class W, int RPW, int NWB, int RDU_ST>
 __global__ void __launch_bounds__(NWB * 32)
     rm_dense_update_kernel(void* Wm, int ldw, int d, float* bias, float* m, float* v, float* mb, float* vb,
-                           const float* X, int ldx, uint32_t* bits, const uint32_t* touched, const uint32_t* ctr,
-                           float* LGd, int64_t ldu, int nq, const OptStep* op) {
+                           const float* X, int ldx, uint32_t* mark, const uint32_t* touched, const uint32_t* ctr,
+                           float* LGd, int64_t ldb, int nq, const OptStep* op) {
   constexpr int RDU_RPW = RPW;
   constexpr int RDU_ROWS = NWB * RPW;  // slots per block
+  static_assert(RDU_ROWS % 4 == 0, "gradient tiles are staged in 16-byte pieces");
   constexpr int NT = NWB * 32;
   const OptStep o = *op;
-  __shared__ __align__(16) float xs[RDU_ST][RDU_S][RDU_COLS];
-  __shared__ __align__(16) float ls[RDU_ST][RDU_S][RDU_ROWS];
+  extern __shared__ __align__(16) float rdu_smem[];
+  float(*xs)[RDU_S][RDU_COLS] = reinterpret_cast<float(*)[RDU_S][RDU_COLS]>(rdu_smem);
+  float(*ls)[RDU_ROWS][RDU_S] = reinterpret_cast<float(*)[RDU_ROWS][RDU_S]>(rdu_smem + RDU_ST * RDU_S * RDU_COLS);
   const int t = threadIdx.x, w = t >> 5, l = t & 31;
   const int n = (int)ctr[0];
   const int nch = (nq + RDU_S - 1) / RDU_S;
@@ -813,7 +837,7 @@ __global__ void __launch_bounds__(NWB * 32)
     const int k0 = (item / ncb) * RDU_ROWS, cb = item % ncb;
     const int c = cb * RDU_COLS + l;
     const bool cin = c < d;
-    auto stage = [&](int ch) {  // 32 samples x 32 columns of X and 32 samples x RDU_ROWS slots of LGd
+    auto stage = [&](int ch) {  // 32 samples x 32 columns of X and RDU_ROWS slots x 32 samples of LGd
       const int bf = ch % RDU_ST;
       const int s0 = ch * RDU_S;
       for (int q = t; q < RDU_S * RDU_COLS / 4; q += NT) {
@@ -824,11 +848,12 @@ __global__ void __launch_bounds__(NWB * 32)
         else
           *reinterpret_cast<float4*>(dx) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
+      // slots k0 .. k0 + RDU_ROWS - 1 and samples s0 .. s0 + 31 lie inside the
+      // allocation (round_up(rows, 32) slots, ldb a multiple of 32); slots past
+      // the touched count and samples nq .. ldb - 1 are zero
       for (int q = t; q < RDU_S * RDU_ROWS / 4; q += NT) {
-        const int lr = q / (RDU_ROWS / 4), lc4 = (q % (RDU_ROWS / 4)) * 4;
-        float* dl = &ls[bf][lr][lc4];
-        if (s0 + lr < nq) cp_async16(dl, LGd + (int64_t)(s0 + lr) * ldu + k0 + lc4);
-        else *reinterpret_cast<float4*>(dl) = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int lr = q / (RDU_S / 4), lc4 = (q % (RDU_S / 4)) * 4;
+        cp_async16(&ls[bf][lr][lc4], LGd + (int64_t)(k0 + lr) * ldb + s0 + lc4);
       }
     };
     // optimizer state of this lane's elements, loaded now and used after the sum
@@ -861,8 +886,8 @@ __global__ void __launch_bounds__(NWB * 32)
       cp_async_wait_group<RDU_ST - 1>();
       __syncthreads();
       const int ns = min(RDU_S, nq - ch * RDU_S);
-      if (cb == 0) rdu_sum_chunk<W, true, RPW, RDU_ROWS>(xs[bf], ls[bf], ns, w, l, g, gb);
-      else rdu_sum_chunk<W, false, RPW, RDU_ROWS>(xs[bf], ls[bf], ns, w, l, g, gb);
+      if (cb == 0) rdu_sum_chunk<W, true, RPW>(xs[bf], ls[bf], ns, w, l, g, gb);
+      else rdu_sum_chunk<W, false, RPW>(xs[bf], ls[bf], ns, w, l, g, gb);
       __syncthreads();  // buffer bf is restaged RDU_ST - 1 chunks later
     }
     cp_async_wait_group<0>();
@@ -883,23 +908,19 @@ __global__ void __launch_bounds__(NWB * 32)
         for (int i = 1; i < RDU_RPW; ++i)
           if (l == i) gbl = gb[i];
         bias_update(bias, mb, vb, row, gbl, o);
-        atomicAnd(bits + (row >> 5), ~(1u << (row & 31)));  // ready for the next step's mark
+        mark[row] = 0u;  // ready for the next step's mark
       }
     }
   }
 }
 
-// LGd[s][slot] = 0 for the slots the update read (restores the zero invariant).
-__global__ void rm_lg_zero_kernel(float* LGd, int64_t ldu, const uint32_t* ctr, int nq) {
-  const int s = blockIdx.x;
-  if (s >= nq) return;
-  const int n = (int)ctr[0];
-  float* row = LGd + (int64_t)s * ldu;
-  for (int k = threadIdx.x * 4; k < n; k += blockDim.x * 4) {
-    if (k + 4 <= n) *reinterpret_cast<float4*>(row + k) = make_float4(0.f, 0.f, 0.f, 0.f);
-    else
-      for (int q = k; q < n; ++q) row[q] = 0.f;
-  }
+// LGd[slot][*] = 0 for the touched slots (restores the zero invariant): one
+// contiguous block of n x ldb floats.
+__global__ void rm_lg_zero_kernel(float* LGd, int64_t ldb, const uint32_t* ctr) {
+  const int64_t n4 = (int64_t)ctr[0] * ldb / 4;
+  float4* p = reinterpret_cast<float4*>(LGd);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // Feature-major (layer 0) update, in two passes.
@@ -1516,10 +1537,10 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
                             cudaStream_t st) {
   (void)stat_touched;
   if (nq <= 0) return;
-  rm_mark_kernel<<<dim3((unsigned)ceil_div(A.stride, 256), nq), 256, 0, st>>>(A, D.bits, D.touched, D.slot_of,
+  rm_mark_kernel<<<dim3((unsigned)ceil_div(A.stride, 256), nq), 256, 0, st>>>(A, D.mark, D.touched, D.slot_of,
                                                                            D.ctr);
   count_launch();
-  rm_dense_scatter_kernel<<<dim3((unsigned)ceil_div(A.stride, 256 * RM_PK), nq), 256, 0, st>>>(A, D.slot_of, D.LGd, D.ldu);
+  rm_dense_scatter_kernel<<<dim3((unsigned)ceil_div(A.stride, 256 * RM_PK), nq), 256, 0, st>>>(A, D.slot_of, D.LGd, D.ldb);
   count_launch();
   const int64_t maxn = std::min<int64_t>((int64_t)N, (int64_t)nq * A.stride);
   const int ncb = (int)ceil_div(d, RDU_COLS);
@@ -1527,11 +1548,20 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
   // of 2 warps x 4 rows (8 rows each) give 4x the blocks of 8 x 4 while each
   // thread keeps 4 rows per staged sample.
   const int nwb = nq >= 512 ? 2 : 8;
+  constexpr int NST = 4;  // cp.async stages (deeper pipelines measured no faster)
   const int grid = (int)std::min<int64_t>((int64_t)upd_grid() * 8 / nwb, ceil_div(maxn, 4 * nwb) * ncb);
   void* Wv = const_cast<void*>(W);
-#define KL_RDU(WT, NW)                                                                                      \
-  rm_dense_update_kernel<WT, 4, NW><<<grid, NW * 32, 0, st>>>(Wv, ldw, d, bias, m, v, mb, vb, X, ldx, D.bits,   \
-                                                              D.touched, D.ctr, D.LGd, D.ldu, nq, o)
+#define KL_RDU(WT, NW)                                                                                        \
+  do {                                                                                                        \
+    const size_t sm = (size_t)NST * RDU_S * (RDU_COLS + NW * 4) * 4;                                          \
+    static OncePerDevice a_;                                                                                  \
+    a_([&] {                                                                                                  \
+      cudaFuncSetAttribute(rm_dense_update_kernel<WT, 4, NW, NST>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                           (int)sm);                                                                          \
+    });                                                                                                       \
+    rm_dense_update_kernel<WT, 4, NW, NST><<<grid, NW * 32, sm, st>>>(Wv, ldw, d, bias, m, v, mb, vb, X, ldx,   \
+                                                                       D.mark, D.touched, D.ctr, D.LGd, D.ldb, nq, o); \
+  } while (0)
   if (wdtype == KL_DTYPE_BF16) {
     if (nwb == 2) KL_RDU(__nv_bfloat16, 2);
     else KL_RDU(__nv_bfloat16, 8);
@@ -1541,7 +1571,7 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
   }
 #undef KL_RDU
   count_launch();
-  rm_lg_zero_kernel<<<nq, 256, 0, st>>>(D.LGd, D.ldu, D.ctr, nq);
+  rm_lg_zero_kernel<<<upd_grid(), 256, 0, st>>>(D.LGd, D.ldb, D.ctr);
   count_launch();
 }
 
