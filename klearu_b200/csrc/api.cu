@@ -926,7 +926,7 @@ __global__ void adaptive_gather_kernel(const void* X, int dtype, int64_t ld_row,
   float v = 0.f;
   if (r < (uint32_t)n) {
     const int64_t o = (int64_t)r * ld_row + (int64_t)c * ld_elem;
-    v = dtype == KL_DTYPE_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(X)[o])
+    v = dtype == KL_DTYPE_BF16 ? to_f(static_cast<const __nv_bfloat16*>(X)[o])
                                : static_cast<const float*>(X)[o];
   }
   out[g] = v;

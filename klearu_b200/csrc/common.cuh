@@ -51,7 +51,11 @@ __host__ __device__ inline int pitch_of(int n) { return (int)round_up(n, 8); }
 
 // ---- weight element access (f32 or bf16 storage, f32 arithmetic) ----
 __device__ __forceinline__ float to_f(float x) { return x; }
-__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+// bf16 -> f32 is exact: a bf16 value is the upper half of the f32 with the
+// same bits, so the widening is a 16-bit shift on the integer pipe.
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) {
+  return __uint_as_float((uint32_t)__bfloat16_as_ushort(x) << 16);
+}
 template <class W>
 __device__ __forceinline__ W from_f(float x);
 template <>

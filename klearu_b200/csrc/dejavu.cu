@@ -158,9 +158,9 @@ __global__ void split3_kernel(const float* __restrict__ x, int T, int n, int ldx
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ld; i += gridDim.x * blockDim.x) {
     const float v = (t < T && i < n) ? x[(int64_t)t * ldx + i] : 0.0f;
     const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-    const float r1 = __fsub_rn(v, __bfloat162float(hi));
+    const float r1 = __fsub_rn(v, to_f(hi));
     const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
-    const float r2 = __fsub_rn(r1, __bfloat162float(mid));
+    const float r2 = __fsub_rn(r1, to_f(mid));
     const __nv_bfloat16 lo = __float2bfloat16_rn(r2);
     const int64_t o = (int64_t)(TC_NP * t) * ld + i;
     out[o] = hi;
@@ -192,11 +192,11 @@ __global__ void splitk_finish_kernel(const float* __restrict__ P, int splits, in
     if (xs_next) {
       const int64_t o = (int64_t)(TC_NP * t) * ld_next + j;
       const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-      const float r1 = __fsub_rn(v, __bfloat162float(hi));
+      const float r1 = __fsub_rn(v, to_f(hi));
       const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
       xs_next[o] = hi;
       xs_next[o + ld_next] = mid;
-      xs_next[o + 2 * (int64_t)ld_next] = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(mid)));
+      xs_next[o + 2 * (int64_t)ld_next] = __float2bfloat16_rn(__fsub_rn(r1, to_f(mid)));
     }
   }
 }
@@ -442,8 +442,8 @@ __global__ void __launch_bounds__(DV_WARPS * 32)
       const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        g = fmaf(__bfloat162float(ge[q]), xv[q], g);
-        u = fmaf(__bfloat162float(ue[q]), xv[q], u);
+        g = fmaf(to_f(ge[q]), xv[q], g);
+        u = fmaf(to_f(ue[q]), xv[q], u);
       }
     }
 #pragma unroll
@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(DV_DN_T)
         if (s + u < s1) {
           uint32_t row = sel[(int64_t)t * k + s + u];
           if (row >= (uint32_t)inter) row = 0;
-          wv[u] = __bfloat162float(downT[(int64_t)row * ldw + j]);
+          wv[u] = to_f(downT[(int64_t)row * ldw + j]);
           av[u] = a[(int64_t)t * k + s + u];
         }
       }
@@ -644,11 +644,11 @@ __global__ void dv_swiglu_mask_kernel(const float* __restrict__ G, const float* 
     }
     const int64_t o = (int64_t)(TC_NP * t) * ldh + i;
     const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-    const float r1 = __fsub_rn(v, __bfloat162float(hi));
+    const float r1 = __fsub_rn(v, to_f(hi));
     const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
     hs[o] = hi;
     hs[o + ldh] = mid;
-    hs[o + 2 * (int64_t)ldh] = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(mid)));
+    hs[o + 2 * (int64_t)ldh] = __float2bfloat16_rn(__fsub_rn(r1, to_f(mid)));
   }
 }
 }  // namespace
