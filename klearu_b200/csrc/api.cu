@@ -1205,7 +1205,7 @@ struct kl_net_s {
   cudaStream_t copy_stream = nullptr;
   // sharded step: the hidden-weight all-gather's stream and its ordering events
   cudaStream_t comm_stream = nullptr;
-  cudaEvent_t ev_hidden = nullptr, ev_gather = nullptr;
+  cudaEvent_t ev_hidden = nullptr, ev_gather = nullptr, ev_cnt = nullptr, ev_cnt_done = nullptr;
   // neuron sharding of the output layer (kl_net_create_sharded)
   int rank = 0, nranks = 1;
   ncclComm_t comm = nullptr;
@@ -1283,6 +1283,8 @@ struct kl_net_s {
     if (ev_join) cudaEventDestroy(ev_join);
     if (ev_hidden) cudaEventDestroy(ev_hidden);
     if (ev_gather) cudaEventDestroy(ev_gather);
+    if (ev_cnt) cudaEventDestroy(ev_cnt);
+    if (ev_cnt_done) cudaEventDestroy(ev_cnt_done);
     if (gexec) cudaGraphExecDestroy(gexec);
     if (cap_stream) cudaStreamDestroy(cap_stream);
     if (comm) ncclCommDestroy(comm);
@@ -1395,6 +1397,33 @@ struct kl_net_s {
   // layers read rows [0, nq) of the previous layer's h.  `after_probe` runs
   // between the probe and the active-row kernels (the sharded step's global
   // empty-selection fallback).
+  // Arguments of the row-major active-row kernel of layer l (l >= 1) for the
+  // examples from s0 of batch b.
+  RmArgs rm_args(int l, const kl_batch& b, int s0, float* hout) {
+    Layer& L = *layers[l];
+    const Layer& P = *layers[l - 1];
+    RmArgs ra{};
+    ra.W = L.W.p;
+    ra.wdtype = wdtype;
+    ra.ldw = L.ldw;
+    ra.d = L.d;
+    ra.bias = L.b.as<float>();
+    ra.act = L.cfg.activation;
+    ra.X = P.h.as<float>();
+    ra.ldx = P.ldN;
+    ra.A = L.act();
+    ra.h = hout;
+    ra.ldh = L.ldN;
+    ra.dxpart = L.dxpart.as<float>();
+    ra.nchunk = L.nchunk;
+    ra.lab_ptr = b.label_ptr + s0;
+    ra.labels = b.labels;
+    ra.labprob = labprob.as<float>();
+    ra.err = ctx->err.as<int>();
+    ra.id_base = L.id_base;
+    ra.only_empty = nullptr;
+    return ra;
+  }
   void forward_layer(int l, const kl_batch& b, int s0, int nq, bool train, int hrow0 = 0,
                      const std::function<void(Layer&)>& after_probe = nullptr) {
     cudaStream_t st = ctx->stream;
@@ -1460,26 +1489,7 @@ struct kl_net_s {
           ck_launch("softmax");
         }
       } else {
-        const Layer& P = *layers[l - 1];
-        RmArgs ra{};
-        ra.W = L.W.p;
-        ra.wdtype = wdtype;
-        ra.ldw = L.ldw;
-        ra.d = L.d;
-        ra.bias = L.b.as<float>();
-        ra.act = L.cfg.activation;
-        ra.X = P.h.as<float>();
-        ra.ldx = P.ldN;
-        ra.A = A;
-        ra.h = hout;
-        ra.ldh = L.ldN;
-        ra.dxpart = L.dxpart.as<float>();
-        ra.nchunk = L.nchunk;
-        ra.lab_ptr = b.label_ptr + s0;
-        ra.labels = b.labels;
-        ra.labprob = labprob.as<float>();
-        ra.err = ctx->err.as<int>();
-        ra.id_base = L.id_base;
+        RmArgs ra = rm_args(l, b, s0, hout);
         const bool softmax = L.cfg.activation == KL_ACT_SOFTMAX;
         const bool fused = last && train && !softmax;
         launch_rm_forward(ra, nq, fused ? RM_FUSED : RM_FWD, st);
@@ -1557,6 +1567,12 @@ struct kl_net_s {
   // captured step graph: two parallel branches).
   cudaStream_t side_stream = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  void ensure_side_stream() {
+    if (side_stream) return;
+    ck(cudaStreamCreateWithFlags(&side_stream, cudaStreamNonBlocking), "side stream");
+    ck(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming), "event");
+    ck(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming), "event");
+  }
   void update_layers(const kl_batch& b, int s0, int nq, double lr) {
     (void)lr;  // the step's optimizer constants are in dopt (upload_opt)
     const int nL = (int)layers.size();
@@ -1564,11 +1580,7 @@ struct kl_net_s {
       for (int l = nL - 1; l >= 0; --l) update_layer(l, b, s0, nq);
       return;
     }
-    if (!side_stream) {
-      ck(cudaStreamCreateWithFlags(&side_stream, cudaStreamNonBlocking), "side stream");
-      ck(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming), "event");
-      ck(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming), "event");
-    }
+    ensure_side_stream();
     cudaStream_t st = ctx->stream;
     ck(cudaEventRecord(ev_fork, st), "event");
     ck(cudaStreamWaitEvent(side_stream, ev_fork, 0), "stream wait");
@@ -1663,13 +1675,39 @@ struct kl_net_s {
       nccl_ck(ncclAllGather(h + (size_t)rank * B * H.ldN, h, (size_t)B * H.ldN, ncclFloat32, comm, st),
               "all-gather hidden activations");
     }
-    // output forward over the global batch; (3) between probe and forward
+    // output forward over the global batch.  (3) runs on the comm stream from
+    // the probe on, beside the forward; an example that no rank selected a
+    // candidate for then takes every local neuron (the fallback) and a second
+    // forward pass computes only those examples.
     forward_layer(1, gb, 0, PB, true, 0, [&](Layer& L) {
-      ck(cudaMemcpyAsync(gcnt.p, L.cnt.p, (size_t)PB * 4, cudaMemcpyDeviceToDevice, st), "copy counts");
-      nccl_ck(ncclAllReduce(gcnt.p, gcnt.p, (size_t)PB, ncclInt32, ncclSum, comm, st), "all-reduce selections");
-      launch_shard_fallback(L.act(), gcnt.as<int32_t>(), L.N, PB, ctx->err.as<int>(), st);
-      ck_launch("shard fallback");
+      ck(cudaEventRecord(ev_cnt, st), "event");
+      ck(cudaStreamWaitEvent(comm_stream, ev_cnt, 0), "stream wait");
+      nccl_ck(ncclAllReduce(L.cnt.p, gcnt.p, (size_t)PB, ncclInt32, ncclSum, comm, comm_stream),
+              "all-reduce selections");
+      ck(cudaEventRecord(ev_cnt_done, comm_stream), "event");
     });
+    {
+      Phase ph(this, 1, KL_PHASE_FORWARD);
+      ck(cudaStreamWaitEvent(st, ev_cnt_done, 0), "stream wait");
+      launch_shard_fallback(O.act(), gcnt.as<int32_t>(), O.N, PB, ctx->err.as<int>(), st);
+      ck_launch("shard fallback");
+      RmArgs ra = rm_args(1, gb, 0, nullptr);
+      ra.only_empty = gcnt.as<int32_t>();
+      launch_rm_forward(ra, PB, RM_FUSED, st);
+      ck_launch("rm forward (fallback examples)");
+    }
+    // The output layer's update needs only its forward (active sets, local
+    // gradients) and the hidden activations: without the phase profiler it
+    // runs on the side stream from here, beside the collectives and the hidden
+    // layer's backward and update below.
+    const bool fork = !prof;
+    if (fork) {
+      ensure_side_stream();
+      ck(cudaEventRecord(ev_fork, st), "event");
+      ck(cudaStreamWaitEvent(side_stream, ev_fork, 0), "stream wait");
+      update_layer(1, gb, 0, PB, side_stream);
+      ck(cudaEventRecord(ev_join, side_stream), "event");
+    }
     // (4) loss probabilities and the output layer's input gradient
     {
       Phase ph(this, 1, KL_PHASE_BACKWARD);
@@ -1703,10 +1741,9 @@ struct kl_net_s {
       launch_shard_or_masks(H.tmask.as<uint32_t>(), tmask_all.as<uint32_t>(), P, nw, st);
       ck_launch("or masks");
     }
-    // (6) The hidden layer's update first, over this rank's feature rows only;
-    // then an in-place all-gather of the updated rows on the comm stream, which
-    // overlaps the output layer's update on the context stream.  The next
-    // step's kernels wait for it.
+    // (6) The hidden layer's update, over this rank's feature rows only; then
+    // an in-place all-gather of the updated rows on the comm stream.  The next
+    // step's kernels wait for it and for the output layer's update.
     update_layer(0, gb, 0, PB);
     {
       const int R = (int)ceil_div(H.d, P);
@@ -1719,7 +1756,8 @@ struct kl_net_s {
               "all-gather hidden weights");
       ck(cudaEventRecord(ev_gather, comm_stream), "event");
     }
-    update_layer(1, gb, 0, PB);
+    if (fork) ck(cudaStreamWaitEvent(st, ev_join, 0), "stream wait");
+    else update_layer(1, gb, 0, PB);
     ck(cudaStreamWaitEvent(st, ev_gather, 0), "stream wait");
   }
 
@@ -2111,9 +2149,15 @@ kl_net_s* create_net(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init
     cap_b.nnz = P * net->nnz_cap;
     cap_b.nlabels = P * net->lab_cap;
     net->ensure_batch_buffers(cap_b);
-    ck(cudaStreamCreateWithFlags(&net->comm_stream, cudaStreamNonBlocking), "comm stream");
+    // the collectives that overlap compute run at the highest stream priority, so
+    // their kernels take SMs ahead of the compute kernels' waiting blocks
+    int prio_lo = 0, prio_hi = 0;
+    ck(cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi), "stream priorities");
+    ck(cudaStreamCreateWithPriority(&net->comm_stream, cudaStreamNonBlocking, prio_hi), "comm stream");
     ck(cudaEventCreateWithFlags(&net->ev_hidden, cudaEventDisableTiming), "event");
     ck(cudaEventCreateWithFlags(&net->ev_gather, cudaEventDisableTiming), "event");
+    ck(cudaEventCreateWithFlags(&net->ev_cnt, cudaEventDisableTiming), "event");
+    ck(cudaEventCreateWithFlags(&net->ev_cnt_done, cudaEventDisableTiming), "event");
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof(id));
     nccl_ck(ncclCommInitRank(&net->comm, nranks, id, rank), "ncclCommInitRank");

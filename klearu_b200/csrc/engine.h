@@ -223,6 +223,8 @@ struct RmArgs {
   float* labprob;
   int* err;
   uint32_t id_base;   // global id of local row 0 (neuron-sharded output layer; labels are global)
+  const int32_t* only_empty;  // nullable: only examples s with only_empty[s] == 0 (the pass after a
+                              // global empty-selection fallback); null: every example
 };
 void launch_rm_forward(const RmArgs& a, int nq, int mode, cudaStream_t st);
 // dX[s][k] = sum over chunks of dxpart (chunk order).

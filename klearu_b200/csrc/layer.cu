@@ -237,6 +237,7 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
   unsigned char* tiles = dyn + xs_bytes;
   float* wpart = reinterpret_cast<float*>(tiles + RM_NWB * 32 * PITCH);
   const int s = blockIdx.y, chunk = blockIdx.x;
+  if (a.only_empty && a.only_empty[s] != 0) return;
   const int na_tot = a.A.cnt[s];
   if (chunk * RM_RPB >= na_tot) return;
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;

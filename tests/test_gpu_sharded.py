@@ -35,13 +35,25 @@ def _cfg():
                        hidden_lsh=LshConfig(num_tables=10, num_hashes=6), rebuild_base=2, rebuild_decay=0.1)
 
 
+def _cfg_fallback():
+    """Output SimHash K=12 over one table: 4096 buckets for 5000 neurons, so
+    some examples find their bucket empty on every shard and take the global
+    all-neurons fallback while the others select candidates."""
+    from klearu_b200 import synthetic as S
+    from klearu_b200.config import HashFunctionType, LshConfig
+
+    return S.config_xc(d_in=2000, hidden=64, n_out=5000, out_hash=HashFunctionType.SimHash, out_k=12, out_l=1,
+                       cap=32, hidden_lsh=LshConfig(num_tables=10, num_hashes=6), rebuild_base=2,
+                       rebuild_decay=0.1)
+
+
 def _close(a, b, bf16_weights=False):
     if bf16_weights:
         return not (np.abs(a - b) > np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -7 + ATOL).any()
     return not (np.abs(a - b) > RTOL * np.abs(b) + ATOL).any()
 
 
-def _worker(rank, world, port, dtype, out):
+def _worker(rank, world, port, dtype, out, fallback=False):
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -49,7 +61,7 @@ def _worker(rank, world, port, dtype, out):
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        _run(rank, world, dtype, out)
+        _run(rank, world, dtype, out, fallback)
     except Exception:  # report instead of leaving the parent waiting
         import traceback
 
@@ -59,14 +71,14 @@ def _worker(rank, world, port, dtype, out):
         dist.destroy_process_group()
 
 
-def _run(rank, world, dtype, out):
+def _run(rank, world, dtype, out, fallback=False):
     import torch.distributed as dist
 
     from klearu_b200 import synthetic as S
     from klearu_b200.core import Context, Network
     from klearu_b200.dist import rank_slice, share_unique_id
 
-    cfg = _cfg()
+    cfg = _cfg_fallback() if fallback else _cfg()
     init = S.make_init(cfg, 42)
     uid = share_unique_id(rank, world)
     net = Network(cfg, init, weight_dtype=dtype, max_batch=24, ctx=Context(rank), shard=(uid, rank, world))
@@ -82,8 +94,14 @@ def _run(rank, world, dtype, out):
         import oracle
 
         o = oracle.Net(cfg, init, weight_dtype=dtype, nshards=world)
-        ol = [o.train_step(hb, 1e-3, mode="batched") for hb in batches]
         msgs = []
+        if fallback:  # the first batch must mix fallback and selecting examples
+            hb = batches[0]
+            n_fb = sum(len(o.forward(hb.idx[hb.rowptr[s]:hb.rowptr[s + 1]], hb.val[hb.rowptr[s]:hb.rowptr[s + 1]])[1][0])
+                       == cfg.network.layers[1].num_neurons for s in range(hb.batch))
+            if not 0 < n_fb < hb.batch:
+                msgs.append(f"{n_fb} of {hb.batch} examples take the fallback: the case is not exercised")
+        ol = [o.train_step(hb, 1e-3, mode="batched") for hb in batches]
         oh, oo = o.get_layer(0), o.get_layer(1)
         for rr, g in enumerate(gathered):
             if g["step"] != 4:
@@ -112,6 +130,25 @@ def test_sharded_two_gpus_match_oracle(dtype):
     q = ctx.Queue()
     port = _free_port()
     ps = [ctx.Process(target=_worker, args=(r, 2, port, dtype, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    msgs = q.get(timeout=240)
+    for p in ps:
+        p.join(120)
+        assert p.exitcode == 0
+    assert not msgs, "\n".join(msgs)
+
+
+def test_sharded_empty_selection_fallback_matches_oracle():
+    """Examples that no shard selects a candidate for take every neuron on
+    every shard (the fallback of the unsharded layer, over the global count);
+    the step still matches the oracle's 2-shard network."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, "f32", q, True)) for r in range(2)]
     for p in ps:
         p.start()
     msgs = q.get(timeout=240)
