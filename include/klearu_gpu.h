@@ -547,22 +547,37 @@ KL_API kl_status kl_dist_get_unique_id(void* id_host);
  *    feature: rank r updates feature rows [r*R, (r+1)*R), R = ceil(d/nranks)
  *    (kl_net_owned_features), and the updated rows are all-gathered.
  *  - Collectives per step (NCCL): all-gather of the batches and of the hidden
- *    activations, all-reduce of per-example selection counts, all-reduce of
- *    the label probabilities with a reduce-scatter of the output layer's
- *    input gradient, all-gather of the hidden local gradients and touched
- *    masks, and all-gather of the updated hidden weight rows (on a second
- *    stream, overlapping the output layer's update).
+ *    activations, all-reduce of per-example selection counts (overlapping the
+ *    output forward), all-reduce of the label probabilities with a
+ *    reduce-scatter of the output layer's input gradient, all-gather of the
+ *    hidden local gradients and touched masks, and all-gather of the updated
+ *    hidden weight rows.  The output layer's update runs on a second stream
+ *    beside the collectives after its forward.
+ *  - Output selection is decided over all shards, as in the unsharded layer.
+ *    Vanilla, and TopK with top_k >= num_tables * bucket_capacity, take every
+ *    candidate; TopK below that (count descending, id ascending) and
+ *    Threshold (count >= threshold, else the single best) sum per-example
+ *    histograms of the local candidates' table counts over the ranks
+ *    (all-reduce), cut there, and all-gather each rank's number of
+ *    candidates at the cut so the lowest ids are taken first.  An example
+ *    that selects nothing on any rank takes every neuron (layer.rs:82-84).
  *  - A rank's batch that cannot be exchanged (another example count, or more
  *    than 512 nnz / 32 labels per example on average) does not make that rank
  *    leave the collective sequence: it is sent empty with a fault flag, every
  *    rank applies the step with a zero learning rate and reports KL_EBOUNDS
  *    (example count) or KL_ECAPACITY at its next synchronising call.
- *  - Supported shapes: two layers, non-softmax output, output sampling that
- *    selects every candidate (Vanilla, or TopK with top_k >= num_tables *
- *    bucket_capacity).  Per example at most 512 input nnz and 32 labels.
- *  - kl_net_forward / kl_net_predict_topk / KL_MODE_EXACT_SEQUENTIAL return
- *    KL_EUNSUPPORTED; kl_net_get_layer / set_layer / layer_output address the
- *    rank's slice of the output layer with local row ids (see kl_net_shard_info).
+ *  - Supported shapes: two layers, non-softmax output.  Per example at most
+ *    512 input nnz and 32 labels.
+ *  - kl_net_forward and kl_net_predict_topk take exactly `max_batch`
+ *    examples per rank, like the train step (labels may be absent).  After
+ *    kl_net_forward, kl_net_layer_output(1) holds the global batch's
+ *    (nranks * max_batch examples, rank order) active sets on this rank's
+ *    slice; kl_net_predict_topk returns the top k over all N neurons of this
+ *    rank's own examples (k <= N / nranks; local top-k lists all-gathered and
+ *    merged).  KL_MODE_EXACT_SEQUENTIAL returns KL_EUNSUPPORTED.
+ *    kl_net_get_layer / set_layer / layer_output address the rank's slice of
+ *    the output layer with local row ids (see kl_net_shard_info); layer
+ *    outputs hold nranks * max_batch rows.
  * `init` holds the FULL parameters (every rank passes the same);
  * `unique_id_host` is kl_dist_get_unique_id's output from rank 0. */
 KL_API kl_status kl_net_create_sharded(kl_ctx_t ctx, const kl_net_config* cfg_host,

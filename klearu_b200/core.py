@@ -629,16 +629,17 @@ class Network:
         d, N, ma = C.c_int(), C.c_int(), C.c_int()
         check(self.lib.kl_net_layer_info(self.h, layer, C.byref(d), C.byref(N), C.byref(ma)))
         stride = ma.value
-        ids = torch.empty(self.max_batch * stride, dtype=torch.int32, device=self._dev)
-        cnt = torch.empty(self.max_batch, dtype=torch.int32, device=self._dev)
-        pre = torch.empty(self.max_batch * stride, dtype=torch.float32, device=self._dev)
-        act = torch.empty(self.max_batch * stride, dtype=torch.float32, device=self._dev)
+        rows = self.max_batch * self.shard_info()[1]  # a sharded net's outputs cover the global batch
+        ids = torch.empty(rows * stride, dtype=torch.int32, device=self._dev)
+        cnt = torch.empty(rows, dtype=torch.int32, device=self._dev)
+        pre = torch.empty(rows * stride, dtype=torch.float32, device=self._dev)
+        act = torch.empty(rows * stride, dtype=torch.float32, device=self._dev)
         check(self.lib.kl_net_layer_output(self.h, layer, _ptr(ids), _ptr(cnt), _ptr(pre), _ptr(act)),
               self.ctx.h, "kl_net_layer_output")
         self.ctx.sync()
-        ids = ids.cpu().numpy().view(np.uint32).reshape(self.max_batch, stride)
-        pre = pre.cpu().numpy().reshape(self.max_batch, stride)
-        act = act.cpu().numpy().reshape(self.max_batch, stride)
+        ids = ids.cpu().numpy().view(np.uint32).reshape(rows, stride)
+        pre = pre.cpu().numpy().reshape(rows, stride)
+        act = act.cpu().numpy().reshape(rows, stride)
         cnt = cnt.cpu().numpy()
         return ([ids[s, :cnt[s]] for s in range(nq)], [pre[s, :cnt[s]] for s in range(nq)],
                 [act[s, :cnt[s]] for s in range(nq)], N.value)

@@ -1151,6 +1151,11 @@ struct Layer {
   size_t ent_cap = 0;
   DBuf stats;  // u64 [3]: active_sum, touched_rows, input_nnz
   uint64_t examples = 0, steps = 0, rebuilds = 0, input_nnz = 0;
+  // sharded output layer with a selection over all shards (TopK below the
+  // candidate count, Threshold): every local candidate with its table count
+  bool shard_select = false;
+  int cstride = 0;
+  DBuf cids, ccnt, ccn;
 
   ActiveSet act() const {
     return ActiveSet{ids.as<uint32_t>(), cnt.as<int32_t>(), stride, pre.as<float>(), post.as<float>(),
@@ -1206,6 +1211,7 @@ struct kl_net_s {
   // sharded step: the hidden-weight all-gather's stream and its ordering events
   cudaStream_t comm_stream = nullptr;
   cudaEvent_t ev_hidden = nullptr, ev_gather = nullptr, ev_cnt = nullptr, ev_cnt_done = nullptr;
+  DBuf sel_hist, sel_cut, sel_eq_all;  // global selection over the output shards
   // neuron sharding of the output layer (kl_net_create_sharded)
   int rank = 0, nranks = 1;
   ncclComm_t comm = nullptr;
@@ -1286,6 +1292,7 @@ struct kl_net_s {
     if (ev_cnt) cudaEventDestroy(ev_cnt);
     if (ev_cnt_done) cudaEventDestroy(ev_cnt_done);
     if (gexec) cudaGraphExecDestroy(gexec);
+    if (sh_gexec) cudaGraphExecDestroy(sh_gexec);
     if (cap_stream) cudaStreamDestroy(cap_stream);
     if (comm) ncclCommDestroy(comm);
     for (auto& e : pending) pool.emplace_back(e.a, e.b);
@@ -1469,6 +1476,14 @@ struct kl_net_s {
       pa.err = ctx->err.as<int>();
       pa.stat_active = L.stats.as<unsigned long long>();
       pa.fallback = !(last && nranks > 1);
+      if (last && L.shard_select) {  // every local candidate; shard_select_exchange selects
+        pa.sampling = KL_SAMPLING_VANILLA;
+        pa.out_ids = L.cids.as<uint32_t>();
+        pa.out_counts = L.ccnt.as<uint32_t>();
+        pa.out_stride = L.cstride;
+        pa.out_n = L.ccn.as<int32_t>();
+        pa.stat_active = nullptr;
+      }
       launch_probe(pa, st);
       ck_launch("probe");
       if (after_probe) after_probe(L);
@@ -1624,6 +1639,30 @@ struct kl_net_s {
     }
   }
 
+  // The output layer's selection over all shards for the nq examples of the
+  // last probe (Layer::shard_select): count histograms summed over the ranks,
+  // the per-example cut, the ranks' numbers of candidates at the cut, and the
+  // compaction of this rank's selected candidates into the active set.
+  void shard_select_exchange(Layer& L, int nq) {
+    cudaStream_t st = ctx->stream;
+    const int Lt = L.cfg.lsh.num_tables;
+    int32_t* hist = sel_hist.as<int32_t>();
+    launch_sel_hist(L.ccnt.as<uint32_t>(), L.ccn.as<int32_t>(), L.cstride, Lt, hist, nq, st);
+    ck_launch("selection histogram");
+    nccl_ck(ncclAllReduce(hist, hist, (size_t)nq * (Lt + 1), ncclInt32, ncclSum, comm, st),
+            "all-reduce selection histograms");
+    int32_t* sc = sel_cut.as<int32_t>();  // cut, need, global size, local count at the cut: [4][nq]
+    launch_sel_cut(hist, Lt, L.cfg.sampling, L.cfg.top_k, L.cfg.sampling_threshold, L.ccnt.as<uint32_t>(),
+                   L.ccn.as<int32_t>(), L.cstride, sc, sc + nq, sc + 2 * nq, sc + 3 * nq, nq, st);
+    ck_launch("selection cut");
+    int32_t* eq_all = sel_eq_all.as<int32_t>();
+    nccl_ck(ncclAllGather(sc + 3 * nq, eq_all, (size_t)nq, ncclInt32, comm, st), "all-gather cut counts");
+    launch_sel_apply(L.cids.as<uint32_t>(), L.ccnt.as<uint32_t>(), L.ccn.as<int32_t>(), L.cstride, sc, sc + nq,
+                     sc + 2 * nq, eq_all, rank, nq, L.N, L.act(), ctx->err.as<int>(),
+                     L.stats.as<unsigned long long>(), st);
+    ck_launch("selection apply");
+  }
+
   // One batched train step of a neuron-sharded network (nranks > 1).  `lb`
   // holds this rank's B examples; the global batch is the P*B examples of all
   // ranks in rank order.  Collectives, all on the context stream:
@@ -1635,23 +1674,40 @@ struct kl_net_s {
   //      reduce-scatter of the output layer's input gradient;
   //  (5) one group: all-gather of the hidden local gradients and touched masks.
   // The replicated hidden layer then applies the same update on every rank.
-  void train_sharded(const kl_batch& lb, double lr) {
-    cudaStream_t st = ctx->stream;
-    // Every collective below is sized by the configured per-rank batch, never by this
-    // rank's data, so that no rank can leave the collective sequence on its own.  A
-    // batch that cannot be exchanged (another example count, or more nnz / labels than
-    // the fixed exchange capacity) is sent as an empty batch with a fault word: every
-    // rank then raises the fault at its next synchronising call and applies the step
-    // with a zero learning rate.
-    const int P = nranks, B = rank_batch, PB = P * B;
+  // Steps (1)-(3) of a sharded step for `lb` (this rank's examples): the
+  // global batch, the hidden layer's forward and the output layer's forward
+  // over the global batch on this rank's slice (with the input-gradient
+  // partials when `train`).  Returns the global batch.
+  kl_batch sharded_forward(const kl_batch& lb, bool train) {
+    shard_pack(lb);
+    return sharded_forward_body(train);
+  }
+  // Every collective of a sharded step is sized by the configured per-rank
+  // batch, never by this rank's data, so that no rank can leave the collective
+  // sequence on its own.  A batch that cannot be exchanged (another example
+  // count, or more nnz / labels than the fixed exchange capacity) is sent as an
+  // empty batch with a fault word: every rank then raises the fault at its next
+  // synchronising call and applies the step with a zero learning rate.
+  // shard_pack copies this rank's batch into the exchange buffer (its only
+  // step that depends on the caller's arrays and sizes); everything after it
+  // reads fixed buffers, so it can be captured in a CUDA graph.
+  static bool shard_batch_ok(const kl_batch& lb, int B, int nnz_cap_, int lab_cap_) {
+    return lb.batch == B && lb.nnz <= nnz_cap_ && !(lb.label_ptr && lb.nlabels > lab_cap_);
+  }
+  void shard_pack(const kl_batch& lb) {
+    const int B = rank_batch;
     uint32_t fault = 0;
     if (lb.batch != B) fault = DERR_BOUNDS;
-    else if (lb.nnz > nnz_cap || lb.nlabels > lab_cap) fault = DERR_CAPACITY;
+    else if (!shard_batch_ok(lb, B, nnz_cap, lab_cap)) fault = DERR_CAPACITY;
+    launch_shard_pack(dsend.as<uint32_t>(), shl, lb, B, fault, ctx->stream);
+    ck_launch("shard pack");
+  }
+  kl_batch sharded_forward_body(bool train) {
+    cudaStream_t st = ctx->stream;
+    const int P = nranks, B = rank_batch, PB = P * B;
     Layer& H = *layers[0];
     Layer& O = *layers[1];
     // (1) the global batch
-    launch_shard_pack(dsend.as<uint32_t>(), shl, lb, B, fault, st);
-    ck_launch("shard pack");
     nccl_ck(ncclAllGather(dsend.p, drecv.p, (size_t)shl.words, ncclUint32, comm, st), "all-gather batches");
     launch_shard_unpack(drecv.as<uint32_t>(), shl, P, B, g_rowptr.as<int32_t>(), g_idx.as<uint32_t>(),
                         g_val.as<float>(), g_lptr.as<int32_t>(), g_labels.as<uint32_t>(), ctx->err.as<int>(),
@@ -1669,7 +1725,7 @@ struct kl_net_s {
     ck(cudaMemsetAsync(loss_acc.p, 0, 4, st), "memset");
     ck(cudaMemsetAsync(labprob.p, 0, (size_t)P * lab_cap * 4, st), "memset");
     // (2) hidden forward of this rank's examples, then every rank's activations
-    forward_layer(0, gb, rank * B, B, true, rank * B);
+    forward_layer(0, gb, rank * B, B, train, rank * B);
     {
       float* h = H.h.as<float>();
       nccl_ck(ncclAllGather(h + (size_t)rank * B * H.ldN, h, (size_t)B * H.ldN, ncclFloat32, comm, st),
@@ -1679,23 +1735,94 @@ struct kl_net_s {
     // the probe on, beside the forward; an example that no rank selected a
     // candidate for then takes every local neuron (the fallback) and a second
     // forward pass computes only those examples.
-    forward_layer(1, gb, 0, PB, true, 0, [&](Layer& L) {
+    forward_layer(1, gb, 0, PB, train, 0, [&](Layer& L) {
+      if (L.shard_select) {  // the selection itself is global (and decides the fallback)
+        shard_select_exchange(L, PB);
+        return;
+      }
       ck(cudaEventRecord(ev_cnt, st), "event");
       ck(cudaStreamWaitEvent(comm_stream, ev_cnt, 0), "stream wait");
       nccl_ck(ncclAllReduce(L.cnt.p, gcnt.p, (size_t)PB, ncclInt32, ncclSum, comm, comm_stream),
               "all-reduce selections");
       ck(cudaEventRecord(ev_cnt_done, comm_stream), "event");
     });
-    {
+    if (!O.shard_select) {
       Phase ph(this, 1, KL_PHASE_FORWARD);
       ck(cudaStreamWaitEvent(st, ev_cnt_done, 0), "stream wait");
       launch_shard_fallback(O.act(), gcnt.as<int32_t>(), O.N, PB, ctx->err.as<int>(), st);
       ck_launch("shard fallback");
       RmArgs ra = rm_args(1, gb, 0, nullptr);
       ra.only_empty = gcnt.as<int32_t>();
-      launch_rm_forward(ra, PB, RM_FUSED, st);
+      launch_rm_forward(ra, PB, train ? RM_FUSED : RM_FWD, st);
       ck_launch("rm forward (fallback examples)");
     }
+    return gb;
+  }
+
+  void train_sharded(const kl_batch& lb, double lr) {
+    (void)lr;  // the step's optimizer constants are in dopt (upload_opt)
+    shard_pack(lb);
+    if (!graph_disabled && !prof && shard_batch_ok(lb, rank_batch, nnz_cap, lab_cap)) {
+      sharded_graph_step();
+      return;
+    }
+    train_sharded_body();
+  }
+  // The sharded step after the pack as one CUDA graph (NCCL collectives
+  // included), replayed per step: the step issues ~70 launches and collectives,
+  // which cost more host time than the GPU spends on them.  First use runs
+  // eagerly, the second captures.  A batch that the exchange must flag takes
+  // the eager body: its collectives are the same, so the ranks stay matched.
+  cudaGraphExec_t sh_gexec = nullptr;
+  bool sh_warm = false;
+  unsigned long long sh_graph_kernels = 0;
+  void sharded_graph_step() {
+    cudaStream_t st = ctx->stream;
+    if (!sh_warm) {
+      sh_warm = true;
+      train_sharded_body();
+      return;
+    }
+    if (!sh_gexec) {
+      if (!cap_stream) ck(cudaStreamCreateWithFlags(&cap_stream, cudaStreamNonBlocking), "capture stream");
+      ensure_side_stream();
+      // the capture stream starts after this call's pack
+      ck(cudaEventRecord(ev_fork, st), "event");
+      ck(cudaStreamWaitEvent(cap_stream, ev_fork, 0), "stream wait");
+      cudaGraph_t g = nullptr;
+      ctx->stream = cap_stream;
+      bool ok = cudaStreamBeginCapture(cap_stream, cudaStreamCaptureModeRelaxed) == cudaSuccess;
+      const unsigned long long n0 = g_launches.load();
+      if (ok) {
+        try {
+          train_sharded_body();
+        } catch (...) {
+          ok = false;
+        }
+        ok = cudaStreamEndCapture(cap_stream, &g) == cudaSuccess && ok && g;
+      }
+      ctx->stream = st;
+      if (ok) ok = cudaGraphInstantiate(&sh_gexec, g, 0) == cudaSuccess;
+      if (g) cudaGraphDestroy(g);
+      cudaGetLastError();
+      if (!ok) {
+        sh_gexec = nullptr;
+        graph_disabled = true;  // eager from now on (same collectives)
+        train_sharded_body();
+        return;
+      }
+      sh_graph_kernels = g_launches.load() - n0;
+      g_launches.fetch_sub(sh_graph_kernels);  // counted again per replay below
+    }
+    ck(cudaGraphLaunch(sh_gexec, st), "graph launch");
+    count_launch((unsigned)sh_graph_kernels);
+  }
+  void train_sharded_body() {
+    cudaStream_t st = ctx->stream;
+    const int P = nranks, B = rank_batch, PB = P * B;
+    Layer& H = *layers[0];
+    Layer& O = *layers[1];
+    const kl_batch gb = sharded_forward_body(true);
     // The output layer's update needs only its forward (active sets, local
     // gradients) and the hidden activations: without the phase profiler it
     // runs on the side stream from here, beside the collectives and the hidden
@@ -2079,11 +2206,7 @@ kl_net_s* create_net(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init
     support(nl == 2, "sharded net: exactly two layers (sparse-input hidden layer + sharded output layer)");
     support(o.activation != KL_ACT_SOFTMAX, "sharded net: softmax output layers are not supported");
     support(o.num_neurons >= nranks, "sharded net: fewer output neurons than ranks");
-    const int cap_shard = std::max(1, o.lsh.bucket_capacity / nranks);
-    const int64_t M = (int64_t)o.lsh.num_tables * cap_shard * nranks;  // candidates per example, all shards
-    support(o.sampling == KL_SAMPLING_VANILLA || (o.sampling == KL_SAMPLING_TOPK && o.top_k >= M),
-            "sharded net: output sampling must select every candidate (Vanilla, or TopK with top_k >= "
-            "num_tables * bucket_capacity)");
+    support(o.lsh.num_tables <= 1024, "sharded net: at most 1024 output tables");
     require(cfg->max_batch <= 4096 / nranks, "sharded net: nranks * max_batch must be <= 4096");
   }
   std::unique_ptr<kl_net_s> net(new kl_net_s());
@@ -2143,6 +2266,23 @@ kl_net_s* create_net(kl_ctx_t ctx, const kl_net_config* cfg, const kl_layer_init
     net->g_val.alloc((size_t)P * net->nnz_cap * 4);
     net->g_labels.alloc((size_t)P * net->lab_cap * 4);
     net->gcnt.alloc((size_t)P * B * 4);
+    {
+      Layer& O = *net->layers[nl - 1];
+      const kl_layer_config& oc = cfg->layers[nl - 1];
+      const int64_t Mloc = (int64_t)oc.lsh.num_tables * std::max(1, oc.lsh.bucket_capacity / P);
+      O.shard_select = oc.sampling == KL_SAMPLING_THRESHOLD ||
+                       (oc.sampling == KL_SAMPLING_TOPK && (int64_t)oc.top_k < Mloc * P);
+      if (O.shard_select) {
+        const int PBn = P * B;
+        O.cstride = (int)Mloc;
+        O.cids.alloc((size_t)PBn * Mloc * 4);
+        O.ccnt.alloc((size_t)PBn * Mloc * 4);
+        O.ccn.alloc((size_t)PBn * 4);
+        net->sel_hist.alloc((size_t)PBn * (oc.lsh.num_tables + 1) * 4);
+        net->sel_cut.alloc((size_t)4 * PBn * 4);
+        net->sel_eq_all.alloc((size_t)P * PBn * 4);
+      }
+    }
     net->tmask_all.alloc((size_t)P * ceil_div(net->layers[0]->N, 32) * 4);
     kl_batch cap_b{};
     cap_b.batch = P * B;
@@ -2351,7 +2491,12 @@ extern "C" kl_status kl_net_train_step_host(kl_net_t net, const kl_batch* hb, do
 extern "C" kl_status kl_net_forward(kl_net_t net, const kl_batch* b) {
   if (!net) return KL_EINVAL;
   KL_API_BEGIN(net->ctx)
-  support(net->nranks == 1, "sharded net: forward without a train step is not supported");
+  if (net->nranks > 1) {
+    require(b != nullptr, "forward: null batch");
+    net->sharded_forward(*b, false);
+    check_device_errors(net->ctx);
+    return KL_OK;
+  }
   validate_batch(net, b);
   if (b->batch == 0) return KL_OK;
   net->ensure_batch_buffers(*b);
@@ -2388,9 +2533,36 @@ extern "C" kl_status kl_net_predict_topk(kl_net_t net, const kl_batch* b, int k,
                                          float* top_scores) {
   if (!net) return KL_EINVAL;
   KL_API_BEGIN(net->ctx)
-  support(net->nranks == 1, "sharded net: predict_top_k is not supported");
-  validate_batch(net, b);
   require(k >= 0 && (k == 0 || top_ids), "predict_topk: bad arguments");
+  if (net->nranks > 1) {
+    require(b != nullptr, "predict_topk: null batch");
+    const int P = net->nranks, B = net->rank_batch, PB = P * B;
+    const Layer& L = *net->layers.back();
+    const int64_t Ntot = net->cfg.layers[net->cfg.num_layers - 1].num_neurons;
+    support(P <= 64, "sharded predict_topk: at most 64 ranks");
+    require(k <= Ntot / P, "sharded predict_topk: k must be <= num_neurons / nranks");
+    net->sharded_forward(*b, false);
+    if (k == 0) return KL_OK;
+    cudaStream_t st = ctx__->stream;
+    DBuf lids, lsc, aids, asc;
+    lids.alloc((size_t)PB * k * 4);
+    lsc.alloc((size_t)PB * k * 4);
+    aids.alloc((size_t)P * PB * k * 4);
+    asc.alloc((size_t)P * PB * k * 4);
+    launch_topk(L.act(), L.N, k, lids.as<uint32_t>(), lsc.as<float>(), PB, st);
+    ck_launch("topk");
+    nccl_ck(ncclGroupStart(), "group");
+    nccl_ck(ncclAllGather(lids.p, aids.p, (size_t)PB * k, ncclUint32, net->comm, st), "all-gather top-k ids");
+    nccl_ck(ncclAllGather(lsc.p, asc.p, (size_t)PB * k, ncclFloat32, net->comm, st), "all-gather top-k scores");
+    nccl_ck(ncclGroupEnd(), "group");
+    launch_shard_topk_merge(aids.as<uint32_t>(), asc.as<float>(), P, PB, k, Ntot, net->rank * B, B, top_ids,
+                            top_scores, st);
+    ck_launch("top-k merge");
+    ck(cudaStreamSynchronize(st), "sync");  // the scratch is freed on return
+    check_device_errors(net->ctx);
+    return KL_OK;
+  }
+  validate_batch(net, b);
   if (b->batch == 0 || k == 0) return KL_OK;
   const Layer& L = *net->layers.back();
   k = std::min(k, L.N);

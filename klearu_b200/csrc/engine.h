@@ -318,6 +318,22 @@ void launch_shard_unpack(const uint32_t* recv, const ShardLayout& Ly, int P, int
                          uint32_t* g_idx, float* g_val, int32_t* g_lptr, uint32_t* g_labels, int* err, OptStep* opt,
                          cudaStream_t st);
 void launch_shard_fallback(ActiveSet A, const int32_t* gcnt, int n_local, int nq, int* err, cudaStream_t st);
+// Global selection over the output shards (TopK below the candidate count,
+// Threshold): per-example count histograms of the local candidates
+// [nq][Lt + 1], the cut from the summed histograms, and the compaction of the
+// local candidates into the active set (see shard.cu).
+void launch_sel_hist(const uint32_t* ccnt, const int32_t* cn, int cstride, int Lt, int32_t* hist, int nq,
+                     cudaStream_t st);
+void launch_sel_cut(const int32_t* ghist, int Lt, int sampling, int top_k, int threshold, const uint32_t* ccnt,
+                    const int32_t* cn, int cstride, int32_t* cut, int32_t* need, int32_t* gsel, int32_t* eqloc,
+                    int nq, cudaStream_t st);
+void launch_sel_apply(const uint32_t* cids, const uint32_t* ccnt, const int32_t* cn, int cstride, const int32_t* cut,
+                      const int32_t* need, const int32_t* gsel, const int32_t* eq_all, int rank, int nq, int n_local,
+                      ActiveSet A, int* err, unsigned long long* stat, cudaStream_t st);
+// The global top k of this rank's B examples (global examples s0 ..) from
+// every rank's local top-k lists ([P][PB][k] local ids and scores, P <= 64).
+void launch_shard_topk_merge(const uint32_t* ids_all, const float* sc_all, int P, int PB, int k, int64_t N, int s0,
+                             int B, uint32_t* top_ids, float* top_scores, cudaStream_t st);
 void launch_shard_or_masks(uint32_t* tmask, const uint32_t* all, int P, int nw, cudaStream_t st);
 
 // ---- Deja Vu sparse FFN (dejavu.cu) ----

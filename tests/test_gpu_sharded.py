@@ -47,13 +47,30 @@ def _cfg_fallback():
                        rebuild_decay=0.1)
 
 
+def _cfg_select(sampling):
+    """Output selection below the candidate count: TopK of 40 out of up to
+    10 x 32 candidates, or Threshold 3 of 10 tables (with its single-best
+    fallback), both decided over all shards."""
+    from klearu_b200 import synthetic as S
+    from klearu_b200.config import LshConfig, SamplingType
+
+    cfg = S.config_xc(d_in=2000, hidden=64, n_out=5000, out_l=10, cap=32,
+                      hidden_lsh=LshConfig(num_tables=10, num_hashes=6), rebuild_base=2, rebuild_decay=0.1,
+                      out_topk=40)
+    o = cfg.network.layers[1]
+    if sampling == "threshold":
+        o.sampling = SamplingType.Threshold
+        o.sampling_threshold = 3
+    return cfg
+
+
 def _close(a, b, bf16_weights=False):
     if bf16_weights:
         return not (np.abs(a - b) > np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -7 + ATOL).any()
     return not (np.abs(a - b) > RTOL * np.abs(b) + ATOL).any()
 
 
-def _worker(rank, world, port, dtype, out, fallback=False):
+def _worker(rank, world, port, dtype, out, variant="all"):
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -61,7 +78,7 @@ def _worker(rank, world, port, dtype, out, fallback=False):
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        _run(rank, world, dtype, out, fallback)
+        _run(rank, world, dtype, out, variant)
     except Exception:  # report instead of leaving the parent waiting
         import traceback
 
@@ -71,14 +88,14 @@ def _worker(rank, world, port, dtype, out, fallback=False):
         dist.destroy_process_group()
 
 
-def _run(rank, world, dtype, out, fallback=False):
+def _run(rank, world, dtype, out, variant="all"):
     import torch.distributed as dist
 
     from klearu_b200 import synthetic as S
     from klearu_b200.core import Context, Network
     from klearu_b200.dist import rank_slice, share_unique_id
 
-    cfg = _cfg_fallback() if fallback else _cfg()
+    cfg = {"all": _cfg, "fallback": _cfg_fallback}.get(variant, lambda: _cfg_select(variant))()
     init = S.make_init(cfg, 42)
     uid = share_unique_id(rank, world)
     net = Network(cfg, init, weight_dtype=dtype, max_batch=24, ctx=Context(rank), shard=(uid, rank, world))
@@ -86,8 +103,11 @@ def _run(rank, world, dtype, out, fallback=False):
     batches = [gen.batch(24 * world) for _ in range(4)]
     losses = [net.train_step_host(rank_slice(hb, rank, world), 1e-3) for hb in batches]
     r, n, base, nloc = net.shard_info()
+    # predict_top_k of this rank's examples of a fresh batch, over all shards
+    phb = gen.batch(24 * world)
+    top = net.predict_top_k_batch(_examples(rank_slice(phb, rank, world)), 10)
     res = {"losses": losses, "hidden": net.get_layer(0), "out": net.get_layer(1), "base": base, "n": nloc,
-           "step": net.step, "feat": net.owned_features()}
+           "step": net.step, "feat": net.owned_features(), "top": top}
     gathered = [None] * world
     dist.all_gather_object(gathered, res)
     if rank == 0:
@@ -95,13 +115,24 @@ def _run(rank, world, dtype, out, fallback=False):
 
         o = oracle.Net(cfg, init, weight_dtype=dtype, nshards=world)
         msgs = []
-        if fallback:  # the first batch must mix fallback and selecting examples
+        if variant == "fallback":  # the first batch must mix fallback and selecting examples
             hb = batches[0]
             n_fb = sum(len(o.forward(hb.idx[hb.rowptr[s]:hb.rowptr[s + 1]], hb.val[hb.rowptr[s]:hb.rowptr[s + 1]])[1][0])
                        == cfg.network.layers[1].num_neurons for s in range(hb.batch))
             if not 0 < n_fb < hb.batch:
                 msgs.append(f"{n_fb} of {hb.batch} examples take the fallback: the case is not exercised")
         ol = [o.train_step(hb, 1e-3, mode="batched") for hb in batches]
+        for rr, g in enumerate(gathered):  # predict_top_k after the steps (net.rs:159-173)
+            ids, sc = g["top"]
+            for i in range(24):
+                s = rr * 24 + i
+                a, b = int(phb.rowptr[s]), int(phb.rowptr[s + 1])
+                oi, _, oa = o.forward(phb.idx[a:b], phb.val[a:b])[-1]
+                dense = np.zeros(cfg.network.layers[1].num_neurons, np.float32)
+                dense[oi] = oa
+                order = sorted(range(dense.size), key=lambda j: (-dense[j], j))[:10]
+                if [int(j) for j in ids[i]] != order or not np.allclose(sc[i], dense[order], rtol=1e-5):
+                    msgs.append(f"rank {rr} example {i}: predict_top_k differs")
         oh, oo = o.get_layer(0), o.get_layer(1)
         for rr, g in enumerate(gathered):
             if g["step"] != 4:
@@ -148,7 +179,7 @@ def test_sharded_empty_selection_fallback_matches_oracle():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, "f32", q, True)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, "f32", q, "fallback")) for r in range(2)]
     for p in ps:
         p.start()
     msgs = q.get(timeout=240)
@@ -156,6 +187,36 @@ def test_sharded_empty_selection_fallback_matches_oracle():
         p.join(120)
         assert p.exitcode == 0
     assert not msgs, "\n".join(msgs)
+
+
+@pytest.mark.parametrize("sampling", ["topk", "threshold"])
+def test_sharded_global_selection_matches_oracle(sampling):
+    """TopK below the candidate count and Threshold select over the candidates
+    of all shards, as the unsharded layer does."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, "f32", q, sampling)) for r in range(2)]
+    for p in ps:
+        p.start()
+    msgs = q.get(timeout=240)
+    for p in ps:
+        p.join(120)
+        assert p.exitcode == 0
+    assert not msgs, "\n".join(msgs)
+
+
+def _examples(hb):
+    from klearu_b200.data import Example, SparseVector
+
+    out = []
+    for s in range(hb.batch):
+        a, b = int(hb.rowptr[s]), int(hb.rowptr[s + 1])
+        c, d = int(hb.label_ptr[s]), int(hb.label_ptr[s + 1])
+        out.append(Example(SparseVector(hb.idx[a:b], hb.val[a:b], 0), list(hb.labels[c:d])))
+    return out
 
 
 def _fault_worker(rank, world, port, out):
