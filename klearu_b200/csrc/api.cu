@@ -3197,10 +3197,13 @@ void topk_check(kl_predictor_t p, int kk) {
           "select_topk: k and output_dim too large for one block's shared memory");
 }
 // select_top_k for T tokens into idx [T][kk]; sc [T][out] receives the scores.
-void predictor_topk_body(kl_predictor_t p, const float* x, int T, int kk, uint32_t* idx, float* sc, cudaStream_t st) {
+// sorted = false: the selection in ascending index order (the sparse MLP's
+// sums then run in neuron order, as its dense-masked path does).
+void predictor_topk_body(kl_predictor_t p, const float* x, int T, int kk, uint32_t* idx, float* sc, cudaStream_t st,
+                         bool sorted = true) {
   topk_check(p, kk);
   predictor_scores(p, x, T, sc, st);
-  launch_topk(sc, T, p->out, p->out, kk, idx, kk, st);
+  launch_topk(sc, T, p->out, p->out, kk, idx, kk, st, sorted);
   ck_launch("topk");
 }
 
@@ -3320,10 +3323,13 @@ extern "C" kl_status kl_sparse_mlp_destroy(kl_sparse_mlp_t m) {
 }
 
 // sparse_mlp::forward_sparse for T tokens on stream st (k >= 1).
+// accumulate (gather path only, n_tokens < KL_DENSE_MIN_TOKENS): out += the
+// MLP's output (a fused residual add) instead of out = it.
 static void sparse_mlp_body(kl_sparse_mlp_t m, const float* x, int n_tokens, const uint32_t* sel, int k, float* out,
-                            cudaStream_t st) {
+                            cudaStream_t st, bool accumulate = false) {
   int* err = m->ctx->err.as<int>();
   if (n_tokens >= KL_DENSE_MIN_TOKENS) {
+    require(!accumulate, "sparse mlp: accumulate needs the gather path");
     for (int t0 = 0; t0 < n_tokens; t0 += TC_LINEAR_MAX_T) {
       const int tn = std::min(TC_LINEAR_MAX_T, n_tokens - t0);
       launch_sparse_mlp_dense(m->gate.as<__nv_bfloat16>(), m->up.as<__nv_bfloat16>(), m->down.as<__nv_bfloat16>(),
@@ -3335,16 +3341,15 @@ static void sparse_mlp_body(kl_sparse_mlp_t m, const float* x, int n_tokens, con
     }
     return;
   }
-  // K splits of the down projection: at most ~32 selected rows per thread,
-  // and enough blocks ((hidden / 256) x splits x tokens) to fill the SMs
-  const int cols = (int)ceil_div(m->hid, 256);
-  const int splits = std::max(1, std::min(k, std::max((int)ceil_div(k, 32),
-                                                      (int)ceil_div(592, (int64_t)cols * n_tokens))));
+  // K splits of the down projection: at least 16 selected rows per split, and
+  // up to enough blocks ((hidden / 2048) x splits x tokens) for 8 per SM
+  const int cols = (int)ceil_div(m->hid, 2048);
+  const int splits = std::max(1, std::min((int)ceil_div(k, 16), (int)ceil_div(1184, (int64_t)cols * n_tokens)));
   m->a.alloc((size_t)n_tokens * k * 4);
   m->part.alloc((size_t)n_tokens * splits * m->ldw * 4);
   launch_sparse_mlp(m->gate.as<__nv_bfloat16>(), m->up.as<__nv_bfloat16>(), m->downT.as<__nv_bfloat16>(), m->hid,
                     m->ldw, m->inter, m->has_bias ? m->bias.as<float>() : nullptr, x, n_tokens, sel, k,
-                    m->a.as<float>(), m->part.as<float>(), splits, out, err, st);
+                    m->a.as<float>(), m->part.as<float>(), splits, out, accumulate, err, st);
   ck_launch("sparse mlp");
 }
 
@@ -3398,10 +3403,16 @@ struct kl_ffn_stack_s {
     for (int l = 0; l < nl; ++l) {
       launch_rmsnorm(hidden, T, hid, normw.as<float>() + (size_t)l * hid, eps, one_plus, norm.as<float>(), st);
       ck_launch("rmsnorm");
-      predictor_topk_body(pred[(size_t)l], norm.as<float>(), T, k, idx.as<uint32_t>(), sc.as<float>(), st);
-      sparse_mlp_body(mlp[(size_t)l], norm.as<float>(), T, idx.as<uint32_t>(), k, out.as<float>(), st);
-      launch_residual_add(hidden, out.as<float>(), (int64_t)T * hid, st);
-      ck_launch("residual add");
+      // the selection in neuron order (no sort): the MLP's sums then run in
+      // neuron order on both of its paths
+      predictor_topk_body(pred[(size_t)l], norm.as<float>(), T, k, idx.as<uint32_t>(), sc.as<float>(), st, false);
+      if (T < KL_DENSE_MIN_TOKENS) {  // residual add fused into the down projection's finish
+        sparse_mlp_body(mlp[(size_t)l], norm.as<float>(), T, idx.as<uint32_t>(), k, hidden, st, true);
+      } else {
+        sparse_mlp_body(mlp[(size_t)l], norm.as<float>(), T, idx.as<uint32_t>(), k, out.as<float>(), st);
+        launch_residual_add(hidden, out.as<float>(), (int64_t)T * hid, st);
+        ck_launch("residual add");
+      }
     }
   }
 };

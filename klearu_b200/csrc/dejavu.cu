@@ -221,7 +221,7 @@ constexpr int TK_NB = 4096;
 constexpr int TK_MAXC = 2048;  // candidates of the threshold bin ranked in shared memory
 
 __global__ void __launch_bounds__(TK_NT) topk_kernel(const float* __restrict__ scores, int n, int lds, int k,
-                                                     uint32_t* __restrict__ idx, int ldi, int pow2) {
+                                                     uint32_t* __restrict__ idx, int ldi, int pow2, int sorted) {
   extern __shared__ __align__(1024) unsigned char tk_smem[];
   uint64_t* keys = reinterpret_cast<uint64_t*>(tk_smem);  // [pow2]
   float* row = reinterpret_cast<float*>(keys + pow2);     // [n]
@@ -234,11 +234,20 @@ __global__ void __launch_bounds__(TK_NT) topk_kernel(const float* __restrict__ s
   const int t = blockIdx.x, tid = threadIdx.x, w = tid >> 5, l = tid & 31;
   const float* grow = scores + (int64_t)t * lds;
   float mn = INFINITY, mx = -INFINITY;
-  for (int i = tid; i < n; i += TK_NT) {
-    const float v = grow[i];
-    row[i] = v;
-    mn = fminf(mn, v);
-    mx = fmaxf(mx, v);
+  if ((n & 3) == 0 && (lds & 3) == 0 && (reinterpret_cast<uintptr_t>(scores) & 15) == 0) {  // 16-byte loads
+    for (int i = tid * 4; i < n; i += TK_NT * 4) {
+      const float4 v = *reinterpret_cast<const float4*>(grow + i);
+      *reinterpret_cast<float4*>(row + i) = v;
+      mn = fminf(mn, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
+      mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    }
+  } else {
+    for (int i = tid; i < n; i += TK_NT) {
+      const float v = grow[i];
+      row[i] = v;
+      mn = fminf(mn, v);
+      mx = fmaxf(mx, v);
+    }
   }
   for (int i = tid; i < TK_NB; i += TK_NT) hist[i] = 0;
   for (int i = tid; i < pow2; i += TK_NT) keys[i] = ~0ull;
@@ -336,6 +345,38 @@ __global__ void __launch_bounds__(TK_NT) topk_kernel(const float* __restrict__ s
     }
   }
   __syncthreads();
+  if (!sorted) {
+    // the selected set in ascending index order: a bitmap over the row (in the
+    // histogram's words, free now) and a block scan of its popcounts
+    __shared__ int scan_tmp[33];
+    const int nwd = (n + 31) / 32;  // <= TK_NB (n <= 131072)
+    for (int i = tid; i < nwd; i += TK_NT) hist[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < k; i += TK_NT) {
+      const uint32_t id = (uint32_t)(keys[i] & 0xffffffffu);
+      atomicOr(&hist[id >> 5], 1u << (id & 31));
+    }
+    __syncthreads();
+    const int WPT = (nwd + TK_NT - 1) / TK_NT;  // words per thread, contiguous
+    int c = 0;
+    for (int q = 0; q < WPT; ++q) {
+      const int wi = tid * WPT + q;
+      if (wi < nwd) c += __popc(hist[wi]);
+    }
+    int tot;
+    int pos = block_excl_scan<TK_NT>(c, scan_tmp, &tot);
+    for (int q = 0; q < WPT; ++q) {
+      const int wi = tid * WPT + q;
+      if (wi >= nwd) break;
+      uint32_t bits = hist[wi];
+      while (bits) {
+        const int b = __ffs(bits) - 1;
+        bits &= bits - 1;
+        idx[(int64_t)t * ldi + pos++] = (uint32_t)(wi * 32 + b);
+      }
+    }
+    return;
+  }
   // bitonic sort ascending of keys[0, pow2)
   if (pow2 == 2 * TK_NT) {
     // two keys per thread (elements 2*tid, 2*tid+1; warp w holds 64w ..
@@ -422,7 +463,14 @@ __global__ void __launch_bounds__(DV_WARPS * 32)
                      float* __restrict__ a, int* err) {
   extern __shared__ __align__(1024) float xs[];
   const int t = blockIdx.y, w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < ldw; i += blockDim.x) xs[i] = i < hid ? x[(int64_t)t * ldx + i] : 0.0f;
+  if ((hid & 3) == 0 && (ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {  // 16-byte loads
+#pragma unroll 4
+    for (int i = threadIdx.x * 4; i < ldw; i += blockDim.x * 4)
+      *reinterpret_cast<float4*>(xs + i) =
+          i < hid ? *reinterpret_cast<const float4*>(x + (int64_t)t * ldx + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
+    for (int i = threadIdx.x; i < ldw; i += blockDim.x) xs[i] = i < hid ? x[(int64_t)t * ldx + i] : 0.0f;
+  }
   __syncthreads();
   for (int s = blockIdx.x * DV_WARPS + w; s < k; s += gridDim.x * DV_WARPS) {
     uint32_t row = sel[(int64_t)t * k + s];
@@ -433,7 +481,7 @@ __global__ void __launch_bounds__(DV_WARPS * 32)
     const uint4* g4 = reinterpret_cast<const uint4*>(gate + (int64_t)row * ldw);
     const uint4* u4 = reinterpret_cast<const uint4*>(up + (int64_t)row * ldw);
     float g = 0.f, u = 0.f;
-#pragma unroll 4
+#pragma unroll 8
     for (int c = l; c < ldw / 8; c += 32) {
       const uint4 gr = g4[c], ur = u4[c];
       const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gr);
@@ -455,77 +503,122 @@ __global__ void __launch_bounds__(DV_WARPS * 32)
   }
 }
 
-constexpr int DV_DN_T = 256;  // output columns per block
-constexpr int DV_PF = 16;     // selected rows in flight per thread
+constexpr int DV_DN_T = 256;  // threads per block, 8 output columns each (16-byte row loads)
+constexpr int DV_DN_C = 8 * DV_DN_T;
+constexpr int DV_PF = 8;      // selected rows in flight per thread
 
 __global__ void __launch_bounds__(DV_DN_T)
     dv_down_kernel(const __nv_bfloat16* __restrict__ downT, int hid, int ldw, const uint32_t* __restrict__ sel, int k,
                    int inter, const float* __restrict__ a, int splits, float* __restrict__ part) {
   const int t = blockIdx.z, sp = blockIdx.y;
-  const int j = blockIdx.x * DV_DN_T + threadIdx.x;
+  const int j0 = (blockIdx.x * DV_DN_T + threadIdx.x) * 8;
   const int per = (k + splits - 1) / splits;
   const int s0 = sp * per, s1 = min(k, s0 + per);
-  float acc = 0.0f;
-  if (j < hid) {
-    for (int s = s0; s < s1; s += DV_PF) {
-      float wv[DV_PF], av[DV_PF];
+  if (j0 >= hid) return;
+  float acc[8];
 #pragma unroll
-      for (int u = 0; u < DV_PF; ++u) {
-        if (s + u < s1) {
-          uint32_t row = sel[(int64_t)t * k + s + u];
-          if (row >= (uint32_t)inter) row = 0;
-          wv[u] = to_f(downT[(int64_t)row * ldw + j]);
-          av[u] = a[(int64_t)t * k + s + u];
-        }
+  for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
+  for (int s = s0; s < s1; s += DV_PF) {
+    uint4 wv[DV_PF];
+    float av[DV_PF];
+#pragma unroll
+    for (int u = 0; u < DV_PF; ++u) {
+      av[u] = 0.0f;
+      if (s + u < s1) {
+        uint32_t row = sel[(int64_t)t * k + s + u];
+        if (row >= (uint32_t)inter) row = 0;
+        wv[u] = *reinterpret_cast<const uint4*>(downT + (int64_t)row * ldw + j0);
+        av[u] = a[(int64_t)t * k + s + u];
       }
-#pragma unroll
-      for (int u = 0; u < DV_PF; ++u)
-        if (s + u < s1 && av[u] != 0.0f) acc = __fadd_rn(acc, __fmul_rn(wv[u], av[u]));
     }
-    part[((int64_t)t * splits + sp) * ldw + j] = acc;
+#pragma unroll
+    for (int u = 0; u < DV_PF; ++u) {
+      if (s + u < s1 && av[u] != 0.0f) {
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&wv[u]);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] = __fadd_rn(acc[c], __fmul_rn(to_f(e[c]), av[u]));
+      }
+    }
   }
+  float4* dst = reinterpret_cast<float4*>(part + ((int64_t)t * splits + sp) * ldw + j0);
+  dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
 __global__ void dv_down_finish_kernel(const float* __restrict__ part, int splits, int hid, int ldw,
-                                      const float* __restrict__ bias, float* __restrict__ out) {
+                                      const float* __restrict__ bias, float* __restrict__ out, int accumulate) {
+  constexpr int FL = 32;  // partial sums in flight per thread, added in split order
   const int t = blockIdx.y;
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < hid; j += gridDim.x * blockDim.x) {
     float s = 0.0f;
-    for (int q0 = 0; q0 < splits; q0 += 8) {  // 8 loads in flight, added in split order
-      float v[8];
+    for (int q0 = 0; q0 < splits; q0 += FL) {
+      float v[FL];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = q0 + u < splits ? part[((int64_t)t * splits + q0 + u) * ldw + j] : 0.0f;
+      for (int u = 0; u < FL; ++u) v[u] = q0 + u < splits ? part[((int64_t)t * splits + q0 + u) * ldw + j] : 0.0f;
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+      for (int u = 0; u < FL; ++u)
         if (q0 + u < splits) s = __fadd_rn(s, v[u]);
     }
-    out[(int64_t)t * hid + j] = bias ? __fadd_rn(s, bias[j]) : s;
+    const float v = bias ? __fadd_rn(s, bias[j]) : s;
+    float* o = out + (int64_t)t * hid + j;
+    *o = accumulate ? __fadd_rn(*o, v) : v;  // accumulate: the residual add h += mlp(x)
   }
 }
 
 // RMSNorm (klearu-llm model/rms_norm.rs): y = x * (1 / sqrt(mean(x^2) + eps))
-// * w (or * (1 + w)), one block per token.  The sum of squares is a block
-// reduction (the reference sums sequentially: equal within f32 rounding).
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, int ld, int n, const float* w, float eps,
-                                                      int one_plus, float* y) {
-  __shared__ float red[8];
+// * w (or * (1 + w)), one block per token.  Each thread holds up to RN_V
+// 4-element vectors of the row in registers, so the row is read once; the
+// sum of squares is a block reduction (the reference sums sequentially:
+// equal within f32 rounding).
+constexpr int RN_NT = 1024, RN_V = 4;
+__global__ void __launch_bounds__(RN_NT) rmsnorm_kernel(const float* x, int ld, int n, const float* w, float eps,
+                                                        int one_plus, float* y) {
+  __shared__ float red[RN_NT / 32];
   const int t = blockIdx.x;
   const float* xr = x + (int64_t)t * ld;
+  const bool vec = (n & 3) == 0 && (ld & 3) == 0 && n <= RN_NT * 4 * RN_V &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) &
+                    15) == 0;
+  float4 v[RN_V];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += 256) ss = fmaf(xr[i], xr[i], ss);
+  if (vec) {
+#pragma unroll
+    for (int q = 0; q < RN_V; ++q) {
+      const int i = (threadIdx.x + q * RN_NT) * 4;
+      v[q] = i < n ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int q = 0; q < RN_V; ++q) ss = fmaf(v[q].x, v[q].x, fmaf(v[q].y, v[q].y, fmaf(v[q].z, v[q].z, fmaf(v[q].w, v[q].w, ss))));
+  } else {
+    for (int i = threadIdx.x; i < n; i += RN_NT) ss = fmaf(xr[i], xr[i], ss);
+  }
   ss = warp_sum_f(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float v = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
-    v = warp_sum_f(v);
-    if (threadIdx.x == 0) red[0] = v;
+    float r = red[threadIdx.x];
+    r = warp_sum_f(r);
+    if (threadIdx.x == 0) red[0] = r;
   }
   __syncthreads();
   const float inv = 1.0f / sqrtf(red[0] / (float)n + eps);
-  for (int i = threadIdx.x; i < n; i += 256) {
-    const float wi = one_plus ? 1.0f + w[i] : w[i];
-    y[(int64_t)t * ld + i] = xr[i] * inv * wi;
+  float* yr = y + (int64_t)t * ld;
+  if (vec) {
+#pragma unroll
+    for (int q = 0; q < RN_V; ++q) {
+      const int i = (threadIdx.x + q * RN_NT) * 4;
+      if (i < n) {
+        float4 wv = *reinterpret_cast<const float4*>(w + i);
+        if (one_plus) wv = make_float4(1.0f + wv.x, 1.0f + wv.y, 1.0f + wv.z, 1.0f + wv.w);
+        *reinterpret_cast<float4*>(yr + i) =
+            make_float4(v[q].x * inv * wv.x, v[q].y * inv * wv.y, v[q].z * inv * wv.z, v[q].w * inv * wv.w);
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += RN_NT) {
+      const float wi = one_plus ? 1.0f + w[i] : w[i];
+      yr[i] = xr[i] * inv * wi;
+    }
   }
 }
 __global__ void residual_add_kernel(float* h, const float* d, int64_t n) {
@@ -608,7 +701,8 @@ void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16
   count_launch();
 }
 
-void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* idx, int ldi, cudaStream_t st) {
+void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* idx, int ldi, cudaStream_t st,
+                 bool sorted) {
   int pow2 = 2 * TK_NT;  // at least the register-sorted size
   while (pow2 < k) pow2 <<= 1;
   const size_t sm = (size_t)pow2 * 8 + (size_t)n * 4;
@@ -616,7 +710,7 @@ void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* id
   attr([&] {  // the kernel's static shared memory (~34 KB) counts against the 227 KB per block
     cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 190 * 1024);
   });
-  topk_kernel<<<T, TK_NT, sm, st>>>(scores, n, lds, k, idx, ldi, pow2);
+  topk_kernel<<<T, TK_NT, sm, st>>>(scores, n, lds, k, idx, ldi, pow2, sorted ? 1 : 0);
   count_launch();
 }
 
@@ -676,22 +770,24 @@ void launch_sparse_mlp_dense(const __nv_bfloat16* gate, const __nv_bfloat16* up,
 
 void launch_sparse_mlp(const __nv_bfloat16* gate, const __nv_bfloat16* up, const __nv_bfloat16* downT, int hid,
                        int ldw, int inter, const float* bias, const float* x, int T, const uint32_t* sel, int k,
-                       float* a, float* part, int splits, float* out, int* err, cudaStream_t st) {
+                       float* a, float* part, int splits, float* out, bool accumulate, int* err,
+                       cudaStream_t st) {
   const int gblocks = std::max(1, std::min((int)ceil_div(k, DV_WARPS), (int)ceil_div(sm_count() * 4, T)));
   dv_gateup_kernel<<<dim3(gblocks, T), DV_WARPS * 32, (size_t)ldw * 4, st>>>(gate, up, hid, ldw, x, hid, sel, k,
                                                                              inter, a, err);
   count_launch();
-  dv_down_kernel<<<dim3((unsigned)ceil_div(hid, DV_DN_T), splits, T), DV_DN_T, 0, st>>>(downT, hid, ldw, sel, k,
+  dv_down_kernel<<<dim3((unsigned)ceil_div(hid, DV_DN_C), splits, T), DV_DN_T, 0, st>>>(downT, hid, ldw, sel, k,
                                                                                        inter, a, splits, part);
   count_launch();
-  dv_down_finish_kernel<<<dim3((unsigned)ceil_div(hid, 256), T), 256, 0, st>>>(part, splits, hid, ldw, bias, out);
+  dv_down_finish_kernel<<<dim3((unsigned)ceil_div(hid, 256), T), 256, 0, st>>>(part, splits, hid, ldw, bias, out,
+                                                                            accumulate ? 1 : 0);
   count_launch();
 }
 
 void launch_rmsnorm(const float* x, int T, int n, const float* w, float eps, int one_plus, float* y,
                     cudaStream_t st) {
   if (T <= 0) return;
-  rmsnorm_kernel<<<T, 256, 0, st>>>(x, n, n, w, eps, one_plus, y);
+  rmsnorm_kernel<<<T, RN_NT, 0, st>>>(x, n, n, w, eps, one_plus, y);
   count_launch();
 }
 void launch_residual_add(float* h, const float* d, int64_t n, cudaStream_t st) {

@@ -352,13 +352,17 @@ void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16
                       __nv_bfloat16* xs_next, int ld_next, int* err, cudaStream_t st);
 // idx[t][0, k) = the k largest of scores[t][0, n) in (score desc, index asc)
 // order; scores non-negative; k <= n.
-void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* idx, int ldi, cudaStream_t st);
+// sorted: (score descending, index ascending); else the selected set in
+// ascending index order (no sort)
+void launch_topk(const float* scores, int T, int n, int lds, int k, uint32_t* idx, int ldi, cudaStream_t st,
+                 bool sorted = true);
 // out[T][hid] = SwiGLU MLP over the selected neurons sel[T][k]; gate/up
 // [inter][ldw], downT [inter][ldw] bf16; a scratch [T][k], part scratch
 // [T][splits][ldw] f32.
 void launch_sparse_mlp(const __nv_bfloat16* gate, const __nv_bfloat16* up, const __nv_bfloat16* downT, int hid,
                        int ldw, int inter, const float* bias, const float* x, int T, const uint32_t* sel, int k,
-                       float* a, float* part, int splits, float* out, int* err, cudaStream_t st);
+                       float* a, float* part, int splits, float* out, bool accumulate, int* err,
+                       cudaStream_t st);
 
 // The same MLP as launch_sparse_mlp through dense tcgen05 GEMMs with the
 // selection as a mask (T <= TC_LINEAR_MAX_T): gate / up [inter][ldg], down
