@@ -1147,6 +1147,7 @@ struct Layer {
   DBuf bkt, ids, cnt, pre, post, lg, h, dx_in, dxpart, lgd, tmask, gfeat;
   DBuf dmark, dtouched, dslot, dlg;  // dense-collision update scratch (row-major layers)
   int64_t dldb = 0;  // sample pitch of the dense update's gradient matrix (0: segmented path)
+  bool premarked = false;  // this step's rows were marked before the forward, which filled the matrix
   DBuf hist, cur, touched, ctr, ent_s, ent_v, fslot, flong;
   size_t ent_cap = 0;
   DBuf stats;  // u64 [3]: active_sum, touched_rows, input_nnz
@@ -1429,7 +1430,14 @@ struct kl_net_s {
     ra.err = ctx->err.as<int>();
     ra.id_base = L.id_base;
     ra.only_empty = nullptr;
+    ra.lgd_dense = nullptr;
+    ra.slot_of = nullptr;
+    ra.ldb = 0;
     return ra;
+  }
+  DenseScratch dense_scratch(Layer& L) {
+    return DenseScratch{L.dmark.as<uint32_t>(), L.dtouched.as<uint32_t>(), L.dslot.as<uint32_t>(),
+                        L.ctr.as<uint32_t>(), L.dlg.as<float>(), L.dldb};
   }
   void forward_layer(int l, const kl_batch& b, int s0, int nq, bool train, int hrow0 = 0,
                      const std::function<void(Layer&)>& after_probe = nullptr) {
@@ -1507,6 +1515,20 @@ struct kl_net_s {
         RmArgs ra = rm_args(l, b, s0, hout);
         const bool softmax = L.cfg.activation == KL_ACT_SOFTMAX;
         const bool fused = last && train && !softmax;
+        // one-GPU fused step with the dense update: mark the rows now so that
+        // the forward stores its gradients straight into the update's matrix
+        // (a sharded step's fallback pass can still change the active sets)
+        L.premarked = false;
+        if (fused && L.dldb > 0 && nranks == 1) {
+          ck(cudaMemsetAsync(L.ctr.p, 0, 16, st), "memset");
+          const DenseScratch D = dense_scratch(L);
+          launch_rm_mark(A, nq, D, st);
+          ck_launch("rm mark");
+          ra.lgd_dense = D.LGd;
+          ra.slot_of = D.slot_of;
+          ra.ldb = D.ldb;
+          L.premarked = true;
+        }
         launch_rm_forward(ra, nq, fused ? RM_FUSED : RM_FWD, st);
         ck_launch("rm forward");
         if (softmax) {
@@ -1612,7 +1634,7 @@ struct kl_net_s {
       Phase ph(this, l, KL_PHASE_UPDATE);
       Layer& L = *layers[l];
       unsigned long long* stat = L.stats.as<unsigned long long>() + 1;
-      ck(cudaMemsetAsync(L.ctr.p, 0, 16, st), "memset");
+      if (!L.premarked) ck(cudaMemsetAsync(L.ctr.p, 0, 16, st), "memset");
       SegScratch S{L.hist.as<uint32_t>(), L.cur.as<uint32_t>(), L.touched.as<uint32_t>(), L.ctr.as<uint32_t>(),
                    L.ent_s.as<uint32_t>(), L.ent_v.as<float>(), L.fslot.as<uint32_t>(), L.flong.as<uint32_t>()};
       if (L.fm) {
@@ -1623,11 +1645,11 @@ struct kl_net_s {
       } else {
         const Layer& P = *layers[l - 1];
         if (L.dldb > 0) {
-          DenseScratch D{L.dmark.as<uint32_t>(), L.dtouched.as<uint32_t>(), L.dslot.as<uint32_t>(),
-                         L.ctr.as<uint32_t>(), L.dlg.as<float>(), L.dldb};
+          const DenseScratch D = dense_scratch(L);
           launch_rm_update_dense(L.W.p, wdtype, L.ldw, L.d, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),
                                  L.mb.as<float>(), L.vb.as<float>(), P.h.as<float>(), P.ldN, L.act(), nq, L.N, D,
-                                 o, stat, st);
+                                 o, stat, st, L.premarked);
+          L.premarked = false;
           launch_count_touched(L.ctr.as<uint32_t>(), stat, st);
         } else {
           launch_rm_update(L.W.p, wdtype, L.ldw, L.d, L.b.as<float>(), L.m.as<float>(), L.v.as<float>(),

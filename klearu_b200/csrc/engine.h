@@ -225,6 +225,11 @@ struct RmArgs {
   uint32_t id_base;   // global id of local row 0 (neuron-sharded output layer; labels are global)
   const int32_t* only_empty;  // nullable: only examples s with only_empty[s] == 0 (the pass after a
                               // global empty-selection fallback); null: every example
+  // FUSED, nullable: also store each local gradient into the dense update's
+  // slot-major matrix, lgd_dense[slot_of[id] * ldb + s] (rows marked before the forward)
+  float* lgd_dense;
+  const uint32_t* slot_of;
+  int64_t ldb;
 };
 void launch_rm_forward(const RmArgs& a, int nq, int mode, cudaStream_t st);
 // dX[s][k] = sum over chunks of dxpart (chunk order).
@@ -274,10 +279,15 @@ struct DenseScratch {
 bool rm_dense_fits(int64_t rows, int nb, int64_t max_bytes);
 // stat += ctr[0] (touched-row counter of the roofline statistics)
 void launch_count_touched(const uint32_t* ctr, unsigned long long* stat, cudaStream_t st);
+// premarked: launch_rm_mark ran before the forward, which stored the
+// gradients into D.LGd itself (mark and scatter are skipped here).
 void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
                             float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
                             DenseScratch D, const OptStep* o, unsigned long long* stat_touched,
-                            cudaStream_t st);
+                            cudaStream_t st, bool premarked = false);
+// The dense update's row marking alone (touched list, slot_of), for a
+// forward that stores its gradients straight into the matrix.
+void launch_rm_mark(ActiveSet A, int nq, DenseScratch D, cudaStream_t st);
 // Feature-major gradient + optimizer over ALL features of the touched neurons
 // (Adam decays every element of an active row, adam.rs:57-68).  G: gradient
 // rows of the touched features, [min(d, nnz)][ldl] f32 scratch.  around_adam

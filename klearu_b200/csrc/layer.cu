@@ -306,6 +306,7 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
         }
         lgv = __fmul_rn(g, act_deriv(pre, post, a.act));
         a.A.lg[arow] = lgv;
+        if (a.lgd_dense) a.lgd_dense[(int64_t)a.slot_of[myid] * a.ldb + s] = lgv;
       }
     }
   } else if (has) {
@@ -1526,6 +1527,12 @@ void launch_count_touched(const uint32_t* ctr, unsigned long long* stat, cudaStr
   count_launch();
 }
 
+void launch_rm_mark(ActiveSet A, int nq, DenseScratch D, cudaStream_t st) {
+  if (nq <= 0) return;
+  rm_mark_kernel<<<dim3((unsigned)ceil_div(A.stride, 256), nq), 256, 0, st>>>(A, D.mark, D.touched, D.slot_of, D.ctr);
+  count_launch();
+}
+
 bool rm_dense_fits(int64_t rows, int nb, int64_t max_bytes) {
   if (max_bytes < 0) return false;
   if (max_bytes == 0) max_bytes = (int64_t)2 << 30;
@@ -1535,14 +1542,15 @@ bool rm_dense_fits(int64_t rows, int nb, int64_t max_bytes) {
 void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bias, float* m, float* v,
                             float* mb, float* vb, const float* X, int ldx, ActiveSet A, int nq, int N,
                             DenseScratch D, const OptStep* o, unsigned long long* stat_touched,
-                            cudaStream_t st) {
+                            cudaStream_t st, bool premarked) {
   (void)stat_touched;
   if (nq <= 0) return;
-  rm_mark_kernel<<<dim3((unsigned)ceil_div(A.stride, 256), nq), 256, 0, st>>>(A, D.mark, D.touched, D.slot_of,
-                                                                           D.ctr);
-  count_launch();
-  rm_dense_scatter_kernel<<<dim3((unsigned)ceil_div(A.stride, 256 * RM_PK), nq), 256, 0, st>>>(A, D.slot_of, D.LGd, D.ldb);
-  count_launch();
+  if (!premarked) {
+    launch_rm_mark(A, nq, D, st);
+    rm_dense_scatter_kernel<<<dim3((unsigned)ceil_div(A.stride, 256 * RM_PK), nq), 256, 0, st>>>(A, D.slot_of, D.LGd,
+                                                                                                 D.ldb);
+    count_launch();
+  }
   const int64_t maxn = std::min<int64_t>((int64_t)N, (int64_t)nq * A.stride);
   const int ncb = (int)ceil_div(d, RDU_COLS);
   // Long sample loops (large batches) meet few touched rows per shard: blocks
