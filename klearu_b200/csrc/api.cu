@@ -1515,11 +1515,11 @@ struct kl_net_s {
         RmArgs ra = rm_args(l, b, s0, hout);
         const bool softmax = L.cfg.activation == KL_ACT_SOFTMAX;
         const bool fused = last && train && !softmax;
-        // one-GPU fused step with the dense update: mark the rows now so that
-        // the forward stores its gradients straight into the update's matrix
-        // (a sharded step's fallback pass can still change the active sets)
+        // fused step with the dense update: mark the rows now so that the
+        // forward stores its gradients straight into the update's matrix (a
+        // sharded step marks its fallback examples' rows before their pass)
         L.premarked = false;
-        if (fused && L.dldb > 0 && nranks == 1) {
+        if (fused && L.dldb > 0) {
           ck(cudaMemsetAsync(L.ctr.p, 0, 16, st), "memset");
           const DenseScratch D = dense_scratch(L);
           launch_rm_mark(A, nq, D, st);
@@ -1775,6 +1775,14 @@ struct kl_net_s {
       ck_launch("shard fallback");
       RmArgs ra = rm_args(1, gb, 0, nullptr);
       ra.only_empty = gcnt.as<int32_t>();
+      if (train && O.premarked) {
+        const DenseScratch D = dense_scratch(O);
+        launch_rm_mark(O.act(), PB, D, st, gcnt.as<int32_t>());
+        ck_launch("rm mark (fallback examples)");
+        ra.lgd_dense = D.LGd;
+        ra.slot_of = D.slot_of;
+        ra.ldb = D.ldb;
+      }
       launch_rm_forward(ra, PB, train ? RM_FUSED : RM_FWD, st);
       ck_launch("rm forward (fallback examples)");
     }

@@ -287,7 +287,8 @@ void launch_rm_update_dense(const void* W, int wdtype, int ldw, int d, float* bi
                             cudaStream_t st, bool premarked = false);
 // The dense update's row marking alone (touched list, slot_of), for a
 // forward that stores its gradients straight into the matrix.
-void launch_rm_mark(ActiveSet A, int nq, DenseScratch D, cudaStream_t st);
+// only_empty (nullable): only examples s with only_empty[s] == 0.
+void launch_rm_mark(ActiveSet A, int nq, DenseScratch D, cudaStream_t st, const int32_t* only_empty = nullptr);
 // Feature-major gradient + optimizer over ALL features of the touched neurons
 // (Adam decays every element of an active row, adam.rs:57-68).  G: gradient
 // rows of the touched features, [min(d, nnz)][ldl] f32 scratch.  around_adam

@@ -461,9 +461,17 @@ __global__ void loss_kernel(const int32_t* lab_ptr, const float* labprob, int nq
     ls[s] = le > lb ? __fdiv_rn(loss, (float)(le - lb)) : 0.0f;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0) {  // in example order; groups of 8 loads ahead of their adds
     float acc = *accum;
-    for (int s = 0; s < nq; ++s) acc = __fadd_rn(acc, ls[s]);
+    int s = 0;
+    for (; s + 8 <= nq; s += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = ls[s + u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+    }
+    for (; s < nq; ++s) acc = __fadd_rn(acc, ls[s]);
     *accum = acc;
   }
 }
@@ -723,8 +731,9 @@ constexpr int RM_PK = 8;
 // One mark word per row: a few hundred samples of a large batch meet the same
 // rows at once, and words shared by 32 rows would serialise their atomics.
 __global__ void rm_mark_kernel(ActiveSet A, uint32_t* mark, uint32_t* touched, uint32_t* slot_of,
-                               uint32_t* ctr) {
+                               uint32_t* ctr, const int32_t* only_empty) {
   const int s = blockIdx.y;
+  if (only_empty && only_empty[s] != 0) return;
   const int a = blockIdx.x * blockDim.x + threadIdx.x;
   if (a >= A.cnt[s]) return;
   const uint32_t id = A.ids[(int64_t)s * A.stride + a];
@@ -1230,24 +1239,24 @@ __global__ void fm_hist_clear_kernel(SegScratch S) {
   }
 }
 
-// Bias gradient over a long batch: block b owns neurons [32b, 32b + 32).
-// Its 4 warps stage the samples' 32-column row segments through shared
-// memory in chunks of 128 rows, double-buffered with cp.async; warp 0 then
-// adds lane j's column in ascending sample order (bit-exact).
-constexpr int FB_CH = 128;
-__global__ void __launch_bounds__(128) fm_bias_stream_kernel(float* bias, float* mb, float* vb, const float* lgd,
-                                                            int ldl, int nq, int N, const uint32_t* tmask,
-                                                            const OptStep* op, unsigned long long* stat_touched) {
-  __shared__ __align__(16) float brows[2][FB_CH][32];
+// Bias gradient over a long batch: block b owns neurons [8b, 8b + 8).  Its 8
+// warps stage the samples' 8-column row segments through shared memory in
+// chunks of FB_CH rows, double-buffered with cp.async (many blocks with large
+// chunks keep enough bytes in flight); lane j of warp 0 then adds column j in
+// ascending sample order (bit-exact).
+constexpr int FB_CB = 8, FB_CH = 1024, FB_NT = 256;
+constexpr size_t FB_SMEM = (size_t)2 * FB_CH * FB_CB * 4;
+__global__ void __launch_bounds__(FB_NT) fm_bias_stream_kernel(float* bias, float* mb, float* vb, const float* lgd,
+                                                              int ldl, int nq, int N, const uint32_t* tmask,
+                                                              const OptStep* op, unsigned long long* stat_touched) {
+  extern __shared__ __align__(16) float brows[];  // [2][FB_CH][FB_CB]
   const OptStep o = *op;
-  const int j0 = blockIdx.x * 32;
-  const int ncol = min(32, ldl - j0);  // columns of this block inside the row pitch (a multiple of 8)
-  const int v4 = ncol / 4;
+  const int j0 = blockIdx.x * FB_CB;  // ldl is a multiple of 8: the block's 8 columns lie inside the row pitch
   auto stage = [&](int s0, int b) {
     const int cn = min(FB_CH, nq - s0);
-    for (int q = threadIdx.x; q < cn * v4; q += 128) {
-      const int r = q / v4, c4 = (q - r * v4) * 4;
-      cp_async16(&brows[b][r][c4], lgd + (int64_t)(s0 + r) * ldl + j0 + c4);
+    for (int q = threadIdx.x; q < cn * 2; q += FB_NT) {
+      const int r = q >> 1, c4 = (q & 1) * 4;
+      cp_async16(&brows[((size_t)b * FB_CH + r) * FB_CB + c4], lgd + (int64_t)(s0 + r) * ldl + j0 + c4);
     }
     cp_async_commit();
   };
@@ -1258,14 +1267,23 @@ __global__ void __launch_bounds__(128) fm_bias_stream_kernel(float* bias, float*
     else cp_async_commit();
     cp_async_wait_group<1>();
     __syncthreads();
-    if (threadIdx.x < 32) {
+    if (threadIdx.x < FB_CB) {
       const int cn = min(FB_CH, nq - s0);
-      for (int r = 0; r < cn; ++r) gb = __fadd_rn(gb, brows[b][r][threadIdx.x]);
+      const float* col = brows + (size_t)b * FB_CH * FB_CB + threadIdx.x;
+      int r = 0;
+      for (; r + 8 <= cn; r += 8) {  // the group's loads first: only the sum is a chain
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = col[(size_t)(r + u) * FB_CB];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) gb = __fadd_rn(gb, v[u]);
+      }
+      for (; r < cn; ++r) gb = __fadd_rn(gb, col[(size_t)r * FB_CB]);
     }
     __syncthreads();
   }
   const int j = j0 + (int)threadIdx.x;
-  if (threadIdx.x < 32 && j < N && ((tmask[j >> 5] >> (j & 31)) & 1u)) {
+  if (threadIdx.x < FB_CB && j < N && ((tmask[j >> 5] >> (j & 31)) & 1u)) {
     if (stat_touched) atomicAdd(stat_touched, 1ull);
     bias_update(bias, mb, vb, (uint32_t)j, gb, o);
   }
@@ -1527,9 +1545,10 @@ void launch_count_touched(const uint32_t* ctr, unsigned long long* stat, cudaStr
   count_launch();
 }
 
-void launch_rm_mark(ActiveSet A, int nq, DenseScratch D, cudaStream_t st) {
+void launch_rm_mark(ActiveSet A, int nq, DenseScratch D, cudaStream_t st, const int32_t* only_empty) {
   if (nq <= 0) return;
-  rm_mark_kernel<<<dim3((unsigned)ceil_div(A.stride, 256), nq), 256, 0, st>>>(A, D.mark, D.touched, D.slot_of, D.ctr);
+  rm_mark_kernel<<<dim3((unsigned)ceil_div(A.stride, 256), nq), 256, 0, st>>>(A, D.mark, D.touched, D.slot_of, D.ctr,
+                                                                           only_empty);
   count_launch();
 }
 
@@ -1675,7 +1694,12 @@ void launch_fm_update(const void* W, int wdtype, int ldw, int d, int f0, int nf,
   }
   if (nq >= 512) {
     // long batches: 32 neurons per block, gradient rows streamed through shared memory
-    fm_bias_stream_kernel<<<(unsigned)ceil_div(N, 32), 128, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask, o,
+    static OncePerDevice fbattr;
+    fbattr([&] {
+      cudaFuncSetAttribute(fm_bias_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FB_SMEM);
+    });
+    fm_bias_stream_kernel<<<(unsigned)ceil_div(N, FB_CB), FB_NT, FB_SMEM, st>>>(bias, mb, vb, lgd, ldl, nq, N,
+                                                                               touched_mask, o,
                                                                       stat_touched);
   } else {
     fm_bias_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(bias, mb, vb, lgd, ldl, nq, N, touched_mask, o,

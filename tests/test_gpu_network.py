@@ -339,13 +339,15 @@ def test_c0_readme_mlp_shape(gpu_ctx, dtype):
 
 
 def test_large_batch_dense_update(gpu_ctx):
-    # a batch of >= 512 examples takes the dense update's 2-warp blocks (the
-    # shape a shard meets over an 8-rank global batch); first Adam moments
-    # equal the oracle's bit for bit (identity output: exact local gradients)
+    # a batch of >= 512 examples takes the dense update's 2-warp blocks and the
+    # streamed hidden bias gradient (the shape a shard meets over an 8-rank
+    # global batch; 1100 examples span two of its 1024-row chunks and a ragged
+    # tail); first Adam moments equal the oracle's bit for bit (identity
+    # output: exact local gradients)
     cfg = xc_small()
     cfg.network.layers[1].activation = ActivationType.Identity
-    g, o = pair(cfg, "f32", max_batch=640)
-    hb = xc_batches(1, 640, seed=31)[0]
+    g, o = pair(cfg, "f32", max_batch=1100)
+    hb = xc_batches(1, 1100, seed=31)[0]
     g.train_step(_examples(hb), 1e-3, mode="batched")
     o.train_step(hb, 1e-3, mode="batched")
     gl, ol = g.get_layer(1), o.get_layer(1)
