@@ -1495,6 +1495,17 @@ struct kl_net_s {
       launch_probe(pa, st);
       ck_launch("probe");
       if (after_probe) after_probe(L);
+      // fused train step with the dense update: mark the touched rows now (part
+      // of building the active sets) so that the forward stores its gradients
+      // straight into the update's matrix; a sharded step marks its fallback
+      // examples' rows before their pass
+      L.premarked = false;
+      if (!L.fm && last && train && L.cfg.activation != KL_ACT_SOFTMAX && L.dldb > 0) {
+        ck(cudaMemsetAsync(L.ctr.p, 0, 16, st), "memset");
+        launch_rm_mark(L.act(), nq, dense_scratch(L), st);
+        ck_launch("rm mark");
+        L.premarked = true;
+      }
       ph_hash.~Phase();
       new (&ph_hash) Phase(this, l, KL_PHASE_FORWARD);
       float* hout = nullptr;
@@ -1515,19 +1526,11 @@ struct kl_net_s {
         RmArgs ra = rm_args(l, b, s0, hout);
         const bool softmax = L.cfg.activation == KL_ACT_SOFTMAX;
         const bool fused = last && train && !softmax;
-        // fused step with the dense update: mark the rows now so that the
-        // forward stores its gradients straight into the update's matrix (a
-        // sharded step marks its fallback examples' rows before their pass)
-        L.premarked = false;
-        if (fused && L.dldb > 0) {
-          ck(cudaMemsetAsync(L.ctr.p, 0, 16, st), "memset");
+        if (fused && L.premarked) {
           const DenseScratch D = dense_scratch(L);
-          launch_rm_mark(A, nq, D, st);
-          ck_launch("rm mark");
           ra.lgd_dense = D.LGd;
           ra.slot_of = D.slot_of;
           ra.ldb = D.ldb;
-          L.premarked = true;
         }
         launch_rm_forward(ra, nq, fused ? RM_FUSED : RM_FWD, st);
         ck_launch("rm forward");
