@@ -42,6 +42,25 @@ def _peak_gbs() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
+def _stack_kernels(stack, hs, reps: int, layers: int) -> dict:
+    """Device time of each kernel inside the FFN stack's replayed graph, µs per
+    layer (CUPTI activity records through torch.profiler)."""
+    import collections
+
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            stack.decode(hs, 0.1)
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(float)
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            name = e.name.replace("(anonymous namespace)::", "").split("(")[0]
+            agg[name] += e.device_time_total
+    return {k: round(v / reps / layers, 2) for k, v in sorted(agg.items(), key=lambda kv: -kv[1])}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", default="1,16,64")
@@ -49,6 +68,8 @@ def main() -> None:
     ap.add_argument("--distinct", type=int, default=2)
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernels", action="store_true",
+                    help="also print each kernel's device time inside the FFN stack (CUPTI through torch.profiler)")
     args = ap.parse_args()
     ctx = default_context(0)
     lib = ctx.lib
@@ -122,6 +143,9 @@ def main() -> None:
             torch.cuda.synchronize()
             ts.append(e0.elapsed_time(e1))
         res["stack_step_ms"] = float(np.median(ts))
+        if args.kernels:
+            print(json.dumps({"bench": "dejavu_ffn_stack_kernels", "tokens": T, "layers": args.layers,
+                              "us_per_layer": _stack_kernels(stack, hs, args.reps, args.layers)}), flush=True)
         del stack
         mlp_bytes = T * k * HID * 2 * 3  # gate, up and down rows gathered per token (bf16)
         step_us = res["layer"] * args.layers
