@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
         const int kmax = (int)round_up(min(EPT, a.d - k0), VE);
         const uint4* rowp = reinterpret_cast<const uint4*>(mt + l * PITCH);
         const float4* x4 = reinterpret_cast<const float4*>(xs + k0);
-        for (int kb = 0; kb < kmax; kb += VE) {
+        auto dot8 = [&](int kb) {  // VE elements from k0 + kb, in order
           const uint4 raw = rowp[kb / VE];
           const W* e = reinterpret_cast<const W*>(&raw);
           float xv[VE];
@@ -278,6 +278,12 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
           }
 #pragma unroll
           for (int u = 0; u < VE; ++u) acc = __fadd_rn(acc, __fmul_rn(to_f(e[u]), xv[u]));
+        };
+        if (kmax == EPT) {  // a whole tile (C1/C2 rows: one tile of 128 / 256 elements): unrolled
+#pragma unroll
+          for (int kb = 0; kb < EPT; kb += VE) dot8(kb);
+        } else {
+          for (int kb = 0; kb < kmax; kb += VE) dot8(kb);
         }
       }
       __syncwarp();
@@ -321,7 +327,7 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
     for (int c = 0; c < CPL; ++c) part[c] = 0.0f;
     // lane l owns the CPL consecutive columns l*CPL.. of the tile (columns
     // beyond d see zero row padding and are not written back)
-    for (int r = 0; r < nw; ++r) {
+    auto dx_row = [&](int r) {
       const float lr = __shfl_sync(FULL, lgv, r);
       const unsigned char* rowb = mt + r * PITCH + l * CPL * (int)sizeof(W);
       if constexpr (sizeof(W) == 2 && CPL == 4) {
@@ -334,6 +340,12 @@ __global__ void __launch_bounds__(RM_RPB) rm_forward_kernel(RmArgs a) {
 #pragma unroll
         for (int c = 0; c < CPL; ++c) part[c] = fmaf(lr, to_f(rowp[c]), part[c]);
       }
+    };
+    if (nw == 32) {  // a full warp of rows: unrolled (constant shuffle lanes and offsets)
+#pragma unroll
+      for (int r = 0; r < 32; ++r) dx_row(r);
+    } else {
+      for (int r = 0; r < nw; ++r) dx_row(r);
     }
 #pragma unroll
     for (int c = 0; c < CPL; ++c) wpart[w * EPT + l * CPL + c] = part[c];
