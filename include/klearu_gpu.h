@@ -588,6 +588,31 @@ KL_API kl_status kl_net_create_sharded(kl_ctx_t ctx, const kl_net_config* cfg_ho
  * unsharded network). */
 KL_API kl_status kl_net_shard_info(kl_net_t net, int* rank_host, int* nranks_host, uint32_t* id_base_host,
                             int* num_local_host);
+/* Failure detection of a sharded network.  The reference has no counterpart:
+ * its Network runs in one process (net.rs:10-173) and reports failures by
+ * panicking (error.rs:3-33 is never returned by it).
+ *
+ * kl_net_set_comm_timeout: 0 (the default) keeps plain blocking waits.  With a
+ * timeout, every wait of this net that depends on other ranks (kl_net_sync,
+ * a train step's host loss read, a sharded forward or predict_top_k, destroy)
+ * polls the net's streams and the communicator's asynchronous error.  A
+ * communicator error returns KL_ENCCL, and no progress within timeout_ms
+ * returns KL_ETIMEOUT; both abort the communicator (the waiting collectives
+ * then return).  Every later call that needs the communicator returns
+ * KL_ENCCL; recreate the network (from a checkpoint) to continue.  Choose a
+ * timeout well above the longest step, including a table rebuild.
+ *
+ * kl_net_sync: waits for this net's work (bounded as above) and reports
+ * device-side faults, like kl_ctx_sync.  After an abort it still waits for
+ * the drained queue (KL_ETIMEOUT if the abort left work pending), so the
+ * net's state can be read back.
+ *
+ * kl_net_comm_abort: aborts the communicator now, for a caller whose own
+ * health check (a heartbeat over the process group's store) found a rank
+ * missing between steps.  A no-op on an unsharded network. */
+KL_API kl_status kl_net_set_comm_timeout(kl_net_t net, int timeout_ms);
+KL_API kl_status kl_net_sync(kl_net_t net);
+KL_API kl_status kl_net_comm_abort(kl_net_t net);
 /* The hidden layer's feature rows [first, first + count) whose Adam moments
  * this rank updates (every feature of an unsharded network).  In
  * kl_net_get_layer(0)'s [neuron][feature] layout these are columns; the

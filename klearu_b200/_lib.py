@@ -143,6 +143,9 @@ _PROTOS = {
     "kl_net_create_sharded": (_S, [_H, C.POINTER(NetConfigC), _P, _P, C.c_int, C.c_int, C.POINTER(_H)]),
     "kl_net_shard_info": (_S, [_H, _P, _P, _P, _P]),
     "kl_net_owned_features": (_S, [_H, _P, _P]),
+    "kl_net_set_comm_timeout": (_S, [_H, C.c_int]),
+    "kl_net_sync": (_S, [_H]),
+    "kl_net_comm_abort": (_S, [_H]),
     "kl_adaptive_create": (_S, [_H, C.c_uint64, C.c_uint64, C.c_float, C.c_float, C.POINTER(_H)]),
     "kl_predictor_create": (_S, [_H, C.c_int, C.c_int, C.c_int, _P, _P, _P, _P, C.POINTER(_H)]),
     "kl_predictor_destroy": (_S, [_H]),

@@ -526,6 +526,21 @@ class Network:
         check(self.lib.kl_net_shard_info(self.h, C.byref(r), C.byref(n), C.byref(base), C.byref(nl)))
         return r.value, n.value, base.value, nl.value
 
+    # -- failure detection of a sharded network ----------------------------
+    def set_comm_timeout(self, timeout_ms: int) -> None:
+        """Bound every wait that depends on other ranks by ``timeout_ms``
+        (0: plain blocking waits).  A wait that runs out raises KL_ETIMEOUT, a
+        communicator error KL_ENCCL; both abort the communicator."""
+        check(self.lib.kl_net_set_comm_timeout(self.h, int(timeout_ms)), self.ctx.h, "kl_net_set_comm_timeout")
+
+    def sync(self) -> None:
+        """Wait for this network's queued work and report device faults."""
+        check(self.lib.kl_net_sync(self.h), self.ctx.h, "kl_net_sync")
+
+    def comm_abort(self) -> None:
+        """Abort the communicator (a peer rank is known to be gone)."""
+        check(self.lib.kl_net_comm_abort(self.h), self.ctx.h, "kl_net_comm_abort")
+
     @property
     def step(self) -> int:
         s, n, c = C.c_uint64(), C.c_uint64(), C.c_uint64()
@@ -562,7 +577,7 @@ class Network:
 
         With ``loss_out`` None the call waits for the step and returns the mean
         loss.  Otherwise ``loss_out`` is a 1-element pinned float32 CPU tensor
-        that receives the loss in stream order (valid after ``ctx.sync()``), and
+        that receives the loss in stream order (valid after ``sync()``), and
         the call returns None without waiting, so consecutive calls overlap the
         next batch's upload with the current step."""
         arrs = [np.ascontiguousarray(getattr(hb, k)) for k in ("rowptr", "idx", "val", "label_ptr", "labels")]
@@ -573,7 +588,7 @@ class Network:
             out = torch.zeros(1, dtype=torch.float32).pin_memory()
             check(self.lib.kl_net_train_step_host(self.h, C.byref(c), float(lr), mode, out.data_ptr()),
                   self.ctx.h, "kl_net_train_step_host")
-            self.ctx.sync()
+            self.sync()
             return float(out[0])
         check(self.lib.kl_net_train_step_host(self.h, C.byref(c), float(lr), mode, loss_out.data_ptr()),
               self.ctx.h, "kl_net_train_step_host")
@@ -586,7 +601,7 @@ class Network:
             out = torch.zeros(1, dtype=torch.float32).pin_memory()
             check(self.lib.kl_net_train_step_host(self.h, C.byref(b), float(lr), mode, out.data_ptr()),
                   self.ctx.h, "kl_net_train_step_host")
-            self.ctx.sync()
+            self.sync()
             return float(out[0])
         check(self.lib.kl_net_train_step_host(self.h, C.byref(b), float(lr), mode, loss_out.data_ptr()),
               self.ctx.h, "kl_net_train_step_host")
@@ -605,7 +620,7 @@ class Network:
             self.train_step_batch_host(b, lr, mode, loss_out=outs[n])
             # the iterator reuses its buffers two draws later; the library copied them at the call
             n += 1
-        self.ctx.sync()
+        self.sync()
         return [float(o[0]) for o in outs[:n]]
 
     # -- inference --------------------------------------------------------
@@ -636,7 +651,7 @@ class Network:
         act = torch.empty(rows * stride, dtype=torch.float32, device=self._dev)
         check(self.lib.kl_net_layer_output(self.h, layer, _ptr(ids), _ptr(cnt), _ptr(pre), _ptr(act)),
               self.ctx.h, "kl_net_layer_output")
-        self.ctx.sync()
+        self.sync()
         ids = ids.cpu().numpy().view(np.uint32).reshape(rows, stride)
         pre = pre.cpu().numpy().reshape(rows, stride)
         act = act.cpu().numpy().reshape(rows, stride)
@@ -658,7 +673,7 @@ class Network:
         sc = torch.empty((db.host.batch, k), dtype=torch.float32, device=self._dev)
         check(self.lib.kl_net_predict_topk(self.h, C.byref(db.c), k, _ptr(ids), _ptr(sc)), self.ctx.h,
               "kl_net_predict_topk")
-        self.ctx.sync()
+        self.sync()
         return ids.cpu().numpy().view(np.uint32), sc.cpu().numpy()
 
     def predict_top_k(self, x, k: int):  # net.rs:159-173

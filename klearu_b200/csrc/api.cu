@@ -23,6 +23,7 @@
 #include <functional>
 
 #include "engine.h"
+#include "watchdog.h"
 
 using namespace kl;
 
@@ -1216,6 +1217,71 @@ struct kl_net_s {
   // neuron sharding of the output layer (kl_net_create_sharded)
   int rank = 0, nranks = 1;
   ncclComm_t comm = nullptr;
+  // Failure detection of a sharded net (kl_net_set_comm_timeout).  With a
+  // timeout set, the net's synchronising waits poll the streams and the
+  // communicator's asynchronous error instead of blocking; a failed or timed-out
+  // wait aborts the communicator, and every later call that needs it returns
+  // KL_ENCCL.  stuck: the streams had not drained after the abort, so the
+  // destructor must not wait on them.
+  int comm_timeout_ms = 0;
+  bool comm_aborted = false, stuck = false;
+  std::string comm_abort_why;
+  void require_comm() {
+    if (comm_aborted) raise(KL_ENCCL, "the communicator was aborted (" + comm_abort_why + "); recreate the network");
+  }
+  void abort_comm(const std::string& why) {
+    if (comm) ncclCommAbort(comm);
+    comm = nullptr;
+    comm_aborted = true;
+    comm_abort_why = why;
+  }
+  bool streams_ready() {
+    const cudaStream_t ss[4] = {ctx->stream, comm_stream, side_stream, copy_stream};
+    for (int i = 0; i < 4; ++i) {
+      if (i > 0 && !ss[i]) continue;  // streams the net has not created yet
+      const cudaError_t e = cudaStreamQuery(ss[i]);
+      if (e == cudaErrorNotReady) return false;
+      ck(e, "stream query");
+    }
+    return true;
+  }
+  // Before a host read that would block inside CUDA (a copy into pageable
+  // memory, an event wait): the bounded wait, when one is set.
+  void guard_blocking_read(const void* host_dst) {
+    if (nranks <= 1 || comm_timeout_ms <= 0 || comm_aborted) return;
+    if (host_dst) {
+      cudaPointerAttributes a{};
+      if (cudaPointerGetAttributes(&a, host_dst) == cudaSuccess && a.type == cudaMemoryTypeHost) return;
+      cudaGetLastError();
+    }
+    wait_streams();
+  }
+  // Wait for the net's streams; on a sharded net with a timeout, a bounded
+  // wait that aborts the communicator on its error or at the deadline.
+  void wait_streams() {
+    if (nranks <= 1 || comm_timeout_ms <= 0 || comm_aborted) {
+      ck(cudaStreamSynchronize(ctx->stream), "sync");
+      return;
+    }
+    const WaitReport r = bounded_wait(
+        [&] { return streams_ready(); },
+        [&] {
+          ncclResult_t a = ncclSuccess;
+          const ncclResult_t q = ncclCommGetAsyncError(comm, &a);
+          if (q != ncclSuccess) return (int)q;
+          return (a == ncclSuccess || a == ncclInProgress) ? 0 : (int)a;
+        },
+        [&] { abort_comm(""); }, wall_ms, sleep_ms, (double)comm_timeout_ms, (double)comm_timeout_ms);
+    if (r.result == WaitResult::kDone) return;
+    stuck = !r.drained;
+    const std::string tail = r.drained ? "" : "; device work was still pending after the abort";
+    if (r.result == WaitResult::kCommError) {
+      comm_abort_why = std::string("NCCL error: ") + ncclGetErrorString((ncclResult_t)r.comm_error);
+      raise(KL_ENCCL, "a peer rank failed (" + comm_abort_why + "); communicator aborted" + tail);
+    }
+    comm_abort_why = "no progress within " + std::to_string(comm_timeout_ms) + " ms";
+    raise(KL_ETIMEOUT, "sharded step made " + comm_abort_why + " (a peer rank is missing?); communicator aborted" + tail);
+  }
   int rank_batch = 0;             // examples per rank per step (cfg max_batch)
   int nnz_cap = 0, lab_cap = 0;   // per-rank capacities of the batch exchange
   ShardLayout shl{};
@@ -2353,7 +2419,13 @@ extern "C" kl_status kl_net_destroy(kl_net_t net) {
   if (!net) return KL_EINVAL;
   {
     DeviceGuard g(net->ctx->device);
-    cudaStreamSynchronize(net->ctx->stream);
+    try {
+      net->wait_streams();
+    } catch (const KlError&) {
+    }
+    // A device queue that an aborted communicator left hung would block the
+    // frees (cudaFree synchronises): the net is leaked instead.
+    if (net->stuck) return KL_OK;
     delete net;
   }
   return KL_OK;
@@ -2372,6 +2444,7 @@ static void train_step_body(kl_net_t net, const kl_batch* b, double lr, int mode
     // when it calls with the same code, raise here.
     require(b != nullptr, "batch is NULL");
     support(mode == KL_MODE_BATCHED, "sharded net: only KL_MODE_BATCHED train steps");
+    net->require_comm();
     net->upload_opt(lr);
     net->train_sharded(*b, lr);
     launch_loss_final(net->loss_acc.as<float>(), net->rank_batch * net->nranks, loss, net->loss_acc.as<float>(), st);
@@ -2432,6 +2505,7 @@ extern "C" kl_status kl_net_train_step(kl_net_t net, const kl_batch* b, double l
   KL_API_BEGIN(net->ctx)
   train_step_body(net, b, lr, mode, loss);
   if (loss_host) {
+    if (net->nranks > 1) net->wait_streams();  // bounded when a comm timeout is set
     ck(cudaMemcpyAsync(loss_host, net->loss_acc.p, 4, cudaMemcpyDeviceToHost, ctx__->stream), "loss copy");
     check_device_errors(ctx__);
   }
@@ -2453,6 +2527,7 @@ extern "C" kl_status kl_net_train_step_host(kl_net_t net, const kl_batch* hb, do
     kl_batch bad{};
     bad.batch = hb->batch;
     train_step_body(net, &bad, lr, mode, nullptr);
+    if (loss_host) net->guard_blocking_read(loss_host);
     if (loss_host) ck(cudaMemcpyAsync(loss_host, net->loss_acc.p, 4, cudaMemcpyDeviceToHost, ctx__->stream), "loss copy");
     return KL_OK;
   }
@@ -2481,6 +2556,7 @@ extern "C" kl_status kl_net_train_step_host(kl_net_t net, const kl_batch* hb, do
   net->hnext ^= 1;
   ck(cudaEventSynchronize(h.h2d), "event sync");  // the slot's previous upload has left the pinned buffer
   if (total > h.cap) {
+    net->guard_blocking_read(nullptr);  // h.used follows a step that waits on peers
     ck(cudaEventSynchronize(h.used), "event sync");
     if (h.pinned) ck(cudaFreeHost(h.pinned), "cudaFreeHost");
     h.pinned = nullptr;
@@ -2517,6 +2593,7 @@ extern "C" kl_status kl_net_train_step_host(kl_net_t net, const kl_batch* hb, do
   db.nlabels = nlab;
   train_step_body(net, &db, lr, mode, nullptr);
   ck(cudaEventRecord(h.used, st), "event");
+  if (loss_host) net->guard_blocking_read(loss_host);  // pinned memory: no wait
   if (loss_host) ck(cudaMemcpyAsync(loss_host, net->loss_acc.p, 4, cudaMemcpyDeviceToHost, st), "loss copy");
   KL_API_END
 }
@@ -2526,7 +2603,9 @@ extern "C" kl_status kl_net_forward(kl_net_t net, const kl_batch* b) {
   KL_API_BEGIN(net->ctx)
   if (net->nranks > 1) {
     require(b != nullptr, "forward: null batch");
+    net->require_comm();
     net->sharded_forward(*b, false);
+    net->wait_streams();
     check_device_errors(net->ctx);
     return KL_OK;
   }
@@ -2574,6 +2653,7 @@ extern "C" kl_status kl_net_predict_topk(kl_net_t net, const kl_batch* b, int k,
     const int64_t Ntot = net->cfg.layers[net->cfg.num_layers - 1].num_neurons;
     support(P <= 64, "sharded predict_topk: at most 64 ranks");
     require(k <= Ntot / P, "sharded predict_topk: k must be <= num_neurons / nranks");
+    net->require_comm();
     net->sharded_forward(*b, false);
     if (k == 0) return KL_OK;
     cudaStream_t st = ctx__->stream;
@@ -2591,7 +2671,13 @@ extern "C" kl_status kl_net_predict_topk(kl_net_t net, const kl_batch* b, int k,
     launch_shard_topk_merge(aids.as<uint32_t>(), asc.as<float>(), P, PB, k, Ntot, net->rank * B, B, top_ids,
                             top_scores, st);
     ck_launch("top-k merge");
-    ck(cudaStreamSynchronize(st), "sync");  // the scratch is freed on return
+    try {
+      net->wait_streams();  // the scratch is freed on return
+    } catch (const KlError&) {
+      if (net->stuck)  // hung device work may still use the scratch: leak it
+        for (DBuf* d : {&lids, &lsc, &aids, &asc}) d->p = nullptr;
+      throw;
+    }
     check_device_errors(net->ctx);
     return KL_OK;
   }
@@ -3040,6 +3126,26 @@ extern "C" kl_status kl_net_owned_features(kl_net_t net, uint32_t* first, uint32
   if (!net) return KL_EINVAL;
   if (first) *first = (uint32_t)net->layers[0]->f0;
   if (count) *count = (uint32_t)net->layers[0]->nf;
+  return KL_OK;
+}
+extern "C" kl_status kl_net_set_comm_timeout(kl_net_t net, int timeout_ms) {
+  if (!net || timeout_ms < 0) return KL_EINVAL;
+  net->comm_timeout_ms = timeout_ms;
+  return KL_OK;
+}
+extern "C" kl_status kl_net_sync(kl_net_t net) {
+  if (!net) return KL_EINVAL;
+  KL_API_BEGIN(net->ctx)
+  if (net->stuck) raise(KL_ETIMEOUT, "device work was still pending after the communicator abort");
+  net->wait_streams();
+  check_device_errors(net->ctx);
+  KL_API_END
+}
+extern "C" kl_status kl_net_comm_abort(kl_net_t net) {
+  if (!net) return KL_EINVAL;
+  if (net->nranks <= 1) return KL_OK;
+  DeviceGuard g(net->ctx->device);
+  if (!net->comm_aborted) net->abort_comm("aborted by the caller");
   return KL_OK;
 }
 extern "C" kl_status kl_net_shard_info(kl_net_t net, int* rank_host, int* nranks_host, uint32_t* id_base_host,

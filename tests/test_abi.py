@@ -39,6 +39,9 @@ def test_abi_version_and_null_handles():
     assert lib.kl_index_destroy(None) == _lib.KL_EINVAL
     assert lib.kl_net_destroy(None) == _lib.KL_EINVAL
     assert lib.kl_net_train_step(None, None, 0.1, 0, None, None) == _lib.KL_EINVAL
+    assert lib.kl_net_set_comm_timeout(None, 1000) == _lib.KL_EINVAL
+    assert lib.kl_net_sync(None) == _lib.KL_EINVAL
+    assert lib.kl_net_comm_abort(None) == _lib.KL_EINVAL
     assert isinstance(lib.kl_last_error(None), bytes)  # this thread's last error (context-free calls)
 
 

@@ -292,3 +292,89 @@ def test_sharded_fault_is_raised_on_every_rank():
         for code, want, moved in got[r]:
             assert code == want, (r, got[r])
             assert not moved, (r, got[r])
+
+
+def _leave_worker(rank, world, port, out):
+    """Rank 1 leaves between steps (nothing of it in flight), announced through
+    the heartbeat.  Rank 0 must learn of it before launching its next step,
+    abort its communicator with nothing in flight, and from then on get
+    KL_ENCCL from every call that needs the communicator, without blocking."""
+    import datetime
+    import time
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    import torch.distributed as dist
+
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=60))
+    try:
+        from klearu_b200 import _lib
+        from klearu_b200 import synthetic as S
+        from klearu_b200.core import Context, Network
+        from klearu_b200.dist import Heartbeat, RankFailure, rank_slice
+
+        lib = _lib.load()
+        if rank == 0:
+            buf = __import__("ctypes").create_string_buffer(lib.kl_dist_unique_id_size())
+            _lib.check(lib.kl_dist_get_unique_id(buf))
+            store.set("uid", bytes(buf.raw))
+        uid = store.get("uid")
+        cfg = _cfg()
+        net = Network(cfg, S.make_init(cfg, 42), weight_dtype="f32", max_batch=24, ctx=Context(rank),
+                      shard=(uid, rank, world))
+        net.set_comm_timeout(20000)
+        hb = Heartbeat(store, rank, world, timeout_s=20.0)
+        gen = S.XcGenerator(2000, 5000, seed=3, mean_nnz=20)
+        events = []
+        for step in range(4):
+            hb.check(step)
+            hb_batch = rank_slice(gen.batch(24 * world), rank, world)
+            net.train_step_host(hb_batch, 1e-3)
+            if rank == 1 and step == 1:
+                net.sync()
+                hb.leave()
+                hb.beat()
+                t0 = time.monotonic()  # leave once rank 0 has finished step 1 too
+                while hb._count("beat/0") < 2 and time.monotonic() - t0 < 60:
+                    time.sleep(0.01)
+                net.comm_abort()
+                events.append("left")
+                break
+            hb.beat()
+            events.append(f"step{step}")
+    except RankFailure as e:
+        events.append(f"failure {e.ranks} {e.reason} {e.step}")
+        net.sync()
+        net.comm_abort()
+        for call in (lambda: net.train_step_host(hb_batch, 1e-3), lambda: net.forward_batch(_examples(hb_batch))):
+            try:
+                call()
+                events.append("ran")
+            except _lib.KlError as k:
+                events.append(_lib.STATUS_NAMES[k.status])
+        net.sync()  # the drained queue still answers
+        events.append("synced")
+    except Exception:
+        import traceback
+
+        events = traceback.format_exc()
+    out.put((rank, events))
+    if rank == 0:
+        time.sleep(1.0)  # the store's server lives in rank 0
+
+
+def test_sharded_rank_leaving_between_steps_is_detected():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_leave_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=240) for _ in range(2))
+    for p in ps:
+        p.join(120)
+        assert p.exitcode == 0
+    assert got[1] == ["step0", "left"], got[1]
+    assert got[0] == ["step0", "step1", "failure [1] left 2", "KL_ENCCL", "KL_ENCCL", "synced"], got[0]
