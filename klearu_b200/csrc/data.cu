@@ -552,6 +552,7 @@ extern "C" kl_status kl_dataset_from_csr(const int64_t* rowptr_host, const uint3
 }
 
 extern "C" kl_status kl_dataset_destroy(kl_dataset_t ds) {
+  if (!ds) return KL_EINVAL;  // as every other destroy call
   delete ds;
   return KL_OK;
 }
@@ -654,6 +655,7 @@ extern "C" kl_status kl_batch_iter_next(kl_batch_iter_t it, kl_batch* batch_host
 }
 
 extern "C" kl_status kl_batch_iter_destroy(kl_batch_iter_t it) {
+  if (!it) return KL_EINVAL;
   delete it;
   return KL_OK;
 }
