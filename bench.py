@@ -2,7 +2,7 @@
 layer at 1/2/4/8 B200, with the dominant kernel's fraction of HBM peak.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c1|c0|c2]
+                    [--config c1|c0|c2|c3|c4]
 
 One step = one batched train step (hash, probe, active-row forward + loss +
 input gradient, segmented gradient reduction + lazy Adam on both layers) over
@@ -11,7 +11,9 @@ one batch of synthetic examples.  Prints ONE JSON line on rank 0.
 Workloads (``--config``): c1 (default) is the 670K-way extreme-classification
 net (135909 -> 128 -> 670091, B=256 per GPU, weak scaling); c0 the README MLP
 (784 -> 1024 -> 10 softmax, B=128); c2 the 3.1M-way net (hidden 256, SimHash
-K9 L50 reservoir) at a fixed global batch of 1024 (strong scaling).
+K9 L50 reservoir) at a fixed global batch of 1024 (strong scaling).  c3 (the
+Deja Vu sparse FFN) and c4 (the LSH index) run the package's micro-benchmarks
+(klearu_b200.bench_dejavu / bench_index) and add their CPU baselines.
 
 * ``value``: samples/s of the whole job with the batches already resident in
   HBM, timed with CUDA events (max over ranks).
@@ -67,7 +69,7 @@ def parse():
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--config", default="c1", choices=["c1", "c0", "c2"])
+    p.add_argument("--config", default="c1", choices=["c1", "c0", "c2", "c3", "c4"])
     p.add_argument("--batch", type=int, default=0, help="examples per GPU (0: the config's)")
     p.add_argument("--pool", type=int, default=8, help="distinct resident batches cycled through")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -75,7 +77,7 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-parity", action="store_true")
     p.add_argument("--no-exact", action="store_true")
-    return p.parse_args()
+    return p.parse_known_args()
 
 
 class Workload:
@@ -207,6 +209,99 @@ def cpu_baseline(wl: Workload, seconds, threads, batch=64):
                       f"(f32, dense inputs as the reference), {t:.1f} s timed; network build {build_s:.1f} s"}
 
 
+def run_microbench(args, extra):
+    """``--config c3`` (Deja Vu sparse FFN) and ``--config c4`` (LSH index):
+    the GPU micro-benchmark of the package (its JSON lines; arguments after
+    the known ones go to it), then the CPU restatement of the reference on a
+    bounded sample of the same workload, one more JSON line with
+    ``"impl": "cpu_baseline"``.  Seeded synthetic data."""
+    import torch
+
+    if args.impl != "reference" and torch.cuda.is_available():
+        if args.config == "c3":
+            from klearu_b200 import bench_dejavu as mb
+        else:
+            from klearu_b200 import bench_index as mb
+        mb.main(extra)
+    if not args.no_cpu_baseline:
+        line = cpu_microbench_c3() if args.config == "c3" else cpu_microbench_c4()
+        print(json.dumps(line), flush=True)
+
+
+def cpu_microbench_c3():
+    """One C3 layer for one token on one host core: the reference's predictor
+    (4096 -> 1000 ReLU -> 11008 sigmoid, top 1101) and sparse SwiGLU MLP
+    (mlp_predictor.rs:102-132, sparse_mlp.rs:4-37), restated in oracle/."""
+    import oracle
+
+    hid, inter, rank_ = 4096, 11008, 1000
+    k = math.ceil(0.1 * inter)
+    rng = np.random.default_rng(5)
+
+    def w(*shape):
+        return (0.02 * rng.standard_normal(shape)).astype(np.float32)
+
+    w1, w2 = w(rank_, hid), w(inter, rank_)
+    b1, b2 = np.zeros(rank_, np.float32), np.zeros(inter, np.float32)
+    gate, up, down = w(inter, hid), w(inter, hid), w(hid, inter)
+    x = rng.standard_normal(hid).astype(np.float32)
+    ts = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        sel = oracle.pred_topk(oracle.pred_predict(w1, b1, w2, b2, x)[0], k)
+        t1 = time.perf_counter()
+        oracle.sparse_mlp(gate, up, down, None, x, sel)
+        t2 = time.perf_counter()
+        ts.append((t1 - t0, t2 - t1))
+    sel_s, mlp_s = (statistics.median(v) for v in zip(*ts))
+    return {"impl": "cpu_baseline", "bench": "dejavu_sparse_ffn", "kind": "port", "cores": 1,
+            "tokens": 1, "predictor_select_ms": sel_s * 1e3, "sparse_mlp_ms": mlp_s * 1e3,
+            "layer_ms": (sel_s + mlp_s) * 1e3, "tokens_per_s_32_layers": 1 / ((sel_s + mlp_s) * 32),
+            "sample": "one layer, one token, median of 3 (CPU restatement of klearu-dejavu / klearu-llm)"}
+
+
+def cpu_microbench_c4(rows=20000, dim=128, nq=256):
+    """The C4 index workload on a bounded sample: rebuild of `rows` unit-norm
+    Gaussian rows (bf16-rounded) and query_union of `nq` queries (half near
+    duplicates), SimHash K6 L50 and DWTA K8 L100, FIFO and reservoir, on one
+    host core through the CPU restatement of lsh/index.rs."""
+    import oracle
+    from klearu_b200 import params as P
+    from klearu_b200.config import BucketType, HashFunctionType as HF
+
+    rng = np.random.default_rng(11)
+
+    def unit(a):
+        return (a / np.maximum(np.linalg.norm(a, axis=1, keepdims=True), 1e-12)).astype(np.float32)
+
+    def bf16(a):  # round to nearest even bf16, back to f32
+        u = a.view(np.uint32).astype(np.uint64)
+        u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+        return u.astype(np.uint32).view(np.float32)
+
+    R = bf16(unit(rng.standard_normal((rows, dim)).astype(np.float32)))
+    pick = rng.integers(0, rows, nq // 2)
+    Q = np.concatenate([unit(R[pick] + 0.05 * rng.standard_normal((nq // 2, dim))),
+                        unit(rng.standard_normal((nq - nq // 2, dim)))]).astype(np.float32)
+    res = []
+    for kind, K, L in ((HF.SimHash, 6, 50), (HF.DwtaHash, 8, 100)):
+        prm = P.hash_params(kind, np.random.default_rng(7), dim, K, L)
+        for bucket in (BucketType.Fifo, BucketType.Reservoir):
+            ix = oracle.Index(oracle.Hash(kind, dim, K, L, 8, prm), int(bucket), 128)
+            t0 = time.perf_counter()
+            ix.clear()
+            ix.insert(np.arange(rows, dtype=np.uint32), R)
+            t1 = time.perf_counter()
+            for q in Q:
+                ix.query(q)
+            t2 = time.perf_counter()
+            res.append({"hash": f"{HF(kind).name} K{K} L{L}", "bucket": BucketType(bucket).name,
+                        "rebuild_rows_per_s": rows / (t1 - t0), "queries_per_s": nq / (t2 - t1)})
+    return {"impl": "cpu_baseline", "bench": "lsh_index", "kind": "port", "cores": 1, "rows": rows, "dim": dim,
+            "queries": nq, "results": res,
+            "sample": f"{rows} rows and {nq} queries (CPU restatement of klearu-core lsh/index.rs)"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -316,7 +411,12 @@ def rebuild_schedule_cost(ms_rebuild: float, ms_step: float, base: int = 100, de
 
 
 def main():
-    args = parse()
+    args, extra = parse()
+    if args.config in ("c3", "c4"):
+        run_microbench(args, extra)
+        return
+    if extra:
+        raise SystemExit(f"unrecognised arguments: {' '.join(extra)}")
     if args.impl == "reference":
         run_reference(args)
         return

@@ -10,9 +10,9 @@ kl_sparse_mlp_forward on the selected neurons; the same step is also timed
 through kl_ffn_stack_decode (adds RMSNorm and the residual add per layer, one
 CUDA graph).  `--distinct` layers of
 weights are cycled (2 x 0.6 GB of bf16 > L2), so every layer reads its
-weights from HBM.  Timed with CUDA events after a warm-up.  The CPU oracle
-runs one layer for one token as a reference.  Prints one JSON line per token
-count.  Synthetic data.
+weights from HBM.  Timed with CUDA events after a warm-up.  Prints one JSON
+line per token count.  Synthetic data.  ``python bench.py --config c3`` runs
+this and adds the CPU baseline of one layer for one token.
 """
 
 from __future__ import annotations
@@ -21,7 +21,6 @@ import argparse
 import ctypes as C
 import json
 import math
-import time
 
 import numpy as np
 import torch
@@ -61,16 +60,16 @@ def _stack_kernels(stack, hs, reps: int, layers: int) -> dict:
     return {k: round(v / reps / layers, 2) for k, v in sorted(agg.items(), key=lambda kv: -kv[1])}
 
 
-def main() -> None:
+def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", default="1,16,64")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--distinct", type=int, default=2)
     ap.add_argument("--reps", type=int, default=5)
-    ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernels", action="store_true",
                     help="also print each kernel's device time inside the FFN stack (CUPTI through torch.profiler)")
-    args = ap.parse_args()
+    ap.add_argument("--no-cpu", action="store_true", help="ignored: bench.py --config c3 times the CPU baseline")
+    args = ap.parse_args(argv)
     ctx = default_context(0)
     lib = ctx.lib
     dev = "cuda:0"
@@ -81,14 +80,11 @@ def main() -> None:
         return (0.02 * torch.randn(*shape, device=dev, generator=g)).cpu().numpy()
 
     layers = []
-    host0 = None
     for i in range(args.distinct):
         w1, w2 = w(RANK, HID), w(INTER, RANK)
         b1, b2 = np.zeros(RANK, np.float32), np.zeros(INTER, np.float32)
         gate, up, down = w(INTER, HID), w(INTER, HID), w(HID, INTER)
         layers.append((SparsityPredictor(w1, b1, w2, b2, ctx=ctx), SparseMlp(gate, up, down, None, ctx=ctx)))
-        if i == 0 and not args.no_cpu:
-            host0 = (w1, b1, w2, b2, gate, up, down)
         del w1, w2, gate, up, down
     peak, peak_kind = _peak_gbs()
     pred_bytes = (RANK * HID + INTER * 1024) * 2  # bf16 predictor weights (K padded to 64)
@@ -161,19 +157,6 @@ def main() -> None:
                 "sparse_mlp_frac_of_hbm": mlp_bytes / (res["sparse_mlp"] * 1e-6) / 1e9 / peak,
                 "peak_gbs": peak, "peak_kind": peak_kind}
         print(json.dumps(line), flush=True)
-    if host0 is not None:
-        import oracle
-
-        w1, b1, w2, b2, gate, up, down = host0
-        xh = np.random.default_rng(1).standard_normal(HID).astype(np.float32)
-        t0 = time.perf_counter()
-        sel = oracle.pred_topk(oracle.pred_predict(w1, b1, w2, b2, xh)[0], k)
-        t1 = time.perf_counter()
-        oracle.sparse_mlp(gate, up, down, None, xh, sel)
-        t2 = time.perf_counter()
-        print(json.dumps({"bench": "dejavu_sparse_ffn_cpu_oracle", "tokens": 1, "cores": 1,
-                          "predictor_select_ms": (t1 - t0) * 1e3, "sparse_mlp_ms": (t2 - t1) * 1e3,
-                          "layer_ms": (t2 - t0) * 1e3, "tokens_per_s_32_layers": 1 / ((t2 - t0) * 32)}), flush=True)
 
 
 if __name__ == "__main__":

@@ -1,22 +1,21 @@
 """LSH index microbenchmark (the C4 workload: 1M-row index) on one B200.
 
-    python -m klearu_b200.bench_index [--rows 1000000] [--queries 4096] [--reps 5] [--cpu-rows 20000]
+    python -m klearu_b200.bench_index [--rows 1000000] [--queries 4096] [--reps 5]
 
 1M rows x 128 bf16 unit-norm Gaussian; SimHash K6 L50 and DWTA K8 L100, each
 with FIFO and reservoir buckets of capacity 128.  For each: a full rebuild
 (kl_index_rebuild, hash + ordered bucket fill) and query_union over 4096
 queries (2048 near-duplicates of indexed rows: row + N(0, 0.05^2) per
 dimension, renormalised; 2048 fresh unit Gaussians), both timed with CUDA
-events after a warm-up.  The CPU oracle's rebuild and query are timed on a
-bounded sample (`--cpu-rows` rows, 256 queries) for reference.  Prints one
-JSON line per configuration.  Synthetic data; no dataset items.
+events after a warm-up.  Prints one JSON line per configuration.  Synthetic
+data; no dataset items.  ``python bench.py --config c4`` runs this and adds
+the CPU baseline of the same workload.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
-import time
 
 import numpy as np
 import torch
@@ -31,14 +30,14 @@ def _unit(x: torch.Tensor) -> torch.Tensor:
     return x / x.norm(dim=1, keepdim=True).clamp_min(1e-12)
 
 
-def main() -> None:
+def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--rows", type=int, default=1_000_000)
     ap.add_argument("--dim", type=int, default=128)
     ap.add_argument("--queries", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=5)
-    ap.add_argument("--cpu-rows", type=int, default=20000)
-    args = ap.parse_args()
+    ap.add_argument("--cpu-rows", type=int, default=0, help="ignored: bench.py --config c4 times the CPU baseline")
+    args = ap.parse_args(argv)
     ctx = default_context(0)
     dev = "cuda:0"
     g = torch.Generator(device=dev).manual_seed(11)
@@ -69,19 +68,6 @@ def main() -> None:
             union = float(offs[-1].item()) / nq
             near_hit = float(np.mean([int(pick[i]) in set(ids[offs[i]:offs[i + 1]].cpu().numpy().tolist())
                                       for i in range(0, nq // 2, 64)]))
-            # CPU oracle on a bounded sample (test infrastructure, reported beside the GPU)
-            import oracle
-
-            ocfg = oracle.Index(oracle.Hash(kind, args.dim, K, L, 8, prm), int(bucket), 128)
-            sub = rows[: args.cpu_rows].float().cpu().numpy()
-            c0 = time.perf_counter()
-            ocfg.clear()
-            ocfg.insert(np.arange(len(sub), dtype=np.uint32), sub)
-            c1 = time.perf_counter()
-            qs = Q[:256].cpu().numpy()
-            for q in qs:
-                ocfg.query(q)
-            c2 = time.perf_counter()
             rb_seq = None
             if kind == HF.SimHash:
                 # the same rebuild with the reference's sequential projection sums
@@ -104,8 +90,6 @@ def main() -> None:
                 "rebuild_ms_sequential_projection": rb_seq,
                 "query_union_ms": q_ms, "queries_per_s": nq / (q_ms / 1e3), "mean_union": union,
                 "near_duplicate_self_hit": near_hit,
-                "cpu_oracle": {"rows": len(sub), "rebuild_rows_per_s": len(sub) / (c1 - c0),
-                               "queries_per_s": len(qs) / (c2 - c1), "threads": 1},
             }), flush=True)
             del ix
 
