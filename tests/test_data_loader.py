@@ -237,3 +237,23 @@ def test_batch_csr_contents():
                 assert np.array_equal(hb.idx[a:b], o[e][0]) and np.array_equal(hb.val[a:b], o[e][1])
                 c, d = hb.label_ptr[s], hb.label_ptr[s + 1]
                 assert list(hb.labels[c:d]) == o[e][2]
+
+
+def test_c1_shaped_text_parses_back_to_the_generator_stream():
+    """The loader bench's C1-shaped text (9 significant digits) parses back to
+    the example stream it was written from, bit for bit; ids shift down by one
+    only where the reference's 1-based detection fires (libsvm.rs:70-75: no
+    id 0 and a minimum of 1)."""
+    from klearu_b200.bench_loader import synthetic_text
+    from klearu_b200.synthetic import XcGenerator
+
+    n = 600
+    ds = LibSvmDataset.load_from_str(synthetic_text(n, seed=3), 135909, 670091, 4)
+    hb = XcGenerator(135909, 670091, seed=3).batch(n)
+    assert len(ds) == n
+    off = 1 if int(hb.idx.min()) == 1 else 0
+    assert np.array_equal(np.asarray(ds.rowptr), hb.rowptr)
+    assert np.array_equal(np.asarray(ds.idx), hb.idx - off)
+    assert np.array_equal(np.asarray(ds.val).view(np.uint32), hb.val.view(np.uint32))
+    assert np.array_equal(np.asarray(ds.label_ptr), hb.label_ptr)
+    assert np.array_equal(np.asarray(ds.labels), hb.labels)
