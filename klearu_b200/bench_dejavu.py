@@ -18,7 +18,6 @@ this and adds the CPU baseline of one layer for one token.
 from __future__ import annotations
 
 import argparse
-import ctypes as C
 import json
 import math
 

@@ -24,7 +24,6 @@ import json
 import os
 import time
 
-import numpy as np
 
 from .data import BatchIterator, LibSvmDataset
 from .synthetic import XcGenerator

@@ -12,7 +12,6 @@ trained network's layer.
 
 from __future__ import annotations
 
-import ctypes as C
 
 import numpy as np
 import torch

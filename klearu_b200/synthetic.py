@@ -20,7 +20,7 @@ import numpy as np
 
 from . import params as P
 from .config import (ActivationType, BucketType, HashFunctionType, LayerConfig, LshConfig, NetworkConfig,
-                     OptimizerType, SamplingType, SlideConfig)
+                     OptimizerType, SlideConfig)
 from .data import HostBatch
 
 

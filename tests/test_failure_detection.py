@@ -10,7 +10,6 @@ trapped).
   the survivor's next launch; healthy ranks pass every check.
 """
 
-import os
 import shutil
 import socket
 import subprocess
