@@ -3274,6 +3274,10 @@ extern "C" kl_status kl_index_query_batch_noalloc(kl_index_t ix, const float* X,
 struct kl_predictor_s {
   kl_ctx_t ctx;
   int in = 0, hid = 0, out = 0, ld_in = 0, ld_hid = 0;
+  // calls of at most this many tokens take the CUDA-core GEMV path; 0 (the
+  // default) keeps the tensor-core GEMM.  Set at creation from the
+  // environment variable KLEARU_PREDICTOR_GEMV_TOKENS (at most 4).
+  int gemv_max = 0;
   DBuf w1, b1, w2, b2, xs, xs2, P, h, sc;
 };
 
@@ -3315,6 +3319,16 @@ void upload_f32(kl_ctx_t ctx, DBuf& dst, const float* host, int64_t n) {
 
 void predictor_scores(kl_predictor_t p, const float* x, int T, float* scores, cudaStream_t st) {
   kl_ctx_t ctx = p->ctx;
+  if (T <= p->gemv_max && (size_t)T * std::max(p->ld_in, p->ld_hid) * 4 <= 200 * 1024) {
+    // a few tokens: one pass over each weight matrix on the CUDA cores (x staged in shared memory)
+    launch_gemv_linear(x, T, p->in, p->in, p->w1.as<__nv_bfloat16>(), p->hid, p->ld_in, p->b1.as<float>(), 0,
+                       p->h.as<float>(), p->hid, st);
+    ck_launch("predictor layer 1 (gemv)");
+    launch_gemv_linear(p->h.as<float>(), T, p->hid, p->hid, p->w2.as<__nv_bfloat16>(), p->out, p->ld_hid,
+                       p->b2.as<float>(), 1, scores, p->out, st);
+    ck_launch("predictor layer 2 (gemv)");
+    return;
+  }
   for (int t0 = 0; t0 < T; t0 += TC_LINEAR_MAX_T) {
     const int tn = std::min(TC_LINEAR_MAX_T, T - t0);
     // layer 1 reads x's pieces from xs and writes h's pieces to xs2 for layer 2
@@ -3371,6 +3385,8 @@ extern "C" kl_status kl_predictor_create(kl_ctx_t ctx, int input_dim, int hidden
   p->P.alloc(std::max(tc_linear_scratch_floats(hidden_dim, p->ld_in), tc_linear_scratch_floats(output_dim, p->ld_hid)) *
              4);
   p->h.alloc((size_t)TC_LINEAR_MAX_T * hidden_dim * 4);
+  if (const char* e = std::getenv("KLEARU_PREDICTOR_GEMV_TOKENS"))
+    p->gemv_max = std::max(0, std::min(std::atoi(e), gemv_linear_max_tokens()));
   ck(cudaStreamSynchronize(ctx->stream), "sync");
   *out = p.release();
   KL_API_END

@@ -201,6 +201,75 @@ __global__ void splitk_finish_kernel(const float* __restrict__ P, int splits, in
   }
 }
 
+// y[t][j] = act(x[t] . W[j] + bias[j]) for a few tokens (TT <= GV_TMAX) on the
+// CUDA cores: one warp per weight row, the row streamed once with 16-byte
+// loads (8 bf16 per lane per chunk, GV_UNROLL chunks in flight), each bf16
+// widened exactly by a 16-bit shift, f32 FMA accumulation, a shuffle-tree
+// reduction.  x is staged once per block in shared memory as f32 [TT][ldw]
+// (zero beyond d).  At one token the weight stream is the whole cost, so this
+// replaces the tensor-core GEMM, its split-K scratch and its finish pass.
+// act as in splitk_finish_kernel.
+constexpr int GV_TMAX = 4;
+constexpr int GV_WARPS = 4;
+constexpr int GV_UNROLL = 8;
+template <int TT>
+__global__ void __launch_bounds__(GV_WARPS * 32)
+    gemv_kernel(const float* __restrict__ x, int ldx, int d, const __nv_bfloat16* __restrict__ W, int ldw, int n,
+                const float* __restrict__ bias, int act, float* __restrict__ y, int ldy) {
+  extern __shared__ float4 gv_smem[];
+  float* xs = reinterpret_cast<float*>(gv_smem);
+  for (int i = threadIdx.x; i < TT * ldw; i += blockDim.x) {
+    const int t = i / ldw, c = i - t * ldw;
+    xs[i] = c < d ? x[(int64_t)t * ldx + c] : 0.0f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nch = ldw >> 3;  // 16-byte chunks per row (ldw is a multiple of 64)
+  for (int j = blockIdx.x * GV_WARPS + warp; j < n; j += gridDim.x * GV_WARPS) {
+    const uint4* wr = reinterpret_cast<const uint4*>(W + (int64_t)j * ldw);
+    float acc[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) acc[t] = 0.0f;
+    for (int c0 = lane; c0 < nch; c0 += 32 * GV_UNROLL) {
+      uint4 q[GV_UNROLL];
+#pragma unroll
+      for (int u = 0; u < GV_UNROLL; ++u) {
+        const int c = c0 + 32 * u;
+        q[u] = c < nch ? __ldg(wr + c) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < GV_UNROLL; ++u) {
+        const int c = c0 + 32 * u;
+        if (c >= nch) break;
+        const uint32_t wv[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          const float4* xv = reinterpret_cast<const float4*>(xs + (size_t)t * ldw + (size_t)c * 8);
+          const float4 a = xv[0], b = xv[1];
+          const float xe[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            acc[t] = fmaf(__uint_as_float(wv[h] << 16), xe[2 * h], acc[t]);
+            acc[t] = fmaf(__uint_as_float(wv[h] & 0xffff0000u), xe[2 * h + 1], acc[t]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      float v = acc[t];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) {
+        if (bias) v = __fadd_rn(v, bias[j]);
+        if (act == 0) v = fmaxf(v, 0.0f);
+        else if (act == 1) v = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+        y[(int64_t)t * ldy + j] = v;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // select_top_k (mlp_predictor.rs:126-132): the k largest scores of a row in
 // (score descending, index ascending) order -- the stable sort's order.  One
@@ -698,6 +767,29 @@ void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16
   const int lim = xs_next ? ld_next : n;
   splitk_finish_kernel<<<dim3((unsigned)ceil_div(lim, 256), T), 256, 0, st>>>(P, splits, ldp, bias, T, n, act, y, ldy,
                                                                             xs_next, ld_next);
+  count_launch();
+}
+
+int gemv_linear_max_tokens() { return GV_TMAX; }
+
+template <int TT>
+static void gemv_launch(const float* x, int ldx, int d, const __nv_bfloat16* W, int n, int ldw, const float* bias,
+                        int act, float* y, int ldy, cudaStream_t st) {
+  const size_t sm = (size_t)TT * ldw * 4;
+  static OncePerDevice attr;
+  attr([&] { cudaFuncSetAttribute(gemv_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); });
+  // enough warps to keep every SM's load queue full, and no more blocks than
+  // rows need (each block stages x once)
+  const int blocks = (int)std::min<int64_t>(ceil_div(n, GV_WARPS), (int64_t)sm_count() * 8);
+  gemv_kernel<TT><<<blocks, GV_WARPS * 32, sm, st>>>(x, ldx, d, W, ldw, n, bias, act, y, ldy);
+}
+
+void launch_gemv_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16* W, int n, int ldw,
+                        const float* bias, int act, float* y, int ldy, cudaStream_t st) {
+  if (T == 1) gemv_launch<1>(x, ldx, d, W, n, ldw, bias, act, y, ldy, st);
+  else if (T == 2) gemv_launch<2>(x, ldx, d, W, n, ldw, bias, act, y, ldy, st);
+  else if (T == 3) gemv_launch<3>(x, ldx, d, W, n, ldw, bias, act, y, ldy, st);
+  else gemv_launch<4>(x, ldx, d, W, n, ldw, bias, act, y, ldy, st);
   count_launch();
 }
 

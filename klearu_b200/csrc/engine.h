@@ -361,6 +361,11 @@ size_t tc_linear_scratch_floats(int n, int ldw);
 void launch_tc_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16* W, int n, int ldw,
                       const float* bias, int act, float* y, int ldy, __nv_bfloat16* xs, float* P,
                       __nv_bfloat16* xs_next, int ld_next, int* err, cudaStream_t st);
+// The same y for T <= gemv_linear_max_tokens() tokens on the CUDA cores (one
+// warp per weight row, f32 FMA sums); x [T][ldx] f32, no scratch.
+int gemv_linear_max_tokens();
+void launch_gemv_linear(const float* x, int T, int d, int ldx, const __nv_bfloat16* W, int n, int ldw,
+                        const float* bias, int act, float* y, int ldy, cudaStream_t st);
 // idx[t][0, k) = the k largest of scores[t][0, n) in (score desc, index asc)
 // order; scores non-negative; k <= n.
 // sorted: (score descending, index ascending); else the selected set in

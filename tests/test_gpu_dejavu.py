@@ -46,6 +46,34 @@ def test_predictor_scores_match_oracle(gpu_ctx, shape, T):
     assert err.max() < 1e-4, err.max()
 
 
+@pytest.mark.skipif(__import__("os").environ.get("KLEARU_TEST_PREDICTOR_GEMV") != "1",
+                    reason="opt-in CUDA-core predictor path (KLEARU_PREDICTOR_GEMV_TOKENS), run on request")
+@pytest.mark.parametrize("shape,T", [((96, 40, 200), 1), ((130, 70, 300), 3), ((4096, 1000, 11008), 1),
+                                     ((4096, 1000, 11008), 4)])
+def test_predictor_gemv_path_matches_oracle(gpu_ctx, monkeypatch, shape, T):
+    """The CUDA-core GEMV predictor path (a few tokens) within the same 1e-4
+    of the oracle as the tensor-core path, and its top-k equal to the oracle's
+    up to scores within that tolerance of the k-th one."""
+    d, hid, out = shape
+    rng = np.random.default_rng(d + 7 * T)
+    w1, b1, w2, b2 = predictor_weights(rng, d, hid, out, std=0.05 if d < 1000 else 0.02)
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    monkeypatch.setenv("KLEARU_PREDICTOR_GEMV_TOKENS", "4")
+    p = SparsityPredictor(w1, b1, w2, b2, ctx=gpu_ctx)
+    monkeypatch.delenv("KLEARU_PREDICTOR_GEMV_TOKENS")
+    got = p.predict(x).cpu().numpy()
+    ref = oracle.pred_predict(bf16(w1), b1, bf16(w2), b2, x)
+    err = np.abs(got - ref) / np.maximum(np.abs(ref), 1e-6)
+    assert err.max() < 1e-4, err.max()
+    k = max(1, out // 10)
+    idx = p.select_top_k(x, k).cpu().numpy()
+    for t in range(T):
+        r = oracle.pred_topk(ref[t], k)
+        kth = ref[t][r[-1]]
+        diff = set(idx[t].tolist()) ^ set(r.tolist())
+        assert all(abs(ref[t][i] - kth) <= 1e-4 * kth for i in diff), len(diff)
+
+
 def test_select_top_k_matches_oracle(gpu_ctx):
     d, hid, out, T, k = 4096, 1000, 11008, 4, 1101  # configs[3]: keep ceil(0.1 * 11008)
     rng = np.random.default_rng(7)
