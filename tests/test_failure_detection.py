@@ -107,3 +107,23 @@ def test_heartbeat_silent_rank():
     # the survivor launched step 2 before the silence showed: on the GPU that
     # step's collectives are what kl_net_set_comm_timeout bounds
     assert got[0] == ["step0", "step1", "step2", "failure [1] silent 3"]
+
+
+def test_heartbeat_single_rank_and_every(tmp_path):
+    """One rank never waits; with every=2 only even steps are checked."""
+    import torch.distributed as dist
+
+    from klearu_b200.dist import Heartbeat, RankFailure
+
+    store = dist.FileStore(str(tmp_path / "store"), 2)
+    Heartbeat(store, 0, 1, timeout_s=0.1).check(5)  # world of one: nothing to wait for
+    hb = Heartbeat(store, 0, 2, timeout_s=0.2, every=2)
+    hb.check(0)  # step 0 needs no finished steps
+    hb.beat()
+    hb.check(1)  # odd step: not checked, the silent peer is not noticed yet
+    hb.beat()
+    t0 = time.monotonic()
+    with pytest.raises(RankFailure) as e:
+        hb.check(2)
+    assert e.value.ranks == [1] and e.value.reason == "silent"
+    assert time.monotonic() - t0 >= 0.2
